@@ -1,0 +1,167 @@
+"""Decode metadata and per-rank state buffers (paged KV cache, conv state, SSM state).
+
+API-compatible with the reference's `harness/state.py` (`DecodeCtx` :17-28, `make_decode_ctx` :31-43,
+seeded generators :46-73, `RankStates` :76-87, `alloc_and_fill` :90-121, `full_states_for_reference`
+:124-135). Contents are keyed by (seed, GLOBAL head), so every layout's shard sees the same numbers and the
+fp32 oracle can rebuild the full states; the per-head seed offsets are the reference's, so the values agree
+with it. Differences, all deliberate:
+
+* Every seeded tensor is drawn on the CPU and then moved, so the values do not depend on the device's RNG
+  (the reference draws on the target device, whose CUDA generator gives other numbers than the CPU's).
+* The SSM state dtype is a parameter (fp32 by default, the precision the layer is specified in; the
+  reference hard-codes bf16).
+* The paged KV fill is one scatter per KV head instead of a Python loop over blocks.
+
+State line 0 is the null line: sequence b owns SSM/conv line ``state_idx[b]`` (1..B by default) and lines
+outside the batch are never touched by a decode step.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .config import FalconH1Dims
+from .sharding import RankPlan
+
+
+@dataclass
+class DecodeCtx:
+    B: int
+    c: int
+    kv_block: int
+    nblk: int
+    positions: torch.Tensor  # [B] int64, position of the new token (= context length c)
+    cu_q: torch.Tensor  # [B+1] int32
+    seqused_k: torch.Tensor  # [B] int32, keys per sequence after this step (= c+1)
+    block_table: torch.Tensor  # [B, nblk] int32
+    slot_mapping: torch.Tensor  # [B] int64, cache slot of the new token
+    state_idx: torch.Tensor  # [B] int32, SSM/conv line per sequence (line 0 is the null line)
+    max_k: int
+
+
+def make_decode_ctx(B: int, c: int, kv_block: int, device: torch.device) -> DecodeCtx:
+    nblk = math.ceil((c + 1) / kv_block)
+    table = torch.arange(B * nblk, dtype=torch.int32).view(B, nblk)
+    slot = table[:, c // kv_block].to(torch.int64) * kv_block + c % kv_block
+    return DecodeCtx(
+        B=B, c=c, kv_block=kv_block, nblk=nblk,
+        positions=torch.full((B,), c, dtype=torch.int64).to(device),
+        cu_q=torch.arange(B + 1, dtype=torch.int32).to(device),
+        seqused_k=torch.full((B,), c + 1, dtype=torch.int32).to(device),
+        block_table=table.to(device),
+        slot_mapping=slot.to(device),
+        state_idx=torch.arange(1, B + 1, dtype=torch.int32).to(device),
+        max_k=c + 1,
+    )
+
+
+def _cpu_gen(seed: int) -> torch.Generator:
+    return torch.Generator().manual_seed(seed)
+
+
+def full_kv_head(seed: int, h: int, B: int, c: int, hd: int, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """Keys and values of global KV head h at positions [0, c): two [B, c, hd] bf16 tensors (0.5 N(0,1))."""
+    g = _cpu_gen(seed * 7919 + 100003 * h + 1)
+    k = (torch.randn(B, c, hd, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, c, hd, generator=g) * 0.5).to(torch.bfloat16)
+    return k.to(device), v.to(device)
+
+
+def full_ssm_head(seed: int, j: int, B: int, p: int, N: int, device: torch.device,
+                  dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """SSM state of global Mamba head j: [B, p, N] (0.1 N(0,1)), rounded to ``dtype``."""
+    g = _cpu_gen(seed * 7919 + 200003 * j + 2)
+    return (torch.randn(B, p, N, generator=g) * 0.1).to(dtype).to(device)
+
+
+def full_conv_state(seed: int, dims: FalconH1Dims, B: int, device: torch.device) -> torch.Tensor:
+    """[B, d_conv-1, conv_rows] bf16 (0.5 N(0,1)), oldest position first."""
+    g = _cpu_gen(seed * 7919 + 300007)
+    return (torch.randn(B, dims.d_conv - 1, dims.conv_rows, generator=g) * 0.5).to(torch.bfloat16).to(device)
+
+
+def input_hidden(seed: int, B: int, H: int, device: torch.device) -> torch.Tensor:
+    g = _cpu_gen(seed * 7919 + 400009)
+    return torch.randn(B, H, generator=g).to(device=device, dtype=torch.bfloat16)
+
+
+def kv_cache_layout(num_blocks: int, block: int, nkv: int, hd: int) -> tuple[tuple[int, ...], str]:
+    """Paged KV layout: (num_blocks, nkv, block, 2*hd) with each token's key and value adjacent, so one
+    (block, head) page of 16 tokens is a single contiguous 8 KB run at hd=128."""
+    return (num_blocks, nkv, block, 2 * hd), "interleaved"
+
+
+def alloc_kv(num_blocks: int, block: int, nkv: int, hd: int, device: torch.device, dtype=torch.bfloat16):
+    """Returns (kv, key_cache, value_cache, kind); key/value caches are [nb, block, nkv, hd] strided views."""
+    shape, kind = kv_cache_layout(num_blocks, block, nkv, hd)
+    kv = torch.zeros(shape, device=device, dtype=dtype)
+    key_cache, value_cache = kv.transpose(1, 2).split(hd, dim=-1)
+    return kv, key_cache, value_cache, kind
+
+
+@dataclass
+class RankStates:
+    kv: torch.Tensor | None = None  # raw paged buffer [nb, nkv, block, 2*hd]
+    key_cache: torch.Tensor | None = None
+    value_cache: torch.Tensor | None = None
+    kv_kind: str = ""
+    conv_state: torch.Tensor | None = None  # [lines, d_conv-1, conv_rows_local] bf16
+    ssm_state: torch.Tensor | None = None  # [lines, nhr, p, N]
+
+    def bytes(self) -> dict[str, int]:
+        nb = lambda t: 0 if t is None else t.numel() * t.element_size()  # noqa: E731
+        return {"kv": nb(self.kv), "conv": nb(self.conv_state), "ssm": nb(self.ssm_state)}
+
+
+def fill_paged(cache: torch.Tensor, block_table: torch.Tensor, vals: torch.Tensor, kv_block: int, local_head: int) -> None:
+    """cache[table[b, t // blk], t % blk, local_head, :] = vals[b, t] for t < vals.shape[1]."""
+    B, c = vals.shape[:2]
+    if c == 0:
+        return
+    t = torch.arange(c, device=cache.device)
+    blocks = block_table.to(cache.device).long()[:, t // kv_block]  # [B, c]
+    offs = (t % kv_block).expand(B, c)
+    cache[blocks, offs, local_head] = vals.to(cache.device, cache.dtype)
+
+
+def alloc_and_fill(plan: RankPlan, dims: FalconH1Dims, ctx: DecodeCtx, seed: int, device: torch.device,
+                   ssm_dtype: torch.dtype = torch.float32) -> RankStates:
+    st = RankStates()
+    B, c = ctx.B, ctx.c
+    a = plan.attn
+    if a is not None:
+        nb = B * ctx.nblk + 1
+        st.kv, st.key_cache, st.value_cache, st.kv_kind = alloc_kv(nb, ctx.kv_block, len(a.kv_heads), dims.head_dim, device)
+        for li, h in enumerate(a.kv_heads):
+            k, v = full_kv_head(seed, h, B, c, dims.head_dim, torch.device("cpu"))
+            fill_paged(st.key_cache, ctx.block_table, k, ctx.kv_block, li)
+            fill_paged(st.value_cache, ctx.block_table, v, ctx.kv_block, li)
+            del k, v
+    s = plan.ssm
+    if s is not None:
+        nhr, p, N = len(s.heads), dims.mamba_head_dim, dims.d_state
+        rows_local = sum(r.stop - r.start for r in s.conv_rows)
+        conv = torch.zeros(B + 1, dims.d_conv - 1, rows_local, dtype=torch.bfloat16)
+        full_conv = full_conv_state(seed, dims, B, torch.device("cpu"))
+        conv[1:] = torch.cat([full_conv[:, :, r] for r in s.conv_rows], -1)
+        st.conv_state = conv.to(device)
+        st.ssm_state = torch.zeros(B + 1, nhr, p, N, device=device, dtype=ssm_dtype)
+        for li, j in enumerate(s.heads):
+            st.ssm_state[1:, li] = full_ssm_head(seed, j, B, p, N, torch.device("cpu"), ssm_dtype).to(device)
+    return st
+
+
+def full_states_for_reference(dims: FalconH1Dims, B: int, c: int, seed: int, device: torch.device,
+                              ssm_dtype: torch.dtype = torch.float32):
+    """Full unsharded initial states: k_cache/v_cache [B, c, n_kv, hd] bf16, conv [B, d_conv-1, rows] bf16,
+    ssm [B, nh, p, N] in ``ssm_dtype``."""
+    cpu = torch.device("cpu")
+    ks, vs = zip(*(full_kv_head(seed, h, B, c, dims.head_dim, cpu) for h in range(dims.n_kv))) if dims.n_kv else ((), ())
+    k_cache = torch.stack(ks, 2).to(device)
+    v_cache = torch.stack(vs, 2).to(device)
+    conv = full_conv_state(seed, dims, B, device)
+    ssm = torch.stack([full_ssm_head(seed, j, B, dims.mamba_head_dim, dims.d_state, cpu, ssm_dtype)
+                       for j in range(dims.n_mamba_heads)], 1).to(device)
+    return k_cache, v_cache, conv, ssm
