@@ -1,0 +1,165 @@
+/*
+ * libmmp_b200 — C ABI of the B200 (sm_100a) kernels behind the hybrid mixer-layer forward.
+ *
+ * Every entry point takes raw device pointers, explicit sizes and element strides, and the CUDA stream
+ * to launch on; it validates its arguments, launches, and returns a status code (MMP_OK = 0). Nothing
+ * here allocates memory or synchronises the host, so every call can be captured in a CUDA graph. The
+ * caller owns all buffers. Strides are in elements. bf16 tensors are passed as `void*`.
+ *
+ * Each function names the reference interface it replaces: the reference harness reaches vLLM's kernels
+ * only through harness/kernels.py (anuragdutt/multi_modal_parallelism), whose wrappers are cited by
+ * file:line below. A binding generator (ctypes, cffi, cgo) needs only this header.
+ */
+#ifndef MMP_B200_H_
+#define MMP_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------------ */
+#define MMP_OK 0
+#define MMP_ERR_INVALID 1      /* bad shape, stride, dtype, alignment or null pointer */
+#define MMP_ERR_CUDA 2         /* a CUDA runtime call or kernel launch failed */
+#define MMP_ERR_UNSUPPORTED 3  /* a valid request this build has no kernel for */
+#define MMP_ERR_TIMEOUT 4      /* a bounded device-side wait ran out */
+
+/* element types */
+#define MMP_F32 0
+#define MMP_BF16 1
+
+/* device error-word bits written by kernels that are given an `err` pointer (never a trap) */
+#define MMP_DEVERR_INDEX 1
+#define MMP_DEVERR_POSITION 2
+#define MMP_DEVERR_TIMEOUT 4
+
+/* Library version (major*10000 + minor*100 + patch). */
+int mmp_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* mmp_last_error(void);
+
+/* ---- Mamba-2 decode: selective state update -------------------------------------------------------
+ * Replaces kernels.ssm_update (harness/kernels.py:137-143), i.e. vLLM selective_state_update with
+ * dt_softplus=True, state_batch_indices=idx_in, dst_state_batch_indices=idx_out.
+ *   dt' = softplus(dt[b,h] + dt_bias[h]) (or dt + dt_bias when dt_softplus == 0)
+ *   s   = state[idx_in[b], h] * exp(dt' A[h]) + dt' x[b,h,:] (outer) B[b,g,:]      -> state[idx_out[b], h]
+ *   y   = s C[b,g,:] + D[h] x[b,h,:];  y *= silu(z[b,h,:]) if z != NULL            -> out[b,h,:]
+ * with g = h / (nh / ngroups). state: [lines, nh, p, N] (N contiguous), fp32 or bf16. x, z, out: [batch,
+ * nh, p] bf16 (p contiguous). dt: [batch, nh] bf16. B, C: [batch, ngroups, N] bf16 (N contiguous).
+ * A, D, dt_bias: [nh] fp32 (D, dt_bias may be NULL). idx_in / idx_out: [batch] int32, NULL = identity.
+ * A row whose idx_in equals pad_slot is skipped (its state lines are not touched; its output row is 0).
+ * Supported: N in {64, 128, 256}; all rows 16-byte aligned.
+ */
+int mmp_ssu_decode(void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
+                   const void* x, int64_t x_b, int64_t x_h,
+                   const void* dt, int64_t dt_b, int64_t dt_h,
+                   const float* A, const float* D, const float* dt_bias,
+                   const void* B, int64_t B_b, int64_t B_g,
+                   const void* C, int64_t C_b, int64_t C_g,
+                   const void* z, int64_t z_b, int64_t z_h,
+                   const int32_t* idx_in, const int32_t* idx_out, int pad_slot,
+                   void* out, int64_t o_b, int64_t o_h,
+                   int batch, int nh, int p, int N, int ngroups, int lines, int dt_softplus,
+                   int* err, void* stream);
+
+/* ---- Mamba-2 decode: causal depthwise conv update -------------------------------------------------
+ * Replaces kernels.conv_update (harness/kernels.py:131-134), i.e. vLLM causal_conv1d_update with
+ * activation "silu" and conv_state_indices. For each row b with line = idx[b]:
+ *   window = [state[line, 0..W-2, c], x[b, c]]; out[b,c] = act(sum_k w[c,k] window[k] + bias[c])
+ *   state[line, k, c] = window[k+1]
+ * x, out: [batch, rows] bf16 (out may alias x). state: element (line, k, c) at line*s_line + k*s_k + c*s_c
+ * (bf16). w: [rows, W] bf16 contiguous; bias: [rows] bf16 or NULL. Rows with idx == pad_slot are
+ * skipped (output row 0). W <= 8.
+ */
+int mmp_conv1d_update(const void* x, int64_t x_b, void* out, int64_t o_b,
+                      void* state, int64_t s_line, int64_t s_k, int64_t s_c,
+                      const void* w, const void* bias, const int32_t* idx, int pad_slot,
+                      int batch, int rows, int W, int lines, int silu, int* err, void* stream);
+
+/* ---- RMSNorm (+ residual) -------------------------------------------------------------------------
+ * Replaces kernels.rms_norm (harness/kernels.py:26-28). out = x * rsqrt(mean(x^2) + eps) * w over rows
+ * of length `hidden`. With `residual` != NULL the normalised value is x + residual, and that sum is also
+ * written to `sum_out` (may alias x or residual) — the layer's `h1 = h + mix` fused with the next norm.
+ * All bf16, row strides in elements, rows 16-byte aligned, hidden % 8 == 0.
+ */
+int mmp_rmsnorm(const void* x, int64_t x_b, const void* residual, int64_t r_b, void* sum_out, int64_t s_b,
+                const void* w, void* out, int64_t o_b, int rows, int hidden, float eps, void* stream);
+
+/* ---- Mamba-2 gated RMSNorm (norm after the gate) --------------------------------------------------
+ * Replaces kernels.gated_rmsnorm (harness/kernels.py:40-52) with its local path (group == None) and
+ * both halves of its tensor-parallel path:
+ *   g = y * silu(z);  out = w * g * rsqrt(sumsq(g over the group) / count + eps)
+ * mode 0 (local): groups of `group_size` columns, reduced inside the kernel.
+ * mode 1 (partial): write each row's per-group sum of squares to sumsq [rows, D/group_size] fp32 and
+ *   nothing else — the caller reduces it across the ranks of the norm group.
+ * mode 2 (apply): use the reduced sums in sumsq with `count` elements per group.
+ * y, z, out: [rows, D] bf16 with row strides; w: [D] bf16.
+ */
+int mmp_gated_rmsnorm(const void* y, int64_t y_b, const void* z, int64_t z_b, const void* w,
+                      void* out, int64_t o_b, float* sumsq, int rows, int D, int group_size,
+                      int mode, float count, float eps, void* stream);
+
+/* ---- RoPE + key multiplier + paged KV write --------------------------------------------------------
+ * Replaces kernels.apply_rope and kernels.write_kv (harness/kernels.py:56-66,112-115) and the layer's
+ * `k * key_mult` (harness/layer.py:35), fused into one pass over the QKV projection output.
+ * q: [batch, nq*hd], k / v: [batch, nkv*hd] bf16 (row strides q_b, k_b, v_b; they may be column slices
+ * of one [q | k | v] row). With positions != NULL, q and k*key_mult are rotated NeoX-style (rotate
+ * halves) at positions[b]; cos/sin come from `cos_sin` ([max_pos, hd] fp32 = cat(cos, sin)) when
+ * non-NULL, else from `inv_freq` ([hd/2] fp32). positions == NULL: no rotation, no multiplier.
+ * Rotated q goes to q_out (may alias q); rotated k to k_out when non-NULL (may alias k). When key_cache is
+ * non-NULL, k and v are written to the paged caches at slot_mapping[b] (skipped when < 0); caches are
+ * [num_blocks, block, nkv, hd] views with element strides (c_block, c_tok, c_head).
+ */
+int mmp_rope_kv_write(const void* q, int64_t q_b, const void* k, int64_t k_b, const void* v, int64_t v_b,
+                      int nq, int nkv, int hd, const int64_t* positions, const float* cos_sin, int max_pos,
+                      const float* inv_freq, float key_mult,
+                      void* q_out, int64_t qo_b, void* k_out, int64_t ko_b,
+                      void* key_cache, void* value_cache, int64_t c_block, int64_t c_tok, int64_t c_head,
+                      int block_size, int num_blocks, const int64_t* slot_mapping,
+                      int batch, int* err, void* stream);
+
+/* ---- SwiGLU activation ----------------------------------------------------------------------------
+ * Replaces kernels.silu_and_mul (harness/kernels.py:31-37) and the MLP's `F.silu(g * gm) * u`
+ * (harness/layer.py:135): out[r, c] = silu(gate_scale * gate[r, c]) * up[r, c], bf16, row strides in
+ * elements (cols % 8 == 0, 16-byte aligned rows).
+ */
+int mmp_silu_mul(const void* gate, int64_t g_b, const void* up, int64_t u_b, void* out, int64_t o_b,
+                 int rows, int cols, float gate_scale, void* stream);
+
+/* ---- paged GQA decode attention -------------------------------------------------------------------
+ * Replaces kernels.attn_decode (harness/kernels.py:118-127), i.e. FlashAttention-2 varlen with
+ * max_seqlen_q = 1, a block table and seqused_k. One query token per sequence; query head i reads KV
+ * head i / (nq / nkv). q: [batch, nq, hd] bf16; caches as in mmp_rope_kv_write; block_table:
+ * [batch, bt_stride] int32; seqlens: [batch] int32 keys per sequence; out: [batch, nq, hd] bf16.
+ * The key range of a sequence is split over `splits` CTAs whose partial results go to `workspace`
+ * (size from mmp_paged_attn_workspace_size) and are merged by a second kernel. splits <= 0 picks a
+ * split count for this GPU. Supported: hd == 128, block % 16 == 0, nq / nkv <= 16.
+ */
+size_t mmp_paged_attn_workspace_size(int batch, int nq, int hd, int splits);
+int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
+                          const void* key_cache, const void* value_cache, int64_t c_block, int64_t c_tok, int64_t c_head,
+                          const int32_t* block_table, int64_t bt_stride, const int32_t* seqlens,
+                          void* out, int64_t o_b, int64_t o_h,
+                          int batch, int nq, int nkv, int hd, int block_size, int num_blocks,
+                          int max_seqlen, float scale, int splits, void* workspace, size_t workspace_bytes,
+                          int* err, void* stream);
+
+/* ---- bf16 GEMM with fused epilogue ----------------------------------------------------------------
+ * Replaces kernels.gemm / gemm_T (harness/kernels.py:147-154) together with the scaling the layer
+ * applies to their results (harness/layer.py:35,80,105): out[m,n] = alpha * colscale[n] * sum_k
+ * a[m,k] w[n,k] + addend[m,n]. a: [M, K] bf16 (row stride lda); w: [N, K] bf16 (row stride ldw);
+ * colscale: [N] fp32 or NULL; addend: [M, N] bf16 (row stride ldd) or NULL; out: [M, N] bf16 (row
+ * stride ldo, may alias addend). K % 8 == 0, strides % 8 == 0, 16-byte aligned bases.
+ */
+int mmp_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
+                  int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MMP_B200_H_ */

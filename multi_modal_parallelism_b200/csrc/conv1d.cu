@@ -1,0 +1,134 @@
+// Mamba-2 decode causal depthwise conv update (replaces vLLM causal_conv1d_update as called by
+// harness/kernels.py:131-134 of the reference).
+//
+// One thread owns 8 consecutive channels of one sequence: 16-byte loads of x, of the W-1 state rows and of
+// the bias, 8 * W taps of weights, 16-byte stores of the output and of the shifted state. Channel-strided
+// state layouts (s_c != 1) take a scalar path.
+#include "mmp_common.cuh"
+
+namespace mmp {
+namespace {
+
+constexpr int MAX_W = 8;
+
+struct ConvParams {
+  const bf16* x; int64_t x_b;
+  bf16* out; int64_t o_b;
+  bf16* state; int64_t s_line, s_k, s_c;
+  const bf16* w; const bf16* bias;
+  const int32_t* idx; int pad_slot;
+  int batch, rows, W, lines, silu;
+  int* err;
+};
+
+template <int W>
+__global__ void __launch_bounds__(128) conv_update_vec_kernel(const ConvParams P) {
+  const int b = blockIdx.y;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= P.rows) return;
+  const int line = P.idx ? P.idx[b] : b;
+  bf16* op = P.out + b * P.o_b + c0;
+  if (line == P.pad_slot) {
+    st16(op, make_uint4(0, 0, 0, 0));
+    return;
+  }
+  if (line < 0 || line >= P.lines) {
+    flag_error(P.err, DEVERR_INDEX);
+    return;
+  }
+  float win[W][8];
+  bf16* sp = P.state + line * P.s_line + c0;
+#pragma unroll
+  for (int k = 0; k < W - 1; ++k) {
+    uint4 u = ld16(sp + k * P.s_k);
+    float2 a = unpack_bf16x2(u.x), bb = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+    win[k][0] = a.x; win[k][1] = a.y; win[k][2] = bb.x; win[k][3] = bb.y;
+    win[k][4] = c.x; win[k][5] = c.y; win[k][6] = d.x; win[k][7] = d.y;
+  }
+  uint4 ux = ld16(P.x + b * P.x_b + c0);
+  {
+    float2 a = unpack_bf16x2(ux.x), bb = unpack_bf16x2(ux.y), c = unpack_bf16x2(ux.z), d = unpack_bf16x2(ux.w);
+    win[W - 1][0] = a.x; win[W - 1][1] = a.y; win[W - 1][2] = bb.x; win[W - 1][3] = bb.y;
+    win[W - 1][4] = c.x; win[W - 1][5] = c.y; win[W - 1][6] = d.x; win[W - 1][7] = d.y;
+  }
+  float acc[8];
+  if (P.bias) {
+    uint4 ub = ld16(P.bias + c0);
+    float2 a = unpack_bf16x2(ub.x), bb = unpack_bf16x2(ub.y), c = unpack_bf16x2(ub.z), d = unpack_bf16x2(ub.w);
+    acc[0] = a.x; acc[1] = a.y; acc[2] = bb.x; acc[3] = bb.y; acc[4] = c.x; acc[5] = c.y; acc[6] = d.x; acc[7] = d.y;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  }
+  // weights [rows, W]: 8 channels x W taps are 8*W contiguous bf16
+  const bf16* wp = P.w + c0 * W;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+#pragma unroll
+    for (int k = 0; k < W; ++k) acc[j] = fmaf(bf2f(wp[j * W + k]), win[k][j], acc[j]);
+  }
+  if (P.silu) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = silu(acc[j]);
+  }
+  // shift the state line (reads of this line are complete: only this thread touches these channels)
+#pragma unroll
+  for (int k = 0; k < W - 2; ++k) st16(sp + k * P.s_k, ld16(sp + (k + 1) * P.s_k));
+  if (W >= 2) st16(sp + (W - 2) * P.s_k, ux);
+  st16(op, make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                      pack_bf16x2(acc[6], acc[7])));
+}
+
+__global__ void __launch_bounds__(128) conv_update_scalar_kernel(const ConvParams P) {
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= P.rows) return;
+  const int line = P.idx ? P.idx[b] : b;
+  if (line == P.pad_slot) {
+    P.out[b * P.o_b + c] = f2bf(0.f);
+    return;
+  }
+  if (line < 0 || line >= P.lines) {
+    flag_error(P.err, DEVERR_INDEX);
+    return;
+  }
+  bf16* sp = P.state + line * P.s_line + c * P.s_c;
+  const bf16 xin = P.x[b * P.x_b + c];
+  float acc = P.bias ? bf2f(P.bias[c]) : 0.f;
+  for (int k = 0; k < P.W - 1; ++k) acc = fmaf(bf2f(P.w[c * P.W + k]), bf2f(sp[k * P.s_k]), acc);
+  acc = fmaf(bf2f(P.w[c * P.W + P.W - 1]), bf2f(xin), acc);
+  if (P.silu) acc = silu(acc);
+  for (int k = 0; k < P.W - 2; ++k) sp[k * P.s_k] = sp[(k + 1) * P.s_k];
+  if (P.W >= 2) sp[(P.W - 2) * P.s_k] = xin;
+  P.out[b * P.o_b + c] = f2bf(acc);
+}
+
+}  // namespace
+}  // namespace mmp
+
+using namespace mmp;
+
+extern "C" int mmp_conv1d_update(const void* x, int64_t x_b, void* out, int64_t o_b,
+                                 void* state, int64_t s_line, int64_t s_k, int64_t s_c,
+                                 const void* w, const void* bias, const int32_t* idx, int pad_slot,
+                                 int batch, int rows, int W, int lines, int silu, int* err, void* stream) {
+  if (batch == 0) return MMP_OK;
+  if (!x || !out || !state || !w) return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_update: null pointer");
+  if (batch < 0 || batch > 65535 || rows <= 0 || W < 1 || W > MAX_W || lines <= 0)
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_update: bad sizes batch=%d rows=%d W=%d lines=%d", batch, rows, W, lines);
+  ConvParams P{static_cast<const bf16*>(x), x_b, static_cast<bf16*>(out), o_b,
+               static_cast<bf16*>(state), s_line, s_k, s_c,
+               static_cast<const bf16*>(w), static_cast<const bf16*>(bias), idx, pad_slot,
+               batch, rows, W, lines, silu, err};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool vec = s_c == 1 && W == 4 && rows % 8 == 0 && aligned16(x) && aligned16(out) && aligned16(state) &&
+                   (!bias || aligned16(bias)) && x_b % 8 == 0 && o_b % 8 == 0 && s_line % 8 == 0 && s_k % 8 == 0;
+  if (vec) {
+    dim3 grid((rows / 8 + 127) / 128, batch);
+    conv_update_vec_kernel<4><<<grid, 128, 0, s>>>(P);
+  } else {
+    dim3 grid((rows + 127) / 128, batch);
+    conv_update_scalar_kernel<<<grid, 128, 0, s>>>(P);
+  }
+  return mmp_check_launch("mmp_conv1d_update");
+}

@@ -1,0 +1,345 @@
+"""The kernel boundary: the same wrapper names and signatures as the reference's `harness/kernels.py`
+(:26-154), implemented over the C ABI of libmmp_b200.so (include/mmp_b200.h) instead of vLLM.
+
+Every wrapper launches on torch's current CUDA stream, allocates nothing when given its output buffers,
+and never synchronises, so a layer step built from them can be captured in a CUDA graph. Shapes or dtypes
+the kernels do not take raise ValueError; there is no fallback path. Extra keyword arguments (output
+buffers, epilogue scales, workspaces) expose the fusions the layer uses.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+from ._lib import MMP_BF16, MMP_F32, MmpError
+from .state import alloc_kv, kv_cache_layout  # noqa: F401  (part of this module's API in the reference)
+
+BF16 = torch.bfloat16
+PAD_SLOT_ID = -1
+
+_err_words: dict[int, torch.Tensor] = {}
+_attn_ws: dict[int, torch.Tensor] = {}
+
+
+# ----------------------------------------------------------------------------- helpers
+def _p(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _cuda(name: str, *ts: torch.Tensor | None) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError(f"{name}: tensors must be on a CUDA device (got {t.device})")
+
+
+def _dtype(name: str, t: torch.Tensor | None, dt: torch.dtype) -> None:
+    if t is not None and t.dtype != dt:
+        raise ValueError(f"{name}: expected {dt}, got {t.dtype}")
+
+
+def _rowmajor(name: str, t: torch.Tensor) -> int:
+    """Row stride of a 2-D tensor whose last dimension is contiguous."""
+    if t.dim() != 2 or (t.shape[1] > 1 and t.stride(1) != 1):
+        raise ValueError(f"{name}: expected a 2-D tensor with a contiguous last dimension, got {tuple(t.shape)} "
+                         f"strides {t.stride()}")
+    return t.stride(0)
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32 word the kernels OR their index/position error bits into."""
+    idx = torch.device(device).index or 0
+    if idx not in _err_words:
+        _err_words[idx] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+    return _err_words[idx]
+
+
+def check_device_errors(device: torch.device | None = None, reset: bool = True) -> None:
+    """Synchronise and raise if any kernel flagged an out-of-range index since the last check."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = error_word(dev)
+    v = int(w.item())
+    if v:
+        if reset:
+            w.zero_()
+        names = [n for bit, n in _lib.DEVERR.items() if v & bit]
+        raise MmpError(f"device error word {v:#x}: {', '.join(names)}")
+
+
+# ----------------------------------------------------------------------------- norms
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
+    _cuda("rms_norm", x, w, out)
+    for t in (x, w, out):
+        _dtype("rms_norm", t, BF16)
+    rows, hidden = x.shape
+    _lib.call("mmp_rmsnorm", _p(x), _rowmajor("x", x), None, 0, None, 0, _p(w), _p(out), _rowmajor("out", out),
+              rows, hidden, float(eps), _stream(x))
+    return out
+
+
+def rms_norm_residual(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor,
+                      sum_out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = rms_norm(x + residual); the bf16 sum also goes to sum_out (may alias x or residual)."""
+    _cuda("rms_norm_residual", x, residual, w, out, sum_out)
+    for t in (x, residual, w, out, sum_out):
+        _dtype("rms_norm_residual", t, BF16)
+    rows, hidden = x.shape
+    _lib.call("mmp_rmsnorm", _p(x), _rowmajor("x", x), _p(residual), _rowmajor("residual", residual), _p(sum_out),
+              0 if sum_out is None else _rowmajor("sum_out", sum_out), _p(w), _p(out), _rowmajor("out", out),
+              rows, hidden, float(eps), _stream(x))
+    return out
+
+
+def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor, gate_scale: float = 1.0) -> torch.Tensor:
+    _cuda("silu_mul", gate, up, out)
+    rows, cols = gate.shape
+    _lib.call("mmp_silu_mul", _p(gate), _rowmajor("gate", gate), _p(up), _rowmajor("up", up), _p(out),
+              _rowmajor("out", out), rows, cols, float(gate_scale), _stream(gate))
+    return out
+
+
+def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x: [T, 2d] with [gate | up] halves -> silu(gate) * up, [T, d]."""
+    d = x.shape[-1] // 2
+    if out is None:
+        out = torch.empty(x.shape[0], d, dtype=x.dtype, device=x.device)
+    return silu_mul(x[:, :d], x[:, d:], out)
+
+
+def gated_rmsnorm(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float, group, group_size: int | None = None,
+                  out: torch.Tensor | None = None, sumsq: torch.Tensor | None = None) -> torch.Tensor:
+    """Mamba-2 gated RMSNorm, gate before the norm. group=None: local norm over groups of `group_size`
+    columns (None -> the whole row). Otherwise the row is one group spread over `group`'s ranks: the
+    [T, 1] fp32 sum of squares is all-reduced over `group` (an object with `all_reduce(t) -> t` and
+    `world_size`, like the reference's coordinator) and the mean is taken over world_size * D."""
+    _cuda("gated_rmsnorm", y, z, w, out)
+    for t in (y, z, w, out):
+        _dtype("gated_rmsnorm", t, BF16)
+    rows, D = y.shape
+    if out is None:
+        out = torch.empty_like(y)
+    ys, zs, os_ = _rowmajor("y", y), _rowmajor("z", z), _rowmajor("out", out)
+    st = _stream(y)
+    if group is None:
+        gs = D if group_size is None else int(group_size)
+        _lib.call("mmp_gated_rmsnorm", _p(y), ys, _p(z), zs, _p(w), _p(out), os_, None, rows, D, gs, 0, 0.0,
+                  float(eps), st)
+        return out
+    if sumsq is None:
+        sumsq = torch.empty(rows, 1, dtype=torch.float32, device=y.device)
+    _lib.call("mmp_gated_rmsnorm", _p(y), ys, _p(z), zs, _p(w), _p(out), os_, _p(sumsq), rows, D, D, 1, 0.0,
+              float(eps), st)
+    total = group.all_reduce(sumsq)
+    _lib.call("mmp_gated_rmsnorm", _p(y), ys, _p(z), zs, _p(w), _p(out), os_, _p(total), rows, D, D, 2,
+              float(group.world_size * D), float(eps), st)
+    return out
+
+
+# ----------------------------------------------------------------------------- rope / kv
+def rope_inv_freq(head_dim: int, theta: float, device: torch.device) -> torch.Tensor:
+    """[hd/2] fp32 inverse frequencies theta^(-2i/hd), computed in fp32 as the fp32 layer does."""
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim)).to(device)
+
+
+def rope_cos_sin_cache(head_dim: int, max_pos: int, theta: float, device: torch.device) -> torch.Tensor:
+    """[max_pos, head_dim] fp32 = cat(cos, sin) over the rotary half-dimension (fp32, unlike vLLM's bf16)."""
+    inv = rope_inv_freq(head_dim, theta, torch.device("cpu"))
+    ang = torch.outer(torch.arange(max_pos, dtype=torch.float32), inv)
+    return torch.cat([ang.cos(), ang.sin()], -1).to(device)
+
+
+def apply_rope(positions: torch.Tensor, q: torch.Tensor, k: torch.Tensor, head_dim: int, cache: torch.Tensor) -> None:
+    """In place, NeoX style. q: [T, nq*hd], k: [T, nkv*hd]; cache from rope_cos_sin_cache."""
+    _cuda("apply_rope", positions, q, k, cache)
+    _dtype("apply_rope", positions, torch.int64)
+    _dtype("apply_rope", cache, torch.float32)
+    T = q.shape[0]
+    nq, nkv = q.shape[1] // head_dim, k.shape[1] // head_dim
+    qs, ks = _rowmajor("q", q), _rowmajor("k", k)
+    _lib.call("mmp_rope_kv_write", _p(q), qs, _p(k), ks, None, 0, nq, nkv, head_dim, _p(positions), _p(cache),
+              cache.shape[0], None, 1.0, _p(q), qs, _p(k), ks, None, None, 0, 0, 0, 0, 0, None, T,
+              _p(error_word(q.device)), _stream(q))
+
+
+def _cache_strides(key_cache: torch.Tensor, value_cache: torch.Tensor) -> tuple[int, int, int, int, int]:
+    if key_cache.stride() != value_cache.stride() or key_cache.stride(3) != 1:
+        raise ValueError("key/value caches must be [num_blocks, block, nkv, hd] views with equal strides")
+    nb, blk = key_cache.shape[0], key_cache.shape[1]
+    return key_cache.stride(0), key_cache.stride(1), key_cache.stride(2), blk, nb
+
+
+def write_kv(k: torch.Tensor, v: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+             slot_mapping: torch.Tensor) -> None:
+    """k, v: [T, nkv, hd] -> paged caches at slot_mapping (slots < 0 skipped)."""
+    _cuda("write_kv", k, v, key_cache, value_cache, slot_mapping)
+    _dtype("write_kv", slot_mapping, torch.int64)
+    T, nkv, hd = k.shape
+    cb, ct, ch, blk, nb = _cache_strides(key_cache, value_cache)
+    k2, v2 = k.reshape(T, nkv * hd), v.reshape(T, nkv * hd)
+    _lib.call("mmp_rope_kv_write", None, 0, _p(k2), _rowmajor("k", k2), _p(v2), _rowmajor("v", v2), 0, nkv, hd,
+              None, None, 0, None, 1.0, None, 0, None, 0, _p(key_cache), _p(value_cache), cb, ct, ch, blk, nb,
+              _p(slot_mapping), T, _p(error_word(k.device)), _stream(k))
+
+
+def qkv_rope_kv_write(qkv: torch.Tensor, nq: int, nkv: int, head_dim: int, positions: torch.Tensor,
+                      inv_freq: torch.Tensor, key_mult: float, q_out: torch.Tensor, key_cache: torch.Tensor,
+                      value_cache: torch.Tensor, slot_mapping: torch.Tensor) -> torch.Tensor:
+    """One pass over the QKV projection [T, (nq + 2 nkv) hd]: rotate q into q_out [T, nq*hd], rotate
+    k * key_mult into the key cache and copy v into the value cache at slot_mapping."""
+    _cuda("qkv_rope_kv_write", qkv, positions, inv_freq, q_out, key_cache, value_cache, slot_mapping)
+    T = qkv.shape[0]
+    rs = _rowmajor("qkv", qkv)
+    cb, ct, ch, blk, nb = _cache_strides(key_cache, value_cache)
+    qp = qkv.data_ptr()
+    esz = qkv.element_size()
+    _lib.call("mmp_rope_kv_write", qp, rs, qp + nq * head_dim * esz, rs, qp + (nq + nkv) * head_dim * esz, rs,
+              nq, nkv, head_dim, _p(positions), None, 0, _p(inv_freq), float(key_mult),
+              _p(q_out), _rowmajor("q_out", q_out), None, 0, _p(key_cache), _p(value_cache), cb, ct, ch, blk, nb,
+              _p(slot_mapping), T, _p(error_word(qkv.device)), _stream(qkv))
+    return q_out
+
+
+# ----------------------------------------------------------------------------- attention
+def attn_workspace(batch: int, nq: int, hd: int, splits: int, device: torch.device) -> torch.Tensor:
+    n = _lib.lib().mmp_paged_attn_workspace_size(batch, nq, hd, splits)
+    return torch.empty(max(1, (n + 3) // 4), dtype=torch.float32, device=device)
+
+
+def attn_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, cu_q: torch.Tensor,
+                seqused_k: torch.Tensor, max_k: int, block_table: torch.Tensor, out: torch.Tensor,
+                workspace: torch.Tensor | None = None, splits: int = 0) -> torch.Tensor:
+    """q: [T, nq, hd]; out: [T, nq, hd]. One query token per sequence (cu_q = arange(T + 1))."""
+    _cuda("attn_decode", q, key_cache, value_cache, seqused_k, block_table, out)
+    _dtype("attn_decode", block_table, torch.int32)
+    _dtype("attn_decode", seqused_k, torch.int32)
+    T, nq, hd = q.shape
+    nkv = key_cache.shape[2]
+    cb, ct, ch, blk, nb = _cache_strides(key_cache, value_cache)
+    if q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("attn_decode: head dimension must be contiguous")
+    if workspace is None:
+        need = _lib.lib().mmp_paged_attn_workspace_size(T, nq, hd, 64)
+        dev = q.device.index or 0
+        ws = _attn_ws.get(dev)
+        if ws is None or ws.numel() * 4 < need:
+            ws = _attn_ws[dev] = torch.empty(max(1, (need + 3) // 4), dtype=torch.float32, device=q.device)
+        workspace = ws
+    _lib.call("mmp_paged_attn_decode", _p(q), q.stride(0), q.stride(1), _p(key_cache), _p(value_cache), cb, ct, ch,
+              _p(block_table), block_table.stride(0), _p(seqused_k), _p(out), out.stride(0), out.stride(1),
+              T, nq, nkv, hd, blk, nb, int(max_k), 1.0 / math.sqrt(hd), int(splits), _p(workspace),
+              workspace.numel() * workspace.element_size(), _p(error_word(q.device)), _stream(q))
+    return out
+
+
+# ----------------------------------------------------------------------------- mamba-2 decode
+def conv_update(xBC: torch.Tensor, conv_state_T: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None,
+                idx: torch.Tensor | None, out: torch.Tensor | None = None, activation: str | None = "silu",
+                pad_slot: int = PAD_SLOT_ID) -> torch.Tensor:
+    """xBC: [T, conv_rows]; conv_state_T: [lines, conv_rows, d_conv-1] view; w: [conv_rows, d_conv].
+    Output defaults to xBC itself (in place, as vLLM's causal_conv1d_update)."""
+    _cuda("conv_update", xBC, conv_state_T, w, b, idx, out)
+    for t in (xBC, conv_state_T, w, b, out):
+        _dtype("conv_update", t, BF16)
+    if idx is not None:
+        _dtype("conv_update", idx, torch.int32)
+    if activation not in (None, "silu", "swish"):
+        raise ValueError(f"conv_update: activation {activation!r} not supported")
+    if not w.is_contiguous():
+        raise ValueError("conv_update: weight must be contiguous [rows, d_conv]")
+    T, rows = xBC.shape
+    out = xBC if out is None else out
+    lines = conv_state_T.shape[0]
+    W = w.shape[1]
+    _lib.call("mmp_conv1d_update", _p(xBC), _rowmajor("xBC", xBC), _p(out), _rowmajor("out", out), _p(conv_state_T),
+              conv_state_T.stride(0), conv_state_T.stride(2), conv_state_T.stride(1), _p(w), _p(b), _p(idx), pad_slot,
+              T, rows, W, lines, 1 if activation else 0, _p(error_word(xBC.device)), _stream(xBC))
+    return out
+
+
+def _per_head(name: str, t: torch.Tensor | None, nh: int) -> torch.Tensor | None:
+    """Reduce a Mamba-2 per-head parameter given as [nh], or broadcast over trailing dims (stride 0), to a
+    contiguous fp32 [nh]; per-(p, N) values are not supported."""
+    if t is None:
+        return None
+    while t.dim() > 1:
+        if t.stride(-1) != 0 and t.shape[-1] != 1:
+            raise ValueError(f"ssm_update: {name} must be per head (broadcast over p/N); per-channel values unsupported")
+        t = t[..., 0]
+    if t.shape[0] != nh:
+        raise ValueError(f"ssm_update: {name} has {t.shape[0]} heads, expected {nh}")
+    if t.dtype != torch.float32 or not t.is_contiguous():
+        raise ValueError(f"ssm_update: {name} must be a contiguous fp32 [nh] tensor (or a broadcast view of one)")
+    return t
+
+
+def ssm_update(state: torch.Tensor, x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor,
+               C: torch.Tensor, D: torch.Tensor | None, dt_bias: torch.Tensor | None, idx: torch.Tensor | None,
+               out: torch.Tensor, z: torch.Tensor | None = None, idx_out: torch.Tensor | None = None,
+               dt_softplus: bool = True, pad_slot: int = PAD_SLOT_ID) -> torch.Tensor:
+    """Shapes as MambaMixer2's decode call: state [lines, nh, p, N] (fp32 or bf16); x/out/z [T, nh, p];
+    dt [T, nh, p] broadcast over p (or [T, nh]); A [nh, p, N] broadcast (or [nh]); B/C [T, ng, N];
+    D/dt_bias [nh, p] broadcast (or [nh]); idx/idx_out [T] int32 state lines (idx_out defaults to idx)."""
+    _cuda("ssm_update", state, x, dt, A, B, C, D, dt_bias, idx, out, z, idx_out)
+    for t in (x, B, C, out, z):
+        _dtype("ssm_update", t, BF16)
+    if state.dtype not in (torch.float32, BF16):
+        raise ValueError("ssm_update: state must be fp32 or bf16")
+    lines, nh, p, N = state.shape
+    T = x.shape[0]
+    if state.stride(3) != 1 or x.stride(2) != 1 or out.stride(2) != 1 or B.stride(2) != 1 or C.stride(2) != 1:
+        raise ValueError("ssm_update: the innermost dimension of state, x, out, B and C must be contiguous")
+    if dt.dim() == 3:
+        if dt.shape[2] > 1 and dt.stride(2) != 0:
+            raise ValueError("ssm_update: dt must be per head (broadcast over p)")
+        dt = dt[:, :, 0]
+    _dtype("ssm_update", dt, BF16)
+    A1, D1, db1 = _per_head("A", A, nh), _per_head("D", D, nh), _per_head("dt_bias", dt_bias, nh)
+    for t in (idx, idx_out):
+        if t is not None:
+            _dtype("ssm_update", t, torch.int32)
+    zs = (z.stride(0), z.stride(1)) if z is not None else (0, 0)
+    _lib.call("mmp_ssu_decode", _p(state), MMP_F32 if state.dtype == torch.float32 else MMP_BF16,
+              state.stride(0), state.stride(1), state.stride(2), _p(x), x.stride(0), x.stride(1),
+              _p(dt), dt.stride(0), dt.stride(1), _p(A1), _p(D1), _p(db1),
+              _p(B), B.stride(0), B.stride(1), _p(C), C.stride(0), C.stride(1), _p(z), zs[0], zs[1],
+              _p(idx), _p(idx_out if idx_out is not None else idx), pad_slot, _p(out), out.stride(0), out.stride(1),
+              T, nh, p, N, B.shape[1], lines, 1 if dt_softplus else 0, _p(error_word(x.device)), _stream(x))
+    return out
+
+
+# ----------------------------------------------------------------------------- gemm
+def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
+         colscale: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
+    """out = alpha * colscale * (x [T, in] @ w[out, in]^T) + addend."""
+    _cuda("gemm", x, w, out, colscale, addend)
+    for t in (x, w, out, addend):
+        _dtype("gemm", t, BF16)
+    _dtype("gemm", colscale, torch.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"gemm: x has K={K}, w has K={w.shape[1]}")
+    if out is None:
+        out = torch.empty(M, N, dtype=BF16, device=x.device)
+    if colscale is not None:
+        colscale = colscale.reshape(-1)
+        if colscale.numel() != N or not colscale.is_contiguous():
+            raise ValueError("gemm: colscale must be a contiguous [N] fp32 vector")
+    _lib.call("mmp_gemm_bf16", _p(x), _rowmajor("x", x), _p(w), _rowmajor("w", w), _p(out), _rowmajor("out", out),
+              M, N, K, float(alpha), _p(colscale), _p(addend), 0 if addend is None else _rowmajor("addend", addend),
+              _stream(x))
+    return out
+
+
+def gemm_T(x: torch.Tensor, wT: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
+           colscale: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
+    """x [T, k] @ wT [k, out]. Fast when wT is the transpose of a row-major [out, k] matrix."""
+    w = wT.t()
+    if w.stride(1) != 1:
+        w = w.contiguous()
+    return gemm(x, w, out, alpha, colscale, addend)
