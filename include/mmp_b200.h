@@ -139,6 +139,8 @@ int mmp_silu_mul(const void* gate, int64_t g_b, const void* up, int64_t u_b, voi
  * split count for this GPU. Supported: hd == 128, block % 16 == 0, nq / nkv <= 16.
  */
 size_t mmp_paged_attn_workspace_size(int batch, int nq, int hd, int splits);
+/* The split count mmp_paged_attn_decode picks for splits <= 0 (for sizing the workspace once). */
+int mmp_paged_attn_default_splits(int batch, int nkv, int max_seqlen);
 int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
                           const void* key_cache, const void* value_cache, int64_t c_block, int64_t c_tok, int64_t c_head,
                           const int32_t* block_table, int64_t bt_stride, const int32_t* seqlens,
@@ -157,6 +159,14 @@ int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
 int mmp_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
                   int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
                   void* stream);
+
+/* ---- elementwise add (residual joins after a collective) -------------------------------------------
+ * Replaces the layer's bf16 `a + b (+ c)` residual sums (harness/layer.py:217-219,225-227):
+ * out = a + b (+ c when c != NULL), computed in fp32, rounded once to bf16. [rows, cols] with row strides
+ * (cols % 8 == 0, 16-byte aligned rows); out may alias an input.
+ */
+int mmp_add(const void* a, int64_t a_b, const void* b, int64_t b_b, const void* c, int64_t c_b,
+            void* out, int64_t o_b, int rows, int cols, void* stream);
 
 #ifdef __cplusplus
 }

@@ -288,6 +288,14 @@ static int choose_splits(int batch, int nkv, int max_tiles) {
   return std::max(1, std::min(s, 64));
 }
 
+extern "C" int mmp_paged_attn_default_splits(int batch, int nkv, int max_seqlen) {
+  if (batch <= 0 || nkv <= 0 || max_seqlen < 0) return 1;
+  const int max_tiles = std::max(1, (max_seqlen + TILE - 1) / TILE);
+  int splits = std::min(choose_splits(batch, nkv, max_tiles), max_tiles);
+  const int tps = (max_tiles + splits - 1) / splits;
+  return (max_tiles + tps - 1) / tps;
+}
+
 extern "C" int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
                                      const void* key_cache, const void* value_cache, int64_t c_block, int64_t c_tok, int64_t c_head,
                                      const int32_t* block_table, int64_t bt_stride, const int32_t* seqlens,

@@ -204,3 +204,41 @@ extern "C" int mmp_silu_mul(const void* gate, int64_t g_b, const void* up, int64
       static_cast<const bf16*>(gate), g_b, static_cast<const bf16*>(up), u_b, static_cast<bf16*>(out), o_b, cols, gate_scale);
   return mmp_check_launch("mmp_silu_mul");
 }
+
+namespace mmp {
+namespace {
+
+__global__ void __launch_bounds__(256) add3_kernel(const bf16* a, int64_t a_b, const bf16* b, int64_t b_b, const bf16* c,
+                                                   int64_t c_b, bf16* out, int64_t o_b, int cols) {
+  const int row = blockIdx.y;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= cols) return;
+  float x[8], y[8];
+  unpack8(ld16(a + row * a_b + c0), x);
+  unpack8(ld16(b + row * b_b + c0), y);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) x[j] += y[j];
+  if (c) {
+    unpack8(ld16(c + row * c_b + c0), y);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] += y[j];
+  }
+  st16(out + row * o_b + c0, pack8(x));
+}
+
+}  // namespace
+}  // namespace mmp
+
+extern "C" int mmp_add(const void* a, int64_t a_b, const void* b, int64_t b_b, const void* c, int64_t c_b,
+                       void* out, int64_t o_b, int rows, int cols, void* stream) {
+  if (rows == 0 || cols == 0) return MMP_OK;
+  if (!a || !b || !out) return mmp_set_error(MMP_ERR_INVALID, "mmp_add: null pointer");
+  if (rows < 0 || rows > 65535 || cols < 0 || cols % 8 || !rows_ok(a, a_b) || !rows_ok(b, b_b) || !rows_ok(c, c_b) ||
+      !rows_ok(out, o_b))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_add: cols %% 8 == 0 and 16-byte aligned rows required");
+  dim3 grid((cols / 8 + 255) / 256, rows);
+  add3_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(a), a_b, static_cast<const bf16*>(b), b_b, static_cast<const bf16*>(c), c_b,
+      static_cast<bf16*>(out), o_b, cols);
+  return mmp_check_launch("mmp_add");
+}

@@ -103,6 +103,15 @@ def silu_mul(gate: torch.Tensor, up: torch.Tensor, out: torch.Tensor, gate_scale
     return out
 
 
+def add(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor, c: torch.Tensor | None = None) -> torch.Tensor:
+    """out = a + b (+ c), bf16 with one rounding."""
+    _cuda("add", a, b, c, out)
+    rows, cols = a.shape
+    _lib.call("mmp_add", _p(a), _rowmajor("a", a), _p(b), _rowmajor("b", b), _p(c),
+              0 if c is None else _rowmajor("c", c), _p(out), _rowmajor("out", out), rows, cols, _stream(a))
+    return out
+
+
 def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """x: [T, 2d] with [gate | up] halves -> silu(gate) * up, [T, d]."""
     d = x.shape[-1] // 2
@@ -205,6 +214,10 @@ def qkv_rope_kv_write(qkv: torch.Tensor, nq: int, nkv: int, head_dim: int, posit
 
 
 # ----------------------------------------------------------------------------- attention
+def attn_default_splits(batch: int, nkv: int, max_seqlen: int) -> int:
+    return int(_lib.lib().mmp_paged_attn_default_splits(batch, nkv, max_seqlen))
+
+
 def attn_workspace(batch: int, nq: int, hd: int, splits: int, device: torch.device) -> torch.Tensor:
     n = _lib.lib().mmp_paged_attn_workspace_size(batch, nq, hd, splits)
     return torch.empty(max(1, (n + 3) // 4), dtype=torch.float32, device=device)

@@ -1,0 +1,294 @@
+"""One Falcon-H1 parallel-hybrid layer (attention ∥ Mamba-2, summed, residual, optional SwiGLU MLP) with the
+per-layout order of kernels and collectives.
+
+Same API as the reference's `harness/layer.py` (`AttentionBranch` :23-54, `SsmBranch` :57-106,
+`SwingMLP` :109-140, `ParallelHybridLayer` :153-228). Every buffer is allocated once, so a step can be
+captured in a CUDA graph; every op is a libmmp_b200 kernel (kernels.py). Fusions relative to the
+reference, each exact in real arithmetic:
+  * attn_in / ssm_in are folded into the QKV / in_proj GEMM scale; the muP multipliers are the in_proj
+    GEMM's per-column scale; attn_out / ssm_out are the o_proj / out_proj GEMM scale;
+  * key_mult, RoPE and the paged-KV write are one kernel over the QKV output;
+  * residual adds ride on GEMM epilogues (1 rank) or on the post-collective norm (`h + mix` fused into the
+    pre-MLP RMSNorm).
+Modes: tp1, tp4 (one all-reduce per branch), tp4_fused (one all-reduce of the summed branches),
+tp4_streams (branches on two streams, one all-reduce), and any branch split split{a}{m} (attention on
+ranks 0..a-1, Mamba-2 on a..a+m-1, one all-reduce); the "tp4" names work at any world size.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import kernels as K
+from .config import FalconH1Dims
+from .dist import Groups
+from .sharding import RankPlan, all_norm_groups, parse_split
+from .state import DecodeCtx, RankStates
+from .timing import NULL, OpTimer
+from .weights import RankWeights
+
+BF16 = torch.bfloat16
+
+
+def _pad8(n: int) -> int:
+    return (n + 7) // 8 * 8
+
+
+class AttentionBranch:
+    name = "attn"
+
+    def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
+                 device: torch.device):
+        a = plan.attn
+        assert a is not None
+        self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
+        self.nq, self.nkv, self.hd = len(a.q_heads), len(a.kv_heads), dims.head_dim
+        self.inv_freq = K.rope_inv_freq(self.hd, dims.rope_theta, device)
+        B = ctx.B
+        self.qkv = torch.empty(B, w.wqkv.shape[0], device=device, dtype=BF16)
+        self.q = torch.empty(B, self.nq * self.hd, device=device, dtype=BF16)
+        self.out = torch.empty(B, self.nq, self.hd, device=device, dtype=BF16)
+        self.splits = K.attn_default_splits(B, self.nkv, ctx.max_k)
+        self.ws = K.attn_workspace(B, self.nq, self.hd, self.splits, device)
+
+    @property
+    def rope_cache(self) -> torch.Tensor:
+        return K.rope_cos_sin_cache(self.hd, self.ctx.c + 2, self.dims.rope_theta, self.inv_freq.device)
+
+    def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
+               x_scale: float = 1.0) -> torch.Tensor:
+        """x: [B, H] (already multiplied by attn_in unless x_scale carries it). Returns the o_proj partial
+        times attn_out (+ addend), written to `out`."""
+        w, ctx, d = self.w, self.ctx, self.dims
+        t.begin("attn.qkv")
+        K.gemm(x, w.wqkv, out=self.qkv, alpha=x_scale)
+        t.end("attn.qkv")
+        t.begin("attn.rope_kv")
+        K.qkv_rope_kv_write(self.qkv, self.nq, self.nkv, self.hd, ctx.positions, self.inv_freq, d.key_mult, self.q,
+                            self.st.key_cache, self.st.value_cache, ctx.slot_mapping)
+        t.end("attn.rope_kv")
+        t.begin("attn.fa")
+        K.attn_decode(self.q.view(ctx.B, self.nq, self.hd), self.st.key_cache, self.st.value_cache, ctx.cu_q,
+                      ctx.seqused_k, ctx.max_k, ctx.block_table, self.out, workspace=self.ws, splits=self.splits)
+        t.end("attn.fa")
+        t.begin("attn.oproj")
+        out = K.gemm(self.out.view(ctx.B, self.nq * self.hd), w.wo, out=out, alpha=d.attn_out, addend=addend)
+        t.end("attn.oproj")
+        return out
+
+
+class _LocalOnly:
+    """Stands in for a coordinator in the no-collectives diagnostic: same arithmetic, no reduction."""
+
+    def __init__(self, world_size: int):
+        self.world_size = world_size
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        return x.mul_(self.world_size)
+
+
+class SsmBranch:
+    name = "ssm"
+
+    def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
+                 device: torch.device, norm_group):
+        s = plan.ssm
+        assert s is not None
+        self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
+        self.norm_group = norm_group
+        z, x, b, c, dt = s.local_in_rows
+        self.sizes = (z, x + b + c, dt)
+        self.xbc_sizes = (x, b, c)
+        self.nhr, self.p, self.N = len(s.heads), dims.mamba_head_dim, dims.d_state
+        self.ng = len(s.groups)
+        self.A_exp = w.A[:, None, None].expand(self.nhr, self.p, self.N)
+        self.D_exp = w.D[:, None].expand(self.nhr, self.p)
+        self.dtb_exp = w.dt_bias[:, None].expand(self.nhr, self.p)
+        B = ctx.B
+        rows = sum(self.sizes)
+        # in_proj output rows padded to 16 bytes so every [z | x | B | C | dt] slice starts aligned
+        self._zx = torch.empty(B, _pad8(rows), device=device, dtype=BF16)
+        self.zxbcdt = self._zx[:, :rows]
+        self.z = self.zxbcdt[:, :z]
+        self.xBC = self.zxbcdt[:, z:z + x + b + c]
+        self.xs = self.xBC[:, :x].view(B, self.nhr, self.p)
+        self.Bm = self.xBC[:, x:x + b].view(B, self.ng, self.N)
+        self.Cm = self.xBC[:, x + b:].view(B, self.ng, self.N)
+        self.dt = self.zxbcdt[:, z + x + b + c:]
+        self.y = torch.empty(B, self.nhr, self.p, device=device, dtype=BF16)
+        self.yn = torch.empty(B, self.nhr * self.p, device=device, dtype=BF16)
+        self.sumsq = torch.empty(B, 1, device=device, dtype=torch.float32)
+        self.conv_state_T = st.conv_state.transpose(-1, -2)  # [lines, rows, d_conv-1] view
+        self.group_size = (self.nhr * self.p) // self.ng if self.ng > 1 else None
+
+    def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
+               x_scale: float = 1.0) -> torch.Tensor:
+        w, ctx, d = self.w, self.ctx, self.dims
+        t.begin("ssm.inproj")
+        K.gemm(x, w.win, out=self.zxbcdt, alpha=x_scale, colscale=w.mup)
+        t.end("ssm.inproj")
+        t.begin("ssm.conv")
+        K.conv_update(self.xBC, self.conv_state_T, w.conv_w, w.conv_b, ctx.state_idx)
+        t.end("ssm.conv")
+        t.begin("ssm.ssu")
+        K.ssm_update(self.st.ssm_state, self.xs, self.dt, w.A, self.Bm, self.Cm, w.D, w.dt_bias, ctx.state_idx, self.y)
+        t.end("ssm.ssu")
+        t.begin("ssm.norm")
+        K.gated_rmsnorm(self.y.view(ctx.B, self.nhr * self.p), self.z, w.norm_w, d.rms_eps, self.norm_group,
+                        self.group_size, out=self.yn, sumsq=self.sumsq)
+        t.end("ssm.norm")
+        t.begin("ssm.outproj")
+        out = K.gemm(self.yn, w.wout, out=out, alpha=d.ssm_out, addend=addend)
+        t.end("ssm.outproj")
+        return out
+
+
+class SwingMLP:
+    """SwiGLU over this rank's contiguous column pool; the per-step assignment only changes the row count."""
+
+    def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, B: int = 0, device: torch.device | None = None):
+        self.plan, self.w, self.dims = plan, w, dims
+        self.m = plan.mlp
+        self.k = plan.mlp.k
+        self.gm, self.dm = dims.mlp_mults
+        n = max(1, w.n_pool)
+        if device is not None and B > 0:
+            self.g = torch.empty(B, n, device=device, dtype=BF16)
+            self.u = torch.empty(B, n, device=device, dtype=BF16)
+
+    def set_k(self, k: int) -> None:
+        self.k = k
+
+    @property
+    def n_active(self) -> int:
+        m = self.m
+        if m.w == 0:
+            return m.n_fixed
+        return m.n_fixed + (self.k if m.role == "attn" else 2 * m.w - self.k)
+
+    def forward(self, y: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None,
+                addend: torch.Tensor | None = None) -> torch.Tensor:
+        w, n, B = self.w, self.n_active, y.shape[0]
+        g, u = self.g[:B, :n], self.u[:B, :n]
+        t.begin("mlp.gateup")
+        K.gemm(y, w.mlp_gate[:n], out=g)
+        K.gemm(y, w.mlp_up[:n], out=u)
+        t.end("mlp.gateup")
+        t.begin("mlp.act")
+        K.silu_mul(g, u, g, self.gm)
+        t.end("mlp.act")
+        t.begin("mlp.down")
+        out = K.gemm(g, w.mlp_down[:, :n], out=out, alpha=self.dm, addend=addend)
+        t.end("mlp.down")
+        return out
+
+
+class ParallelHybridLayer:
+    def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
+                 ctx: DecodeCtx, device: torch.device, collectives: bool = True):
+        self.plan, self.w, self.dims, self.groups, self.ctx = plan, w, dims, groups, ctx
+        self.collectives = collectives
+        self.device = device
+        self.mode = plan.mode
+        if not (self.mode in ("tp1", "tp4", "tp4_fused", "tp4_streams") or parse_split(self.mode)):
+            raise ValueError(self.mode)
+        self.B, self.H = ctx.B, dims.hidden
+        world = groups.world_size
+        if world > 1 and collectives:
+            groups.ensure(all_norm_groups(self.mode, world, dims))  # collective: every rank, same order
+        self.attn = AttentionBranch(plan, w, dims, st, ctx, device) if plan.attn is not None else None
+        norm_group = None
+        if plan.ssm is not None and len(plan.ssm.norm_ranks) > 1:
+            norm_group = groups.group_for_ranks(plan.ssm.norm_ranks) if collectives else _LocalOnly(len(plan.ssm.norm_ranks))
+        self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group) if plan.ssm is not None else None
+        self.has_mlp = dims.intermediate > 0
+        self.mlp = SwingMLP(plan, w, dims, ctx.B, device) if self.has_mlp else None
+        B, H = ctx.B, dims.hidden
+        mk = lambda: torch.empty(B, H, device=device, dtype=BF16)  # noqa: E731
+        self.xn, self.yn, self.out = mk(), mk(), mk()
+        self.h1 = mk() if self.has_mlp else self.out
+        self.mix, self.part_a, self.part_s, self.mlp_part = mk(), mk(), mk(), mk()
+        self.tp = groups.tp
+        if self.mode == "tp4_streams":
+            self.s_attn = torch.cuda.Stream(device=device)
+            self.s_ssm = torch.cuda.Stream(device=device)
+
+    @property
+    def _local(self) -> bool:
+        return self.groups.world_size == 1 or not self.collectives
+
+    def _ar(self, x: torch.Tensor, name: str, t: OpTimer) -> torch.Tensor:
+        if self._local:
+            return x
+        t.begin(name)
+        self.tp.all_reduce(x)
+        t.end(name)
+        return x
+
+    def _join(self, h: torch.Tensor, mix: torch.Tensor, t: OpTimer) -> None:
+        """h1 = h + mix; with an MLP the sum is fused into the pre-MLP norm, which then writes yn."""
+        t.begin("residual")
+        if self.has_mlp:
+            K.rms_norm_residual(h, mix, self.w.ff_norm, self.dims.rms_eps, self.yn, self.h1)
+        else:
+            K.add(h, mix, self.out)
+        t.end("residual")
+
+    def step(self, h: torch.Tensor, t: OpTimer = NULL) -> torch.Tensor:
+        dims = self.dims
+        t.begin("norm_in")
+        x = K.rms_norm(h, self.w.in_norm, dims.rms_eps, self.xn)
+        t.end("norm_in")
+        mode = self.mode
+        y_ready = False
+        if mode == "tp1":
+            self.attn.decode(x, t, out=self.h1, addend=h, x_scale=dims.attn_in)
+            self.ssm.decode(x, t, out=self.h1, addend=self.h1, x_scale=dims.ssm_in)
+        elif mode == "tp4":
+            self._ar(self.attn.decode(x, t, out=self.part_a, x_scale=dims.attn_in), "ar.attn", t)
+            self._ar(self.ssm.decode(x, t, out=self.part_s, x_scale=dims.ssm_in), "ar.ssm", t)
+            t.begin("residual")
+            K.add(h, self.part_a, self.h1, c=self.part_s)
+            t.end("residual")
+        elif mode == "tp4_fused":
+            self.attn.decode(x, t, out=self.mix, x_scale=dims.attn_in)
+            self.ssm.decode(x, t, out=self.mix, addend=self.mix, x_scale=dims.ssm_in)
+            self._ar(self.mix, "ar.mixer", t)
+            self._join(h, self.mix, t)
+            y_ready = self.has_mlp
+        elif mode == "tp4_streams":
+            cur = torch.cuda.current_stream(self.device)
+            self.s_attn.wait_stream(cur)
+            self.s_ssm.wait_stream(cur)
+            with torch.cuda.stream(self.s_attn):
+                self.attn.decode(x, t, out=self.part_a, x_scale=dims.attn_in)
+            with torch.cuda.stream(self.s_ssm):
+                self.ssm.decode(x, t, out=self.part_s, x_scale=dims.ssm_in)
+            cur.wait_stream(self.s_attn)
+            cur.wait_stream(self.s_ssm)
+            K.add(self.part_a, self.part_s, self.mix)
+            self._ar(self.mix, "ar.mixer", t)
+            self._join(h, self.mix, t)
+            y_ready = self.has_mlp
+        else:  # split{a}{m}
+            if self.attn is not None:
+                self.attn.decode(x, t, out=self.mix, x_scale=dims.attn_in)
+            else:
+                self.ssm.decode(x, t, out=self.mix, x_scale=dims.ssm_in)
+            self._ar(self.mix, "ar.mixer", t)
+            self._join(h, self.mix, t)
+            y_ready = self.has_mlp
+        if not self.has_mlp:
+            return self.out
+        if not y_ready:
+            t.begin("norm_ff")
+            K.rms_norm(self.h1, self.w.ff_norm, dims.rms_eps, self.yn)
+            t.end("norm_ff")
+        if self._local:
+            self.mlp.forward(self.yn, t, out=self.out, addend=self.h1)
+        else:
+            self.mlp.forward(self.yn, t, out=self.mlp_part)
+            self._ar(self.mlp_part, "ar.mlp", t)
+            t.begin("residual2")
+            K.add(self.h1, self.mlp_part, self.out)
+            t.end("residual2")
+        return self.out
