@@ -1,0 +1,363 @@
+#!/usr/bin/env python
+"""Hybrid-layer decode benchmark: tokens/s and p50 step latency of one Falcon-H1-7B-like mixer layer
+(attention 12q/2kv x 128 ∥ Mamba-2 24 x 128, d_state 256, fp32 SSM state, bf16 activations) at decode
+batch 64, context 2048, on 1-8 GPUs.
+
+    python bench.py [--gpus 1] [--steps K] [--warmup W]                 # our arm
+    python bench.py --impl reference [--steps K] [--warmup W]           # the CPU fp32 layer (oracle port)
+    torchrun --nproc-per-node N bench.py --gpus N ...                   # N > 1: branch split and TP recipes
+
+A step is one CUDA-graph replay of the whole layer step (every kernel ours, collectives NCCL); value =
+batch tokens / device step time, max over ranks. Inputs are larger than L2 (403 MB of SSM state), so no
+flush is needed between steps. Prints one JSON line on rank 0.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "hybrid-layer decode tokens/s (p50 decode-step latency alongside)"
+UNIT = "tokens/s"
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=200)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--dims", default="falcon_h1_7b_like")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--ctx", type=int, default=2048)
+    ap.add_argument("--soak-s", type=float, default=1.5, help="replays before timing, with clocks sampled")
+    ap.add_argument("--cpu-s", type=float, default=12.0, help="seconds of CPU fp32 layer timing (rank 0, N=1)")
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args()
+
+
+def workload(args) -> dict:
+    return {"workload": f"{args.dims} mixer layer decode, batch {args.batch}, context {args.ctx}",
+            "dims": args.dims, "batch": args.batch, "ctx": args.ctx, "kv_block": 16, "ssm_state": "fp32",
+            "activations": "bf16", "l2": "inputs larger than L2 (SSM state alone 403 MB), no flush"}
+
+
+# ------------------------------------------------------------------------------------------- CPU layer
+def cpu_layer_tokens_per_s(args, budget_s: float, max_steps: int | None = None) -> dict:
+    """Time the oracle's fp32 layer (a numpy port of the reference's harness/reference.py:decode_step) on
+    this host's cores, full batch, on the same seeded inputs."""
+    import numpy as np
+    import torch
+
+    import oracle
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.state import full_states_for_reference, input_hidden
+    from multi_modal_parallelism_b200.weights import random_layer
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # pragma: no cover
+        threads = os.cpu_count()
+    dims = preset(args.dims)
+    cpu = torch.device("cpu")
+    full = {k: oracle.to_numpy(v) for k, v in random_layer(dims, args.seed).items()}
+    kc, vc, conv, ssm = full_states_for_reference(dims, args.batch, args.ctx, args.seed, cpu)
+    kc, vc, conv, ssm = (oracle.to_numpy(t) for t in (kc, vc, conv, ssm))
+    h = oracle.to_numpy(input_hidden(args.seed, args.batch, dims.hidden, cpu))
+    oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx)  # warm
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while (not times or time.perf_counter() < t_end) and (max_steps is None or len(times) < max_steps):
+        t0 = time.perf_counter()
+        oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": args.batch / med, "unit": UNIT, "cores": int(threads), "kind": "port",
+            "sample": f"{len(times)} full decode steps (batch {args.batch}, context {args.ctx}) of the numpy fp32 "
+                      f"layer, median {med * 1e3:.1f} ms/step, {threads} BLAS threads on {os.cpu_count()} host cores",
+            "ms_per_step": med * 1e3, "steps_timed": len(times)}
+
+
+def reference_arm(args, rank: int) -> None:
+    if rank != 0:
+        return
+    budget = min(120.0, max(10.0, 0.05 * (args.steps + args.warmup)))
+    r = cpu_layer_tokens_per_s(args, budget, max_steps=max(1, args.steps))
+    line = {"metric": METRIC, "value": r["value"], "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": r["steps_timed"], "warmup": 1, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+            "config": {**workload(args), "parallelism": "cpu"},
+            "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": r["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------------------------------- clocks
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------------------- our arm
+def roofline_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+        except Exception:
+            pass
+    return 6650.0, "fallback"
+
+
+def profiled_traffic(name: str) -> float | None:
+    """DRAM bytes per launch from the committed ncu summary of this kernel and workload, if any."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for ln in p.read_text().splitlines():
+        if ln.lower().startswith("dram bytes per launch:"):
+            try:
+                return float(ln.split(":", 1)[1].split()[0].replace(",", ""))
+            except ValueError:
+                return None
+    return None
+
+
+def build_layer(args, mode, groups, dims, full):
+    import torch
+
+    from multi_modal_parallelism_b200.layer import ParallelHybridLayer
+    from multi_modal_parallelism_b200.sharding import plan_for
+    from multi_modal_parallelism_b200.state import alloc_and_fill, input_hidden, make_decode_ctx
+    from multi_modal_parallelism_b200.weights import shard_to_device
+
+    dev = groups.device
+    plan = plan_for(mode, groups.rank, groups.world_size, dims)
+    rw = shard_to_device(full, plan, dims, dev)
+    ctx = make_decode_ctx(args.batch, args.ctx, 16, dev)
+    st = alloc_and_fill(plan, dims, ctx, args.seed, dev, ssm_dtype=torch.float32)
+    h = input_hidden(args.seed, args.batch, dims.hidden, dev)
+    layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev)
+    return layer, h
+
+
+def max_over_ranks(x: float, groups) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if groups.world_size == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=groups.device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def time_replays(fn, steps: int, warmup: int, groups) -> tuple[float, float]:
+    """(ms per step, p50 ms) over `steps` calls, device-timed, max over ranks."""
+    import torch
+
+    from multi_modal_parallelism_b200.dist import barrier_sync
+
+    for _ in range(warmup):
+        fn()
+    barrier_sync()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    ev[0].record()
+    for i in range(steps):
+        fn()
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(steps)]
+    total = ev[0].elapsed_time(ev[-1])
+    barrier_sync()
+    return max_over_ranks(total / steps, groups), max_over_ranks(statistics.median(per), groups)
+
+
+def ssu_roofline(layer, n: int = 50) -> dict | None:
+    """Time the SSU kernel alone on this rank's SSM branch (CUDA events on the launching stream)."""
+    import torch
+
+    from multi_modal_parallelism_b200 import kernels as K
+
+    s = layer.ssm
+    if s is None:
+        return None
+    w, ctx = s.w, s.ctx
+    run = lambda: K.ssm_update(s.st.ssm_state, s.xs, s.dt, w.A, s.Bm, s.Cm, w.D, w.dt_bias, ctx.state_idx, s.y)  # noqa: E731
+    for _ in range(5):
+        run()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(n):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / n
+    B, nh, p, N = ctx.B, s.nhr, s.p, s.N
+    esz = s.st.ssm_state.element_size()
+    # algorithmic bytes: state line read + write, x, dt, B, C, y (bf16), slot indices
+    nbytes = 2 * B * nh * p * N * esz + B * nh * p * 2 * 2 + B * nh * 2 + 2 * B * s.ng * N * 2 + B * 4
+    return {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
+
+
+def our_arm(args) -> None:
+    import torch
+
+    from multi_modal_parallelism_b200 import _lib
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
+    from multi_modal_parallelism_b200.timing import GraphedStep
+    from multi_modal_parallelism_b200.weights import random_layer
+
+    groups = init_groups()
+    world = groups.world_size
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    dims = preset(args.dims)
+    full = random_layer(dims, args.seed)
+    modes = ["tp1"] if world == 1 else [f"split{world // 2}{world // 2}", "tp4_fused"]
+    results = {}
+    keep = {}
+    for mode in modes:
+        layer, h = build_layer(args, mode, groups, dims, full)
+        layer.step(h)  # eager warm-up (allocations, library init)
+        n0 = _lib.LAUNCHES[0]
+        layer.step(h)
+        launches_per_step = _lib.LAUNCHES[0] - n0
+        gs = GraphedStep(layer, groups, h)
+        ms, p50 = time_replays(gs.replay, args.steps, args.warmup, groups)
+        results[mode] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": args.batch / ms * 1e3,
+                         "launches_per_step": launches_per_step}
+        keep[mode] = (layer, h, gs)
+    best = min(results, key=lambda m: results[m]["ms_per_step"])
+    layer, h, gs = keep[best]
+    for m in modes:
+        if m != best:
+            keep[m][2].release()
+
+    # clocks over a soak plus a second timed pass of the headline recipe
+    with Clocks(groups.local_rank) as clk:
+        t_end = time.perf_counter() + args.soak_s
+        while time.perf_counter() < t_end:
+            for _ in range(50):
+                gs.replay()
+            torch.cuda.synchronize()
+        ms2, p50_2 = time_replays(gs.replay, args.steps, 0, groups)
+    clocks = clk.summary()
+    results[best]["ms_per_step_under_clock_sampling"] = ms2
+
+    # end to end through the public call: pinned host input -> device, replay, output -> pinned host
+    h_host = h.detach().cpu().pin_memory()
+    out_host = torch.empty(layer.out.shape, dtype=layer.out.dtype).pin_memory()
+    e2e_ms, _ = time_replays(lambda: gs(h_host, out_host), args.steps, max(3, args.warmup // 10), groups)
+    nbytes_io = h.numel() * h.element_size()
+
+    roof_local = ssu_roofline(layer)
+    if world > 1:
+        import torch.distributed as dist
+
+        allr = [None] * world
+        dist.all_gather_object(allr, roof_local)
+        cands = [r for r in allr if r is not None]
+        roof_local = max(cands, key=lambda r: r["us"]) if cands else None
+    gs.release()
+    for m in modes:
+        keep[m][2].release()
+    barrier_sync()
+
+    cpu = None
+    if groups.rank == 0 and world == 1 and args.cpu_s > 0:
+        cpu = cpu_layer_tokens_per_s(args, args.cpu_s)
+    if groups.rank == 0:
+        peak, peak_src = roofline_peak()
+        roof = None
+        if roof_local is not None:
+            roof = {"kernel": "ssu_decode (mmp_ssu_decode, fp32 state)", "bound": "hbm",
+                    "achieved": roof_local["gbs"], "peak": peak, "unit": "GB/s",
+                    "frac": roof_local["gbs"] / peak, "peak_source": f"{peak_src} hbm_gbs",
+                    "bytes_per_launch": roof_local["bytes"], "us_per_launch": roof_local["us"],
+                    "traffic": profiled_traffic(f"ssu_decode_{args.dims}_b{args.batch}.md")}
+        r = results[best]
+        line = {
+            "metric": METRIC, "value": r["tokens_per_s"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {**workload(args), "parallelism": best,
+                       "recipes": {m: {k: round(v, 5) if isinstance(v, float) else v for k, v in x.items()}
+                                   for m, x in results.items()}},
+            "e2e": {"value": args.batch / e2e_ms * 1e3, "unit": UNIT, "h2d_bytes_per_step": nbytes_io,
+                    "d2h_bytes_per_step": nbytes_io, "ms_per_step": e2e_ms},
+            "gpu_launches": r["launches_per_step"] * args.steps,
+            "roofline": roof,
+            "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    destroy()
+
+
+def main() -> None:
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        reference_arm(args, rank)
+        return
+    our_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -65,5 +65,9 @@ def check(rc: int, what: str) -> None:
         raise MmpError(f"{what}: status {rc}: {msg}")
 
 
-def call(name: str, *args) -> None:
+LAUNCHES = [0]  # kernel launches issued through this module (a counter for launch accounting)
+
+
+def call(name: str, *args, kernels: int = 1) -> None:
     check(getattr(lib(), name)(*args), name)
+    LAUNCHES[0] += kernels

@@ -242,10 +242,12 @@ def attn_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Ten
         if ws is None or ws.numel() * 4 < need:
             ws = _attn_ws[dev] = torch.empty(max(1, (need + 3) // 4), dtype=torch.float32, device=q.device)
         workspace = ws
+    eff = int(splits) if splits > 0 else attn_default_splits(T, nkv, int(max_k))
     _lib.call("mmp_paged_attn_decode", _p(q), q.stride(0), q.stride(1), _p(key_cache), _p(value_cache), cb, ct, ch,
               _p(block_table), block_table.stride(0), _p(seqused_k), _p(out), out.stride(0), out.stride(1),
               T, nq, nkv, hd, blk, nb, int(max_k), 1.0 / math.sqrt(hd), int(splits), _p(workspace),
-              workspace.numel() * workspace.element_size(), _p(error_word(q.device)), _stream(q))
+              workspace.numel() * workspace.element_size(), _p(error_word(q.device)), _stream(q),
+              kernels=2 if eff > 1 else 1)
     return out
 
 

@@ -101,3 +101,31 @@ def time_graph(layer, h: torch.Tensor, n_warm: int, n_iter: int, groups: Groups)
     torch.cuda.synchronize()
     wall = (time.perf_counter() - t0) * 1e3 / n_iter
     return {"step": stats([s.elapsed_time(e) for s, e in events])}, wall
+
+
+class GraphedStep:
+    """A layer decode step captured once and replayed: the serving call. `__call__(h_host, out_host)` copies
+    the step's input from (pinned) host memory into the captured input buffer, replays the step, and copies
+    the output back to host memory, all on the current stream."""
+
+    def __init__(self, layer, groups: Groups, h_static: torch.Tensor):
+        self.layer = layer
+        self.h = h_static
+        self.graph = capture_step(layer, h_static, groups)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.layer.out
+
+    def __call__(self, h_host: torch.Tensor | None = None, out_host: torch.Tensor | None = None) -> torch.Tensor:
+        if h_host is not None:
+            self.h.copy_(h_host, non_blocking=True)
+        self.graph.replay()
+        if out_host is None:
+            return self.layer.out
+        out_host.copy_(self.layer.out, non_blocking=True)
+        return out_host
+
+    def release(self) -> None:
+        """Drop the graph (graphs holding NCCL calls must go before the process group is destroyed)."""
+        self.graph = None
