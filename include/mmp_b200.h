@@ -149,6 +149,24 @@ int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
                           int max_seqlen, float scale, int splits, void* workspace, size_t workspace_bytes,
                           int* err, void* stream);
 
+/* ---- paged GQA decode attention without a caller workspace --------------------------------------------
+ * No counterpart in the reference. For callers that cannot allocate device memory — an engine that has
+ * already reserved the free HBM for its own pools, code that must not call cudaFree (it synchronises the
+ * device), or a foreign-language host that binds only this ABI — this variant of mmp_paged_attn_decode
+ * keeps its split-K partials in a fixed scratch array of MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES (8 MiB) inside
+ * the library, held by every GPU that loads it until the process exits. Same arguments and results as
+ * mmp_paged_attn_decode without the workspace; returns MMP_ERR_INVALID when batch x nq x splits x
+ * (hd + 2) x 4 bytes exceeds the array. The first call on a device looks up the array's address there:
+ * make it before any stream capture. Calls share the array: calls that overlap on the GPU race.
+ */
+#define MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
+int mmp_paged_attn_decode_noalloc(const void* q, int64_t q_b, int64_t q_h,
+                                  const void* key_cache, const void* value_cache, int64_t c_block, int64_t c_tok,
+                                  int64_t c_head, const int32_t* block_table, int64_t bt_stride,
+                                  const int32_t* seqlens, void* out, int64_t o_b, int64_t o_h,
+                                  int batch, int nq, int nkv, int hd, int block_size, int num_blocks,
+                                  int max_seqlen, float scale, int splits, int* err, void* stream);
+
 /* ---- bf16 GEMM with fused epilogue ----------------------------------------------------------------
  * Replaces kernels.gemm / gemm_T (harness/kernels.py:147-154) together with the scaling the layer
  * applies to their results (harness/layer.py:35,80,105): out[m,n] = alpha * colscale[n] * sum_k

@@ -337,3 +337,71 @@ extern "C" int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
   paged_attn_merge_kernel<128><<<dim3(nq, batch), 128, 0, s>>>(P);
   return mmp_check_launch("mmp_paged_attn_decode(merge)");
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// Allocation-free variant of the paged decode attention.
+//
+// Some callers cannot hand us a workspace: a serving engine that reserved all free HBM for its KV-cache pool
+// at start-up (a later cudaMalloc fails or fragments that pool), code that must not call cudaFree (it
+// synchronises the whole device), and hosts in other languages that bind only this C ABI and own no device
+// allocator. For them the split-K partials live in the fixed array below, which every GPU that loads this
+// library holds until the process exits. Its device address is looked up once per device with that device
+// current (cudaGetSymbolAddress) on the first call there; make that first call before any stream capture.
+// All calls share the array, so calls that overlap on the GPU (two streams, two threads) race on it; every
+// partial slot the merge reads is rewritten by the same call, so nothing needs clearing between calls.
+#include <mutex>
+
+static __device__ __align__(256) float g_attn_noalloc_scratch[MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+constexpr int kMaxDevices = 64;
+void* g_noalloc_addr[kMaxDevices] = {};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void** addr) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return mmp_set_error(MMP_ERR_UNSUPPORTED, "mmp_paged_attn_decode_noalloc: device %d", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_noalloc_addr[dev] = p;
+  }
+  *addr = g_noalloc_addr[dev];
+  return MMP_OK;
+}
+}  // namespace
+
+extern "C" int mmp_paged_attn_decode_noalloc(const void* q, int64_t q_b, int64_t q_h,
+                                             const void* key_cache, const void* value_cache, int64_t c_block, int64_t c_tok,
+                                             int64_t c_head, const int32_t* block_table, int64_t bt_stride,
+                                             const int32_t* seqlens, void* out, int64_t o_b, int64_t o_h,
+                                             int batch, int nq, int nkv, int hd, int block_size, int num_blocks,
+                                             int max_seqlen, float scale, int splits, int* err, void* stream) {
+  if (batch == 0) return MMP_OK;
+  if (batch < 0 || nq <= 0 || nkv <= 0 || hd <= 0 || max_seqlen < 0)
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_paged_attn_decode_noalloc: bad sizes");
+  // the split count the kernel will run with, as mmp_paged_attn_decode normalises it
+  const int max_tiles = std::max(1, (max_seqlen + TILE - 1) / TILE);
+  int s = splits > 0 ? std::min(splits, max_tiles) : mmp_paged_attn_default_splits(batch, nkv, max_seqlen);
+  const int tps = (max_tiles + s - 1) / s;
+  s = (max_tiles + tps - 1) / tps;
+  const size_t need = mmp_paged_attn_workspace_size(batch, nq, hd, s);
+  if (need > MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES)
+    return mmp_set_error(MMP_ERR_INVALID,
+                         "mmp_paged_attn_decode_noalloc: batch %d x %d heads x %d splits needs %zu bytes of scratch, "
+                         "more than the %zu bytes this entry point holds; use fewer splits or mmp_paged_attn_decode "
+                         "with a workspace", batch, nq, s, need, (size_t)MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES);
+  void* ws = nullptr;
+  if (need > 0) {
+    const int rc = noalloc_scratch(&ws);
+    if (rc != MMP_OK) return rc;
+  }
+  return mmp_paged_attn_decode(q, q_b, q_h, key_cache, value_cache, c_block, c_tok, c_head, block_table, bt_stride,
+                               seqlens, out, o_b, o_h, batch, nq, nkv, hd, block_size, num_blocks, max_seqlen, scale, s,
+                               ws, need > 0 ? (size_t)MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES : 0, err, stream);
+}

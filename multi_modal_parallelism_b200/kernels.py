@@ -251,6 +251,31 @@ def attn_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Ten
     return out
 
 
+def attn_decode_noalloc(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, seqused_k: torch.Tensor,
+                        max_k: int, block_table: torch.Tensor, out: torch.Tensor, splits: int = 0) -> torch.Tensor:
+    """attn_decode for callers that cannot allocate device memory (an engine that has reserved the free HBM
+    for its own pools, code that must not call cudaFree, hosts that only bind the C ABI): the split-K
+    partials go to a fixed 8 MiB array inside the library instead of a workspace. This wrapper allocates
+    nothing either. Calls share that array, so calls that overlap on the GPU race; the first call on a device
+    sets the array up and should come before any stream capture. Raises ValueError when the request needs more
+    scratch than the array holds."""
+    _cuda("attn_decode_noalloc", q, key_cache, value_cache, seqused_k, block_table, out)
+    _dtype("attn_decode_noalloc", block_table, torch.int32)
+    _dtype("attn_decode_noalloc", seqused_k, torch.int32)
+    T, nq, hd = q.shape
+    nkv = key_cache.shape[2]
+    cb, ct, ch, blk, nb = _cache_strides(key_cache, value_cache)
+    if q.stride(2) != 1 or out.stride(2) != 1:
+        raise ValueError("attn_decode_noalloc: head dimension must be contiguous")
+    eff = int(splits) if splits > 0 else attn_default_splits(T, nkv, int(max_k))
+    err = _err_words.get(q.device.index or 0)
+    _lib.call("mmp_paged_attn_decode_noalloc", _p(q), q.stride(0), q.stride(1), _p(key_cache), _p(value_cache), cb,
+              ct, ch, _p(block_table), block_table.stride(0), _p(seqused_k), _p(out), out.stride(0), out.stride(1),
+              T, nq, nkv, hd, blk, nb, int(max_k), 1.0 / math.sqrt(hd), int(splits), _p(err), _stream(q),
+              kernels=2 if eff > 1 else 1)
+    return out
+
+
 # ----------------------------------------------------------------------------- mamba-2 decode
 def conv_update(xBC: torch.Tensor, conv_state_T: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None,
                 idx: torch.Tensor | None, out: torch.Tensor | None = None, activation: str | None = "silu",
