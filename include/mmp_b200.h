@@ -178,6 +178,16 @@ int mmp_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* 
                   int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
                   void* stream);
 
+/* ---- bf16 GEMM on the tensor cores (tcgen05 / TMEM / TMA) ---------------------------------------------
+ * Same contract as mmp_gemm_bf16 (harness/kernels.py:147-154 plus the layer's scalings), computed with
+ * 128-row UMMA tiles fed by TMA: M <= 256 runs weight-streaming (the weight rows are the MMA's M side,
+ * split-K over a thread-block cluster when the tiles cannot fill the GPU); larger M runs 128 x 256 tiles.
+ * err: optional device error word (MMP_DEVERR_TIMEOUT if a pipeline wait ran out).
+ */
+int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
+                     int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
+                     int* err, void* stream);
+
 /* ---- elementwise add (residual joins after a collective) -------------------------------------------
  * Replaces the layer's bf16 `a + b (+ c)` residual sums (harness/layer.py:217-219,225-227):
  * out = a + b (+ c when c != NULL), computed in fp32, rounded once to bf16. [rows, cols] with row strides

@@ -49,24 +49,38 @@ __device__ __forceinline__ uint32_t word(const uint4& u, int j) {
   return j == 0 ? u.x : j == 1 ? u.y : j == 2 ? u.z : u.w;
 }
 
-// Address of token `tok` of sequence b for KV head kh, or nullptr if the token is past the end or its
-// block index is out of range (flagged).
-__device__ __forceinline__ const bf16* token_row(const AttnParams& P, const bf16* cache, int b, int kh, int tok,
-                                                 int seqlen) {
-  if (tok >= seqlen) return nullptr;
-  const int col = tok / P.block_size;
-  const int blk = col < P.bt_stride ? P.block_table[b * P.bt_stride + col] : -1;
-  if (blk < 0 || blk >= P.num_blocks) {
-    flag_error(P.err, DEVERR_INDEX);
-    return nullptr;
-  }
-  return cache + blk * P.c_block + (tok % P.block_size) * P.c_tok + kh * P.c_head;
+constexpr int STAGES = 3;           // pages in flight per warp
+constexpr int PAGE_BYTES = TILE * 512; // 16 tokens x (128 keys + 128 values) x bf16
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N)); }
+__device__ __forceinline__ uint4 lds16(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+// byte offset of 16-byte chunk c (0..15 keys, 16..31 values) of token row r inside a page; rows r and r^1 use
+// opposite halves of the bank space so a quarter-warp reading rows g, g+1 never conflicts
+__device__ __forceinline__ uint32_t page_off(int r, int c) { return r * 512 + ((c ^ ((r & 1) << 2)) << 4); }
+
+// Block id holding tile `tile` of sequence b (a 16-token tile never straddles a block: block % 16 == 0),
+// or -1 past the table / out of range (flagged).
+__device__ __forceinline__ int tile_block(const AttnParams& P, int b, int tile) {
+  const int col = (tile * TILE) / P.block_size;
+  if (col >= P.bt_stride) return -1;
+  const int blk = P.block_table[b * P.bt_stride + col];
+  return (blk >= 0 && blk < P.num_blocks) ? blk : -1;
 }
 
 template <int HD, int MAXH>
 __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const AttnParams P) {
   static_assert(HD == 128, "head_dim 128");
-  constexpr int KP = HD / 32;  // 32-dim slabs: one 16-byte load per lane per token row
+  constexpr int KP = HD / 32;  // 32-dim slabs: one 16-byte chunk per lane per token row
+  extern __shared__ __align__(128) uint8_t smem[];
   const int split = blockIdx.x, kh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -76,6 +90,27 @@ __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const Attn
   const int ntiles = (seqlen + TILE - 1) / TILE;
   const int tile_lo = split * P.tiles_per_split;
   const int tile_hi = min(ntiles, tile_lo + P.tiles_per_split);
+  // this warp's tiles: tile_lo + warp + i * WARPS, i < n_w
+  const int n_w = tile_hi > tile_lo + warp ? (tile_hi - tile_lo - warp + WARPS - 1) / WARPS : 0;
+  const uint32_t ring = static_cast<uint32_t>(__cvta_generic_to_shared(smem)) + warp * STAGES * PAGE_BYTES;
+
+  // Copy page i of this warp into ring slot i % STAGES: lane l moves chunk l of each of the 16 token rows
+  // (chunks 0-15 from the key row, 16-31 from the value row); rows past the sequence are zero-filled.
+  int blk_next = n_w > 0 ? tile_block(P, b, tile_lo + warp) : -1;
+  auto issue = [&](int i) {
+    const int tile = tile_lo + warp + i * WARPS;
+    const int blk = blk_next;
+    if (i + 1 < n_w) blk_next = tile_block(P, b, tile + WARPS);  // one page ahead: hides the table read
+    if (blk < 0 && tile * TILE < seqlen) flag_error(P.err, DEVERR_INDEX);
+    const int off0 = (tile * TILE) % P.block_size;
+    const bf16* base = (lane < 16 ? P.kc : P.vc) + (blk < 0 ? 0 : blk) * P.c_block + kh * P.c_head + (lane & 15) * 8;
+    const uint32_t dst = ring + (i % STAGES) * PAGE_BYTES;
+#pragma unroll
+    for (int r = 0; r < TILE; ++r) {
+      const bool valid = blk >= 0 && tile * TILE + r < seqlen;
+      cp_async16(dst + page_off(r, lane), base + (off0 + r) * P.c_tok, valid);
+    }
+  };
 
   // Query fragments: rows g and g+8 are query heads head0+g, head0+g+8 (zero beyond hpk).
   uint4 qa[KP], qb[KP];
@@ -97,23 +132,27 @@ __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const Attn
       for (int e = 0; e < 4; ++e) o[a][j][e] = 0.f;
   float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
 
-  for (int tile = tile_lo + warp; tile < tile_hi; tile += WARPS) {
-    const int tok_a = tile * TILE + g, tok_b = tok_a + 8;
-    const bf16* ka = token_row(P, P.kc, b, kh, tok_a, seqlen);
-    const bf16* kb = token_row(P, P.kc, b, kh, tok_b, seqlen);
-    const bf16* va = token_row(P, P.vc, b, kh, tok_a, seqlen);
-    const bf16* vb = token_row(P, P.vc, b, kh, tok_b, seqlen);
+#pragma unroll
+  for (int s = 0; s < STAGES - 1; ++s) {
+    if (s < n_w) issue(s);
+    cp_async_commit();
+  }
+  for (int i = 0; i < n_w; ++i) {
+    if (i + STAGES - 1 < n_w) issue(i + STAGES - 1);
+    cp_async_commit();
+    cp_async_wait<STAGES - 1>();
+    __syncwarp();
+    const uint32_t page = ring + (i % STAGES) * PAGE_BYTES;
+    const int tile = tile_lo + warp + i * WARPS;
     uint4 kr[2][KP], vr[2][KP];
 #pragma unroll
     for (int kp = 0; kp < KP; ++kp) {
-      kr[0][kp] = ka ? ld_stream16(ka + kp * 32 + 8 * t) : make_uint4(0, 0, 0, 0);
-      kr[1][kp] = kb ? ld_stream16(kb + kp * 32 + 8 * t) : make_uint4(0, 0, 0, 0);
+      kr[0][kp] = lds16(page + page_off(g, kp * 4 + t));
+      kr[1][kp] = lds16(page + page_off(g + 8, kp * 4 + t));
+      vr[0][kp] = lds16(page + page_off(g, 16 + kp * 4 + t));
+      vr[1][kp] = lds16(page + page_off(g + 8, 16 + kp * 4 + t));
     }
-#pragma unroll
-    for (int kp = 0; kp < KP; ++kp) {
-      vr[0][kp] = va ? ld_stream16(va + kp * 32 + 8 * t) : make_uint4(0, 0, 0, 0);
-      vr[1][kp] = vb ? ld_stream16(vb + kp * 32 + 8 * t) : make_uint4(0, 0, 0, 0);
-    }
+    __syncwarp();  // the ring slot may be refilled by the next iteration's copy
     // S = Q K^T for the two 8-token halves
     float s[2][4];
 #pragma unroll
@@ -181,6 +220,7 @@ __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const Attn
       }
     }
   }
+  cp_async_wait<0>();
 
   // row sums live spread over the 4 lanes of a row group
 #pragma unroll
@@ -189,9 +229,11 @@ __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const Attn
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
   }
 
-  // merge the warps in shared memory
-  __shared__ float sm_o[WARPS][MAXH][HD];
-  __shared__ float sm_m[WARPS][MAXH], sm_l[WARPS][MAXH];
+  // merge the warps in shared memory (reusing the page rings)
+  __syncthreads();
+  float (*sm_o)[MAXH][HD] = reinterpret_cast<float (*)[MAXH][HD]>(smem);
+  float (*sm_m)[MAXH] = reinterpret_cast<float (*)[MAXH]>(smem + WARPS * MAXH * HD * 4);
+  float (*sm_l)[MAXH] = reinterpret_cast<float (*)[MAXH]>(smem + WARPS * MAXH * HD * 4 + WARPS * MAXH * 4);
   if (t == 0) {
     sm_m[warp][g] = m_lo;
     sm_l[warp][g] = l_lo;
@@ -241,6 +283,9 @@ __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const Attn
   }
 }
 
+constexpr int SPLIT_SMEM = WARPS * STAGES * PAGE_BYTES;  // >= the merge area (4 x 16 x 128 x 4 + 2 x 4 x 16 x 4)
+static_assert(SPLIT_SMEM >= WARPS * 16 * 128 * 4 + 2 * WARPS * 16 * 4, "merge area must fit in the page rings");
+
 template <int HD>
 __global__ void __launch_bounds__(HD) paged_attn_merge_kernel(const AttnParams P) {
   const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
@@ -259,6 +304,7 @@ __global__ void __launch_bounds__(HD) paged_attn_merge_kernel(const AttnParams P
 }
 
 int g_num_sms = 0;
+bool g_smem_attr[64] = {};
 
 int sm_count() {
   if (g_num_sms == 0) {
@@ -280,12 +326,23 @@ extern "C" size_t mmp_paged_attn_workspace_size(int batch, int nq, int hd, int s
   return static_cast<size_t>(batch) * nq * splits * (hd + 2) * sizeof(float);
 }
 
-// Split count: enough CTAs for ~4 waves of resident CTAs, at least 4 tiles per split.
+// Split count from a waves x tiles-per-warp cost model (2 resident CTAs per SM, STAGES-1 pages of pipeline
+// fill per warp, one extra unit for the merge pass when split).
 static int choose_splits(int batch, int nkv, int max_tiles) {
-  const int target = 4 * sm_count();
-  int s = (target + batch * nkv - 1) / (batch * nkv);
-  s = std::min(s, std::max(1, max_tiles / 4));
-  return std::max(1, std::min(s, 64));
+  const int slots = 2 * sm_count();
+  int best = 1;
+  long best_cost = -1;
+  for (int s = 1; s <= std::min(64, max_tiles); ++s) {
+    const long ctas = static_cast<long>(batch) * nkv * s;
+    const long waves = (ctas + slots - 1) / slots;
+    const int tps = (max_tiles + s - 1) / s;
+    const long cost = waves * ((tps + WARPS - 1) / WARPS + STAGES - 1) + (s > 1 ? 1 : 0);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 extern "C" int mmp_paged_attn_default_splits(int batch, int nkv, int max_seqlen) {
@@ -330,8 +387,15 @@ extern "C" int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
                scale * 1.4426950408889634f, err};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(splits, nkv, batch);
-  if (nq / nkv <= 8) paged_attn_split_kernel<128, 8><<<grid, WARPS * 32, 0, s>>>(P);
-  else paged_attn_split_kernel<128, 16><<<grid, WARPS * 32, 0, s>>>(P);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !g_smem_attr[dev]) {
+    cudaFuncSetAttribute(paged_attn_split_kernel<128, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, SPLIT_SMEM);
+    cudaFuncSetAttribute(paged_attn_split_kernel<128, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SPLIT_SMEM);
+    g_smem_attr[dev] = true;
+  }
+  if (nq / nkv <= 8) paged_attn_split_kernel<128, 8><<<grid, WARPS * 32, SPLIT_SMEM, s>>>(P);
+  else paged_attn_split_kernel<128, 16><<<grid, WARPS * 32, SPLIT_SMEM, s>>>(P);
   int rc = mmp_check_launch("mmp_paged_attn_decode");
   if (rc != MMP_OK || splits == 1) return rc;
   paged_attn_merge_kernel<128><<<dim3(nq, batch), 128, 0, s>>>(P);

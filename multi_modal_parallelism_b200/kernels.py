@@ -376,6 +376,27 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, alph
     return out
 
 
+def gemm_tc(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
+            colscale: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
+    """gemm on the tcgen05 tensor-core kernel."""
+    _cuda("gemm_tc", x, w, out, colscale, addend)
+    for t in (x, w, out, addend):
+        _dtype("gemm_tc", t, BF16)
+    _dtype("gemm_tc", colscale, torch.float32)
+    M, K = x.shape
+    N = w.shape[0]
+    if w.shape[1] != K:
+        raise ValueError(f"gemm_tc: x has K={K}, w has K={w.shape[1]}")
+    if out is None:
+        out = torch.empty(M, N, dtype=BF16, device=x.device)
+    if colscale is not None:
+        colscale = colscale.reshape(-1)
+    _lib.call("mmp_gemm_bf16_tc", _p(x), _rowmajor("x", x), _p(w), _rowmajor("w", w), _p(out), _rowmajor("out", out),
+              M, N, K, float(alpha), _p(colscale), _p(addend), 0 if addend is None else _rowmajor("addend", addend),
+              _p(error_word(x.device)), _stream(x))
+    return out
+
+
 def gemm_T(x: torch.Tensor, wT: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
            colscale: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
     """x [T, k] @ wT [k, out]. Fast when wT is the transpose of a row-major [out, k] matrix."""

@@ -269,3 +269,19 @@ def test_gemm_strided_operands():
     out = torch.zeros(64, 3008, dtype=BF, device=DEV)[:, :3000]
     K.gemm(x, wd, out=out)
     close(npf(out), (big[:, 1024:3072].float() @ w[:, :2048].float().T).numpy())
+
+
+@pytest.mark.parametrize("M,N,K_", [(64, 6680, 3072), (64, 2048, 3072), (64, 3072, 1536), (2, 100, 64), (1, 8, 8),
+                                    (128, 5120, 8192), (100, 640, 520), (256, 512, 1024), (300, 200, 136),
+                                    (2048, 6680, 3072), (1000, 1000, 1000)])
+def test_gemm_tc_matches_fp32(M, N, K_):
+    g = torch.Generator().manual_seed(M * 3 + N + K_)
+    x = torch.randn(M, K_, generator=g).to(BF)
+    w = (torch.randn(N, K_, generator=g) * 0.02).to(BF)
+    cs = torch.rand(N, generator=g) + 0.5
+    add = torch.randn(M, N, generator=g).to(BF)
+    ref = (x.float() @ w.float().T) * 0.7 * cs + add.float()
+    out = K.gemm_tc(x.to(DEV), w.to(DEV), alpha=0.7, colscale=cs.to(DEV), addend=add.to(DEV))
+    close(npf(out), ref.numpy())
+    out2 = K.gemm_tc(x.to(DEV), w.to(DEV))
+    close(npf(out2), (x.float() @ w.float().T).numpy())
