@@ -188,6 +188,17 @@ int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64_t ldw, voi
                      int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
                      int* err, void* stream);
 
+/* ---- bf16 GEMM over two K segments with their own scales ---------------------------------------------
+ * Replaces the reference layer's two output projections and their sum (harness/layer.py:51-53,103-105,
+ * 213-219: o_proj * attn_out + out_proj * ssm_out) when one rank holds both branches: with the two
+ * activations side by side in `a` and the two weights side by side in `w`,
+ *   out = alpha * a[:, :k_seg] w[:, :k_seg]^T + alpha2 * a[:, k_seg:] w[:, k_seg:]^T, then colscale, addend.
+ * k_seg is a multiple of 64 (k_seg >= K: one segment). Otherwise as mmp_gemm_bf16_tc.
+ */
+int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
+                      int M, int N, int K, float alpha, int k_seg, float alpha2, const float* colscale,
+                      const void* addend, int64_t ldd, int* err, void* stream);
+
 /* ---- elementwise add (residual joins after a collective) -------------------------------------------
  * Replaces the layer's bf16 `a + b (+ c)` residual sums (harness/layer.py:217-219,225-227):
  * out = a + b (+ c when c != NULL), computed in fp32, rounded once to bf16. [rows, cols] with row strides

@@ -37,6 +37,7 @@ SIGNATURES: dict[str, tuple] = {
                                             I32, I32, I32, I32, F32, I32, P, P]),
     "mmp_gemm_bf16": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, F32, P, P, I64, P]),
     "mmp_gemm_bf16_tc": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, F32, P, P, I64, P, P]),
+    "mmp_gemm_bf16_seg": (I32, [P, I64, P, I64, P, I64, I32, I32, I32, F32, I32, F32, P, P, I64, P, P]),
     "mmp_add": (I32, [P, I64, P, I64, P, I64, P, I64, I32, I32, P]),
 }
 

@@ -34,6 +34,8 @@ struct TcParams {
   int k_tiles_per_split;
   bf16* out; int64_t ldo;
   float alpha;
+  int k_seg_tile;  // k-tiles from here on accumulate into a second TMEM accumulator scaled by alpha2
+  float alpha2;
   const float* colscale;
   const bf16* addend; int64_t ldd;
   int* err;
@@ -129,12 +131,32 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 }
 
+// 16 accumulator columns of this thread's TMEM lane, scaled: alpha * acc0 + alpha2 * acc1 (an accumulator
+// this CTA never wrote contributes nothing). Warp-collective.
+template <int BN>
+__device__ __forceinline__ void load_scaled_bn(const TcParams& P, uint32_t taddr, bool has0, bool has1, float* v) {
+  float a[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) v[j] = 0.f;
+  if (has0) {
+    tmem_ld16(taddr, a);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = a[j] * P.alpha;
+  }
+  if (has1) {
+    tmem_ld16(taddr + BN, a);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = fmaf(a[j], P.alpha2, v[j]);
+  }
+}
+#define load_scaled(P, taddr, h0, h1, v) load_scaled_bn<BN>(P, taddr, h0, h1, v)
+
 // out element (a_row i, b_row j): transposed tiles write out[j][i], plain tiles out[i][j]; colscale is
 // indexed by the output column.
 template <bool TRANS>
-__device__ __forceinline__ void store_out(const TcParams& P, int i, int j, float acc) {
+__device__ __forceinline__ void store_out(const TcParams& P, int i, int j, float scaled) {
   const int r = TRANS ? j : i, c = TRANS ? i : j;
-  float v = acc * P.alpha;
+  float v = scaled;
   if (P.colscale) v *= P.colscale[c];
   if (P.addend) v += bf2f(P.addend[static_cast<int64_t>(r) * P.ldd + c]);
   P.out[static_cast<int64_t>(r) * P.ldo + c] = f2bf(v);
@@ -154,6 +176,9 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   const int k_tiles = (P.K + TBK - 1) / TBK;
   const int kt0 = blockIdx.z * P.k_tiles_per_split;
   const int nkt = max(0, min(k_tiles, kt0 + P.k_tiles_per_split) - kt0);
+  // K segments: tiles [0, k_seg_tile) go to accumulator 0 (alpha), the rest to accumulator 1 (alpha2)
+  const bool has0 = kt0 < min(kt0 + nkt, P.k_seg_tile), has1 = kt0 + nkt > max(kt0, P.k_seg_tile);
+  const uint32_t tmem_cols = P.k_seg_tile < k_tiles ? 2 * BN : BN;
   auto full_bar = [&](int s) { return sbase + L::BARS + 8 * s; };
   auto empty_bar = [&](int s) { return sbase + L::BARS + 8 * (STAGES + s); };
   const uint32_t done_bar = sbase + L::BARS + 8 * (2 * STAGES);
@@ -172,7 +197,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tmem_slot)), "r"(BN));
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tmem_slot)), "r"(tmem_cols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
   }
   tc_fence_before();
@@ -200,14 +225,18 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc<BN>();
+      bool started0 = false, started1 = false;
       for (int i = 0; i < nkt; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait(full_bar(s), (i / STAGES) & 1, abort_flag, P.err)) break;
         tc_fence_after();
         const uint32_t a_s = sbase + s * L::STAGE_BYTES, b_s = a_s + L::A_BYTES;
+        const int acc = kt0 + i >= P.k_seg_tile ? 1 : 0;
 #pragma unroll
         for (int kk = 0; kk < TBK / 16; ++kk)
-          umma_f16(tmem, umma_desc(a_s + kk * 32), umma_desc(b_s + kk * 32), idesc, (i | kk) != 0);
+          umma_f16(tmem + acc * BN, umma_desc(a_s + kk * 32), umma_desc(b_s + kk * 32), idesc,
+                   (acc ? started1 : started0) || kk != 0);
+        if (acc) started1 = true; else started0 = true;
         umma_commit(empty_bar(s));
       }
       umma_commit(done_bar);  // arrives once every MMA issued above has completed
@@ -227,7 +256,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
-        tmem_ld16(t_lane + c0, v);
+        load_scaled(P, t_lane + c0, has0, has1, v);
         if (arow < P.a_rows) {
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -265,7 +294,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
       for (int c0 = 0; c0 < BN; c0 += 16) {
         float v[16];
         if (have) {
-          tmem_ld16(t_lane + c0, v);
+          load_scaled(P, t_lane + c0, has0, has1, v);
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] = 0.f;
@@ -301,7 +330,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(BN));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(tmem_cols));
   }
 }
 
@@ -375,12 +404,20 @@ using namespace mmp;
 extern "C" int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
                                 int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
                                 int* err, void* stream) {
+  return mmp_gemm_bf16_seg(a, lda, w, ldw, out, ldo, M, N, K, alpha, K, alpha, colscale, addend, ldd, err, stream);
+}
+
+extern "C" int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
+                                 int M, int N, int K, float alpha, int k_seg, float alpha2, const float* colscale,
+                                 const void* addend, int64_t ldd, int* err, void* stream) {
   if (M == 0 || N == 0) return MMP_OK;
   if (!a || !w || !out) return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_tc: null pointer");
   if (M < 0 || N < 0 || K <= 0 || K % 8 || lda % 8 || ldw % 8 || !aligned16(a) || !aligned16(w) || lda < K ||
       ldw < K || ldo < N || (addend && ldd < N))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_tc: M=%d N=%d K=%d lda=%lld ldw=%lld: K and strides must be "
                          "multiples of 8 with 16-byte aligned bases", M, N, K, (long long)lda, (long long)ldw);
+  if (k_seg < K && (k_seg <= 0 || k_seg % TBK))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_seg: k_seg %d must be a positive multiple of %d", k_seg, TBK);
   int rc = get_encoder();
   if (rc != MMP_OK) return rc;
   if (g_tc_sms == 0) {
@@ -391,7 +428,9 @@ extern "C" int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64
   }
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int k_tiles = (K + TBK - 1) / TBK;
-  TcParams P{0, 0, K, k_tiles, static_cast<bf16*>(out), ldo, alpha, colscale, static_cast<const bf16*>(addend), ldd, err};
+  const int k_seg_tile = k_seg < K ? k_seg / TBK : k_tiles;
+  TcParams P{0, 0, K, k_tiles, static_cast<bf16*>(out), ldo, alpha, k_seg_tile, alpha2, colscale,
+             static_cast<const bf16*>(addend), ldd, err};
   CUtensorMap ma, mb;
   if (M <= 256) {
     // decode: swap-AB, A = weight rows (the 128-row M side of the MMA), B = the <= 256 activation rows

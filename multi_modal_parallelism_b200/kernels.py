@@ -354,8 +354,10 @@ def ssm_update(state: torch.Tensor, x: torch.Tensor, dt: torch.Tensor, A: torch.
 
 # ----------------------------------------------------------------------------- gemm
 def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, alpha: float = 1.0,
-         colscale: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
-    """out = alpha * colscale * (x [T, in] @ w[out, in]^T) + addend."""
+         colscale: torch.Tensor | None = None, addend: torch.Tensor | None = None, k_seg: int | None = None,
+         alpha2: float | None = None) -> torch.Tensor:
+    """out = alpha * colscale * (x [T, in] @ w[out, in]^T) + addend, on the tcgen05 tensor cores.
+    With k_seg, columns [k_seg, in) of x and w are a second segment scaled by alpha2 instead of alpha."""
     _cuda("gemm", x, w, out, colscale, addend)
     for t in (x, w, out, addend):
         _dtype("gemm", t, BF16)
@@ -370,9 +372,11 @@ def gemm(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, alph
         colscale = colscale.reshape(-1)
         if colscale.numel() != N or not colscale.is_contiguous():
             raise ValueError("gemm: colscale must be a contiguous [N] fp32 vector")
-    _lib.call("mmp_gemm_bf16", _p(x), _rowmajor("x", x), _p(w), _rowmajor("w", w), _p(out), _rowmajor("out", out),
-              M, N, K, float(alpha), _p(colscale), _p(addend), 0 if addend is None else _rowmajor("addend", addend),
-              _stream(x))
+    ks = K if k_seg is None else int(k_seg)
+    a2 = float(alpha if alpha2 is None else alpha2)
+    _lib.call("mmp_gemm_bf16_seg", _p(x), _rowmajor("x", x), _p(w), _rowmajor("w", w), _p(out), _rowmajor("out", out),
+              M, N, K, float(alpha), ks, a2, _p(colscale), _p(addend), 0 if addend is None else _rowmajor("addend", addend),
+              _p(error_word(x.device)), _stream(x))
     return out
 
 

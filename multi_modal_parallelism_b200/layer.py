@@ -37,16 +37,20 @@ class AttentionBranch:
     name = "attn"
 
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
-                 device: torch.device):
+                 device: torch.device, qkv: torch.Tensor | None = None, out: torch.Tensor | None = None):
+        """qkv / out: optional [B, qkv rows] and [B, nq*hd] views into buffers shared with the other branch
+        (the fused projections of a rank that holds both)."""
         a = plan.attn
         assert a is not None
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
         self.nq, self.nkv, self.hd = len(a.q_heads), len(a.kv_heads), dims.head_dim
         self.inv_freq = K.rope_inv_freq(self.hd, dims.rope_theta, device)
         B = ctx.B
-        self.qkv = torch.empty(B, w.wqkv.shape[0], device=device, dtype=BF16)
+        self.qkv = qkv if qkv is not None else torch.empty(B, w.wqkv.shape[0], device=device, dtype=BF16)
         self.q = torch.empty(B, self.nq * self.hd, device=device, dtype=BF16)
-        self.out = torch.empty(B, self.nq, self.hd, device=device, dtype=BF16)
+        o2 = out if out is not None else torch.empty(B, self.nq * self.hd, device=device, dtype=BF16)
+        self.out = o2.view(B, self.nq, self.hd)
+        self.out2d = o2
         self.splits = K.attn_default_splits(B, self.nkv, ctx.max_k)
         self.ws = K.attn_workspace(B, self.nq, self.hd, self.splits, device)
 
@@ -54,26 +58,36 @@ class AttentionBranch:
     def rope_cache(self) -> torch.Tensor:
         return K.rope_cos_sin_cache(self.hd, self.ctx.c + 2, self.dims.rope_theta, self.inv_freq.device)
 
-    def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
-               x_scale: float = 1.0) -> torch.Tensor:
-        """x: [B, H] (already multiplied by attn_in unless x_scale carries it). Returns the o_proj partial
-        times attn_out (+ addend), written to `out`."""
-        w, ctx, d = self.w, self.ctx, self.dims
+    def project_in(self, x: torch.Tensor, t: OpTimer, x_scale: float = 1.0) -> None:
         t.begin("attn.qkv")
-        K.gemm(x, w.wqkv, out=self.qkv, alpha=x_scale)
+        K.gemm(x, self.w.wqkv, out=self.qkv, alpha=x_scale)
         t.end("attn.qkv")
+
+    def core(self, t: OpTimer) -> None:
+        """key_mult + RoPE + paged KV write, then paged decode attention into self.out."""
+        ctx = self.ctx
         t.begin("attn.rope_kv")
-        K.qkv_rope_kv_write(self.qkv, self.nq, self.nkv, self.hd, ctx.positions, self.inv_freq, d.key_mult, self.q,
-                            self.st.key_cache, self.st.value_cache, ctx.slot_mapping)
+        K.qkv_rope_kv_write(self.qkv, self.nq, self.nkv, self.hd, ctx.positions, self.inv_freq, self.dims.key_mult,
+                            self.q, self.st.key_cache, self.st.value_cache, ctx.slot_mapping)
         t.end("attn.rope_kv")
         t.begin("attn.fa")
         K.attn_decode(self.q.view(ctx.B, self.nq, self.hd), self.st.key_cache, self.st.value_cache, ctx.cu_q,
                       ctx.seqused_k, ctx.max_k, ctx.block_table, self.out, workspace=self.ws, splits=self.splits)
         t.end("attn.fa")
+
+    def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
         t.begin("attn.oproj")
-        out = K.gemm(self.out.view(ctx.B, self.nq * self.hd), w.wo, out=out, alpha=d.attn_out, addend=addend)
+        out = K.gemm(self.out2d, self.w.wo, out=out, alpha=self.dims.attn_out, addend=addend)
         t.end("attn.oproj")
         return out
+
+    def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
+               x_scale: float = 1.0) -> torch.Tensor:
+        """x: [B, H] (already multiplied by attn_in unless x_scale carries it). Returns the o_proj partial
+        times attn_out (+ addend), written to `out`."""
+        self.project_in(x, t, x_scale)
+        self.core(t)
+        return self.project_out(t, out, addend)
 
 
 class _LocalOnly:
@@ -90,7 +104,8 @@ class SsmBranch:
     name = "ssm"
 
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
-                 device: torch.device, norm_group):
+                 device: torch.device, norm_group, zxbcdt: torch.Tensor | None = None, yn: torch.Tensor | None = None):
+        """zxbcdt / yn: optional [B, in rows] and [B, nhr*p] views into buffers shared with the other branch."""
         s = plan.ssm
         assert s is not None
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
@@ -105,9 +120,10 @@ class SsmBranch:
         self.dtb_exp = w.dt_bias[:, None].expand(self.nhr, self.p)
         B = ctx.B
         rows = sum(self.sizes)
-        # in_proj output rows padded to 16 bytes so every [z | x | B | C | dt] slice starts aligned
-        self._zx = torch.empty(B, _pad8(rows), device=device, dtype=BF16)
-        self.zxbcdt = self._zx[:, :rows]
+        if zxbcdt is None:
+            # in_proj output rows padded to 16 bytes so every [z | x | B | C | dt] slice starts aligned
+            zxbcdt = torch.empty(B, _pad8(rows), device=device, dtype=BF16)[:, :rows]
+        self.zxbcdt = zxbcdt
         self.z = self.zxbcdt[:, :z]
         self.xBC = self.zxbcdt[:, z:z + x + b + c]
         self.xs = self.xBC[:, :x].view(B, self.nhr, self.p)
@@ -115,17 +131,19 @@ class SsmBranch:
         self.Cm = self.xBC[:, x + b:].view(B, self.ng, self.N)
         self.dt = self.zxbcdt[:, z + x + b + c:]
         self.y = torch.empty(B, self.nhr, self.p, device=device, dtype=BF16)
-        self.yn = torch.empty(B, self.nhr * self.p, device=device, dtype=BF16)
+        self.yn = yn if yn is not None else torch.empty(B, self.nhr * self.p, device=device, dtype=BF16)
         self.sumsq = torch.empty(B, 1, device=device, dtype=torch.float32)
         self.conv_state_T = st.conv_state.transpose(-1, -2)  # [lines, rows, d_conv-1] view
         self.group_size = (self.nhr * self.p) // self.ng if self.ng > 1 else None
 
-    def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
-               x_scale: float = 1.0) -> torch.Tensor:
-        w, ctx, d = self.w, self.ctx, self.dims
+    def project_in(self, x: torch.Tensor, t: OpTimer, x_scale: float = 1.0) -> None:
         t.begin("ssm.inproj")
-        K.gemm(x, w.win, out=self.zxbcdt, alpha=x_scale, colscale=w.mup)
+        K.gemm(x, self.w.win, out=self.zxbcdt, alpha=x_scale, colscale=self.w.mup)
         t.end("ssm.inproj")
+
+    def core(self, t: OpTimer) -> None:
+        """conv update, selective state update, gated RMSNorm into self.yn."""
+        w, ctx, d = self.w, self.ctx, self.dims
         t.begin("ssm.conv")
         K.conv_update(self.xBC, self.conv_state_T, w.conv_w, w.conv_b, ctx.state_idx)
         t.end("ssm.conv")
@@ -136,10 +154,18 @@ class SsmBranch:
         K.gated_rmsnorm(self.y.view(ctx.B, self.nhr * self.p), self.z, w.norm_w, d.rms_eps, self.norm_group,
                         self.group_size, out=self.yn, sumsq=self.sumsq)
         t.end("ssm.norm")
+
+    def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
         t.begin("ssm.outproj")
-        out = K.gemm(self.yn, w.wout, out=out, alpha=d.ssm_out, addend=addend)
+        out = K.gemm(self.yn, self.w.wout, out=out, alpha=self.dims.ssm_out, addend=addend)
         t.end("ssm.outproj")
         return out
+
+    def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
+               x_scale: float = 1.0) -> torch.Tensor:
+        self.project_in(x, t, x_scale)
+        self.core(t)
+        return self.project_out(t, out, addend)
 
 
 class SwingMLP:
@@ -195,11 +221,26 @@ class ParallelHybridLayer:
         world = groups.world_size
         if world > 1 and collectives:
             groups.ensure(all_norm_groups(self.mode, world, dims))  # collective: every rank, same order
-        self.attn = AttentionBranch(plan, w, dims, st, ctx, device) if plan.attn is not None else None
+        # A rank holding both branches runs their input projections as one GEMM (shared input) and their
+        # output projections as one two-segment GEMM (shared output), except in tp4 / tp4_streams, whose point
+        # is separate branch outputs.
+        self.fused = (plan.attn is not None and plan.ssm is not None and w.w_in_cat is not None
+                      and self.mode in ("tp1", "tp4_fused"))
+        qkv = zx = ao = yn = None
+        B = ctx.B
+        if self.fused:
+            nqkv, nin = w.wqkv.shape[0], w.win.shape[0]
+            self.in_buf = torch.empty(B, _pad8(nqkv + nin), device=device, dtype=BF16)[:, :nqkv + nin]
+            qkv, zx = self.in_buf[:, :nqkv], self.in_buf[:, nqkv:]
+            qc, yc = w.wo.shape[1], w.wout.shape[1]
+            self.mid_buf = torch.empty(B, qc + yc, device=device, dtype=BF16)
+            ao, yn = self.mid_buf[:, :qc], self.mid_buf[:, qc:]
+            self.k_seg = qc
+        self.attn = AttentionBranch(plan, w, dims, st, ctx, device, qkv, ao) if plan.attn is not None else None
         norm_group = None
         if plan.ssm is not None and len(plan.ssm.norm_ranks) > 1:
             norm_group = groups.group_for_ranks(plan.ssm.norm_ranks) if collectives else _LocalOnly(len(plan.ssm.norm_ranks))
-        self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group) if plan.ssm is not None else None
+        self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn) if plan.ssm is not None else None
         self.has_mlp = dims.intermediate > 0
         self.mlp = SwingMLP(plan, w, dims, ctx.B, device) if self.has_mlp else None
         B, H = ctx.B, dims.hidden
@@ -208,6 +249,8 @@ class ParallelHybridLayer:
         self.h1 = mk() if self.has_mlp else self.out
         self.mix, self.part_a, self.part_s, self.mlp_part = mk(), mk(), mk(), mk()
         self.tp = groups.tp
+        if self.fused:
+            self.s_side = torch.cuda.Stream(device=device)
         if self.mode == "tp4_streams":
             self.s_attn = torch.cuda.Stream(device=device)
             self.s_ssm = torch.cuda.Stream(device=device)
@@ -240,7 +283,31 @@ class ParallelHybridLayer:
         t.end("norm_in")
         mode = self.mode
         y_ready = False
-        if mode == "tp1":
+        if self.fused:
+            t.begin("mixer.inproj")
+            K.gemm(x, self.w.w_in_cat, out=self.in_buf, colscale=self.w.in_colscale)
+            t.end("mixer.inproj")
+            # the two branches are independent until the output projection: attention on a side stream,
+            # Mamba-2 on this one (both HBM-bound; overlapping them fills each other's ramps and tails)
+            cur = torch.cuda.current_stream(self.device)
+            self.s_side.wait_stream(cur)
+            with torch.cuda.stream(self.s_side):
+                self.attn.core(t)
+            self.ssm.core(t)
+            cur.wait_stream(self.s_side)
+            t.begin("mixer.outproj")
+            if mode == "tp1":
+                K.gemm(self.mid_buf, self.w.w_out_cat, out=self.h1, alpha=dims.attn_out, k_seg=self.k_seg,
+                       alpha2=dims.ssm_out, addend=h)
+            else:
+                K.gemm(self.mid_buf, self.w.w_out_cat, out=self.mix, alpha=dims.attn_out, k_seg=self.k_seg,
+                       alpha2=dims.ssm_out)
+            t.end("mixer.outproj")
+            if mode == "tp4_fused":
+                self._ar(self.mix, "ar.mixer", t)
+                self._join(h, self.mix, t)
+                y_ready = self.has_mlp
+        elif mode == "tp1":
             self.attn.decode(x, t, out=self.h1, addend=h, x_scale=dims.attn_in)
             self.ssm.decode(x, t, out=self.h1, addend=self.h1, x_scale=dims.ssm_in)
         elif mode == "tp4":

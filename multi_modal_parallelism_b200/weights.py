@@ -109,6 +109,11 @@ class RankWeights:
     # norms
     in_norm: torch.Tensor | None = None
     ff_norm: torch.Tensor | None = None
+    # both branches on one rank: the projections that share an input or an output, concatenated (wqkv/win
+    # and wo/wout are views into these)
+    w_in_cat: torch.Tensor | None = None  # [q+k+v rows + in rows, H]
+    in_colscale: torch.Tensor | None = None  # [q+k+v rows + in rows] fp32: attn_in, then ssm_in * muP
+    w_out_cat: torch.Tensor | None = None  # [H, q cols + d_ssm local]
 
     @property
     def mlp_downT(self) -> torch.Tensor | None:
@@ -154,6 +159,15 @@ def shard_to_device(full: dict[str, torch.Tensor], plan: RankPlan, dims: FalconH
         rw.norm_w = put(full["mamba.norm.weight"][s.norm_cols])
         rw.wout = put(full["mamba.out_proj.weight"][:, s.out_cols])
         rw.mup = put(build_mup_vector(dims, s), torch.float32)
+    if a is not None and s is not None:
+        nqkv, nin = rw.wqkv.shape[0], rw.win.shape[0]
+        rw.w_in_cat = torch.cat([rw.wqkv, rw.win], 0).contiguous()
+        rw.wqkv, rw.win = rw.w_in_cat[:nqkv], rw.w_in_cat[nqkv:]
+        rw.in_colscale = torch.cat([torch.full((nqkv,), float(dims.attn_in), device=device),
+                                    rw.mup.reshape(-1) * float(dims.ssm_in)]).contiguous()
+        qc = rw.wo.shape[1]
+        rw.w_out_cat = torch.cat([rw.wo, rw.wout], 1).contiguous()
+        rw.wo, rw.wout = rw.w_out_cat[:, :qc], rw.w_out_cat[:, qc:]
     m = plan.mlp
     cols = torch.tensor(m.col_order, dtype=torch.long)
     rw.mlp_gate = put(full["feed_forward.gate_proj.weight"][cols])

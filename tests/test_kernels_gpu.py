@@ -285,3 +285,16 @@ def test_gemm_tc_matches_fp32(M, N, K_):
     close(npf(out), ref.numpy())
     out2 = K.gemm_tc(x.to(DEV), w.to(DEV))
     close(npf(out2), (x.float() @ w.float().T).numpy())
+
+
+@pytest.mark.parametrize("M,N,K_,kseg", [(64, 3072, 4608, 1536), (2, 300, 256, 64), (128, 1024, 640, 512), (64, 3072, 4608, 4608)])
+def test_gemm_two_segments(M, N, K_, kseg):
+    """out = a1 * x[:, :kseg] w[:, :kseg]^T + a2 * x[:, kseg:] w[:, kseg:]^T + addend (fused o_proj + out_proj)."""
+    g = torch.Generator().manual_seed(M + N + K_ + kseg)
+    x = torch.randn(M, K_, generator=g).to(BF)
+    w = (torch.randn(N, K_, generator=g) * 0.02).to(BF)
+    add = torch.randn(M, N, generator=g).to(BF)
+    xf, wf = x.float(), w.float()
+    ref = 0.3 * (xf[:, :kseg] @ wf[:, :kseg].T) + 1.7 * (xf[:, kseg:] @ wf[:, kseg:].T) + add.float()
+    out = K.gemm(x.to(DEV), w.to(DEV), alpha=0.3, k_seg=kseg, alpha2=1.7, addend=add.to(DEV))
+    close(npf(out), ref.numpy())
