@@ -38,6 +38,11 @@ extern "C" {
 
 /* Library version (major*10000 + minor*100 + patch). */
 int mmp_version(void);
+/* Programmatic dependent launch (no counterpart in the reference), a bit mask: bit 0 = the tensor-core GEMMs,
+ * bit 1 = every other kernel. A kernel so launched starts during the previous kernel's tail and waits for it
+ * before touching its outputs; the GEMMs stream their weight operand before that wait. Default 1 (GEMMs only,
+ * the faster setting measured on B200). Returns the previous mask. Process-wide; set before capturing graphs. */
+int mmp_set_pdl(int enable);
 /* Message of the last failing call on this host thread ("" if none). */
 const char* mmp_last_error(void);
 

@@ -20,6 +20,16 @@ int mmp_check_launch(const char* what) {
   return MMP_OK;
 }
 
+static int g_pdl = 1;  // measured: helps the GEMMs (weight prefetch), hurts the short kernels
+
+bool mmp::pdl_enabled(int kind) { return (g_pdl & (kind == 1 ? 1 : 2)) != 0; }
+
+extern "C" int mmp_set_pdl(int enable) {
+  const int prev = g_pdl;
+  g_pdl = enable & 3;
+  return prev;
+}
+
 extern "C" int mmp_version(void) { return 100; }
 
 extern "C" const char* mmp_last_error(void) { return g_last_error; }

@@ -78,6 +78,8 @@ __device__ __forceinline__ int tile_block(const AttnParams& P, int b, int tile) 
 
 template <int HD, int MAXH>
 __global__ void __launch_bounds__(WARPS * 32) paged_attn_split_kernel(const AttnParams P) {
+  pdl_trigger();
+  pdl_wait();
   static_assert(HD == 128, "head_dim 128");
   constexpr int KP = HD / 32;  // 32-dim slabs: one 16-byte chunk per lane per token row
   extern __shared__ __align__(128) uint8_t smem[];
@@ -288,6 +290,8 @@ static_assert(SPLIT_SMEM >= WARPS * 16 * 128 * 4 + 2 * WARPS * 16 * 4, "merge ar
 
 template <int HD>
 __global__ void __launch_bounds__(HD) paged_attn_merge_kernel(const AttnParams P) {
+  pdl_trigger();
+  pdl_wait();
   const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int64_t base = (static_cast<int64_t>(b) * P.nq + head) * P.splits;
   float M = -INFINITY;
@@ -394,11 +398,14 @@ extern "C" int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
     cudaFuncSetAttribute(paged_attn_split_kernel<128, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, SPLIT_SMEM);
     g_smem_attr[dev] = true;
   }
-  if (nq / nkv <= 8) paged_attn_split_kernel<128, 8><<<grid, WARPS * 32, SPLIT_SMEM, s>>>(P);
-  else paged_attn_split_kernel<128, 16><<<grid, WARPS * 32, SPLIT_SMEM, s>>>(P);
+  cudaError_t e = nq / nkv <= 8
+                      ? mmp::launch(paged_attn_split_kernel<128, 8>, grid, dim3(WARPS * 32), SPLIT_SMEM, s, nullptr, 0, P)
+                      : mmp::launch(paged_attn_split_kernel<128, 16>, grid, dim3(WARPS * 32), SPLIT_SMEM, s, nullptr, 0, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_decode: %s", cudaGetErrorString(e));
   int rc = mmp_check_launch("mmp_paged_attn_decode");
   if (rc != MMP_OK || splits == 1) return rc;
-  paged_attn_merge_kernel<128><<<dim3(nq, batch), 128, 0, s>>>(P);
+  e = mmp::launch(paged_attn_merge_kernel<128>, dim3(nq, batch), dim3(128), 0, s, nullptr, 0, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_decode(merge): %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_paged_attn_decode(merge)");
 }
 

@@ -23,6 +23,8 @@ struct ConvParams {
 
 template <int W>
 __global__ void __launch_bounds__(128) conv_update_vec_kernel(const ConvParams P) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y;
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= P.rows) return;
@@ -80,6 +82,8 @@ __global__ void __launch_bounds__(128) conv_update_vec_kernel(const ConvParams P
 }
 
 __global__ void __launch_bounds__(128) conv_update_scalar_kernel(const ConvParams P) {
+  pdl_trigger();
+  pdl_wait();
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= P.rows) return;
@@ -125,10 +129,12 @@ extern "C" int mmp_conv1d_update(const void* x, int64_t x_b, void* out, int64_t 
                    (!bias || aligned16(bias)) && x_b % 8 == 0 && o_b % 8 == 0 && s_line % 8 == 0 && s_k % 8 == 0;
   if (vec) {
     dim3 grid((rows / 8 + 127) / 128, batch);
-    conv_update_vec_kernel<4><<<grid, 128, 0, s>>>(P);
+    cudaError_t e = mmp::launch(conv_update_vec_kernel<4>, grid, dim3(128), 0, s, nullptr, 0, P);
+    if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_conv1d_update: %s", cudaGetErrorString(e));
   } else {
     dim3 grid((rows + 127) / 128, batch);
-    conv_update_scalar_kernel<<<grid, 128, 0, s>>>(P);
+    cudaError_t e = mmp::launch(conv_update_scalar_kernel, grid, dim3(128), 0, s, nullptr, 0, P);
+    if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_conv1d_update: %s", cudaGetErrorString(e));
   }
   return mmp_check_launch("mmp_conv1d_update");
 }

@@ -167,6 +167,10 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
                                                              const __grid_constant__ CUtensorMap tmB,
                                                              const TcParams P) {
   using L = TcLayout<BN, STAGES>;
+  pdl_trigger();
+  // Warp 0 (barrier set-up, TMEM allocation, TMA producer) waits for the previous kernel only once its lane 0
+  // has started streaming the weight operand; warp-collective instructions stay convergent.
+  if ((threadIdx.x >> 5) != 0) pdl_wait();
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_addr(smem);
@@ -210,9 +214,25 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   int issued = 0;  // TMA stages issued by thread 0 (drained at teardown)
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nkt; ++i) {
+      // The weight operand (A when swapped for small M, else B) never depends on the previous kernel: its first
+      // STAGES boxes are requested before waiting for that kernel, hiding their DRAM latency behind its tail.
+      const int pre = min(nkt, STAGES);
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t a_s = sbase + i * L::STAGE_BYTES, b_s = a_s + L::A_BYTES;
+        mbar_expect_tx(full_bar(i), L::STAGE_BYTES);
+        if (TRANS) tma_load_2d(a_s, &tmA, full_bar(i), (kt0 + i) * TBK, m0);
+        else tma_load_2d(b_s, &tmB, full_bar(i), (kt0 + i) * TBK, n0);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) {
+        const uint32_t a_s = sbase + i * L::STAGE_BYTES, b_s = a_s + L::A_BYTES;
+        if (TRANS) tma_load_2d(b_s, &tmB, full_bar(i), (kt0 + i) * TBK, n0);
+        else tma_load_2d(a_s, &tmA, full_bar(i), (kt0 + i) * TBK, m0);
+      }
+      issued = pre;
+      for (int i = pre; i < nkt; ++i) {
         const int s = i % STAGES;
-        if (i >= STAGES && !mbar_wait(empty_bar(s), ((i / STAGES) - 1) & 1, abort_flag, P.err)) break;
+        if (!mbar_wait(empty_bar(s), ((i / STAGES) - 1) & 1, abort_flag, P.err)) break;
         const uint32_t a_s = sbase + s * L::STAGE_BYTES, b_s = a_s + L::A_BYTES;
         mbar_expect_tx(full_bar(s), L::STAGE_BYTES);
         const int kx = (kt0 + i) * TBK;
@@ -222,6 +242,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
       }
     }
     __syncwarp();
+    if (lane != 0) pdl_wait();
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc<BN>();
@@ -377,21 +398,12 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& P, d
     if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "gemm_tc: smem attribute: %s", cudaGetErrorString(e));
     attr_set[dev] = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(TTHREADS);
-  cfg.dynamicSmemBytes = L::DYN;
-  cfg.stream = s;
   cudaLaunchAttribute attr[1];
-  if (CLUSTER) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = split;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ma, mb, P);
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = split;
+  cudaError_t e = mmp::launch_kind(1, kern, grid, dim3(TTHREADS), L::DYN, s, attr, CLUSTER ? 1 : 0, ma, mb, P);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "gemm_tc: launch failed: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_gemm_bf16_tc");
 }

@@ -5,6 +5,8 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "mmp_b200.h"
 
 namespace mmp {
@@ -70,6 +72,43 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 }
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Programmatic dependent launch. Every kernel lets the next kernel in the stream start launching as soon as
+// all of its own CTAs are running (pdl_trigger), and waits for the previous kernel to finish and flush its
+// memory (pdl_wait) before touching anything that kernel may have written.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;\n" ::); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
+// bit 0: tensor-core GEMMs, bit 1: every other kernel
+bool pdl_enabled(int kind = 2);
+
+// Launch with the programmatic-stream-serialization attribute (when enabled) plus optional extra attributes.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kind(int kind, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                               const cudaLaunchAttribute* extra, int n_extra, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[4];
+  int n = 0;
+  for (int i = 0; i < n_extra && n < 3; ++i) attr[n++] = extra[i];
+  if (pdl_enabled(kind)) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                          const cudaLaunchAttribute* extra, int n_extra, Args&&... args) {
+  return launch_kind(2, kern, grid, block, smem, s, extra, n_extra, std::forward<Args>(args)...);
+}
 
 }  // namespace mmp
 

@@ -30,6 +30,8 @@ struct RmsParams {
 // Up to MAXV vectors per thread are kept in registers between the two passes.
 template <int MAXV>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const RmsParams P) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nvec = P.hidden / 8;
@@ -82,6 +84,8 @@ struct GnParams {
 // grid: (groups, rows). mode 0 = local, 1 = write partial sums, 2 = apply given sums.
 template <int MAXV>
 __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const GnParams P) {
+  pdl_trigger();
+  pdl_wait();
   __shared__ float red[32];
   const int grp = blockIdx.x, row = blockIdx.y, ngroups = gridDim.x;
   const int nvec = P.group_size / 8;
@@ -146,9 +150,9 @@ extern "C" int mmp_rmsnorm(const void* x, int64_t x_b, const void* residual, int
               static_cast<const bf16*>(w), static_cast<bf16*>(out), o_b, hidden, eps};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int nvec = hidden / 8;
-  if (nvec <= 256 * 2) rmsnorm_kernel<2><<<rows, 256, 0, s>>>(P);
-  else if (nvec <= 256 * 4) rmsnorm_kernel<4><<<rows, 256, 0, s>>>(P);
-  else rmsnorm_kernel<8><<<rows, 256, 0, s>>>(P);
+  if (nvec <= 256 * 2) { cudaError_t e = mmp::launch(rmsnorm_kernel<2>, dim3(rows), dim3(256), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_rmsnorm: %s", cudaGetErrorString(e)); }
+  else if (nvec <= 256 * 4) { cudaError_t e = mmp::launch(rmsnorm_kernel<4>, dim3(rows), dim3(256), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_rmsnorm: %s", cudaGetErrorString(e)); }
+  else { cudaError_t e = mmp::launch(rmsnorm_kernel<8>, dim3(rows), dim3(256), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_rmsnorm: %s", cudaGetErrorString(e)); }
   return mmp_check_launch("mmp_rmsnorm");
 }
 
@@ -168,9 +172,9 @@ extern "C" int mmp_gated_rmsnorm(const void* y, int64_t y_b, const void* z, int6
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   dim3 grid(D / group_size, rows);
   const int nvec = group_size / 8;
-  if (nvec <= 256) gated_rmsnorm_kernel<1><<<grid, 256, 0, s>>>(P);
-  else if (nvec <= 512) gated_rmsnorm_kernel<2><<<grid, 256, 0, s>>>(P);
-  else gated_rmsnorm_kernel<4><<<grid, 256, 0, s>>>(P);
+  if (nvec <= 256) { cudaError_t e = mmp::launch(gated_rmsnorm_kernel<1>, grid, dim3(256), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_gated_rmsnorm: %s", cudaGetErrorString(e)); }
+  else if (nvec <= 512) { cudaError_t e = mmp::launch(gated_rmsnorm_kernel<2>, grid, dim3(256), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_gated_rmsnorm: %s", cudaGetErrorString(e)); }
+  else { cudaError_t e = mmp::launch(gated_rmsnorm_kernel<4>, grid, dim3(256), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_gated_rmsnorm: %s", cudaGetErrorString(e)); }
   return mmp_check_launch("mmp_gated_rmsnorm");
 }
 
@@ -179,6 +183,8 @@ namespace {
 
 __global__ void __launch_bounds__(256) silu_mul_kernel(const bf16* gate, int64_t g_b, const bf16* up, int64_t u_b,
                                                        bf16* out, int64_t o_b, int cols, float gs) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= cols) return;
@@ -200,8 +206,10 @@ extern "C" int mmp_silu_mul(const void* gate, int64_t g_b, const void* up, int64
   if (rows < 0 || rows > 65535 || cols < 0 || cols % 8 || !rows_ok(gate, g_b) || !rows_ok(up, u_b) || !rows_ok(out, o_b))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_silu_mul: cols %% 8 == 0 and 16-byte aligned rows required");
   dim3 grid((cols / 8 + 255) / 256, rows);
-  silu_mul_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const bf16*>(gate), g_b, static_cast<const bf16*>(up), u_b, static_cast<bf16*>(out), o_b, cols, gate_scale);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = mmp::launch(silu_mul_kernel, grid, dim3(256), 0, s, nullptr, 0, static_cast<const bf16*>(gate), g_b,
+                              static_cast<const bf16*>(up), u_b, static_cast<bf16*>(out), o_b, cols, gate_scale);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_silu_mul: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_silu_mul");
 }
 
@@ -210,6 +218,8 @@ namespace {
 
 __global__ void __launch_bounds__(256) add3_kernel(const bf16* a, int64_t a_b, const bf16* b, int64_t b_b, const bf16* c,
                                                    int64_t c_b, bf16* out, int64_t o_b, int cols) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.y;
   const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= cols) return;
@@ -237,8 +247,10 @@ extern "C" int mmp_add(const void* a, int64_t a_b, const void* b, int64_t b_b, c
       !rows_ok(out, o_b))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_add: cols %% 8 == 0 and 16-byte aligned rows required");
   dim3 grid((cols / 8 + 255) / 256, rows);
-  add3_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const bf16*>(a), a_b, static_cast<const bf16*>(b), b_b, static_cast<const bf16*>(c), c_b,
-      static_cast<bf16*>(out), o_b, cols);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = mmp::launch(add3_kernel, grid, dim3(256), 0, s, nullptr, 0, static_cast<const bf16*>(a), a_b,
+                              static_cast<const bf16*>(b), b_b, static_cast<const bf16*>(c), c_b, static_cast<bf16*>(out),
+                              o_b, cols);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_add: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_add");
 }

@@ -29,6 +29,8 @@ struct RopeParams {
 
 template <int HD>
 __global__ void __launch_bounds__(128) rope_kv_kernel(const RopeParams P) {
+  pdl_trigger();
+  pdl_wait();
   constexpr int PER = HD / 64;  // rotation pairs per lane
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int head = blockIdx.x * 4 + warp;
@@ -125,9 +127,9 @@ extern "C" int mmp_rope_kv_write(const void* q, int64_t q_b, const void* k, int6
   dim3 grid((nq + 2 * nkv + 3) / 4, batch);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (hd) {
-    case 64: rope_kv_kernel<64><<<grid, 128, 0, s>>>(P); break;
-    case 128: rope_kv_kernel<128><<<grid, 128, 0, s>>>(P); break;
-    case 256: rope_kv_kernel<256><<<grid, 128, 0, s>>>(P); break;
+    case 64: { cudaError_t e = mmp::launch(rope_kv_kernel<64>, grid, dim3(128), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_rope_kv_write: %s", cudaGetErrorString(e)); break; }
+    case 128: { cudaError_t e = mmp::launch(rope_kv_kernel<128>, grid, dim3(128), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_rope_kv_write: %s", cudaGetErrorString(e)); break; }
+    case 256: { cudaError_t e = mmp::launch(rope_kv_kernel<256>, grid, dim3(128), 0, s, nullptr, 0, P); if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_rope_kv_write: %s", cudaGetErrorString(e)); break; }
     default: return mmp_set_error(MMP_ERR_UNSUPPORTED, "mmp_rope_kv_write: head_dim %d not in {64, 128, 256}", hd);
   }
   return mmp_check_launch("mmp_rope_kv_write");

@@ -74,6 +74,8 @@ struct SsuShape {
 
 template <typename ST, int N, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) ssu_decode_kernel(const SsuParams P) {
+  pdl_trigger();
+  pdl_wait();
   using S = SsuShape<ST, N, WARPS>;
   constexpr int EV = S::EV, VPL = S::VPL, LPR = S::LPR, RPP = S::RPP, R = S::R;
   const int b = blockIdx.z, h = blockIdx.y;
@@ -184,7 +186,8 @@ int launch(const SsuParams& P, cudaStream_t stream) {
   constexpr int WARPS = 4;
   using S = SsuShape<ST, N, WARPS>;
   dim3 grid((P.p + S::ROWS_CTA - 1) / S::ROWS_CTA, P.nh, P.batch);
-  ssu_decode_kernel<ST, N, WARPS><<<grid, WARPS * 32, 0, stream>>>(P);
+  cudaError_t e = mmp::launch(ssu_decode_kernel<ST, N, WARPS>, grid, dim3(WARPS * 32), 0, stream, nullptr, 0, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_ssu_decode: launch failed: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_ssu_decode");
 }
 

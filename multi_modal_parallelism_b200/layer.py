@@ -210,7 +210,9 @@ class SwingMLP:
 
 class ParallelHybridLayer:
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
-                 ctx: DecodeCtx, device: torch.device, collectives: bool = True):
+                 ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True):
+        """overlap_branches: on a rank holding both branches (fused projections), run the attention core on a
+        side stream concurrently with the Mamba-2 core."""
         self.plan, self.w, self.dims, self.groups, self.ctx = plan, w, dims, groups, ctx
         self.collectives = collectives
         self.device = device
@@ -249,7 +251,8 @@ class ParallelHybridLayer:
         self.h1 = mk() if self.has_mlp else self.out
         self.mix, self.part_a, self.part_s, self.mlp_part = mk(), mk(), mk(), mk()
         self.tp = groups.tp
-        if self.fused:
+        self.overlap = self.fused and overlap_branches
+        if self.overlap:
             self.s_side = torch.cuda.Stream(device=device)
         if self.mode == "tp4_streams":
             self.s_attn = torch.cuda.Stream(device=device)
@@ -289,12 +292,16 @@ class ParallelHybridLayer:
             t.end("mixer.inproj")
             # the two branches are independent until the output projection: attention on a side stream,
             # Mamba-2 on this one (both HBM-bound; overlapping them fills each other's ramps and tails)
-            cur = torch.cuda.current_stream(self.device)
-            self.s_side.wait_stream(cur)
-            with torch.cuda.stream(self.s_side):
+            if self.overlap:
+                cur = torch.cuda.current_stream(self.device)
+                self.s_side.wait_stream(cur)
+                with torch.cuda.stream(self.s_side):
+                    self.attn.core(t)
+                self.ssm.core(t)
+                cur.wait_stream(self.s_side)
+            else:
                 self.attn.core(t)
-            self.ssm.core(t)
-            cur.wait_stream(self.s_side)
+                self.ssm.core(t)
             t.begin("mixer.outproj")
             if mode == "tp1":
                 K.gemm(self.mid_buf, self.w.w_out_cat, out=self.h1, alpha=dims.attn_out, k_seg=self.k_seg,
