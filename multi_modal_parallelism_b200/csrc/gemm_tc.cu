@@ -52,8 +52,12 @@ struct TcLayout {
   static constexpr int ABORT = TMEM_SLOT + 4;
   static constexpr int USED = ABORT + 4;
   static constexpr int DYN = USED + 1024;                  // slack to align the ring to 1024 bytes
-  static constexpr int RLD4 = BN + 4;  // fp32 receive row (split-K): 16-byte aligned, conflict-free float4 columns
-  static_assert((TBM + 8) * RLD4 * 4 <= PIPE, "split-K receive slots must fit in the ring");
+  // staged fp32 tile: plain tiles row-major [TBM][BN + 4]; swapped tiles column-major [BN][TBM + 4]
+  static constexpr int SLD = BN + 4;
+  static constexpr int TLD = TBM + 4;
+  static_assert(TBM * SLD * 4 <= PIPE && BN * TLD * 4 <= PIPE, "the staged tile must fit in the ring");
+  // split-K (swapped tiles) adds receive slots [ns][BN][rows_per], rows_per = round8(ceil(128 / ns)) <= 168 / ns
+  static constexpr bool SPLIT_FITS = (BN * TLD + BN * 168) * 4 <= PIPE;
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -151,15 +155,70 @@ __device__ __forceinline__ void load_scaled_bn(const TcParams& P, uint32_t taddr
 }
 #define load_scaled(P, taddr, h0, h1, v) load_scaled_bn<BN>(P, taddr, h0, h1, v)
 
-// out element (a_row i, b_row j): transposed tiles write out[j][i], plain tiles out[i][j]; colscale is
-// indexed by the output column.
-template <bool TRANS>
-__device__ __forceinline__ void store_out(const TcParams& P, int i, int j, float scaled) {
-  const int r = TRANS ? j : i, c = TRANS ? i : j;
-  float v = scaled;
-  if (P.colscale) v *= P.colscale[c];
-  if (P.addend) v += bf2f(P.addend[static_cast<int64_t>(r) * P.ldd + c]);
-  P.out[static_cast<int64_t>(r) * P.ldo + c] = f2bf(v);
+// Write 8 consecutive output elements (row r, columns c0..c0+7, the first n valid) = vals + addend.
+__device__ __forceinline__ void store8(const TcParams& P, int r, int c0, const float* vals, int n) {
+  bf16* dst = P.out + static_cast<int64_t>(r) * P.ldo + c0;
+  const bf16* add = P.addend ? P.addend + static_cast<int64_t>(r) * P.ldd + c0 : nullptr;
+  if (n == 8 && aligned16(dst) && (!add || aligned16(add))) {
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (add) {
+      const uint4 u = *reinterpret_cast<const uint4*>(add);
+      const float2 p0 = unpack_bf16x2(u.x), p1 = unpack_bf16x2(u.y), p2 = unpack_bf16x2(u.z), p3 = unpack_bf16x2(u.w);
+      a[0] = p0.x; a[1] = p0.y; a[2] = p1.x; a[3] = p1.y; a[4] = p2.x; a[5] = p2.y; a[6] = p3.x; a[7] = p3.y;
+    }
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(vals[0] + a[0], vals[1] + a[1]), pack_bf16x2(vals[2] + a[2], vals[3] + a[3]),
+                                                pack_bf16x2(vals[4] + a[4], vals[5] + a[5]), pack_bf16x2(vals[6] + a[6], vals[7] + a[7]));
+    return;
+  }
+  for (int k = 0; k < n; ++k) dst[k] = f2bf(vals[k] + (add ? bf2f(add[k]) : 0.f));
+}
+
+// Sum `ns` staged fp32 blocks of tile rows [row0, row0 + nrows) (block q at src + q * src_stride; swapped
+// tiles column-major [BN][ld], plain tiles row-major [nrows][ld]) and write them with the addend. Swapped:
+// 8 consecutive tile rows are 8 consecutive output columns of one output row; plain: 8 consecutive columns of
+// one tile row. Consecutive threads take consecutive chunks: 16-byte, coalesced, bank-conflict-free.
+template <bool TRANS, int BN>
+__device__ __forceinline__ void finish_tile(const TcParams& P, const float* src, int ns, int src_stride, int ld,
+                                            int row0, int nrows, int m0, int n0) {
+  if (nrows <= 0) return;
+  if constexpr (TRANS) {
+    // source blocks are column-major [BN][ld]: tile rows g*8 .. g*8+7 of column c are two float4
+    const int groups = (nrows + 7) / 8;
+    for (int idx = threadIdx.x; idx < groups * BN; idx += TTHREADS) {
+      const int g = idx % groups, c = idx / groups;
+      const int orow = n0 + c, ocol = m0 + row0 + g * 8;
+      if (orow >= P.b_rows) continue;
+      const int n = min(8, min(nrows - g * 8, P.a_rows - ocol));
+      if (n <= 0) continue;
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+      for (int q = 0; q < ns; ++q) {
+        const float4* b = reinterpret_cast<const float4*>(src + q * src_stride + c * ld + g * 8);
+        const float4 x = b[0], y = b[1];
+        v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w; v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
+      }
+      store8(P, orow, ocol, v, n);
+    }
+  } else {
+    constexpr int CH = BN / 8;
+    for (int idx = threadIdx.x; idx < nrows * CH; idx += TTHREADS) {
+      const int i = idx / CH, ch = idx % CH;
+      const int orow = m0 + row0 + i, ocol = n0 + ch * 8;
+      if (orow >= P.a_rows) continue;
+      const int n = min(8, P.b_rows - ocol);
+      if (n <= 0) continue;
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = 0.f;
+      for (int q = 0; q < ns; ++q) {
+        const float4* b = reinterpret_cast<const float4*>(src + q * src_stride + i * ld + ch * 8);
+        const float4 x = b[0], y = b[1];
+        v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w; v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
+      }
+      store8(P, orow, ocol, v, n);
+    }
+  }
 }
 
 template <int BN, int STAGES, bool TRANS, bool CLUSTER>
@@ -270,81 +329,77 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   bool ok = mbar_wait(done_bar, 0, abort_flag, P.err);
   ok = __all_sync(0xffffffffu, ok && !*abort_flag);
   tc_fence_after();
-  const int arow = m0 + warp * 32 + lane;
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-  if constexpr (!CLUSTER) {
-    if (ok && nkt > 0) {
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        load_scaled(P, t_lane + c0, has0, has1, v);
-        if (arow < P.a_rows) {
-#pragma unroll
-          for (int j = 0; j < 16; ++j)
-            if (n0 + c0 + j < P.b_rows) store_out<TRANS>(P, arow, n0 + c0 + j, v[j]);
-        }
-      }
-    }
-  }
+  const bool have = ok && nkt > 0;
 
-  // teardown: drain this CTA's copies (an aborted pipeline can leave some in flight), then free TMEM
+  // teardown of the ring: drain this CTA's copies (an aborted pipeline can leave some in flight)
   if (tid == 0) {
     for (int i = 0; i < issued; ++i) {
       const int use = i / STAGES;
       if (i + STAGES >= issued) mbar_wait(full_bar(i % STAGES), use & 1, abort_flag, P.err);
     }
   }
+  __syncthreads();  // the ring is free: every MMA finished (done barrier), every copy landed (drain)
 
-  if constexpr (CLUSTER) {
-    // split-K reduce-scatter through distributed shared memory: A rows are dealt to the cluster's CTAs in
-    // contiguous blocks; every CTA pushes each of its rows (16-byte remote stores, no round trips) into the
-    // owner's receive slot for that CTA, then each owner sums its rows' slots locally and runs the epilogue.
-    cg::cluster_group cluster = cg::this_cluster();
-    const int ns = static_cast<int>(cluster.num_blocks());
-    const int me = static_cast<int>(cluster.block_rank());
-    const int rows_per = (TBM + ns - 1) / ns;
-    float* recv = reinterpret_cast<float*>(smem);  // [ns][rows_per][RLD4], overlays the drained ring
-    const bool have = ok && nkt > 0;
-    __syncthreads();
-    cluster.sync();  // every CTA's ring is drained before anyone writes into it
-    {
-      const int row = warp * 32 + lane;
-      const int owner = row / rows_per, rl = row % rows_per;
-      float* dst = cluster.map_shared_rank(recv, owner) + (me * rows_per + rl) * L::RLD4;
+  // Stage the scaled fp32 tile in shared memory (tile row r = this thread's TMEM lane): alpha / alpha2 per K
+  // segment and the column scale of the output column (a tile row when swapped, a tile column otherwise).
+  float* stage = reinterpret_cast<float*>(smem);
+  {
+    const int r = warp * 32 + lane;
+    const float cs_row = (TRANS && P.colscale && m0 + r < P.a_rows) ? P.colscale[m0 + r] : 1.f;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        float v[16];
-        if (have) {
-          load_scaled(P, t_lane + c0, has0, has1, v);
-        } else {
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16];
+      if (have) {
+        load_scaled(P, t_lane + c0, has0, has1, v);
+      } else {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = 0.f;
+        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+      }
+      if constexpr (TRANS) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) stage[(c0 + j) * L::TLD + r] = v[j] * cs_row;  // consecutive lanes: consecutive words
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int c = n0 + c0 + j;
+          if (P.colscale) v[j] *= c < P.b_rows ? P.colscale[c] : 0.f;
         }
 #pragma unroll
         for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<float4*>(dst + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          *reinterpret_cast<float4*>(stage + r * L::SLD + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
     }
-    cluster.sync();  // all pushes have landed
-    const int my_rows = min(rows_per, TBM - me * rows_per);
-    for (int idx = tid; idx < my_rows * (BN / 4); idx += TTHREADS) {
-      const int rl = idx % my_rows, c4 = idx / my_rows;  // consecutive threads: consecutive rows
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int q = 0; q < ns; ++q) {
-        const float4 v = *reinterpret_cast<const float4*>(recv + (q * rows_per + rl) * L::RLD4 + c4 * 4);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      const int i = m0 + me * rows_per + rl, j = n0 + c4 * 4;
-      if (i < P.a_rows) {
-        if (j < P.b_rows) store_out<TRANS>(P, i, j, acc.x);
-        if (j + 1 < P.b_rows) store_out<TRANS>(P, i, j + 1, acc.y);
-        if (j + 2 < P.b_rows) store_out<TRANS>(P, i, j + 2, acc.z);
-        if (j + 3 < P.b_rows) store_out<TRANS>(P, i, j + 3, acc.w);
+  }
+
+  if constexpr (CLUSTER) {
+    static_assert(TRANS && L::SPLIT_FITS, "split-K runs swapped (weight-streaming) tiles whose receive slots fit");
+    // split-K reduce-scatter through distributed shared memory: tile rows are dealt to the cluster's CTAs in
+    // blocks of rows_per (a multiple of 8); each CTA copies every owner's rows of its staged tile (one
+    // contiguous run per column) into the owner's receive slot for it, then each owner sums its slots.
+    cg::cluster_group cluster = cg::this_cluster();
+    const int ns = static_cast<int>(cluster.num_blocks());
+    const int me = static_cast<int>(cluster.block_rank());
+    const int rows_per = ((TBM + ns - 1) / ns + 7) / 8 * 8;
+    float* recv = stage + BN * L::TLD;  // [ns][BN][rows_per]
+    __syncthreads();
+    cluster.sync();  // every CTA has staged its tile and stopped using its ring
+    for (int o = 0; o < ns; ++o) {
+      const int r0 = o * rows_per, nr = max(0, min(rows_per, TBM - r0));  // a multiple of 8
+      const int v4 = nr / 4;
+      float* dst = cluster.map_shared_rank(recv, o) + me * BN * rows_per;
+      for (int k = tid; k < BN * v4; k += TTHREADS) {
+        const int c = k / v4, j = k % v4;
+        *reinterpret_cast<float4*>(dst + c * rows_per + j * 4) =
+            *reinterpret_cast<const float4*>(stage + c * L::TLD + r0 + j * 4);
       }
     }
+    cluster.sync();  // every push has landed
+    const int my_rows = max(0, min(rows_per, TBM - me * rows_per));
+    finish_tile<TRANS, BN>(P, recv, ns, BN * rows_per, rows_per, me * rows_per, my_rows, m0, n0);
+  } else {
+    __syncthreads();
+    finish_tile<TRANS, BN>(P, stage, 1, 0, TRANS ? L::TLD : L::SLD, 0, TBM, m0, n0);
   }
 
   tc_fence_before();
@@ -445,25 +500,23 @@ extern "C" int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int6
              static_cast<const bf16*>(addend), ldd, err};
   CUtensorMap ma, mb;
   if (M <= 256) {
-    // decode: swap-AB, A = weight rows (the 128-row M side of the MMA), B = the <= 256 activation rows
-    const int bn = M <= 64 ? 64 : M <= 128 ? 128 : 256;
+    // decode: swap-AB, A = weight rows (the 128-row M side of the MMA), B = the activation rows (N)
+    const int bn = M <= 64 ? 64 : 128;
     P.a_rows = N;
     P.b_rows = M;
     if ((rc = make_map(&ma, w, N, K, ldw, TBM)) || (rc = make_map(&mb, a, M, K, lda, bn))) return rc;
     const int tiles = (N + TBM - 1) / TBM;
+    const int ntiles_b = (M + bn - 1) / bn;
     const int slots = (bn == 64 ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
     int split = 1;
-    if (tiles < slots) split = std::min(8, std::max(1, std::min(slots / tiles, k_tiles / 2)));
+    if (tiles * ntiles_b < slots) split = std::min(8, std::max(1, std::min(slots / (tiles * ntiles_b), k_tiles / 2)));
     const int ktps = (k_tiles + split - 1) / split;
     split = (k_tiles + ktps - 1) / ktps;
     P.k_tiles_per_split = ktps;
-    dim3 grid(1, tiles, split);
+    dim3 grid(ntiles_b, tiles, split);
     const bool cl = split > 1;
-    switch (bn) {
-      case 64: return cl ? launch_tc<64, 4, true, true>(ma, mb, P, grid, split, s) : launch_tc<64, 4, true, false>(ma, mb, P, grid, 1, s);
-      case 128: return cl ? launch_tc<128, 4, true, true>(ma, mb, P, grid, split, s) : launch_tc<128, 4, true, false>(ma, mb, P, grid, 1, s);
-      default: return cl ? launch_tc<256, 4, true, true>(ma, mb, P, grid, split, s) : launch_tc<256, 4, true, false>(ma, mb, P, grid, 1, s);
-    }
+    if (bn == 64) return cl ? launch_tc<64, 4, true, true>(ma, mb, P, grid, split, s) : launch_tc<64, 4, true, false>(ma, mb, P, grid, 1, s);
+    return cl ? launch_tc<128, 5, true, true>(ma, mb, P, grid, split, s) : launch_tc<128, 5, true, false>(ma, mb, P, grid, 1, s);
   }
   // large M (prefill): A = activations, B = weight rows, 128 x 256 output tiles
   P.a_rows = M;

@@ -71,7 +71,7 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+__host__ __device__ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Programmatic dependent launch. Every kernel lets the next kernel in the stream start launching as soon as
 // all of its own CTAs are running (pdl_trigger), and waits for the previous kernel to finish and flush its
