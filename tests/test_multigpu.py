@@ -1,0 +1,56 @@
+"""Every parallel layout on 2 (and, where visible, 4) GPUs through the harness entry point
+(`run.py --check`): one process per GPU over NCCL, rank outputs bitwise identical across ranks and within
+tolerance of the fp32 layer on the full weights and states. Skipped when fewer GPUs are visible."""
+import os
+import re
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def ngpu() -> int:
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def run_check(world, mode, tmp_path, extra=()):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           "-m", "multi_modal_parallelism_b200.run", "--mode", mode, "--dims-yaml", "falcon_h1_7b_like",
+           "--batch", "16", "--ctx", "512", "--variant", "graph", "--n-warm", "3", "--n-iter", "10", "--check",
+           "--out", str(tmp_path / "runs.csv"), "--correctness-out", str(tmp_path / "corr.csv"), *extra]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "600", *cmd], cwd=ROOT, env=env, capture_output=True, text=True)
+    out = r.stdout + r.stderr
+    m = re.search(r"\[check\].*pass=(True|False)", out)
+    assert r.returncode == 0 and m and m.group(1) == "True", out[-3000:]
+    return out
+
+
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["split11", "tp4", "tp4_fused", "tp4_streams"])
+def test_two_gpu_layouts(mode, tmp_path):
+    run_check(2, mode, tmp_path)
+
+
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+def test_two_gpu_full_layer_with_mlp(tmp_path):
+    run_check(2, "split11", tmp_path, ("--dims-yaml", "falcon_h1_7b", "--swing", "0.2"))
+
+
+@pytest.mark.skipif(ngpu() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("mode", ["split22", "split13", "tp4", "tp4_fused"])
+def test_four_gpu_layouts(mode, tmp_path):
+    run_check(4, mode, tmp_path)

@@ -108,3 +108,17 @@ def test_oracle_prefill_matches_chunked_scan_on_the_mamba_path():
     A = -np.exp(full["mamba.A_log"])
     _, s_chunk = oracle.ssd_chunked(xm, dtp, A, Bm, Cm, full["mamba.D"], 4)
     assert rel_l2(s_chunk, ssm[0]) < 1e-5
+
+
+@pytest.mark.parametrize("name", sorted(HASHES))
+def test_package_fp32_layer_matches_reference(name):
+    """multi_modal_parallelism_b200.reference (the run.py --check gate) against the reference's outputs."""
+    from multi_modal_parallelism_b200 import reference as R
+
+    meta, dims, full, h, (kc, vc, conv, ssm) = case_inputs(name)
+    g = np.load(GOLDEN / f"golden_{name}.npz")
+    inter = {}
+    out = R.decode_step(full, dims, h, kc, vc, conv, ssm, meta["ctx"], intermediates=inter).numpy()
+    assert rel_l2(out, g["out"]) < 2e-6
+    for key in ("x", "q", "k", "attn", "zxbcdt", "conv", "y_ssm", "ssm", "h1"):
+        assert rel_l2(inter[key].numpy().reshape(g["inter_" + key].shape), g["inter_" + key]) < 2e-5, key
