@@ -204,6 +204,49 @@ int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int64_t ldw, vo
                       int M, int N, int K, float alpha, int k_seg, float alpha2, const float* colscale,
                       const void* addend, int64_t ldd, int* err, void* stream);
 
+/* ---- prefill: causal depthwise conv over variable-length sequences --------------------------------------
+ * The prefill counterpart of mmp_conv1d_update (vLLM causal_conv1d_fn in the stack the reference measures;
+ * the reference harness itself only decodes). Tokens [cu_seqlens[i], cu_seqlens[i+1]) form sequence i:
+ * out[t, c] = act(bias[c] + sum_k w[c, k] x[t - W + 1 + k, c]), inputs before the sequence's first token taken
+ * from state line state_idx[i] (oldest first) when has_init[i] != 0, else zero; then the line receives the
+ * sequence's last W-1 inputs. x, out: [ntok, rows] bf16 (out must not alias x); state element (line, k, c) at
+ * line*s_line + k*s_k + c. W == 4, rows % 8 == 0, 16-byte aligned rows. has_init may be NULL (no initial state).
+ */
+int mmp_conv1d_prefill(const void* x, int64_t x_t, void* out, int64_t o_t, void* state, int64_t s_line, int64_t s_k,
+                       const void* w, const void* bias, const int32_t* cu_seqlens, const int32_t* state_idx,
+                       const int32_t* has_init, int nseq, int ntok, int rows, int W, int lines, int silu,
+                       int* err, void* stream);
+
+/* ---- prefill: Mamba-2 chunked SSD scan over variable-length sequences ---------------------------------
+ * The prefill counterpart of mmp_ssu_decode (vLLM mamba_chunk_scan_combined_varlen in the stack the reference
+ * measures). For each sequence i and head h, runs s_t = exp(dt'_t A) s_{t-1} + dt'_t x_t B_t^T,
+ * y_t = s_t C_t + D x_t over its tokens (dt' = softplus(dt + dt_bias)), starting from state line state_idx[i]
+ * when has_init[i] != 0 (else zero) and writing the final state back to that line; evaluated chunk-wise (64
+ * tokens) on the tensor cores. x, out: [ntok, nh, p] bf16; dt: [ntok, nh] bf16; B, C: [ntok, ngroups, N] bf16;
+ * state as mmp_ssu_decode. N in {64, 128, 256}, p % 8 == 0, 16-byte aligned rows.
+ */
+int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h,
+                    const float* A, const float* D, const float* dt_bias,
+                    const void* B, int64_t B_t, int64_t B_g, const void* C, int64_t C_t, int64_t C_g,
+                    void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
+                    const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init,
+                    void* out, int64_t o_t, int64_t o_h,
+                    int nseq, int nh, int p, int N, int ngroups, int lines, int* err, void* stream);
+
+/* ---- prefill: causal GQA attention over the paged KV cache ----------------------------------------------
+ * The prefill counterpart of mmp_paged_attn_decode (FlashAttention-2 varlen, causal). Query token j of
+ * sequence i (rows [cu_q[i], cu_q[i+1]) of q) sits at position ctx_start[i] + j and attends to cache positions
+ * 0 .. ctx_start[i] + j of that sequence, whose keys/values (the new tokens' included) are already in the
+ * cache. q: [ntok, nq, hd]; out: [ntok, nq, hd] bf16; caches and block_table as mmp_paged_attn_decode.
+ * hd == 128; max_q_len bounds cu_q[i+1] - cu_q[i].
+ */
+int mmp_paged_attn_prefill(const void* q, int64_t q_t, int64_t q_h,
+                           const void* key_cache, const void* value_cache, int64_t c_block, int64_t c_tok,
+                           int64_t c_head, const int32_t* block_table, int64_t bt_stride,
+                           const int32_t* cu_q, const int32_t* ctx_start, void* out, int64_t o_t, int64_t o_h,
+                           int nseq, int max_q_len, int nq, int nkv, int hd, int block_size, int num_blocks,
+                           float scale, int* err, void* stream);
+
 /* ---- elementwise add (residual joins after a collective) -------------------------------------------
  * Replaces the layer's bf16 `a + b (+ c)` residual sums (harness/layer.py:217-219,225-227):
  * out = a + b (+ c when c != NULL), computed in fp32, rounded once to bf16. [rows, cols] with row strides

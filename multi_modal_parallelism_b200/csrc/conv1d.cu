@@ -138,3 +138,137 @@ extern "C" int mmp_conv1d_update(const void* x, int64_t x_b, void* out, int64_t 
   }
   return mmp_check_launch("mmp_conv1d_update");
 }
+
+// ---------------------------------------------------------------------------------------------------------
+// Prefill: the causal depthwise conv over variable-length sequences (vLLM causal_conv1d_fn in the serving
+// stack; the reference harness itself only decodes). Token t of a sequence starting at `start` sees inputs
+// t-W+1 .. t; inputs before `start` come from the sequence's conv-state line (oldest first) when it has an
+// initial state, else are zero. A second launch writes each sequence's last W-1 inputs back to its line.
+namespace mmp {
+namespace {
+
+struct ConvPrefillParams {
+  const bf16* x; int64_t x_t;
+  bf16* out; int64_t o_t;
+  bf16* state; int64_t s_line, s_k;  // channels contiguous
+  const bf16* w; const bf16* bias;
+  const int32_t* cu_seqlens; const int32_t* state_idx; const int32_t* has_init;
+  int nseq, rows, lines, silu;
+  int* err;
+};
+
+__device__ __forceinline__ int seq_of(const int32_t* cu, int nseq, int t) {
+  int lo = 0, hi = nseq - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void unpack8f(const uint4& u, float* f) {
+  float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y), c = unpack_bf16x2(u.z), d = unpack_bf16x2(u.w);
+  f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
+}
+
+template <int W>
+__global__ void __launch_bounds__(128) conv_prefill_kernel(const ConvPrefillParams P) {
+  pdl_trigger();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int c0 = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= P.rows) return;
+  const int seq = seq_of(P.cu_seqlens, P.nseq, t);
+  const int start = P.cu_seqlens[seq];
+  const int line = P.state_idx[seq];
+  const bool init = P.has_init && P.has_init[seq];
+  if (init && (line < 0 || line >= P.lines)) {
+    flag_error(P.err, DEVERR_INDEX);
+    return;
+  }
+  float acc[8];
+  if (P.bias) {
+    unpack8f(ld16(P.bias + c0), acc);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  }
+  const bf16* wp = P.w + c0 * W;
+#pragma unroll
+  for (int k = 0; k < W; ++k) {
+    const int u = t - (W - 1) + k;
+    float v[8];
+    if (u >= start) {
+      unpack8f(ld16(P.x + static_cast<int64_t>(u) * P.x_t + c0), v);
+    } else if (init) {
+      unpack8f(ld16(P.state + line * P.s_line + (u - start + W - 1) * P.s_k + c0), v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = fmaf(bf2f(wp[j * W + k]), v[j], acc[j]);
+  }
+  if (P.silu) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = silu(acc[j]);
+  }
+  st16(P.out + static_cast<int64_t>(t) * P.o_t + c0,
+       make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                  pack_bf16x2(acc[6], acc[7])));
+}
+
+template <int W>
+__global__ void __launch_bounds__(128) conv_prefill_state_kernel(const ConvPrefillParams P) {
+  pdl_trigger();
+  pdl_wait();
+  const int seq = blockIdx.y;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (c0 >= P.rows) return;
+  const int start = P.cu_seqlens[seq], end = P.cu_seqlens[seq + 1], len = end - start;
+  const int line = P.state_idx[seq];
+  if (line < 0 || line >= P.lines) {
+    flag_error(P.err, DEVERR_INDEX);
+    return;
+  }
+  const bool init = P.has_init && P.has_init[seq];
+  bf16* sp = P.state + line * P.s_line + c0;
+  uint4 nv[W - 1];
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) {  // read everything first: short sequences shift the old line
+    const int u = end - (W - 1) + j;
+    if (u >= start) nv[j] = ld16(P.x + static_cast<int64_t>(u) * P.x_t + c0);
+    else if (init) nv[j] = ld16(sp + (len + j) * P.s_k);
+    else nv[j] = make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) st16(sp + j * P.s_k, nv[j]);
+}
+
+}  // namespace
+}  // namespace mmp
+
+extern "C" int mmp_conv1d_prefill(const void* x, int64_t x_t, void* out, int64_t o_t, void* state, int64_t s_line,
+                                  int64_t s_k, const void* w, const void* bias, const int32_t* cu_seqlens,
+                                  const int32_t* state_idx, const int32_t* has_init, int nseq, int ntok, int rows,
+                                  int W, int lines, int silu, int* err, void* stream) {
+  if (nseq == 0 || ntok == 0) return MMP_OK;
+  if (!x || !out || !state || !w || !cu_seqlens || !state_idx)
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: null pointer");
+  if (x == out) return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: out must not alias x");
+  if (nseq < 0 || nseq > 65535 || ntok < 0 || rows <= 0 || rows % 8 || W != 4 || lines <= 0 ||
+      !aligned16(x) || !aligned16(out) || !aligned16(state) || (bias && !aligned16(bias)) || x_t % 8 || o_t % 8 ||
+      s_line % 8 || s_k % 8)
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: needs W == 4, rows %% 8 == 0, 16-byte aligned rows");
+  ConvPrefillParams P{static_cast<const bf16*>(x), x_t, static_cast<bf16*>(out), o_t, static_cast<bf16*>(state), s_line,
+                      s_k, static_cast<const bf16*>(w), static_cast<const bf16*>(bias), cu_seqlens, state_idx, has_init,
+                      nseq, rows, lines, silu, err};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int bx = (rows / 8 + 127) / 128;
+  if (bx > 65535) return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: too many channels");
+  cudaError_t e = mmp::launch(conv_prefill_kernel<4>, dim3(ntok, bx), dim3(128), 0, s, nullptr, 0, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_conv1d_prefill: %s", cudaGetErrorString(e));
+  e = mmp::launch(conv_prefill_state_kernel<4>, dim3(bx, nseq), dim3(128), 0, s, nullptr, 0, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_conv1d_prefill(state): %s", cudaGetErrorString(e));
+  return mmp_check_launch("mmp_conv1d_prefill");
+}

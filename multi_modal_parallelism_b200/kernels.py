@@ -408,3 +408,52 @@ def gemm_T(x: torch.Tensor, wT: torch.Tensor, out: torch.Tensor | None = None, a
     if w.stride(1) != 1:
         w = w.contiguous()
     return gemm(x, w, out, alpha, colscale, addend)
+
+
+# ----------------------------------------------------------------------------- prefill
+def conv_prefill(xBC: torch.Tensor, conv_state_T: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None,
+                 cu_seqlens: torch.Tensor, state_idx: torch.Tensor, has_init: torch.Tensor | None,
+                 out: torch.Tensor, activation: str | None = "silu") -> torch.Tensor:
+    """Causal conv over variable-length sequences (tokens [cu[i], cu[i+1]) of xBC [T, rows]); initial windows
+    from conv_state_T[state_idx[i]] ([lines, rows, d_conv-1] view) where has_init[i], final windows back."""
+    _cuda("conv_prefill", xBC, conv_state_T, w, b, cu_seqlens, state_idx, has_init, out)
+    T, rows = xBC.shape
+    nseq = cu_seqlens.numel() - 1
+    if conv_state_T.stride(1) != 1:
+        raise ValueError("conv_prefill: conv state channels must be contiguous")
+    _lib.call("mmp_conv1d_prefill", _p(xBC), _rowmajor("xBC", xBC), _p(out), _rowmajor("out", out), _p(conv_state_T),
+              conv_state_T.stride(0), conv_state_T.stride(2), _p(w), _p(b), _p(cu_seqlens), _p(state_idx),
+              _p(has_init), nseq, T, rows, w.shape[1], conv_state_T.shape[0], 1 if activation else 0,
+              _p(error_word(xBC.device)), _stream(xBC), kernels=2)
+    return out
+
+
+def ssd_prefill(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                D: torch.Tensor | None, dt_bias: torch.Tensor | None, state: torch.Tensor, cu_seqlens: torch.Tensor,
+                state_idx: torch.Tensor, has_init: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+    """Mamba-2 chunked scan over variable-length sequences. x/out [T, nh, p]; dt [T, nh] (raw); B/C [T, G, N];
+    A/D/dt_bias [nh] fp32; state [lines, nh, p, N] (initial from state_idx where has_init, final written back)."""
+    _cuda("ssd_prefill", x, dt, A, B, C, D, dt_bias, state, cu_seqlens, state_idx, has_init, out)
+    T, nh, p = x.shape
+    lines, _, _, N = state.shape
+    nseq = cu_seqlens.numel() - 1
+    _lib.call("mmp_ssd_prefill", _p(x), x.stride(0), x.stride(1), _p(dt), dt.stride(0), dt.stride(1), _p(A), _p(D),
+              _p(dt_bias), _p(B), B.stride(0), B.stride(1), _p(C), C.stride(0), C.stride(1), _p(state),
+              MMP_F32 if state.dtype == torch.float32 else MMP_BF16, state.stride(0), state.stride(1), state.stride(2),
+              _p(cu_seqlens), _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1),
+              nseq, nh, p, N, B.shape[1], lines, _p(error_word(x.device)), _stream(x))
+    return out
+
+
+def attn_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor,
+                 cu_q: torch.Tensor, ctx_start: torch.Tensor, max_q_len: int, out: torch.Tensor) -> torch.Tensor:
+    """Causal GQA attention of new tokens q [T, nq, hd] over the paged cache (which already holds them)."""
+    _cuda("attn_prefill", q, key_cache, value_cache, block_table, cu_q, ctx_start, out)
+    T, nq, hd = q.shape
+    nkv = key_cache.shape[2]
+    cb, ct, ch, blk, nb = _cache_strides(key_cache, value_cache)
+    nseq = cu_q.numel() - 1
+    _lib.call("mmp_paged_attn_prefill", _p(q), q.stride(0), q.stride(1), _p(key_cache), _p(value_cache), cb, ct, ch,
+              _p(block_table), block_table.stride(0), _p(cu_q), _p(ctx_start), _p(out), out.stride(0), out.stride(1),
+              nseq, int(max_q_len), nq, nkv, hd, blk, nb, 1.0 / math.sqrt(hd), _p(error_word(q.device)), _stream(q))
+    return out
