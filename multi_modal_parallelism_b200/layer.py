@@ -10,6 +10,9 @@ reference, each exact in real arithmetic:
   * key_mult, RoPE and the paged-KV write are one kernel over the QKV output;
   * residual adds ride on GEMM epilogues (1 rank) or on the post-collective norm (`h + mix` fused into the
     pre-MLP RMSNorm).
+Prefill (`ParallelHybridLayer.prefill`) runs the same per-layout order over T packed tokens of ragged sequences,
+with the prefill cores: causal paged GQA attention over the cache, and the varlen causal conv followed by
+the chunked SSD scan, each reading and writing the sequence's state line.
 Modes: tp1, tp4 (one all-reduce per branch), tp4_fused (one all-reduce of the summed branches),
 tp4_streams (branches on two streams, one all-reduce), and any branch split split{a}{m} (attention on
 ranks 0..a-1, Mamba-2 on a..a+m-1, one all-reduce); the "tp4" names work at any world size.
@@ -22,7 +25,7 @@ from . import kernels as K
 from .config import FalconH1Dims
 from .dist import Groups
 from .sharding import RankPlan, all_norm_groups, parse_split
-from .state import DecodeCtx, RankStates
+from .state import DecodeCtx, PrefillCtx, RankStates
 from .timing import NULL, OpTimer
 from .weights import RankWeights
 
@@ -45,14 +48,16 @@ class AttentionBranch:
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
         self.nq, self.nkv, self.hd = len(a.q_heads), len(a.kv_heads), dims.head_dim
         self.inv_freq = K.rope_inv_freq(self.hd, dims.rope_theta, device)
-        B = ctx.B
+        self.prefill = isinstance(ctx, PrefillCtx)
+        B = ctx.rows
         self.qkv = qkv if qkv is not None else torch.empty(B, w.wqkv.shape[0], device=device, dtype=BF16)
         self.q = torch.empty(B, self.nq * self.hd, device=device, dtype=BF16)
         o2 = out if out is not None else torch.empty(B, self.nq * self.hd, device=device, dtype=BF16)
         self.out = o2.view(B, self.nq, self.hd)
         self.out2d = o2
-        self.splits = K.attn_default_splits(B, self.nkv, ctx.max_k)
-        self.ws = K.attn_workspace(B, self.nq, self.hd, self.splits, device)
+        if not self.prefill:
+            self.splits = K.attn_default_splits(B, self.nkv, ctx.max_k)
+            self.ws = K.attn_workspace(B, self.nq, self.hd, self.splits, device)
 
     @property
     def rope_cache(self) -> torch.Tensor:
@@ -64,13 +69,19 @@ class AttentionBranch:
         t.end("attn.qkv")
 
     def core(self, t: OpTimer) -> None:
-        """key_mult + RoPE + paged KV write, then paged decode attention into self.out."""
+        """key_mult + RoPE + paged KV write, then paged attention into self.out (one query per sequence for
+        decode; causal over the sequence's new and cached tokens for prefill)."""
         ctx = self.ctx
         t.begin("attn.rope_kv")
         K.qkv_rope_kv_write(self.qkv, self.nq, self.nkv, self.hd, ctx.positions, self.inv_freq, self.dims.key_mult,
                             self.q, self.st.key_cache, self.st.value_cache, ctx.slot_mapping)
         t.end("attn.rope_kv")
         t.begin("attn.fa")
+        if self.prefill:
+            K.attn_prefill(self.q.view(ctx.T, self.nq, self.hd), self.st.key_cache, self.st.value_cache,
+                           ctx.block_table, ctx.cu_seqlens, ctx.ctx_start, ctx.max_len, self.out)
+            t.end("attn.fa")
+            return
         K.attn_decode(self.q.view(ctx.B, self.nq, self.hd), self.st.key_cache, self.st.value_cache, ctx.cu_q,
                       ctx.seqused_k, ctx.max_k, ctx.block_table, self.out, workspace=self.ws, splits=self.splits)
         t.end("attn.fa")
@@ -118,7 +129,8 @@ class SsmBranch:
         self.A_exp = w.A[:, None, None].expand(self.nhr, self.p, self.N)
         self.D_exp = w.D[:, None].expand(self.nhr, self.p)
         self.dtb_exp = w.dt_bias[:, None].expand(self.nhr, self.p)
-        B = ctx.B
+        self.prefill = isinstance(ctx, PrefillCtx)
+        B = ctx.rows
         rows = sum(self.sizes)
         if zxbcdt is None:
             # in_proj output rows padded to 16 bytes so every [z | x | B | C | dt] slice starts aligned
@@ -130,6 +142,12 @@ class SsmBranch:
         self.Bm = self.xBC[:, x:x + b].view(B, self.ng, self.N)
         self.Cm = self.xBC[:, x + b:].view(B, self.ng, self.N)
         self.dt = self.zxbcdt[:, z + x + b + c:]
+        if self.prefill:
+            # the prefill conv writes a separate buffer (its output rows overlap later tokens' input windows)
+            self.xBCc = torch.empty(B, _pad8(x + b + c), device=device, dtype=BF16)[:, :x + b + c]
+            self.xs_c = self.xBCc[:, :x].view(B, self.nhr, self.p)
+            self.Bm_c = self.xBCc[:, x:x + b].view(B, self.ng, self.N)
+            self.Cm_c = self.xBCc[:, x + b:].view(B, self.ng, self.N)
         self.y = torch.empty(B, self.nhr, self.p, device=device, dtype=BF16)
         self.yn = yn if yn is not None else torch.empty(B, self.nhr * self.p, device=device, dtype=BF16)
         self.sumsq = torch.empty(B, 1, device=device, dtype=torch.float32)
@@ -142,17 +160,32 @@ class SsmBranch:
         t.end("ssm.inproj")
 
     def core(self, t: OpTimer) -> None:
-        """conv update, selective state update, gated RMSNorm into self.yn."""
+        """conv update, selective state update, gated RMSNorm into self.yn (prefill: varlen causal conv and the
+        chunked SSD scan from / back to each sequence's state line)."""
         w, ctx, d = self.w, self.ctx, self.dims
+        if self.prefill:
+            t.begin("ssm.conv")
+            K.conv_prefill(self.xBC, self.conv_state_T, w.conv_w, w.conv_b, ctx.cu_seqlens, ctx.state_idx,
+                           ctx.has_init, self.xBCc)
+            t.end("ssm.conv")
+            t.begin("ssm.ssd")
+            K.ssd_prefill(self.xs_c, self.dt, w.A, self.Bm_c, self.Cm_c, w.D, w.dt_bias, self.st.ssm_state,
+                          ctx.cu_seqlens, ctx.state_idx, ctx.has_init, self.y)
+            t.end("ssm.ssd")
+            self._norm(t)
+            return
         t.begin("ssm.conv")
         K.conv_update(self.xBC, self.conv_state_T, w.conv_w, w.conv_b, ctx.state_idx)
         t.end("ssm.conv")
         t.begin("ssm.ssu")
         K.ssm_update(self.st.ssm_state, self.xs, self.dt, w.A, self.Bm, self.Cm, w.D, w.dt_bias, ctx.state_idx, self.y)
         t.end("ssm.ssu")
+        self._norm(t)
+
+    def _norm(self, t: OpTimer) -> None:
         t.begin("ssm.norm")
-        K.gated_rmsnorm(self.y.view(ctx.B, self.nhr * self.p), self.z, w.norm_w, d.rms_eps, self.norm_group,
-                        self.group_size, out=self.yn, sumsq=self.sumsq)
+        K.gated_rmsnorm(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.w.norm_w, self.dims.rms_eps,
+                        self.norm_group, self.group_size, out=self.yn, sumsq=self.sumsq)
         t.end("ssm.norm")
 
     def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
@@ -212,14 +245,18 @@ class ParallelHybridLayer:
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
                  ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True):
         """overlap_branches: on a rank holding both branches (fused projections), run the attention core on a
-        side stream concurrently with the Mamba-2 core."""
+        side stream concurrently with the Mamba-2 core. `ctx` is a DecodeCtx (step() is one decode step) or a
+        PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer)."""
         self.plan, self.w, self.dims, self.groups, self.ctx = plan, w, dims, groups, ctx
+        self.st = st
+        self.overlap_branches = overlap_branches
+        self._prefill_twins: dict[int, ParallelHybridLayer] = {}
         self.collectives = collectives
         self.device = device
         self.mode = plan.mode
         if not (self.mode in ("tp1", "tp4", "tp4_fused", "tp4_streams") or parse_split(self.mode)):
             raise ValueError(self.mode)
-        self.B, self.H = ctx.B, dims.hidden
+        self.B, self.H = ctx.rows, dims.hidden
         world = groups.world_size
         if world > 1 and collectives:
             groups.ensure(all_norm_groups(self.mode, world, dims))  # collective: every rank, same order
@@ -229,7 +266,7 @@ class ParallelHybridLayer:
         self.fused = (plan.attn is not None and plan.ssm is not None and w.w_in_cat is not None
                       and self.mode in ("tp1", "tp4_fused"))
         qkv = zx = ao = yn = None
-        B = ctx.B
+        B = ctx.rows
         if self.fused:
             nqkv, nin = w.wqkv.shape[0], w.win.shape[0]
             self.in_buf = torch.empty(B, _pad8(nqkv + nin), device=device, dtype=BF16)[:, :nqkv + nin]
@@ -244,8 +281,8 @@ class ParallelHybridLayer:
             norm_group = groups.group_for_ranks(plan.ssm.norm_ranks) if collectives else _LocalOnly(len(plan.ssm.norm_ranks))
         self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn) if plan.ssm is not None else None
         self.has_mlp = dims.intermediate > 0
-        self.mlp = SwingMLP(plan, w, dims, ctx.B, device) if self.has_mlp else None
-        B, H = ctx.B, dims.hidden
+        self.mlp = SwingMLP(plan, w, dims, ctx.rows, device) if self.has_mlp else None
+        B, H = ctx.rows, dims.hidden
         mk = lambda: torch.empty(B, H, device=device, dtype=BF16)  # noqa: E731
         self.xn, self.yn, self.out = mk(), mk(), mk()
         self.h1 = mk() if self.has_mlp else self.out
@@ -257,6 +294,29 @@ class ParallelHybridLayer:
         if self.mode == "tp4_streams":
             self.s_attn = torch.cuda.Stream(device=device)
             self.s_ssm = torch.cuda.Stream(device=device)
+
+    def _bind(self, ctx) -> None:
+        self.ctx = ctx
+        for br in (self.attn, self.ssm):
+            if br is not None:
+                br.ctx = ctx
+
+    def prefill(self, h: torch.Tensor, ctx: PrefillCtx, t: OpTimer = NULL) -> torch.Tensor:
+        """Prefill of ctx.nseq ragged sequences packed into h [T, H]: the layer output [T, H], with every new
+        token's key/value written to the paged cache and each sequence's final conv and SSM state written to
+        its line, so decode steps continue from there. The kernels and collectives per layout are those of
+        step(); buffers for T rows are allocated on the first prefill of that size and reused."""
+        if h.shape[0] != ctx.T:
+            raise ValueError(f"prefill: h has {h.shape[0]} rows, the context {ctx.T} tokens")
+        twin = self._prefill_twins.get(ctx.T)
+        if twin is None:
+            twin = ParallelHybridLayer(self.plan, self.w, self.dims, self.groups, self.st, ctx, self.device,
+                                       self.collectives, self.overlap_branches)
+            self._prefill_twins[ctx.T] = twin
+        twin._bind(ctx)
+        if self.mlp is not None:
+            twin.mlp.set_k(self.mlp.k)
+        return twin.step(h, t)
 
     @property
     def _local(self) -> bool:

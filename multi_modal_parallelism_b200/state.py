@@ -17,6 +17,7 @@ outside the batch are never touched by a decode step.
 """
 from __future__ import annotations
 
+import itertools
 import math
 from dataclasses import dataclass
 
@@ -39,6 +40,88 @@ class DecodeCtx:
     slot_mapping: torch.Tensor  # [B] int64, cache slot of the new token
     state_idx: torch.Tensor  # [B] int32, SSM/conv line per sequence (line 0 is the null line)
     max_k: int
+
+    @property
+    def rows(self) -> int:
+        """Rows of the layer input: one new token per sequence."""
+        return self.B
+
+
+@dataclass
+class PrefillCtx:
+    """One prefill pass: nseq sequences, lens[i] new tokens each, packed into T rows (sequence i owns rows
+    [cu_seqlens[i], cu_seqlens[i+1])). A sequence may continue from ctx_start[i] cached tokens (chunked
+    prefill): its keys/values at positions < ctx_start[i] are already in the paged cache and, where
+    has_init[i], its conv/SSM state line holds the state after them."""
+    nseq: int
+    T: int
+    kv_block: int
+    nblk: int
+    lens: list[int]
+    starts: list[int]
+    cu_seqlens: torch.Tensor  # [nseq+1] int32
+    positions: torch.Tensor  # [T] int64, ctx_start[i] + j
+    slot_mapping: torch.Tensor  # [T] int64, cache slot of every new token
+    block_table: torch.Tensor  # [nseq, nblk] int32
+    ctx_start: torch.Tensor  # [nseq] int32
+    state_idx: torch.Tensor  # [nseq] int32
+    has_init: torch.Tensor  # [nseq] int32
+    max_len: int
+
+    @property
+    def rows(self) -> int:
+        return self.T
+
+
+def make_prefill_ctx(lens: list[int], kv_block: int, device: torch.device, starts: list[int] | None = None,
+                     state_idx: list[int] | None = None, block_table: torch.Tensor | None = None,
+                     has_init: list[int] | None = None, reserve: int = 1) -> PrefillCtx:
+    """Defaults: fresh sequences (starts 0, no initial state) on state lines 1..nseq, each owning a contiguous
+    run of cache blocks with room for `reserve` further tokens (the decode steps that follow)."""
+    nseq = len(lens)
+    starts = [0] * nseq if starts is None else list(starts)
+    if len(starts) != nseq or any(L < 0 for L in lens) or any(s < 0 for s in starts):
+        raise ValueError("make_prefill_ctx: lens and starts must be non-negative, one per sequence")
+    totals = [s + L for s, L in zip(starts, lens)]
+    nblk = max(1, math.ceil((max(totals, default=0) + reserve) / kv_block))
+    if block_table is None:
+        block_table = torch.arange(nseq * nblk, dtype=torch.int32).view(nseq, nblk)
+    table = block_table.cpu().to(torch.int32)
+    nblk = table.shape[1]
+    if any(math.ceil(t / kv_block) > nblk for t in totals):
+        raise ValueError("make_prefill_ctx: block table too short for the sequences")
+    pos = torch.cat([torch.arange(s, s + L, dtype=torch.int64) for s, L in zip(starts, lens)]) if nseq else \
+        torch.zeros(0, dtype=torch.int64)
+    seq = torch.repeat_interleave(torch.arange(nseq), torch.tensor(lens, dtype=torch.int64))
+    slot = table[seq, pos // kv_block].to(torch.int64) * kv_block + pos % kv_block
+    cu = torch.tensor([0] + list(itertools.accumulate(lens)), dtype=torch.int32)
+    if state_idx is None:
+        state_idx = list(range(1, nseq + 1))
+    if has_init is None:
+        has_init = [int(s > 0) for s in starts]
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32).to(device)  # noqa: E731
+    return PrefillCtx(
+        nseq=nseq, T=int(sum(lens)), kv_block=kv_block, nblk=nblk, lens=list(lens), starts=starts,
+        cu_seqlens=cu.to(device), positions=pos.to(device), slot_mapping=slot.to(device),
+        block_table=table.to(device), ctx_start=i32(starts), state_idx=i32(state_idx), has_init=i32(has_init),
+        max_len=max(lens, default=0),
+    )
+
+
+def decode_ctx_after(pc: PrefillCtx) -> DecodeCtx:
+    """The decode step that follows a prefill: one new token per sequence at position starts[i] + lens[i],
+    same block table and state lines."""
+    tot = torch.tensor([s + L for s, L in zip(pc.starts, pc.lens)], dtype=torch.int64)
+    table = pc.block_table.cpu()
+    if int(tot.max()) // pc.kv_block >= table.shape[1]:
+        raise ValueError("decode_ctx_after: no cache block reserved for the next token")
+    slot = table[torch.arange(pc.nseq), tot // pc.kv_block].to(torch.int64) * pc.kv_block + tot % pc.kv_block
+    dev = pc.block_table.device
+    return DecodeCtx(
+        B=pc.nseq, c=int(tot.max()), kv_block=pc.kv_block, nblk=table.shape[1], positions=tot.to(dev),
+        cu_q=torch.arange(pc.nseq + 1, dtype=torch.int32).to(dev), seqused_k=(tot + 1).to(torch.int32).to(dev),
+        block_table=pc.block_table, slot_mapping=slot.to(dev), state_idx=pc.state_idx, max_k=int(tot.max()) + 1,
+    )
 
 
 def make_decode_ctx(B: int, c: int, kv_block: int, device: torch.device) -> DecodeCtx:
@@ -150,6 +233,23 @@ def alloc_and_fill(plan: RankPlan, dims: FalconH1Dims, ctx: DecodeCtx, seed: int
         st.ssm_state = torch.zeros(B + 1, nhr, p, N, device=device, dtype=ssm_dtype)
         for li, j in enumerate(s.heads):
             st.ssm_state[1:, li] = full_ssm_head(seed, j, B, p, N, torch.device("cpu"), ssm_dtype).to(device)
+    return st
+
+
+def alloc_states(plan: RankPlan, dims: FalconH1Dims, lines: int, num_blocks: int, kv_block: int,
+                 device: torch.device, ssm_dtype: torch.dtype = torch.float32) -> RankStates:
+    """Zeroed states of this rank's shard: `lines` conv/SSM lines (line 0 the null line) and a paged KV cache
+    of `num_blocks` blocks (the starting point of a prefill)."""
+    st = RankStates()
+    if plan.attn is not None:
+        st.kv, st.key_cache, st.value_cache, st.kv_kind = alloc_kv(num_blocks, kv_block, len(plan.attn.kv_heads),
+                                                                   dims.head_dim, device)
+    s = plan.ssm
+    if s is not None:
+        rows_local = sum(r.stop - r.start for r in s.conv_rows)
+        st.conv_state = torch.zeros(lines, dims.d_conv - 1, rows_local, device=device, dtype=torch.bfloat16)
+        st.ssm_state = torch.zeros(lines, len(s.heads), dims.mamba_head_dim, dims.d_state, device=device,
+                                   dtype=ssm_dtype)
     return st
 
 
