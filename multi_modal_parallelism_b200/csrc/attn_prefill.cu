@@ -3,8 +3,8 @@
 //
 // Query token j of sequence i sits at position ctx_start[i] + j and attends to cache positions
 // [0, ctx_start[i] + j] of that sequence (the new tokens' keys/values are already in the cache), so the same
-// kernel serves prefill from scratch (ctx_start = 0) and chunked prefill over cached context. CTA = 64 query
-// tokens of one query head; 4 warps x 16 query rows; K/V tiles of 64 tokens gathered page by page from the
+// kernel serves prefill from scratch (ctx_start = 0) and chunked prefill over cached context. CTA = 128 query
+// tokens of one query head; 4 warps x two 16-row m-tiles (each K/V fragment feeds both); K/V tiles of 64 tokens gathered page by page from the
 // cache into a double-buffered cp.async ring; S = Q K^T and O += P V on mma.m16n8k16 (bf16 in, fp32
 // accumulate) with an online softmax in the exp2 domain.
 #include <algorithm>
@@ -14,7 +14,9 @@
 namespace mmp {
 namespace {
 
-constexpr int BQ = 64, BKV = 64, HD = 128, ATHR = 128;
+constexpr int MT = 2;                       // 16-row m-tiles per warp
+constexpr int NW = 4;                       // warps
+constexpr int BQ = 16 * MT * NW, BKV = 64, HD = 128, ATHR = 32 * NW;
 constexpr int ROWB = HD * 2;  // bytes per K/V/Q row
 
 struct AttnPrefillParams {
@@ -25,6 +27,7 @@ struct AttnPrefillParams {
   const int32_t* ctx_start;
   bf16* out; int64_t o_t, o_h;
   int nq, nkv, block_size, num_blocks;
+  int block_shift;  // log2(block_size) when it is a power of two, else -1
   float scale_log2;
   int* err;
 };
@@ -45,17 +48,24 @@ __device__ __forceinline__ void mma16816(float* c, const uint32_t* a, uint32_t b
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ float ex2(float x) {  // 2^x on the MUFU unit (ex2.approx.ftz; 2^-inf = 0)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0));
 }
 
 constexpr int Q_OFF = 0, K_OFF = BQ * ROWB, V_OFF = K_OFF + 2 * BKV * ROWB, SMEM = V_OFF + 2 * BKV * ROWB;
 
-__global__ void __launch_bounds__(ATHR) attn_prefill_kernel(const AttnPrefillParams P) {
+// grid (nq, nseq, q tiles): tile index from the slowest dimension, reversed, so the CTAs with the longest key
+// ranges (last query tiles) start first and the short ones fill the tail.
+__global__ void __launch_bounds__(ATHR, 2) attn_prefill_kernel(const AttnPrefillParams P) {
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_trigger();
   pdl_wait();
-  const int j0 = blockIdx.x * BQ, head = blockIdx.y, seq = blockIdx.z;
+  const int head = blockIdx.x, seq = blockIdx.y, j0 = (gridDim.z - 1 - blockIdx.z) * BQ;
   const int q0 = P.cu_q[seq], qlen = P.cu_q[seq + 1] - q0;
   if (j0 >= qlen) return;
   const int start = P.ctx_start[seq];
@@ -73,118 +83,151 @@ __global__ void __launch_bounds__(ATHR) attn_prefill_kernel(const AttnPrefillPar
     const bool v = j0 + r < qlen;
     cp16(base + Q_OFF + swz(r, c), P.q + static_cast<int64_t>(q0 + (v ? j0 + r : 0)) * P.q_t + head * P.q_h + c * 8, v);
   }
+  // K/V tile rows: thread t copies 16-byte chunk (t % 16) of rows t / 16 + 8 n
+  const int kv_c = tid % (ROWB / 16), kv_r0 = tid / (ROWB / 16);
+  constexpr int KV_ROWS_PER_PASS = ATHR / (ROWB / 16);
+  const int32_t* btab = P.block_table + static_cast<int64_t>(seq) * P.bt_stride;
+  const int64_t head_off = kh * P.c_head + kv_c * 8;
   auto issue_kv = [&](int kt, int stage) {
-    for (int i = tid; i < BKV * (ROWB / 16); i += ATHR) {
-      const int r = i / (ROWB / 16), c = i % (ROWB / 16);
+#pragma unroll
+    for (int n = 0; n < BKV / KV_ROWS_PER_PASS; ++n) {
+      const int r = kv_r0 + n * KV_ROWS_PER_PASS;
       const int tok = kt * BKV + r;
-      int blk = -1;
+      int blk = -1, in_blk = 0;
       if (tok < total) {
-        const int col = tok / P.block_size;
-        blk = col < P.bt_stride ? P.block_table[seq * P.bt_stride + col] : -1;
+        int col;
+        if (P.block_shift >= 0) {
+          col = tok >> P.block_shift;
+          in_blk = tok & (P.block_size - 1);
+        } else {
+          col = tok / P.block_size;
+          in_blk = tok - col * P.block_size;
+        }
+        blk = col < P.bt_stride ? __ldg(btab + col) : -1;
         if (blk < 0 || blk >= P.num_blocks) {
           flag_error(P.err, DEVERR_INDEX);
           blk = -1;
         }
       }
-      const int64_t off = blk < 0 ? 0 : blk * P.c_block + (tok % P.block_size) * P.c_tok + kh * P.c_head + c * 8;
-      cp16(base + K_OFF + stage * BKV * ROWB + swz(r, c), P.kc + off, blk >= 0);
-      cp16(base + V_OFF + stage * BKV * ROWB + swz(r, c), P.vc + off, blk >= 0);
+      const int64_t off = blk < 0 ? 0 : blk * P.c_block + in_blk * P.c_tok + head_off;
+      cp16(base + K_OFF + stage * BKV * ROWB + swz(r, kv_c), P.kc + off, blk >= 0);
+      cp16(base + V_OFF + stage * BKV * ROWB + swz(r, kv_c), P.vc + off, blk >= 0);
     }
   };
   issue_kv(0, 0);
   asm volatile("cp.async.commit_group;\n" ::);
 
-  const int r0 = warp * 16;                       // this warp's 16 query rows
-  const int qpos_lo = start + j0 + r0 + g;        // positions of rows g and g+8
-  const int qpos_hi = qpos_lo + 8;
-  const int warp_kend = start + min(j0 + r0 + 15, qlen - 1) + 1;
-  uint32_t qf[HD / 16][4];
-  float o[HD / 8][4];
+  // this warp's query rows: m-tile i covers tile rows warp*16 + i*64 .. +15; lane rows g and g + 8
+  const int warp_first = start + j0 + warp * 16;  // smallest query position of the warp
+  const int warp_kend = start + min(j0 + warp * 16 + (MT - 1) * 16 * NW + 15, qlen - 1) + 1;
+  float o[MT][HD / 8][4];
 #pragma unroll
-  for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  for (int i = 0; i < MT; ++i)
+#pragma unroll
+    for (int n = 0; n < HD / 8; ++n) o[i][n][0] = o[i][n][1] = o[i][n][2] = o[i][n][3] = 0.f;
+  float m[MT][2], l[MT][2];
+#pragma unroll
+  for (int i = 0; i < MT; ++i) m[i][0] = m[i][1] = -INFINITY, l[i][0] = l[i][1] = 0.f;
   const int mat = lane >> 3, r8 = lane & 7;
+  const float sc = P.scale_log2;
 
   for (int kt = 0; kt < nkt; ++kt) {
     if (kt + 1 < nkt) issue_kv(kt + 1, (kt + 1) & 1);
     asm volatile("cp.async.commit_group;\n" ::);
     asm volatile("cp.async.wait_group 1;\n" ::);
     __syncthreads();
-    if (kt == 0) {
-#pragma unroll
-      for (int k = 0; k < HD / 16; ++k) ldsm_x4(base + Q_OFF + swz(r0 + (mat & 1) * 8 + r8, k * 2 + (mat >> 1)), qf[k]);
-    }
     const int k0 = kt * BKV;
     if (k0 < warp_kend) {
       const uint32_t sK = base + K_OFF + (kt & 1) * BKV * ROWB, sV = base + V_OFF + (kt & 1) * BKV * ROWB;
-      float s[BKV / 8][4];
+      float s[MT][BKV / 8][4];
 #pragma unroll
-      for (int i = 0; i < BKV / 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
+      for (int i = 0; i < MT; ++i)
+#pragma unroll
+        for (int n = 0; n < BKV / 8; ++n) s[i][n][0] = s[i][n][1] = s[i][n][2] = s[i][n][3] = 0.f;
 #pragma unroll
       for (int k = 0; k < HD / 16; ++k) {
+        uint32_t qf[MT][4];
+#pragma unroll
+        for (int i = 0; i < MT; ++i)
+          ldsm_x4(base + Q_OFF + swz(warp * 16 + i * 16 * NW + (mat & 1) * 8 + r8, k * 2 + (mat >> 1)), qf[i]);
 #pragma unroll
         for (int np = 0; np < BKV / 16; ++np) {
           uint32_t b[4];
           ldsm_x4(sK + swz(np * 16 + (mat >> 1) * 8 + r8, k * 2 + (mat & 1)), b);
-          mma16816(s[2 * np], qf[k], b[0], b[1]);
-          mma16816(s[2 * np + 1], qf[k], b[2], b[3]);
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            mma16816(s[i][2 * np], qf[i], b[0], b[1]);
+            mma16816(s[i][2 * np + 1], qf[i], b[2], b[3]);
+          }
         }
       }
-      float mx_lo = -INFINITY, mx_hi = -INFINITY;
+      // a tile wholly inside every row's visible range needs no mask
+      const bool full = k0 + BKV - 1 <= warp_first && k0 + BKV <= total;
 #pragma unroll
-      for (int nt = 0; nt < BKV / 8; ++nt) {
+      for (int i = 0; i < MT; ++i) {
+        float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int kp = k0 + nt * 8 + 2 * tq + (e & 1);
-          const int qp = e < 2 ? qpos_lo : qpos_hi;
-          s[nt][e] = (kp <= qp && kp < total) ? s[nt][e] * P.scale_log2 : -INFINITY;
+        for (int nt = 0; nt < BKV / 8; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kp = k0 + nt * 8 + 2 * tq + (e & 1);
+            const int qp = warp_first + i * 16 * NW + g + (e >> 1) * 8;
+            if (!full && !(kp <= qp && kp < total)) s[i][nt][e] = -INFINITY;
+          }
+          mx0 = fmaxf(mx0, fmaxf(s[i][nt][0], s[i][nt][1]));
+          mx1 = fmaxf(mx1, fmaxf(s[i][nt][2], s[i][nt][3]));
         }
-        mx_lo = fmaxf(mx_lo, fmaxf(s[nt][0], s[nt][1]));
-        mx_hi = fmaxf(mx_hi, fmaxf(s[nt][2], s[nt][3]));
-      }
 #pragma unroll
-      for (int off = 1; off <= 2; off <<= 1) {
-        mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, off));
-        mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, off));
-      }
-      const float mn_lo = fmaxf(m_lo, mx_lo), mn_hi = fmaxf(m_hi, mx_hi);
-      // rows with nothing visible yet keep a zero base so exp2 stays finite
-      const float b_lo = mn_lo == -INFINITY ? 0.f : mn_lo, b_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
-      const float al_lo = exp2f(m_lo - b_lo), al_hi = exp2f(m_hi - b_hi);
-      m_lo = mn_lo;
-      m_hi = mn_hi;
-      float sum_lo = 0.f, sum_hi = 0.f;
+        for (int off = 1; off <= 2; off <<= 1) {
+          mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+          mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+        }
+        // running maxima are kept on raw scores; p = 2^(s * scale_log2 - m * scale_log2) is one FFMA + ex2
+        const float mn0 = fmaxf(m[i][0], mx0), mn1 = fmaxf(m[i][1], mx1);
+        // rows with nothing visible yet keep a zero base so the exponent stays finite
+        const float b0 = mn0 == -INFINITY ? 0.f : mn0 * sc, b1 = mn1 == -INFINITY ? 0.f : mn1 * sc;
+        const float al0 = ex2(fmaf(m[i][0], sc, -b0)), al1 = ex2(fmaf(m[i][1], sc, -b1));
+        m[i][0] = mn0;
+        m[i][1] = mn1;
+        float sum0 = 0.f, sum1 = 0.f;
 #pragma unroll
-      for (int nt = 0; nt < BKV / 8; ++nt) {
-        s[nt][0] = exp2f(s[nt][0] - b_lo);
-        s[nt][1] = exp2f(s[nt][1] - b_lo);
-        s[nt][2] = exp2f(s[nt][2] - b_hi);
-        s[nt][3] = exp2f(s[nt][3] - b_hi);
-        sum_lo += s[nt][0] + s[nt][1];
-        sum_hi += s[nt][2] + s[nt][3];
-      }
-      l_lo = l_lo * al_lo + sum_lo;
-      l_hi = l_hi * al_hi + sum_hi;
+        for (int nt = 0; nt < BKV / 8; ++nt) {
+          s[i][nt][0] = ex2(fmaf(s[i][nt][0], sc, -b0));
+          s[i][nt][1] = ex2(fmaf(s[i][nt][1], sc, -b0));
+          s[i][nt][2] = ex2(fmaf(s[i][nt][2], sc, -b1));
+          s[i][nt][3] = ex2(fmaf(s[i][nt][3], sc, -b1));
+          sum0 += s[i][nt][0] + s[i][nt][1];
+          sum1 += s[i][nt][2] + s[i][nt][3];
+        }
+        l[i][0] = l[i][0] * al0 + sum0;
+        l[i][1] = l[i][1] * al1 + sum1;
 #pragma unroll
-      for (int i = 0; i < HD / 8; ++i) {
-        o[i][0] *= al_lo;
-        o[i][1] *= al_lo;
-        o[i][2] *= al_hi;
-        o[i][3] *= al_hi;
+        for (int n = 0; n < HD / 8; ++n) {
+          o[i][n][0] *= al0;
+          o[i][n][1] *= al0;
+          o[i][n][2] *= al1;
+          o[i][n][3] *= al1;
+        }
       }
 #pragma unroll
       for (int kk = 0; kk < BKV / 16; ++kk) {  // O += P V, K = keys
-        uint32_t a[4];
-        a[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-        a[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-        a[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-        a[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        uint32_t a[MT][4];
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          a[i][0] = pack_bf16x2(s[i][2 * kk][0], s[i][2 * kk][1]);
+          a[i][1] = pack_bf16x2(s[i][2 * kk][2], s[i][2 * kk][3]);
+          a[i][2] = pack_bf16x2(s[i][2 * kk + 1][0], s[i][2 * kk + 1][1]);
+          a[i][3] = pack_bf16x2(s[i][2 * kk + 1][2], s[i][2 * kk + 1][3]);
+        }
 #pragma unroll
         for (int np = 0; np < HD / 16; ++np) {
           uint32_t b[4];  // V[key][d]: transposed load gives (k = key, n = d) fragments for d-tiles 2np, 2np + 1
           ldsm_x4_t(sV + swz(kk * 16 + (mat & 1) * 8 + r8, np * 2 + (mat >> 1)), b);
-          mma16816(o[2 * np], a, b[0], b[1]);
-          mma16816(o[2 * np + 1], a, b[2], b[3]);
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            mma16816(o[i][2 * np], a[i], b[0], b[1]);
+            mma16816(o[i][2 * np + 1], a[i], b[2], b[3]);
+          }
         }
       }
     }
@@ -192,21 +235,24 @@ __global__ void __launch_bounds__(ATHR) attn_prefill_kernel(const AttnPrefillPar
   }
   asm volatile("cp.async.wait_group 0;\n" ::);
 #pragma unroll
-  for (int off = 1; off <= 2; off <<= 1) {
-    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, off);
-    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, off);
-  }
-  const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
-  const int jr_lo = j0 + r0 + g, jr_hi = jr_lo + 8;
+  for (int i = 0; i < MT; ++i) {
 #pragma unroll
-  for (int nt = 0; nt < HD / 8; ++nt) {
-    const int d = nt * 8 + 2 * tq;
-    if (jr_lo < qlen)
-      *reinterpret_cast<uint32_t*>(P.out + static_cast<int64_t>(q0 + jr_lo) * P.o_t + head * P.o_h + d) =
-          pack_bf16x2(o[nt][0] * inv_lo, o[nt][1] * inv_lo);
-    if (jr_hi < qlen)
-      *reinterpret_cast<uint32_t*>(P.out + static_cast<int64_t>(q0 + jr_hi) * P.o_t + head * P.o_h + d) =
-          pack_bf16x2(o[nt][2] * inv_hi, o[nt][3] * inv_hi);
+    for (int off = 1; off <= 2; off <<= 1) {
+      l[i][0] += __shfl_xor_sync(0xffffffffu, l[i][0], off);
+      l[i][1] += __shfl_xor_sync(0xffffffffu, l[i][1], off);
+    }
+    const float inv0 = l[i][0] > 0.f ? 1.f / l[i][0] : 0.f, inv1 = l[i][1] > 0.f ? 1.f / l[i][1] : 0.f;
+    const int jr0 = j0 + warp * 16 + i * 16 * NW + g, jr1 = jr0 + 8;
+#pragma unroll
+    for (int nt = 0; nt < HD / 8; ++nt) {
+      const int d = nt * 8 + 2 * tq;
+      if (jr0 < qlen)
+        *reinterpret_cast<uint32_t*>(P.out + static_cast<int64_t>(q0 + jr0) * P.o_t + head * P.o_h + d) =
+            pack_bf16x2(o[i][nt][0] * inv0, o[i][nt][1] * inv0);
+      if (jr1 < qlen)
+        *reinterpret_cast<uint32_t*>(P.out + static_cast<int64_t>(q0 + jr1) * P.o_t + head * P.o_h + d) =
+            pack_bf16x2(o[i][nt][2] * inv1, o[i][nt][3] * inv1);
+    }
   }
 }
 
@@ -234,6 +280,7 @@ extern "C" int mmp_paged_attn_prefill(const void* q, int64_t q_t, int64_t q_h,
   AttnPrefillParams P{static_cast<const bf16*>(q), q_t, q_h, static_cast<const bf16*>(key_cache),
                       static_cast<const bf16*>(value_cache), c_block, c_tok, c_head, block_table, bt_stride, cu_q,
                       ctx_start, static_cast<bf16*>(out), o_t, o_h, nq, nkv, block_size, num_blocks,
+                      (block_size & (block_size - 1)) == 0 ? __builtin_ctz(block_size) : -1,
                       scale * 1.4426950408889634f, err};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   static bool attr[64] = {};
@@ -244,7 +291,9 @@ extern "C" int mmp_paged_attn_prefill(const void* q, int64_t q_t, int64_t q_h,
     if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_prefill: %s", cudaGetErrorString(e));
     attr[dev] = true;
   }
-  dim3 grid((max_q_len + BQ - 1) / BQ, nq, nseq);
+  const int tiles = (max_q_len + BQ - 1) / BQ;
+  if (tiles > 65535) return mmp_set_error(MMP_ERR_INVALID, "mmp_paged_attn_prefill: max_q_len too large");
+  dim3 grid(nq, nseq, tiles);
   cudaError_t e = mmp::launch(attn_prefill_kernel, grid, dim3(ATHR), SMEM, s, nullptr, 0, P);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_prefill: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_paged_attn_prefill");

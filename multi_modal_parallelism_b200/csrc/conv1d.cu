@@ -171,51 +171,105 @@ __device__ __forceinline__ void unpack8f(const uint4& u, float* f) {
   f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y; f[4] = c.x; f[5] = c.y; f[6] = d.x; f[7] = d.y;
 }
 
+constexpr int CONV_RUN = 32;  // tokens per thread
+constexpr int CONV_PF = 8;    // token rows loaded ahead
+
+// One thread: 8 channels over a run of CONV_RUN consecutive packed tokens (which may cross sequence ends). The
+// last W-1 inputs live in registers, so each input row is read once; the weights (W taps x 8 channels, 64
+// contiguous bytes) are read once per thread. A warp covers 256 contiguous channels of a token row.
 template <int W>
-__global__ void __launch_bounds__(128) conv_prefill_kernel(const ConvPrefillParams P) {
+__global__ void __launch_bounds__(128) conv_prefill_kernel(const ConvPrefillParams P, int ntok) {
   pdl_trigger();
   pdl_wait();
-  const int t = blockIdx.x;
-  const int c0 = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  const int c0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   if (c0 >= P.rows) return;
-  const int seq = seq_of(P.cu_seqlens, P.nseq, t);
-  const int start = P.cu_seqlens[seq];
-  const int line = P.state_idx[seq];
-  const bool init = P.has_init && P.has_init[seq];
-  if (init && (line < 0 || line >= P.lines)) {
-    flag_error(P.err, DEVERR_INDEX);
-    return;
+  const int t0 = blockIdx.y * CONV_RUN;
+  const int t1 = min(t0 + CONV_RUN, ntok);
+  float wk[W][8];
+  {
+    static_assert(W * 8 % 8 == 0, "taps x 8 channels in 16-byte loads");
+    float wf[W * 8];
+#pragma unroll
+    for (int i = 0; i < W; ++i) unpack8f(ld16(P.w + static_cast<int64_t>(c0) * W + i * 8), wf + i * 8);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int k = 0; k < W; ++k) wk[k][j] = wf[j * W + k];  // w[c][k] for c = c0 + j
   }
-  float acc[8];
+  float bias[8];
   if (P.bias) {
-    unpack8f(ld16(P.bias + c0), acc);
+    unpack8f(ld16(P.bias + c0), bias);
   } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    for (int j = 0; j < 8; ++j) bias[j] = 0.f;
   }
-  const bf16* wp = P.w + c0 * W;
-#pragma unroll
-  for (int k = 0; k < W; ++k) {
-    const int u = t - (W - 1) + k;
-    float v[8];
-    if (u >= start) {
-      unpack8f(ld16(P.x + static_cast<int64_t>(u) * P.x_t + c0), v);
-    } else if (init) {
-      unpack8f(ld16(P.state + line * P.s_line + (u - start + W - 1) * P.s_k + c0), v);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = 0.f;
+  int seq = seq_of(P.cu_seqlens, P.nseq, t0);
+  int s_end = P.cu_seqlens[seq + 1];
+  float win[W - 1][8];  // inputs t-W+1 .. t-1, oldest first
+  // history of a sequence whose first token in this run is t: inputs before its start come from its
+  // conv-state line (when it has an initial state) or are zero
+  auto load_history = [&](int t) -> bool {
+    const int start = P.cu_seqlens[seq];
+    const int line = P.state_idx[seq];
+    const bool init = P.has_init && P.has_init[seq];
+    if (init && (line < 0 || line >= P.lines)) {
+      flag_error(P.err, DEVERR_INDEX);
+      return false;
     }
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = fmaf(bf2f(wp[j * W + k]), v[j], acc[j]);
-  }
-  if (P.silu) {
+    for (int k = 0; k < W - 1; ++k) {
+      const int u = t - (W - 1) + k;
+      if (u >= start) {
+        unpack8f(ld16(P.x + static_cast<int64_t>(u) * P.x_t + c0), win[k]);
+      } else if (init) {
+        unpack8f(ld16(P.state + line * P.s_line + (u - start + W - 1) * P.s_k + c0), win[k]);
+      } else {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[j] = silu(acc[j]);
+        for (int j = 0; j < 8; ++j) win[k][j] = 0.f;
+      }
+    }
+    return true;
+  };
+  if (!load_history(t0)) return;
+  for (int tb = t0; tb < t1; tb += CONV_PF) {
+    uint4 rows[CONV_PF];
+#pragma unroll
+    for (int i = 0; i < CONV_PF; ++i)
+      if (tb + i < t1) rows[i] = ld16(P.x + static_cast<int64_t>(tb + i) * P.x_t + c0);
+#pragma unroll
+    for (int i = 0; i < CONV_PF; ++i) {
+      const int t = tb + i;
+      if (t >= t1) break;
+      if (t >= s_end) {  // first token of a later sequence (skipping empty ones)
+        while (seq < P.nseq - 1 && t >= P.cu_seqlens[seq + 1]) ++seq;
+        s_end = P.cu_seqlens[seq + 1];
+        if (t >= s_end) {  // offsets that do not cover the packed tokens
+          flag_error(P.err, DEVERR_INDEX);
+          return;
+        }
+        if (!load_history(t)) return;
+      }
+      float v[8], acc[8];
+      unpack8f(rows[i], v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float a = bias[j];
+#pragma unroll
+        for (int k = 0; k < W - 1; ++k) a = fmaf(wk[k][j], win[k][j], a);
+        a = fmaf(wk[W - 1][j], v[j], a);
+        acc[j] = P.silu ? silu(a) : a;
+      }
+#pragma unroll
+      for (int k = 0; k < W - 2; ++k)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) win[k][j] = win[k + 1][j];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) win[W - 2][j] = v[j];
+      st16(P.out + static_cast<int64_t>(t) * P.o_t + c0,
+           make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                      pack_bf16x2(acc[6], acc[7])));
+    }
   }
-  st16(P.out + static_cast<int64_t>(t) * P.o_t + c0,
-       make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
-                  pack_bf16x2(acc[6], acc[7])));
 }
 
 template <int W>
@@ -258,15 +312,16 @@ extern "C" int mmp_conv1d_prefill(const void* x, int64_t x_t, void* out, int64_t
   if (x == out) return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: out must not alias x");
   if (nseq < 0 || nseq > 65535 || ntok < 0 || rows <= 0 || rows % 8 || W != 4 || lines <= 0 ||
       !aligned16(x) || !aligned16(out) || !aligned16(state) || (bias && !aligned16(bias)) || x_t % 8 || o_t % 8 ||
-      s_line % 8 || s_k % 8)
+      s_line % 8 || s_k % 8 || !aligned16(w))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: needs W == 4, rows %% 8 == 0, 16-byte aligned rows");
   ConvPrefillParams P{static_cast<const bf16*>(x), x_t, static_cast<bf16*>(out), o_t, static_cast<bf16*>(state), s_line,
                       s_k, static_cast<const bf16*>(w), static_cast<const bf16*>(bias), cu_seqlens, state_idx, has_init,
                       nseq, rows, lines, silu, err};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int bx = (rows / 8 + 127) / 128;
-  if (bx > 65535) return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: too many channels");
-  cudaError_t e = mmp::launch(conv_prefill_kernel<4>, dim3(ntok, bx), dim3(128), 0, s, nullptr, 0, P);
+  const int runs = (ntok + mmp::CONV_RUN - 1) / mmp::CONV_RUN;
+  if (bx > 65535 || runs > 65535) return mmp_set_error(MMP_ERR_INVALID, "mmp_conv1d_prefill: too many channels or tokens");
+  cudaError_t e = mmp::launch(conv_prefill_kernel<4>, dim3(bx, runs), dim3(128), 0, s, nullptr, 0, P, ntok);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_conv1d_prefill: %s", cudaGetErrorString(e));
   e = mmp::launch(conv_prefill_state_kernel<4>, dim3(bx, nseq), dim3(128), 0, s, nullptr, 0, P);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_conv1d_prefill(state): %s", cudaGetErrorString(e));

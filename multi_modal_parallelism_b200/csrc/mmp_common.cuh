@@ -42,7 +42,8 @@ __device__ __forceinline__ void st_stream16(void* p, uint4 v) { __stcs(reinterpr
 __device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ void st16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 
-__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+// x * sigmoid(x) with the fast divide (2 ulp; x / inf -> 0 for very negative x): outputs are bf16
+__device__ __forceinline__ float silu(float x) { return __fdividef(x, 1.f + __expf(-x)); }
 
 __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
