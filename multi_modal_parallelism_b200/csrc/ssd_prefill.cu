@@ -8,9 +8,10 @@
 //   S_out = exp(cum_last) S + sum_s x_s (outer) B_s exp(cum_last - cum_s) dt_s
 // which is the recurrence s_t = exp(a_t) s_{t-1} + dt_t x_t B_t^T, y_t = s_t C_t + D x_t unrolled over the
 // chunk (Dao & Gu 2024). One CTA owns a 64-row slice of one head's p dimension for one sequence and walks its
-// chunks of 64 tokens in order; the fp32 state stays in shared memory. The four contractions per chunk
-// (C B^T, masked . x, C S^T, x^T . B-weighted) are bf16 tensor-core MMAs (mma.m16n8k16, fp32 accumulate) fed by
-// ldmatrix from 128-byte-swizzled shared memory. Initial state: the sequence's state line (or zeros);
+// chunks of 64 tokens in order; the fp32 state lives in the warps' mma accumulators for the whole walk, and
+// the next chunk's C, B and x are loaded (cp.async, two stages) under the current chunk's math. The four
+// contractions per chunk (C B^T, x^T . M^T, S . C^T, x^T . B-weighted) are bf16 tensor-core MMAs
+// (mma.m16n8k16, fp32 accumulate) fed by ldmatrix from 128-byte-swizzled shared memory. Initial state: the sequence's state line (or zeros);
 // final state: written back to it.
 #include <algorithm>
 
@@ -63,27 +64,36 @@ __device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool valid) 
 
 template <int N>
 struct SsdSmem {
-  static constexpr int RB = N * 2;                    // bf16 row bytes of B / C / S_bf
-  static constexpr int C_OFF = 0;                     // [QC][N] bf16
-  static constexpr int B_OFF = C_OFF + QC * RB;       // [QC][N] bf16, later the weighted B
-  static constexpr int X_OFF = B_OFF + QC * RB;       // [QC][PT] bf16 (row 128 bytes)
-  static constexpr int M_OFF = X_OFF + QC * PT * 2;   // [QC][QC] bf16 (row 128 bytes)
-  static constexpr int SB_OFF = M_OFF + QC * QC * 2;  // [PT][N] bf16 state copy
-  static constexpr int S_OFF = SB_OFF + PT * RB;      // [PT][N] fp32 state
-  static constexpr int CUM_OFF = S_OFF + PT * N * 4;  // [QC] fp32 cumulative log-decay
+  static constexpr int RB = N * 2;                    // bf16 row bytes of B / C
+  static constexpr int CB_BYTES = QC * RB;            // one chunk of C or B
+  static constexpr int X_BYTES = QC * PT * 2;         // one chunk of x (row 128 bytes)
+  static constexpr int STAGE = 2 * CB_BYTES + X_BYTES;  // C | B | x of one chunk; two stages
+  static constexpr int M_OFF = 2 * STAGE;             // [QC][QC] bf16 masked, weighted C B^T
+  static constexpr int YLD = QC + 8;                  // fp32 row stride of the partial exchange
+  static constexpr int YP_OFF = M_OFF + QC * QC * 2;  // [PT][YLD] fp32 partials; then the y tile [QC][PT+8] bf16
+  static constexpr int YT_LD = (PT + 8) * 2;          // byte row stride of the y tile
+  static constexpr int CUM_OFF = YP_OFF + PT * YLD * 4;  // [QC] fp32 cumulative log-decay
   static constexpr int DT_OFF = CUM_OFF + QC * 4;     // [QC] fp32 dt
   static constexpr int BYTES = DT_OFF + QC * 4;
+  static_assert(QC * YT_LD <= PT * YLD * 4, "y tile fits the partial buffer");
 };
 
+// Warp roles (8 warps): warp w owns state rows p = (w & 3) * 16 .. +15 and state columns n in half (w >> 2),
+// as mma accumulators in registers for the whole walk. Its output work is the y^T tile of the same 16 rows
+// and token half (w >> 2): the state term sum_n S[p][n] C[t][n] is computed over its own column half for all
+// 64 tokens (A operand = the accumulators repacked to bf16), and the two warps of a row tile swap the halves
+// they do not own through shared memory.
 template <typename ST, int N>
 __global__ void __launch_bounds__(THR, 1) ssd_prefill_kernel(const SsdParams P) {
   using L = SsdSmem<N>;
+  constexpr int NH = N / 2;   // state columns per warp
+  constexpr int NT = NH / 8;  // state n8-tiles per warp
   extern __shared__ __align__(128) uint8_t smem[];
   pdl_trigger();
   pdl_wait();
   const int p0 = blockIdx.x * PT, h = blockIdx.y, seq = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, tq = lane & 3;
+  const int g = lane >> 2, tq = lane & 3, mat = lane >> 3, r8 = lane & 7;
   const int t_begin = P.cu_seqlens[seq], t_end = P.cu_seqlens[seq + 1];
   const int line = P.state_idx[seq];
   if (line < 0 || line >= P.lines) {
@@ -92,48 +102,73 @@ __global__ void __launch_bounds__(THR, 1) ssd_prefill_kernel(const SsdParams P) 
   }
   const int grp = h / (P.nh / P.ngroups);
   const float A = P.A[h], Dh = P.D ? P.D[h] : 0.f, dtb = P.dt_bias ? P.dt_bias[h] : 0.f;
-  float* sS = reinterpret_cast<float*>(smem + L::S_OFF);
   float* sCum = reinterpret_cast<float*>(smem + L::CUM_OFF);
   float* sDt = reinterpret_cast<float*>(smem + L::DT_OFF);
+  float* sYP = reinterpret_cast<float*>(smem + L::YP_OFF);
   const uint32_t base = sa(smem);
   ST* gstate = reinterpret_cast<ST*>(P.state) + line * P.s_line + h * P.s_head + static_cast<int64_t>(p0) * P.s_p;
+  const int pr = (warp & 3) * 16;      // state / output rows of this warp
+  const int half = warp >> 2;
+  const int nh0 = half * NH;           // state columns of this warp
+  const int th0 = half * (QC / 2);     // output tokens of this warp
 
-  // initial state
-  const bool init = P.has_init && P.has_init[seq];
-  for (int i = tid; i < PT * N; i += THR) {
-    const int r = i / N, n = i % N;
-    const float v = (init && p0 + r < P.p) ? static_cast<float>(gstate[r * P.s_p + n]) : 0.f;
-    sS[i] = v;  // and the bf16 copy that feeds the C S^T contraction
-    *reinterpret_cast<bf16*>(smem + L::SB_OFF + swz(r, n >> 3, L::RB) + (n & 7) * 2) = f2bf(v);
+  // ---- initial state into the accumulators (rows pr+g, pr+g+8; columns nh0 + nt*8 + 2tq, +1)
+  float S[NT][4];
+  {
+    const bool init = P.has_init && P.has_init[seq];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const int n = nh0 + nt * 8 + 2 * tq;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = pr + g + (e >> 1) * 8;
+        S[nt][e] = (init && p0 + r < P.p) ? static_cast<float>(gstate[r * P.s_p + n + (e & 1)]) : 0.f;
+      }
+    }
   }
 
-  for (int c0 = t_begin; c0 < t_end; c0 += QC) {
+  constexpr int CPR = N / 8;  // 16-byte chunks per B/C row
+  auto issue = [&](int c0, int stage) {
     const int qn = min(QC, t_end - c0);
-    __syncthreads();  // previous chunk fully consumed
-    // ---- loads: C, B rows (N bf16), x slice (PT bf16), dt
-    constexpr int CPR = N / 8;  // 16-byte chunks per B/C row
+    const uint32_t sC = base + stage * L::STAGE, sB = sC + L::CB_BYTES, sX = sB + L::CB_BYTES;
     for (int i = tid; i < QC * CPR; i += THR) {
       const int r = i / CPR, c = i % CPR;
       const bool v = r < qn;
       const int64_t t = c0 + (v ? r : 0);
-      cp16(base + L::C_OFF + swz(r, c, L::RB), P.C + t * P.C_t + grp * P.C_g + c * 8, v);
-      cp16(base + L::B_OFF + swz(r, c, L::RB), P.B + t * P.B_t + grp * P.B_g + c * 8, v);
+      cp16(sC + swz(r, c, L::RB), P.C + t * P.C_t + grp * P.C_g + c * 8, v);
+      cp16(sB + swz(r, c, L::RB), P.B + t * P.B_t + grp * P.B_g + c * 8, v);
     }
     for (int i = tid; i < QC * (PT / 8); i += THR) {
       const int r = i / (PT / 8), c = i % (PT / 8);
       const bool v = r < qn && p0 + c * 8 < P.p;
       const int64_t t = c0 + (r < qn ? r : 0);
-      cp16(base + L::X_OFF + swz(r, c, PT * 2), P.x + t * P.x_t + h * P.x_h + p0 + c * 8, v);
+      cp16(sX + swz(r, c, PT * 2), P.x + t * P.x_t + h * P.x_h + p0 + c * 8, v);
     }
     asm volatile("cp.async.commit_group;\n" ::);
+  };
+  float dnext[2] = {0.f, 0.f};  // warp 0: raw dt of tokens 2 lane, 2 lane + 1 of the next chunk
+  auto load_dt = [&](int c0) {
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = lane * 2 + j;
+        dnext[j] = c0 + r < t_end ? bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) : 0.f;
+      }
+    }
+  };
+  if (t_begin < t_end) {
+    issue(t_begin, 0);
+    load_dt(t_begin);
+  }
+
+  int stage = 0;
+  for (int c0 = t_begin; c0 < t_end; c0 += QC, stage ^= 1) {
+    const int qn = min(QC, t_end - c0);
     if (warp == 0) {
       // dt' = softplus(dt + bias) and the inclusive running sum of dt' A over the chunk (two tokens per lane)
       float d[2], cs[2];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = lane * 2 + j;
-        d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) + dtb) : 0.f;
-      }
+      for (int j = 0; j < 2; ++j) d[j] = lane * 2 + j < qn ? softplus(dnext[j] + dtb) : 0.f;
       cs[0] = d[0] * A;
       cs[1] = cs[0] + d[1] * A;
       float run = cs[1];
@@ -149,22 +184,30 @@ __global__ void __launch_bounds__(THR, 1) ssd_prefill_kernel(const SsdParams P) 
         sCum[lane * 2 + j] = excl + cs[j];
       }
     }
-    asm volatile("cp.async.wait_group 0;\n" ::);
+    // next chunk's loads run under this chunk's math (its stage was released by the last barrier)
+    if (c0 + QC < t_end) {
+      issue(c0 + QC, stage ^ 1);
+      load_dt(c0 + QC);
+      asm volatile("cp.async.wait_group 1;\n" ::);
+    } else {
+      asm volatile("cp.async.wait_group 0;\n" ::);
+    }
     __syncthreads();
     const float cum_last = sCum[qn - 1];
+    const uint32_t sC = base + stage * L::STAGE, sB = sC + L::CB_BYTES, sX = sB + L::CB_BYTES;
+    uint8_t* pB = smem + stage * L::STAGE + L::CB_BYTES;
 
     // ---- G = C B^T (QC x QC), masked and weighted into M[t][s] = G exp(cum_t - cum_s) dt_s (s <= t)
     {
       const int r0 = (warp >> 1) * 16, s0 = (warp & 1) * 32;
       float acc[4][4] = {};
-      const int mat = lane >> 3, r8 = lane & 7;
 #pragma unroll 4
       for (int k = 0; k < N / 16; ++k) {
         uint32_t a[4], b[2][4];
-        ldsm_x4(base + L::C_OFF + swz(r0 + (mat & 1) * 8 + r8, k * 2 + (mat >> 1), L::RB), a);
+        ldsm_x4(sC + swz(r0 + (mat & 1) * 8 + r8, k * 2 + (mat >> 1), L::RB), a);
 #pragma unroll
         for (int np = 0; np < 2; ++np)
-          ldsm_x4(base + L::B_OFF + swz(s0 + np * 16 + (mat >> 1) * 8 + r8, k * 2 + (mat & 1), L::RB), b[np]);
+          ldsm_x4(sB + swz(s0 + np * 16 + (mat >> 1) * 8 + r8, k * 2 + (mat & 1), L::RB), b[np]);
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt) mma16816(acc[nt], a, b[nt >> 1][(nt & 1) * 2], b[nt >> 1][(nt & 1) * 2 + 1]);
       }
@@ -180,57 +223,72 @@ __global__ void __launch_bounds__(THR, 1) ssd_prefill_kernel(const SsdParams P) 
         }
       }
     }
-    __syncthreads();
 
-    // ---- y = M x + exp(cum_t) C S^T + D x for this chunk (QC tokens x PT rows)
-    {
-      const int r0 = (warp >> 1) * 16, c0p = (warp & 1) * 32;
-      const int mat = lane >> 3, r8 = lane & 7;
-      float yi[4][4] = {}, ys[4][4] = {};
+    // ---- state term, this warp's column half, all tokens: ys[p][t] = sum_{n in half} S[p][n] C[t][n]
+    float ys[QC / 8][4] = {};
 #pragma unroll
-      for (int k = 0; k < QC / 16; ++k) {  // intra-chunk: K = tokens s
-        uint32_t a[4], b[2][4];
-        ldsm_x4(base + L::M_OFF + swz(r0 + (mat & 1) * 8 + r8, k * 2 + (mat >> 1), QC * 2), a);
+    for (int kk = 0; kk < NH / 16; ++kk) {
+      uint32_t a[4];  // accumulator n8-tiles 2kk, 2kk+1 are the A fragment of this k16 step
+      a[0] = pack_bf16x2(S[2 * kk][0], S[2 * kk][1]);
+      a[1] = pack_bf16x2(S[2 * kk][2], S[2 * kk][3]);
+      a[2] = pack_bf16x2(S[2 * kk + 1][0], S[2 * kk + 1][1]);
+      a[3] = pack_bf16x2(S[2 * kk + 1][2], S[2 * kk + 1][3]);
 #pragma unroll
-        for (int np = 0; np < 2; ++np)  // x is [s][pp]: transposed load gives the (k = s, n = pp) fragment
-          ldsm_x4_t(base + L::X_OFF + swz(k * 16 + (mat & 1) * 8 + r8, (c0p + np * 16) / 8 + (mat >> 1), PT * 2), b[np]);
-#pragma unroll
-        for (int nt = 0; nt < 4; ++nt) mma16816(yi[nt], a, b[nt >> 1][(nt & 1) * 2], b[nt >> 1][(nt & 1) * 2 + 1]);
+      for (int np = 0; np < QC / 16; ++np) {
+        uint32_t b[4];  // C[t][n]: rows t, k = n
+        ldsm_x4(sC + swz(np * 16 + (mat >> 1) * 8 + r8, (nh0 + kk * 16) / 8 + (mat & 1), L::RB), b);
+        mma16816(ys[2 * np], a, b[0], b[1]);
+        mma16816(ys[2 * np + 1], a, b[2], b[3]);
       }
-#pragma unroll 4
-      for (int k = 0; k < N / 16; ++k) {  // state term: K = n
-        uint32_t a[4], b[2][4];
-        ldsm_x4(base + L::C_OFF + swz(r0 + (mat & 1) * 8 + r8, k * 2 + (mat >> 1), L::RB), a);
+    }
+    // hand the other token half to the partner warp
 #pragma unroll
-        for (int np = 0; np < 2; ++np)
-          ldsm_x4(base + L::SB_OFF + swz(c0p + np * 16 + (mat >> 1) * 8 + r8, k * 2 + (mat & 1), L::RB), b[np]);
+    for (int nt = 0; nt < QC / 8; ++nt) {
+      if ((nt >= QC / 16) == (half == 1)) continue;  // own half
+      const int t = nt * 8 + 2 * tq;
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) mma16816(ys[nt], a, b[nt >> 1][(nt & 1) * 2], b[nt >> 1][(nt & 1) * 2 + 1]);
-      }
-      const bf16* sX = reinterpret_cast<const bf16*>(smem + L::X_OFF);
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) {
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int t = r0 + g + (e >> 1) * 8, pp = c0p + nt * 8 + 2 * tq;
-          if (t >= qn || p0 + pp >= P.p) continue;
-          const float dec = __expf(sCum[t]);
-          const bf16* xr = reinterpret_cast<const bf16*>(smem + L::X_OFF + swz(t, pp >> 3, PT * 2)) + (pp & 7);
-          (void)sX;
-          const float y0 = yi[nt][e] + dec * ys[nt][e] + Dh * bf2f(xr[0]);
-          const float y1 = yi[nt][e + 1] + dec * ys[nt][e + 1] + Dh * bf2f(xr[1]);
-          *reinterpret_cast<uint32_t*>(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + p0 + pp) =
-              pack_bf16x2(y0, y1);
-        }
-      }
+      for (int e = 0; e < 4; e += 2)
+        *reinterpret_cast<float2*>(sYP + (pr + g + (e >> 1) * 8) * L::YLD + t) = make_float2(ys[nt][e], ys[nt][e + 1]);
     }
     __syncthreads();
 
-    // ---- weight B rows in place: W[s][n] = B[s][n] exp(cum_last - cum_s) dt_s
+    // ---- intra-chunk term for this warp's token half: yi[p][t] = sum_s x[s][p] M[t][s]; combine
+    float yv[QC / 16][4];
+    {
+      float yi[QC / 16][4] = {};
+#pragma unroll
+      for (int ks = 0; ks < QC / 16; ++ks) {
+        uint32_t a[4];  // A[p][s] from x[s][p]: transposed 8x8 blocks
+        ldsm_x4_t(sX + swz(ks * 16 + (mat >> 1) * 8 + r8, pr / 8 + (mat & 1), PT * 2), a);
+#pragma unroll
+        for (int np = 0; np < QC / 32; ++np) {
+          uint32_t b[4];  // M[t][s]: rows t, k = s
+          ldsm_x4(base + L::M_OFF + swz(th0 + np * 16 + (mat >> 1) * 8 + r8, ks * 2 + (mat & 1), QC * 2), b);
+          mma16816(yi[2 * np], a, b[0], b[1]);
+          mma16816(yi[2 * np + 1], a, b[2], b[3]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < QC / 16; ++j) {
+        float own[4];  // state-term partial of this warp's token half (static register indexing)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) own[e] = half ? ys[QC / 16 + j][e] : ys[j][e];
+        const int t = th0 + j * 8 + 2 * tq;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int r = pr + g + (e >> 1) * 8, tt = t + (e & 1);
+          const float part = sYP[r * L::YLD + tt];
+          const float xv = bf2f(*reinterpret_cast<const bf16*>(smem + stage * L::STAGE + 2 * L::CB_BYTES +
+                                                                swz(tt, r >> 3, PT * 2) + (r & 7) * 2));
+          yv[j][e] = yi[j][e] + __expf(sCum[tt]) * (own[e] + part) + Dh * xv;
+        }
+      }
+    }
+    // weight B rows in place for the state update: W[s][n] = B[s][n] exp(cum_last - cum_s) dt_s
     for (int i = tid; i < QC * CPR; i += THR) {
       const int r = i / CPR, c = i % CPR;
       const float w = r < qn ? __expf(cum_last - sCum[r]) * sDt[r] : 0.f;
-      uint4* ptr = reinterpret_cast<uint4*>(smem + L::B_OFF + swz(r, c, L::RB));
+      uint4* ptr = reinterpret_cast<uint4*>(pB + swz(r, c, L::RB));
       uint4 u = *ptr;
       float2 a0 = unpack_bf16x2(u.x), a1 = unpack_bf16x2(u.y), a2 = unpack_bf16x2(u.z), a3 = unpack_bf16x2(u.w);
       *ptr = make_uint4(pack_bf16x2(a0.x * w, a0.y * w), pack_bf16x2(a1.x * w, a1.y * w),
@@ -238,54 +296,53 @@ __global__ void __launch_bounds__(THR, 1) ssd_prefill_kernel(const SsdParams P) 
     }
     __syncthreads();
 
-    // ---- S = exp(cum_last) S + x^T W  (PT x N), K = tokens s
-    {
-      constexpr int NW = N / 2;            // columns per warp (2 warps across n)
-      constexpr int NT = NW / 8;           // n-tiles per warp
-      const int r0 = (warp & 3) * 16, n0 = (warp >> 2) * NW;
-      const float dec = __expf(cum_last);
-      float acc[NT][4];
+    // ---- y tile [t][p] (bf16) into the partial buffer; S = exp(cum_last) S + x^T W
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int n = n0 + nt * 8 + 2 * tq;
-        acc[nt][0] = dec * sS[(r0 + g) * N + n];
-        acc[nt][1] = dec * sS[(r0 + g) * N + n + 1];
-        acc[nt][2] = dec * sS[(r0 + g + 8) * N + n];
-        acc[nt][3] = dec * sS[(r0 + g + 8) * N + n + 1];
+    for (int j = 0; j < QC / 16; ++j) {
+      const int t = th0 + j * 8 + 2 * tq;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = pr + g + (e >> 1) * 8;
+        *reinterpret_cast<bf16*>(smem + L::YP_OFF + (t + (e & 1)) * L::YT_LD + r * 2) = f2bf(yv[j][e]);
       }
-      const int mat = lane >> 3, r8 = lane & 7;
+    }
+    {
+      const float dec = __expf(cum_last);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) S[nt][e] *= dec;
 #pragma unroll
       for (int k = 0; k < QC / 16; ++k) {
         uint32_t a[4];
-        // A[pp][s] from x[s][pp]: 8x8 blocks (pp 0-7, s 0-7), (pp 8-15, s 0-7), (pp 0-7, s 8-15), (pp 8-15, s 8-15)
-        ldsm_x4_t(base + L::X_OFF + swz(k * 16 + (mat >> 1) * 8 + r8, r0 / 8 + (mat & 1), PT * 2), a);
+        ldsm_x4_t(sX + swz(k * 16 + (mat >> 1) * 8 + r8, pr / 8 + (mat & 1), PT * 2), a);
 #pragma unroll
         for (int np = 0; np < NT / 2; ++np) {
           uint32_t b[4];  // W[s][n]: transposed load gives (k = s, n) fragments for n-tiles 2np, 2np + 1
-          ldsm_x4_t(base + L::B_OFF + swz(k * 16 + (mat & 1) * 8 + r8, (n0 + np * 16) / 8 + (mat >> 1), L::RB), b);
-          mma16816(acc[2 * np], a, b[0], b[1]);
-          mma16816(acc[2 * np + 1], a, b[2], b[3]);
-        }
-      }
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int n = n0 + nt * 8 + 2 * tq;
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          const int r = r0 + g + (e >> 1) * 8;
-          sS[r * N + n] = acc[nt][e];
-          sS[r * N + n + 1] = acc[nt][e + 1];
-          *reinterpret_cast<uint32_t*>(smem + L::SB_OFF + swz(r, n >> 3, L::RB) + (n & 7) * 2) =
-              pack_bf16x2(acc[nt][e], acc[nt][e + 1]);
+          ldsm_x4_t(sB + swz(k * 16 + (mat & 1) * 8 + r8, (nh0 + np * 16) / 8 + (mat >> 1), L::RB), b);
+          mma16816(S[2 * np], a, b[0], b[1]);
+          mma16816(S[2 * np + 1], a, b[2], b[3]);
         }
       }
     }
+    __syncthreads();
+    // ---- coalesced store of the y tile: 8 threads x 16 bytes per token row
+    for (int i = tid; i < QC * (PT / 8); i += THR) {
+      const int t = i / (PT / 8), c = i % (PT / 8);
+      if (t < qn && p0 + c * 8 < P.p)
+        st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + p0 + c * 8,
+             *reinterpret_cast<const uint4*>(smem + L::YP_OFF + t * L::YT_LD + c * 16));
+    }
   }
-  __syncthreads();
   // final state -> the sequence's line
-  for (int i = tid; i < PT * N; i += THR) {
-    const int r = i / N, n = i % N;
-    if (p0 + r < P.p) gstate[r * P.s_p + n] = static_cast<ST>(sS[i]);
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const int n = nh0 + nt * 8 + 2 * tq;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = pr + g + (e >> 1) * 8;
+      if (p0 + r < P.p) gstate[r * P.s_p + n + (e & 1)] = static_cast<ST>(S[nt][e]);
+    }
   }
 }
 
@@ -325,8 +382,8 @@ extern "C" int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const vo
   if (nseq < 0 || nseq > 65535 || nh <= 0 || nh > 65535 || p <= 0 || p % 8 || ngroups <= 0 || nh % ngroups || lines <= 0)
     return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: bad sizes nh=%d p=%d ngroups=%d", nh, p, ngroups);
   if (!aligned16(x) || !aligned16(B) || !aligned16(C) || x_t % 8 || x_h % 8 || B_t % 8 || B_g % 8 || C_t % 8 || C_g % 8 ||
-      (o_t | o_h) & 1 || (reinterpret_cast<uintptr_t>(out) & 3))
-    return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: x, B, C rows must be 16-byte aligned, out 4-byte aligned");
+      o_t % 8 || o_h % 8 || !aligned16(out))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: x, B, C and out rows must be 16-byte aligned");
   if (state_dtype != MMP_F32 && state_dtype != MMP_BF16)
     return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: state dtype must be fp32 or bf16");
   SsdParams P{static_cast<const bf16*>(x), x_t, x_h, static_cast<const bf16*>(dt), dt_t, dt_h, A, D, dt_bias,
