@@ -10,6 +10,10 @@ batch 64, context 2048, on 1-8 GPUs.
 A step is one CUDA-graph replay of the whole layer step (every kernel ours, collectives NCCL); value =
 batch tokens / device step time, max over ranks. Inputs are larger than L2 (403 MB of SSM state), so no
 flush is needed between steps. Prints one JSON line on rank 0.
+
+The same line carries a `prefill` object: the layer's prefill of 8 fresh sequences x 2048 tokens
+(ParallelHybridLayer.prefill, same layout), device-timed, with its algorithmic TFLOP (GEMMs, causal
+attention, chunked SSD at chunk 256) against the measured bf16 peak.
 """
 from __future__ import annotations
 
@@ -41,6 +45,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--soak-s", type=float, default=1.5, help="replays before timing, with clocks sampled")
     ap.add_argument("--cpu-s", type=float, default=12.0, help="seconds of CPU fp32 layer timing (rank 0, N=1)")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--prefill-seqs", type=int, default=8)
+    ap.add_argument("--prefill-len", type=int, default=2048, help="0 skips the prefill measurement")
+    ap.add_argument("--prefill-steps", type=int, default=20)
     return ap.parse_args()
 
 
@@ -160,6 +167,70 @@ def roofline_peak() -> tuple[float, str]:
         except Exception:
             pass
     return 6650.0, "fallback"
+
+
+def bf16_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+        except Exception:
+            pass
+    return 1590.0, "fallback"
+
+
+def prefill_flops(dims, lens: list[int], chunk: int = 256) -> dict:
+    """Algorithmic FLOPs of one whole-layer prefill: projections (and MLP), causal GQA attention (QK^T and PV
+    over the visible half), Mamba-2 SSD counted in its chunked form (per chunk: C B^T per group, then per head
+    the masked product with x, the chunk state and the state output)."""
+    T = sum(lens)
+    H, hd, nq, nkv = dims.hidden, dims.head_dim, dims.n_q, dims.n_kv
+    nh, p, N, G = dims.n_mamba_heads, dims.mamba_head_dim, dims.d_state, dims.n_groups
+    in_rows = (nq + 2 * nkv) * hd + 2 * dims.d_ssm + 2 * G * N + nh
+    gemm = 2 * T * H * in_rows + 2 * T * (nq * hd + dims.d_ssm) * H + 2 * T * H * 3 * dims.intermediate
+    attn = sum(4 * (L * (L + 1) / 2) * hd * nq for L in lens)
+    ssd = 0.0
+    for L in lens:
+        for c0 in range(0, L, chunk):
+            q = min(chunk, L - c0)
+            ssd += 2 * q * q * N * G + nh * (2 * q * q * p + 4 * q * N * p)
+    return {"gemm": gemm, "attn": attn, "ssd": ssd, "total": gemm + attn + ssd}
+
+
+def time_prefill(args, layer, groups) -> dict | None:
+    """Prefill of args.prefill_seqs fresh sequences of args.prefill_len tokens on the decode layer's own
+    cache blocks and state lines (the decode timing is over), device-timed, max over ranks."""
+    import torch
+
+    from multi_modal_parallelism_b200.dist import barrier_sync
+    from multi_modal_parallelism_b200.state import make_prefill_ctx
+
+    nseq, L = args.prefill_seqs, args.prefill_len
+    if L <= 0 or nseq <= 0 or nseq > args.batch or L > args.ctx:
+        return None
+    dev = groups.device
+    pc = make_prefill_ctx([L] * nseq, 16, dev, block_table=layer.ctx.block_table[:nseq].cpu(), reserve=0)
+    g = torch.Generator().manual_seed(args.seed + 1)
+    h = torch.randn(pc.T, layer.dims.hidden, generator=g).to(dev, torch.bfloat16)
+    for _ in range(3):
+        layer.prefill(h, pc)
+    barrier_sync()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.prefill_steps + 1)]
+    ev[0].record()
+    for i in range(args.prefill_steps):
+        layer.prefill(h, pc)
+        ev[i + 1].record()
+    torch.cuda.synchronize()
+    per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.prefill_steps)]
+    ms = max_over_ranks(statistics.median(per), groups)
+    barrier_sync()
+    fl = prefill_flops(layer.dims, [L] * nseq)
+    peak, src = bf16_peak()
+    tfs = fl["total"] / ms / 1e9
+    return {"workload": f"{nseq} fresh sequences x {L} tokens", "tokens": pc.T, "ms_per_step": ms,
+            "tokens_per_s": pc.T / ms * 1e3, "alg_tflop": {k: round(v / 1e12, 4) for k, v in fl.items()},
+            "achieved_tflops": tfs, "peak_tflops": peak, "frac": tfs / peak, "peak_source": f"{src} bf16_tflops",
+            "timing": "eager, median of device-timed steps, max over ranks"}
 
 
 def profiled_traffic(name: str) -> float | None:
@@ -318,6 +389,7 @@ def our_arm(args) -> None:
     for m in modes:
         keep[m][2].release()
     barrier_sync()
+    prefill = time_prefill(args, layer, groups)
 
     cpu = None
     if groups.rank == 0 and world == 1 and args.cpu_s > 0:
@@ -345,6 +417,7 @@ def our_arm(args) -> None:
             "roofline": roof,
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind", "sample")},
             "clocks": clocks,
+            "prefill": prefill,
         }
         print(json.dumps(line), flush=True)
     destroy()
