@@ -47,8 +47,8 @@ struct TcLayout {
   static constexpr int B_BYTES = BN * TBK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int PIPE = STAGES * STAGE_BYTES;
-  static constexpr int BARS = PIPE;                        // full[S], empty[S], done: 8 bytes each
-  static constexpr int TMEM_SLOT = BARS + 8 * (2 * STAGES + 1);
+  static constexpr int BARS = PIPE;                        // full[S], empty[S], done, recv: 8 bytes each
+  static constexpr int TMEM_SLOT = BARS + 8 * (2 * STAGES + 2);
   static constexpr int ABORT = TMEM_SLOT + 4;
   static constexpr int USED = ABORT + 4;
   static constexpr int DYN = USED + 1024;                  // slack to align the ring to 1024 bytes
@@ -57,7 +57,13 @@ struct TcLayout {
   static constexpr int TLD = TBM + 4;
   static_assert(TBM * SLD * 4 <= PIPE && BN * TLD * 4 <= PIPE, "the staged tile must fit in the ring");
   // split-K (swapped tiles) adds receive slots [ns][BN][rows_per], rows_per = round8(ceil(128 / ns)) <= 168 / ns
-  static constexpr bool SPLIT_FITS = (BN * TLD + BN * 168) * 4 <= PIPE;
+  // split-K over ns CTAs: each stages its tile as ns owner blocks [BN][rows_per] (OSTR floats apart, padded
+  // so the two owners a warp writes fall in different banks) and receives ns blocks [ns][BN][rows_per]
+  static __host__ __device__ constexpr int rows_per(int ns) { return ((TBM + ns - 1) / ns + 7) / 8 * 8; }
+  static __host__ __device__ constexpr int ostr(int ns) { return BN * rows_per(ns) + 16; }
+  static __host__ __device__ constexpr bool split_fits(int ns) {
+    return (ns * ostr(ns) + ns * BN * rows_per(ns)) * 4 <= PIPE;
+  }
 };
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) { return static_cast<uint32_t>(__cvta_generic_to_shared(p)); }
@@ -123,37 +129,33 @@ __device__ __forceinline__ void umma_commit(uint32_t bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
 
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
-  uint32_t r[16];
+// shared::cluster address of the same shared-memory location in cluster CTA `rank`
+__device__ __forceinline__ uint32_t mapa(uint32_t saddr, int rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;\n" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// bulk copy of `bytes` from this CTA's shared memory into a cluster CTA's shared memory, completing on that
+// CTA's mbarrier (copy engine; dst and bar are shared::cluster addresses)
+__device__ __forceinline__ void bulk_s2cluster(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+               ::"r"(dst), "r"(src), "r"(bytes), "r"(bar) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
+}
+
+// 16 consecutive TMEM columns of this thread's lane, without waiting (pair with tmem_wait)
+__device__ __forceinline__ void tmem_ld16_nw(uint32_t taddr, uint32_t* r) {
   asm volatile(
       "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
         "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
       : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]);
 }
+__device__ __forceinline__ void tmem_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory"); }
 
-// 16 accumulator columns of this thread's TMEM lane, scaled: alpha * acc0 + alpha2 * acc1 (an accumulator
-// this CTA never wrote contributes nothing). Warp-collective.
-template <int BN>
-__device__ __forceinline__ void load_scaled_bn(const TcParams& P, uint32_t taddr, bool has0, bool has1, float* v) {
-  float a[16];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) v[j] = 0.f;
-  if (has0) {
-    tmem_ld16(taddr, a);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = a[j] * P.alpha;
-  }
-  if (has1) {
-    tmem_ld16(taddr + BN, a);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) v[j] = fmaf(a[j], P.alpha2, v[j]);
-  }
-}
-#define load_scaled(P, taddr, h0, h1, v) load_scaled_bn<BN>(P, taddr, h0, h1, v)
+
 
 // Write 8 consecutive output elements (row r, columns c0..c0+7, the first n valid) = vals + addend.
 __device__ __forceinline__ void store8(const TcParams& P, int r, int c0, const float* vals, int n) {
@@ -245,6 +247,11 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   auto full_bar = [&](int s) { return sbase + L::BARS + 8 * s; };
   auto empty_bar = [&](int s) { return sbase + L::BARS + 8 * (STAGES + s); };
   const uint32_t done_bar = sbase + L::BARS + 8 * (2 * STAGES);
+  const uint32_t recv_bar = sbase + L::BARS + 8 * (2 * STAGES + 1);  // split-K partials received
+  // swapped tiles scale each tile row (an output column) by the column scale: a weight-side constant, read
+  // now so its latency hides under the main loop
+  const int trow = warp * 32 + lane;
+  const float cs_row = (TRANS && P.colscale && m0 + trow < P.a_rows) ? __ldg(P.colscale + m0 + trow) : 1.f;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT);
 
@@ -254,6 +261,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
       mbar_init(empty_bar(s), 1);
     }
     mbar_init(done_bar, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
@@ -267,6 +275,16 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+
+  // Output rows this CTA writes: split-K owners take rows_per tile rows each.
+  int ns = 1, me = 0, rp = TBM;
+  if constexpr (CLUSTER) {
+    cg::cluster_group cluster = cg::this_cluster();
+    ns = static_cast<int>(cluster.num_blocks());
+    me = static_cast<int>(cluster.block_rank());
+    rp = L::rows_per(ns);
+  }
+  const int own_row0 = me * rp, own_rows = max(0, min(rp, TBM - me * rp));
 
   // Roles. The other lanes of the producer and MMA warps park at __syncwarp: a lane spinning in
   // mbarrier.try_wait can suspend its whole warp and starve the one lane that issues the copies or MMAs.
@@ -302,6 +320,25 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
     }
     __syncwarp();
     if (lane != 0) pdl_wait();
+  } else if (warp >= 2) {
+    // idle during the main loop: pull the addend this CTA adds in its epilogue into L2 (32-byte sectors)
+    if (P.addend && own_rows > 0) {
+      if constexpr (TRANS) {  // output rows n0 + c, columns m0 + own_row0 ..
+        const int secs = (own_rows * 2 + 31) / 32;
+        for (int i = tid - 64; i < BN * secs; i += 64) {
+          const int c = i / secs, sc = i % secs;
+          if (n0 + c < P.b_rows && m0 + own_row0 + sc * 16 < P.a_rows)
+            prefetch_l2(P.addend + static_cast<int64_t>(n0 + c) * P.ldd + m0 + own_row0 + sc * 16);
+        }
+      } else {  // output rows m0 + i, columns n0 ..
+        constexpr int SECS = BN * 2 / 32;
+        for (int i = tid - 64; i < own_rows * SECS; i += 64) {
+          const int rr = i / SECS, sc = i % SECS;
+          if (m0 + own_row0 + rr < P.a_rows && n0 + sc * 16 < P.b_rows)
+            prefetch_l2(P.addend + static_cast<int64_t>(m0 + own_row0 + rr) * P.ldd + n0 + sc * 16);
+        }
+      }
+    }
   } else if (warp == 1) {
     if (lane == 0) {
       const uint32_t idesc = umma_idesc<BN>();
@@ -332,8 +369,9 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
   const bool have = ok && nkt > 0;
 
-  // teardown of the ring: drain this CTA's copies (an aborted pipeline can leave some in flight)
-  if (tid == 0) {
+  // teardown of the ring: an aborted pipeline can leave copies in flight, so drain them. Otherwise the MMA
+  // thread waited on every issued stage before the done barrier fired and nothing is left.
+  if (tid == 0 && *abort_flag) {
     for (int i = 0; i < issued; ++i) {
       const int use = i / STAGES;
       if (i + STAGES >= issued) mbar_wait(full_bar(i % STAGES), use & 1, abort_flag, P.err);
@@ -344,59 +382,71 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   // Stage the scaled fp32 tile in shared memory (tile row r = this thread's TMEM lane): alpha / alpha2 per K
   // segment and the column scale of the output column (a tile row when swapped, a tile column otherwise).
   float* stage = reinterpret_cast<float*>(smem);
-  {
-    const int r = warp * 32 + lane;
-    const float cs_row = (TRANS && P.colscale && m0 + r < P.a_rows) ? P.colscale[m0 + r] : 1.f;
+  const int ostr = CLUSTER ? L::ostr(ns) : 0;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      float v[16];
-      if (have) {
-        load_scaled(P, t_lane + c0, has0, has1, v);
-      } else {
+  for (int cb = 0; cb < BN; cb += 32) {
+    // 32 accumulator columns per batch: both tcgen05.ld of an accumulator issued before one wait
+    float v[32];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) v[j] = 0.f;
+    for (int j = 0; j < 32; ++j) v[j] = 0.f;
+    if (have) {
+      uint32_t t[32];
+      if (has0) {
+        tmem_ld16_nw(t_lane + cb, t);
+        tmem_ld16_nw(t_lane + cb + 16, t + 16);
+        tmem_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(t[j]) * P.alpha;
       }
-      if constexpr (TRANS) {
+      if (has1) {
+        tmem_ld16_nw(t_lane + BN + cb, t);
+        tmem_ld16_nw(t_lane + BN + cb + 16, t + 16);
+        tmem_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) stage[(c0 + j) * L::TLD + r] = v[j] * cs_row;  // consecutive lanes: consecutive words
-      } else {
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int c = n0 + c0 + j;
-          if (P.colscale) v[j] *= c < P.b_rows ? P.colscale[c] : 0.f;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; j += 4)
-          *reinterpret_cast<float4*>(stage + r * L::SLD + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        for (int j = 0; j < 32; ++j) v[j] = fmaf(__uint_as_float(t[j]), P.alpha2, v[j]);
       }
+    }
+    if constexpr (TRANS && CLUSTER) {
+      // owner-major blocks [owner][column][row within the owner's rows]
+      float* dst = stage + (trow / rp) * ostr + trow % rp + cb * rp;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) dst[j * rp] = v[j] * cs_row;
+    } else if constexpr (TRANS) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) stage[(cb + j) * L::TLD + trow] = v[j] * cs_row;  // consecutive lanes: consecutive words
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const int c = n0 + cb + j;
+        if (P.colscale) v[j] *= c < P.b_rows ? P.colscale[c] : 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(stage + trow * L::SLD + cb + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
     }
   }
 
   if constexpr (CLUSTER) {
-    static_assert(TRANS && L::SPLIT_FITS, "split-K runs swapped (weight-streaming) tiles whose receive slots fit");
-    // split-K reduce-scatter through distributed shared memory: tile rows are dealt to the cluster's CTAs in
-    // blocks of rows_per (a multiple of 8); each CTA copies every owner's rows of its staged tile (one
-    // contiguous run per column) into the owner's receive slot for it, then each owner sums its slots.
+    static_assert(TRANS, "split-K runs swapped (weight-streaming) tiles");
+    // split-K reduce-scatter through distributed shared memory: owner o sums tile rows [o*rp, o*rp + rp).
+    // Every CTA hands owner o its block with one bulk copy (copy engine) into the owner's receive slot for
+    // it, completing on the owner's receive barrier; each owner then sums its ns slots.
     cg::cluster_group cluster = cg::this_cluster();
-    const int ns = static_cast<int>(cluster.num_blocks());
-    const int me = static_cast<int>(cluster.block_rank());
-    const int rows_per = ((TBM + ns - 1) / ns + 7) / 8 * 8;
-    float* recv = stage + BN * L::TLD;  // [ns][BN][rows_per]
+    const uint32_t blk_bytes = BN * rp * 4;
+    const uint32_t recv_s = sbase + ns * ostr * 4;
+    float* recv = stage + ns * ostr;  // [ns][BN][rp]
+    if (tid == 0) mbar_expect_tx(recv_bar, ns * blk_bytes);
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // staged words -> the copy engine
     __syncthreads();
-    cluster.sync();  // every CTA has staged its tile and stopped using its ring
-    for (int o = 0; o < ns; ++o) {
-      const int r0 = o * rows_per, nr = max(0, min(rows_per, TBM - r0));  // a multiple of 8
-      const int v4 = nr / 4;
-      float* dst = cluster.map_shared_rank(recv, o) + me * BN * rows_per;
-      for (int k = tid; k < BN * v4; k += TTHREADS) {
-        const int c = k / v4, j = k % v4;
-        *reinterpret_cast<float4*>(dst + c * rows_per + j * 4) =
-            *reinterpret_cast<const float4*>(stage + c * L::TLD + r0 + j * 4);
-      }
+    cluster.sync();  // every CTA has staged its tile, stopped using its ring and armed its receive barrier
+    if (tid == 0) {
+      for (int o = 0; o < ns; ++o)
+        bulk_s2cluster(mapa(recv_s + me * blk_bytes, o), sbase + o * ostr * 4, blk_bytes, mapa(recv_bar, o));
+      asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
     }
-    cluster.sync();  // every push has landed
-    const int my_rows = max(0, min(rows_per, TBM - me * rows_per));
-    finish_tile<TRANS, BN>(P, recv, ns, BN * rows_per, rows_per, me * rows_per, my_rows, m0, n0);
+    const bool got = mbar_wait(recv_bar, 0, abort_flag, P.err);
+    if (got) finish_tile<TRANS, BN>(P, recv, ns, BN * rp, rp, own_row0, own_rows, m0, n0);
+    if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");  // our blocks have left
   } else {
     __syncthreads();
     finish_tile<TRANS, BN>(P, stage, 1, 0, TRANS ? L::TLD : L::SLD, 0, TBM, m0, n0);
@@ -510,8 +560,16 @@ extern "C" int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int6
     const int slots = (bn == 64 ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
     int split = 1;
     if (tiles * ntiles_b < slots) split = std::min(8, std::max(1, std::min(slots / (tiles * ntiles_b), k_tiles / 2)));
-    const int ktps = (k_tiles + split - 1) / split;
+    // the staged and received owner blocks must fit in the ring
+    auto fits = [&](int ns) {
+      return ns == 1 || (bn == 64 ? TcLayout<64, 4>::split_fits(ns) : TcLayout<128, 5>::split_fits(ns));
+    };
+    int ktps = (k_tiles + split - 1) / split;
     split = (k_tiles + ktps - 1) / ktps;
+    while (split > 1 && !fits(split)) {
+      ktps = (k_tiles + split - 2) / (split - 1);
+      split = (k_tiles + ktps - 1) / ktps;
+    }
     P.k_tiles_per_split = ktps;
     dim3 grid(ntiles_b, tiles, split);
     const bool cl = split > 1;
