@@ -54,3 +54,39 @@ def test_two_gpu_full_layer_with_mlp(tmp_path):
 @pytest.mark.parametrize("mode", ["split22", "split13", "tp4", "tp4_fused"])
 def test_four_gpu_layouts(mode, tmp_path):
     run_check(4, mode, tmp_path)
+
+
+@pytest.mark.skipif(ngpu() < 8, reason="needs 8 GPUs")
+@pytest.mark.parametrize("mode", ["split44", "tp4_fused"])
+def test_eight_gpu_layouts(mode, tmp_path):
+    run_check(8, mode, tmp_path)
+
+
+def run_prefill_check(world, mode):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()),
+           str(ROOT / "tests" / "_prefill_ranks.py"), "--mode", mode]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "600", *cmd], cwd=ROOT, env=env, capture_output=True, text=True)
+    out = r.stdout + r.stderr
+    m = re.search(r"\[prefill-check\].*pass=(True|False)", out)
+    assert r.returncode == 0 and m and m.group(1) == "True", out[-3000:]
+
+
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("mode", ["split11", "tp4", "tp4_fused"])
+def test_two_gpu_prefill(mode):
+    """Prefill (and the decode step after it) in each layout equals the single-rank prefill."""
+    run_prefill_check(2, mode)
+
+
+@pytest.mark.skipif(ngpu() < 4, reason="needs 4 GPUs")
+@pytest.mark.parametrize("mode", ["split22", "tp4_fused"])
+def test_four_gpu_prefill(mode):
+    run_prefill_check(4, mode)
+
+
+@pytest.mark.skipif(ngpu() < 8, reason="needs 8 GPUs")
+@pytest.mark.parametrize("mode", ["split44", "tp4_fused"])
+def test_eight_gpu_prefill(mode):
+    run_prefill_check(8, mode)
