@@ -95,6 +95,14 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   return true;
 }
 
+// Teardown drain after an abort: waits for copies already in flight (they land within microseconds) whatever
+// the abort flag says, with a short budget of its own.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity) && clock64() - t0 < WAIT_BUDGET_CYCLES / 16) {
+  }
+}
+
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n"
@@ -372,10 +380,7 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   // teardown of the ring: an aborted pipeline can leave copies in flight, so drain them. Otherwise the MMA
   // thread waited on every issued stage before the done barrier fired and nothing is left.
   if (tid == 0 && *abort_flag) {
-    for (int i = 0; i < issued; ++i) {
-      const int use = i / STAGES;
-      if (i + STAGES >= issued) mbar_wait(full_bar(i % STAGES), use & 1, abort_flag, P.err);
-    }
+    for (int i = max(0, issued - STAGES); i < issued; ++i) mbar_drain(full_bar(i % STAGES), (i / STAGES) & 1);
   }
   __syncthreads();  // the ring is free: every MMA finished (done barrier), every copy landed (drain)
 
@@ -460,6 +465,211 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   }
 }
 
+// ------------------------------------------------------------------------------------ persistent (prefill)
+// Large M: one CTA per SM walks output tiles (tile t, t + gridDim.x, ...; N fastest, so the CTAs in flight
+// share their A row panels and the whole weight stays in L2). Warp 0 lane 0 streams A/B boxes through the
+// STAGES-deep ring across tile boundaries; warp 1 lane 0 issues the MMAs of tile i into TMEM accumulator
+// buffer i % 2; warps 2-5 drain buffer (i-1) % 2 meanwhile (tcgen05.ld, scales, addend, 32-byte row stores)
+// and hand it back through the acc_empty barrier. ACC = accumulators per tile (2 = two K segments).
+constexpr int PTHREADS = 192;
+
+template <int BN, int STAGES, int ACC>
+struct PLayout {
+  static constexpr int A_BYTES = TBM * TBK * 2;
+  static constexpr int B_BYTES = BN * TBK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int PIPE = STAGES * STAGE_BYTES;
+  static constexpr int BARS = PIPE;  // full[S], empty[S], acc_full[2], acc_empty[2]
+  static constexpr int TMEM_SLOT = BARS + 8 * (2 * STAGES + 4);
+  static constexpr int ABORT = TMEM_SLOT + 4;
+  static constexpr int USED = ABORT + 4;
+  static constexpr int DYN = USED + 1024;
+  static constexpr uint32_t TMEM_COLS = 2 * ACC * BN;
+  static_assert(TMEM_COLS <= 512, "two accumulator buffers must fit in TMEM");
+};
+
+template <int BN, int STAGES, int ACC>
+__global__ void __launch_bounds__(PTHREADS, 1) gemm_tc_persistent(const __grid_constant__ CUtensorMap tmA,
+                                                                 const __grid_constant__ CUtensorMap tmB,
+                                                                 const TcParams P, int tiles_n, int ntiles) {
+  using L = PLayout<BN, STAGES, ACC>;
+  pdl_trigger();
+  extern __shared__ uint8_t dsmem[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_addr(smem);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int k_tiles = (P.K + TBK - 1) / TBK;
+  auto full_bar = [&](int s) { return sbase + L::BARS + 8 * s; };
+  auto empty_bar = [&](int s) { return sbase + L::BARS + 8 * (STAGES + s); };
+  auto accf_bar = [&](int b) { return sbase + L::BARS + 8 * (2 * STAGES + b); };
+  auto acce_bar = [&](int b) { return sbase + L::BARS + 8 * (2 * STAGES + 2 + b); };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::ABORT);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::TMEM_SLOT);
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accf_bar(b), 1);
+      mbar_init(acce_bar(b), 4);  // one elected lane per epilogue warp
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tmem_slot)), "r"(L::TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int issued = 0;  // TMA stages issued by the producer (drained at teardown after an abort)
+  if (warp == 0) {
+    if (lane == 0) {
+      // B (weights) never depends on the previous kernel: the first ring's worth of B boxes is requested
+      // before waiting for it
+      const int first = blockIdx.x;
+      const int pre = first < ntiles ? min(k_tiles, STAGES) : 0;
+      if (pre > 0) {
+        const int n0 = (first % tiles_n) * BN;
+        for (int i = 0; i < pre; ++i) {
+          mbar_expect_tx(full_bar(i), L::STAGE_BYTES);
+          tma_load_2d(sbase + i * L::STAGE_BYTES + L::A_BYTES, &tmB, full_bar(i), i * TBK, n0);
+        }
+      }
+      pdl_wait();
+      int kc = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x) {
+        const int m0 = (t / tiles_n) * TBM, n0 = (t % tiles_n) * BN;
+        for (int kt = 0; kt < k_tiles; ++kt, ++kc) {
+          const int s = kc % STAGES;
+          const uint32_t a_s = sbase + s * L::STAGE_BYTES, b_s = a_s + L::A_BYTES;
+          if (kc < pre) {  // B already requested
+            tma_load_2d(a_s, &tmA, full_bar(s), kt * TBK, m0);
+            ++issued;
+            continue;
+          }
+          if (kc >= STAGES && !mbar_wait(empty_bar(s), ((kc / STAGES) - 1) & 1, abort_flag, P.err)) break;
+          mbar_expect_tx(full_bar(s), L::STAGE_BYTES);
+          tma_load_2d(a_s, &tmA, full_bar(s), kt * TBK, m0);
+          tma_load_2d(b_s, &tmB, full_bar(s), kt * TBK, n0);
+          ++issued;
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    pdl_wait();
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc<BN>();
+      int kc = 0, tc = 0;
+      for (int t = blockIdx.x; t < ntiles && !*abort_flag; t += gridDim.x, ++tc) {
+        const int buf = tc & 1;
+        if (tc >= 2 && !mbar_wait(acce_bar(buf), ((tc >> 1) - 1) & 1, abort_flag, P.err)) break;
+        tc_fence_after();
+        bool started0 = false, started1 = false;
+        bool ok = true;
+        for (int kt = 0; kt < k_tiles; ++kt, ++kc) {
+          const int s = kc % STAGES;
+          if (!mbar_wait(full_bar(s), (kc / STAGES) & 1, abort_flag, P.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_s = sbase + s * L::STAGE_BYTES, b_s = a_s + L::A_BYTES;
+          const bool seg1 = ACC == 2 && kt >= P.k_seg_tile;
+          const uint32_t d = tmem + (buf * ACC + (seg1 ? 1 : 0)) * BN;
+          const bool started = seg1 ? started1 : started0;
+#pragma unroll
+          for (int kk = 0; kk < TBK / 16; ++kk)
+            umma_f16(d, umma_desc(a_s + kk * 32), umma_desc(b_s + kk * 32), idesc, started || kk != 0);
+          if (seg1) started1 = true; else started0 = true;
+          umma_commit(empty_bar(s));
+        }
+        if (!ok) break;
+        umma_commit(accf_bar(buf));  // arrives once every MMA of this tile has completed
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps 2-5: warp w reads TMEM lanes 32 (w % 4) .. +31 = tile rows
+    pdl_wait();
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const bool has0 = ACC == 1 || P.k_seg_tile > 0, has1 = ACC == 2 && P.k_seg_tile < k_tiles;
+    int tc = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x, ++tc) {
+      const int buf = tc & 1;
+      bool ok = mbar_wait(accf_bar(buf), (tc >> 1) & 1, abort_flag, P.err);
+      ok = __all_sync(0xffffffffu, ok && !*abort_flag);
+      if (!ok) break;
+      tc_fence_after();
+      const int m0 = (t / tiles_n) * TBM, n0 = (t % tiles_n) * BN;
+      const int row = m0 + r;
+      const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16) + buf * ACC * BN;
+#pragma unroll 1
+      for (int cb = 0; cb < BN; cb += 16) {
+        uint32_t a0[16], a1[16];
+        if (has0) tmem_ld16_nw(t_lane + cb, a0);
+        if (has1) tmem_ld16_nw(t_lane + BN + cb, a1);
+        tmem_wait();
+        if (row >= P.a_rows) continue;
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float x = has0 ? __uint_as_float(a0[j]) * P.alpha : 0.f;
+          if (has1) x = fmaf(__uint_as_float(a1[j]), P.alpha2, x);
+          v[j] = x;
+        }
+        const int c0 = n0 + cb;
+        if (P.colscale) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] *= c0 + j < P.b_rows ? __ldg(P.colscale + c0 + j) : 0.f;
+        }
+        bf16* dst = P.out + static_cast<int64_t>(row) * P.ldo + c0;
+        const bf16* add = P.addend ? P.addend + static_cast<int64_t>(row) * P.ldd + c0 : nullptr;
+        if (c0 + 16 <= P.b_rows && aligned16(dst) && (!add || aligned16(add))) {
+          if (add) {
+            const uint4 u0 = reinterpret_cast<const uint4*>(add)[0], u1 = reinterpret_cast<const uint4*>(add)[1];
+            const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float2 f = unpack_bf16x2(w[j]);
+              v[2 * j] += f.x;
+              v[2 * j + 1] += f.y;
+            }
+          }
+          reinterpret_cast<uint4*>(dst)[0] = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                                        pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+          reinterpret_cast<uint4*>(dst)[1] = make_uint4(pack_bf16x2(v[8], v[9]), pack_bf16x2(v[10], v[11]),
+                                                        pack_bf16x2(v[12], v[13]), pack_bf16x2(v[14], v[15]));
+        } else {  // ragged right edge or unaligned rows
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            if (c0 + j < P.b_rows) dst[j] = f2bf(v[j] + (add ? bf2f(add[j]) : 0.f));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(acce_bar(buf)) : "memory");
+    }
+  }
+
+  // teardown: after an abort the producer's copies may still be in flight
+  if (tid == 0 && *abort_flag) {
+    for (int i = max(0, issued - STAGES); i < issued; ++i) mbar_drain(full_bar(i % STAGES), (i / STAGES) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(L::TMEM_COLS));
+  }
+}
+
 // ---------------------------------------------------------------------------------------------- host side
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 std::mutex g_encode_mu;
@@ -509,6 +719,25 @@ int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& P, d
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = split;
   cudaError_t e = mmp::launch_kind(1, kern, grid, dim3(TTHREADS), L::DYN, s, attr, CLUSTER ? 1 : 0, ma, mb, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "gemm_tc: launch failed: %s", cudaGetErrorString(e));
+  return mmp_check_launch("mmp_gemm_bf16_tc");
+}
+
+template <int BN, int STAGES, int ACC>
+int launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& P, int tiles_n, int ntiles,
+                      cudaStream_t s) {
+  using L = PLayout<BN, STAGES, ACC>;
+  auto kern = gemm_tc_persistent<BN, STAGES, ACC>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::DYN);
+    if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "gemm_tc: smem attribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  const int grid = std::min(ntiles, g_tc_sms);
+  cudaError_t e = mmp::launch_kind(1, kern, dim3(grid), dim3(PTHREADS), L::DYN, s, nullptr, 0, ma, mb, P, tiles_n, ntiles);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "gemm_tc: launch failed: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_gemm_bf16_tc");
 }
@@ -576,11 +805,16 @@ extern "C" int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int6
     if (bn == 64) return cl ? launch_tc<64, 4, true, true>(ma, mb, P, grid, split, s) : launch_tc<64, 4, true, false>(ma, mb, P, grid, 1, s);
     return cl ? launch_tc<128, 5, true, true>(ma, mb, P, grid, split, s) : launch_tc<128, 5, true, false>(ma, mb, P, grid, 1, s);
   }
-  // large M (prefill): A = activations, B = weight rows, 128 x 256 output tiles
+  // large M (prefill): A = activations, B = weight rows; a persistent CTA per SM over 128 x 256 output tiles
+  // (128 x 128 when two K segments need two accumulators per tile)
   P.a_rows = M;
   P.b_rows = N;
-  if ((rc = make_map(&ma, a, M, K, lda, TBM)) || (rc = make_map(&mb, w, N, K, ldw, 256))) return rc;
-  dim3 grid((N + 255) / 256, (M + TBM - 1) / TBM, 1);
-  if (grid.y > 65535) return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_tc: M=%d too large", M);
-  return launch_tc<256, 4, false, false>(ma, mb, P, grid, 1, s);
+  const bool two = k_seg_tile < k_tiles;
+  const int bn = two ? 128 : 256;
+  if ((rc = make_map(&ma, a, M, K, lda, TBM)) || (rc = make_map(&mb, w, N, K, ldw, bn))) return rc;
+  const int tiles_n = (N + bn - 1) / bn;
+  const long long ntiles = static_cast<long long>(tiles_n) * ((M + TBM - 1) / TBM);
+  if (ntiles > (1LL << 30)) return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_tc: M=%d too large", M);
+  if (two) return launch_persistent<128, 6, 2>(ma, mb, P, tiles_n, static_cast<int>(ntiles), s);
+  return launch_persistent<256, 4, 1>(ma, mb, P, tiles_n, static_cast<int>(ntiles), s);
 }

@@ -108,6 +108,22 @@ def make_prefill_ctx(lens: list[int], kv_block: int, device: torch.device, start
     )
 
 
+def advance_decode_ctx(ctx: DecodeCtx, n: int = 1) -> None:
+    """Move every sequence of `ctx` n tokens on, in place (positions, keys used, cache slots): the context of
+    the next decode step of the same batch. The block table must already hold the new positions."""
+    table = ctx.block_table
+    pos = ctx.positions + n
+    blk = pos // ctx.kv_block
+    if int(blk.max()) >= table.shape[1]:
+        raise ValueError("advance_decode_ctx: block table too short for the next position")
+    ctx.positions.copy_(pos)
+    ctx.seqused_k.add_(n)
+    rows = torch.arange(ctx.B, device=table.device)
+    ctx.slot_mapping.copy_(table[rows, blk].to(torch.int64) * ctx.kv_block + pos % ctx.kv_block)
+    ctx.c += n
+    ctx.max_k += n
+
+
 def decode_ctx_after(pc: PrefillCtx) -> DecodeCtx:
     """The decode step that follows a prefill: one new token per sequence at position starts[i] + lens[i],
     same block table and state lines."""

@@ -273,7 +273,7 @@ def test_gemm_strided_operands():
 
 @pytest.mark.parametrize("M,N,K_", [(64, 6680, 3072), (64, 2048, 3072), (64, 3072, 1536), (2, 100, 64), (1, 8, 8),
                                     (128, 5120, 8192), (100, 640, 520), (256, 512, 1024), (300, 200, 136),
-                                    (2048, 6680, 3072), (1000, 1000, 1000)])
+                                    (2048, 6680, 3072), (1000, 1000, 1000), (40000, 264, 72), (777, 4104, 8)])
 def test_gemm_tc_matches_fp32(M, N, K_):
     g = torch.Generator().manual_seed(M * 3 + N + K_)
     x = torch.randn(M, K_, generator=g).to(BF)
@@ -287,7 +287,8 @@ def test_gemm_tc_matches_fp32(M, N, K_):
     close(npf(out2), (x.float() @ w.float().T).numpy())
 
 
-@pytest.mark.parametrize("M,N,K_,kseg", [(64, 3072, 4608, 1536), (2, 300, 256, 64), (128, 1024, 640, 512), (64, 3072, 4608, 4608)])
+@pytest.mark.parametrize("M,N,K_,kseg", [(64, 3072, 4608, 1536), (2, 300, 256, 64), (128, 1024, 640, 512), (64, 3072, 4608, 4608),
+                                         (1000, 700, 640, 256), (2048, 3072, 4608, 1536), (300, 136, 128, 64)])
 def test_gemm_two_segments(M, N, K_, kseg):
     """out = a1 * x[:, :kseg] w[:, :kseg]^T + a2 * x[:, kseg:] w[:, kseg:]^T + addend (fused o_proj + out_proj)."""
     g = torch.Generator().manual_seed(M + N + K_ + kseg)

@@ -43,3 +43,17 @@ def test_rejects_short_tables_and_bad_lengths():
         make_prefill_ctx([20], 16, CPU, block_table=torch.zeros(1, 1, dtype=torch.int32))
     with pytest.raises(ValueError):
         make_prefill_ctx([-1], 16, CPU)
+
+
+def test_advance_decode_ctx():
+    from multi_modal_parallelism_b200.state import advance_decode_ctx
+
+    pc = make_prefill_ctx([15, 3], 16, CPU, reserve=2)
+    d = decode_ctx_after(pc)
+    assert d.positions.tolist() == [15, 3]
+    advance_decode_ctx(d)
+    assert d.positions.tolist() == [16, 4] and d.seqused_k.tolist() == [17, 5] and d.max_k == 17
+    assert d.slot_mapping.tolist() == [int(pc.block_table[0, 1]) * 16, int(pc.block_table[1, 0]) * 16 + 4]
+    advance_decode_ctx(d)
+    with pytest.raises(ValueError):
+        advance_decode_ctx(d, 20)
