@@ -115,12 +115,15 @@ class SsmBranch:
     name = "ssm"
 
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
-                 device: torch.device, norm_group, zxbcdt: torch.Tensor | None = None, yn: torch.Tensor | None = None):
-        """zxbcdt / yn: optional [B, in rows] and [B, nhr*p] views into buffers shared with the other branch."""
+                 device: torch.device, norm_group, zxbcdt: torch.Tensor | None = None, yn: torch.Tensor | None = None,
+                 norm_w: torch.Tensor | None = None):
+        """zxbcdt / yn: optional [B, in rows] and [B, nhr*p] views into buffers shared with the other branch;
+        norm_w: the gated norm's weight when it carries an extra output scale (default w.norm_w)."""
         s = plan.ssm
         assert s is not None
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
         self.norm_group = norm_group
+        self.norm_w = w.norm_w if norm_w is None else norm_w
         z, x, b, c, dt = s.local_in_rows
         self.sizes = (z, x + b + c, dt)
         self.xbc_sizes = (x, b, c)
@@ -184,7 +187,7 @@ class SsmBranch:
 
     def _norm(self, t: OpTimer) -> None:
         t.begin("ssm.norm")
-        K.gated_rmsnorm(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.w.norm_w, self.dims.rms_eps,
+        K.gated_rmsnorm(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.norm_w, self.dims.rms_eps,
                         self.norm_group, self.group_size, out=self.yn, sumsq=self.sumsq)
         t.end("ssm.norm")
 
@@ -266,6 +269,7 @@ class ParallelHybridLayer:
         self.fused = (plan.attn is not None and plan.ssm is not None and w.w_in_cat is not None
                       and self.mode in ("tp1", "tp4_fused"))
         qkv = zx = ao = yn = None
+        self.out_ratio = None
         B = ctx.rows
         if self.fused:
             nqkv, nin = w.wqkv.shape[0], w.win.shape[0]
@@ -275,11 +279,17 @@ class ParallelHybridLayer:
             self.mid_buf = torch.empty(B, qc + yc, device=device, dtype=BF16)
             ao, yn = self.mid_buf[:, :qc], self.mid_buf[:, qc:]
             self.k_seg = qc
+            # attn_out * (o Wo^T) + ssm_out * (yn Wout^T) = attn_out * ([o | r yn] [Wo | Wout]^T), r = ssm_out /
+            # attn_out carried by the gated norm's weight: the output projection is one single-accumulator GEMM
+            self.out_ratio = dims.ssm_out / dims.attn_out if dims.attn_out != 0 else None
         self.attn = AttentionBranch(plan, w, dims, st, ctx, device, qkv, ao) if plan.attn is not None else None
         norm_group = None
         if plan.ssm is not None and len(plan.ssm.norm_ranks) > 1:
             norm_group = groups.group_for_ranks(plan.ssm.norm_ranks) if collectives else _LocalOnly(len(plan.ssm.norm_ranks))
-        self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn) if plan.ssm is not None else None
+        norm_w = None
+        if self.fused and self.out_ratio is not None:
+            norm_w = (w.norm_w.float() * self.out_ratio).to(BF16)
+        self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w) if plan.ssm is not None else None
         self.has_mlp = dims.intermediate > 0
         self.mlp = SwingMLP(plan, w, dims, ctx.rows, device) if self.has_mlp else None
         B, H = ctx.rows, dims.hidden
@@ -363,12 +373,11 @@ class ParallelHybridLayer:
                 self.attn.core(t)
                 self.ssm.core(t)
             t.begin("mixer.outproj")
+            seg = {} if self.out_ratio is not None else {"k_seg": self.k_seg, "alpha2": dims.ssm_out}
             if mode == "tp1":
-                K.gemm(self.mid_buf, self.w.w_out_cat, out=self.h1, alpha=dims.attn_out, k_seg=self.k_seg,
-                       alpha2=dims.ssm_out, addend=h)
+                K.gemm(self.mid_buf, self.w.w_out_cat, out=self.h1, alpha=dims.attn_out, addend=h, **seg)
             else:
-                K.gemm(self.mid_buf, self.w.w_out_cat, out=self.mix, alpha=dims.attn_out, k_seg=self.k_seg,
-                       alpha2=dims.ssm_out)
+                K.gemm(self.mid_buf, self.w.w_out_cat, out=self.mix, alpha=dims.attn_out, **seg)
             t.end("mixer.outproj")
             if mode == "tp4_fused":
                 self._ar(self.mix, "ar.mixer", t)
