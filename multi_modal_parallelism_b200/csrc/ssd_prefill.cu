@@ -369,14 +369,24 @@ int launch_ssd(const SsdParams& P, int nseq, cudaStream_t s) {
 
 using namespace mmp;
 
+namespace mmp {
+int ssd_prefill_tc(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h, const float* A,
+                   const float* D, const float* dt_bias, const void* B, int64_t B_t, int64_t B_g, const void* C,
+                   int64_t C_t, int64_t C_g, void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
+                   const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init, void* out,
+                   int64_t o_t, int64_t o_h, int nseq, int ntok, int nh, int p, int N, int ngroups, int lines, int* err,
+                   cudaStream_t stream);
+}  // namespace mmp
+
 extern "C" int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h,
                                const float* A, const float* D, const float* dt_bias,
                                const void* B, int64_t B_t, int64_t B_g, const void* C, int64_t C_t, int64_t C_g,
                                void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
                                const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init,
                                void* out, int64_t o_t, int64_t o_h,
-                               int nseq, int nh, int p, int N, int ngroups, int lines, int* err, void* stream) {
-  if (nseq == 0) return MMP_OK;
+                               int nseq, int ntok, int nh, int p, int N, int ngroups, int lines, int* err,
+                               void* stream) {
+  if (nseq == 0 || ntok == 0) return MMP_OK;
   if (!x || !dt || !A || !B || !C || !state || !cu_seqlens || !state_idx || !out)
     return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: null pointer");
   if (nseq < 0 || nseq > 65535 || nh <= 0 || nh > 65535 || p <= 0 || p % 8 || ngroups <= 0 || nh % ngroups || lines <= 0)
@@ -391,6 +401,12 @@ extern "C" int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const vo
               state, s_line, s_head, s_p, cu_seqlens, state_idx, has_init,
               static_cast<bf16*>(out), o_t, o_h, nh, p, ngroups, lines, err};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (ntok < 0) return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: ntok %d", ntok);
+  // head dim 128 with d_state 128 / 256: the tcgen05 kernel (ssd_prefill_tc.cu)
+  const int tc = ssd_prefill_tc(x, x_t, x_h, dt, dt_t, dt_h, A, D, dt_bias, B, B_t, B_g, C, C_t, C_g, state,
+                                state_dtype, s_line, s_head, s_p, cu_seqlens, state_idx, has_init, out, o_t, o_h,
+                                nseq, ntok, nh, p, N, ngroups, lines, err, s);
+  if (tc != MMP_ERR_UNSUPPORTED) return tc;
   const bool f32 = state_dtype == MMP_F32;
   switch (N) {
     case 64: return f32 ? launch_ssd<float, 64>(P, nseq, s) : launch_ssd<bf16, 64>(P, nseq, s);

@@ -441,7 +441,7 @@ def ssd_prefill(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Ten
               _p(dt_bias), _p(B), B.stride(0), B.stride(1), _p(C), C.stride(0), C.stride(1), _p(state),
               MMP_F32 if state.dtype == torch.float32 else MMP_BF16, state.stride(0), state.stride(1), state.stride(2),
               _p(cu_seqlens), _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1),
-              nseq, nh, p, N, B.shape[1], lines, _p(error_word(x.device)), _stream(x))
+              nseq, T, nh, p, N, B.shape[1], lines, _p(error_word(x.device)), _stream(x))
     return out
 
 
