@@ -10,10 +10,11 @@
 //   * G = C B^T (tcgen05.mma M=64, N=64, K=N) into TMEM; meanwhile the threads write the bf16 copy of S to
 //     shared memory and exp(cum_last) S back to TMEM;
 //   * the threads turn G into M[t][s] = G exp(cum_t - cum_s) dt_s (s <= t), plus D on the diagonal (so the
-//     intra-chunk product carries the D x skip term), scale C rows by exp(cum_t) and B rows by
-//     w_s = exp(cum_last - cum_s) dt_s in place;
-//   * y^T = x^T M^T + S C'^T (M=128 over p, N=64 over t) and S += x^T (w B) (M=128, N=N); x and B are read as
-//     MN-major operands straight from their TMA boxes, M, C' and the bf16 S as K-major ones;
+//     intra-chunk product carries the D x skip term), and scale B rows by w_s = exp(cum_last - cum_s) dt_s
+//     in place;
+//   * y^T = x^T M^T and ys^T = S C^T into two TMEM accumulators (M=128 over p, N=64 over t), combined as
+//     y = y + exp(cum_t) ys in the epilogue; S += x^T (w B) (M=128, N=N); x and B are read as MN-major
+//     operands straight from their TMA boxes, M, C and the bf16 S as K-major ones;
 //   * once the MMAs are done the next chunk's loads go out, and the y tile is staged and written (16-byte
 //     stores) under them.
 // Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out of budget flags the error word, leaves
@@ -50,15 +51,15 @@ struct TcSsdSmem {
   static constexpr int SB_OFF = M_OFF + 8192;         // bf16 S: KB blocks [128 p x 128 B]
   static constexpr int YLD = SP * 2 + 16;             // y tile row bytes (padded)
   static constexpr int Y_OFF = SB_OFF + KB * 16384;   // y tile [64 t][128 p] bf16
-  static constexpr int CUM_OFF = Y_OFF + SQ * YLD;    // cum[64], dt[64], w[64] fp32
-  static constexpr int BAR_OFF = CUM_OFF + 3 * SQ * 4 + 16;
+  static constexpr int CUM_OFF = Y_OFF + SQ * YLD;    // cum[64], dt[64], w[64], exp(cum)[64] fp32
+  static constexpr int BAR_OFF = CUM_OFF + 4 * SQ * 4 + 16;
   static constexpr int USED = BAR_OFF + 8 * 4 + 16;
   static constexpr int DYN = USED + 1024;
   static constexpr uint32_t LOAD_BYTES = 2 * KB * 8192 + 2 * 8192;
 };
 
 // TMEM columns
-constexpr uint32_t T_S = 0, T_Y = 256, T_G = 320;
+constexpr uint32_t T_S = 0, T_Y = 256, T_G = 320, T_YS = 384;
 
 // byte offset of 16-byte chunk c of row r in a 128-byte-swizzled block of 128-byte rows
 __device__ __forceinline__ uint32_t sw(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -76,6 +77,19 @@ __device__ __forceinline__ uint64_t umma_desc_mn(uint32_t saddr, uint32_t mn_blo
   return d;
 }
 constexpr uint32_t IDESC_A_MN = 1u << 15, IDESC_B_MN = 1u << 16;
+
+// bf16 copy of 64 state columns (this thread's row p) into the K-major operand blocks of the state term
+template <int N>
+__device__ __forceinline__ void store_sb(uint8_t* smem, int p, int c0n, const uint32_t* r) {
+  uint8_t* rowp = smem + TcSsdSmem<N>::SB_OFF + (c0n >> 6) * 16384;
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<uint4*>(rowp + sw(p, c)) = make_uint4(
+        pack_bf16x2(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1])),
+        pack_bf16x2(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])),
+        pack_bf16x2(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])),
+        pack_bf16x2(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])));
+}
 
 template <typename ST, int N>
 __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_constant__ CUtensorMap mapX,
@@ -102,7 +116,8 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   float* sCum = reinterpret_cast<float*>(smem + L::CUM_OFF);
   float* sDt = sCum + SQ;
   float* sW = sDt + SQ;
-  float* sDec = sW + SQ;  // exp(cum_last)
+  float* sE = sW + SQ;    // exp(cum_t)
+  float* sDec = sE + SQ;  // exp(cum_last)
   const uint32_t bar_load = sb + L::BAR_OFF, bar_g = bar_load + 8, bar_y = bar_load + 16, bar_s = bar_load + 24;
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 32);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 36);
@@ -131,16 +146,18 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   const int p = q * 32 + lane;
   const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
 
-  // ---- initial state into TMEM (or zeros)
+  // ---- initial state into TMEM (or zeros) and its bf16 copy for the first chunk's state term
   {
     const bool init = P.has_init && P.has_init[seq];
 #pragma unroll 1
-    for (int c0 = half * (N / 2); c0 < (half + 1) * (N / 2); c0 += 16) {
-      uint32_t r[16];
+    for (int c0n = half * (N / 2); c0n < (half + 1) * (N / 2); c0n += 64) {
+      uint32_t r[64];
 #pragma unroll
-      for (int j = 0; j < 16; ++j)
-        r[j] = __float_as_uint(init ? static_cast<float>(gstate[p * P.s_p + c0 + j]) : 0.f);
-      tmem_st16(t_lane + T_S + c0, r);
+      for (int j = 0; j < 64; ++j)
+        r[j] = __float_as_uint(init ? static_cast<float>(gstate[p * P.s_p + c0n + j]) : 0.f);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tmem_st16(t_lane + T_S + c0n + 16 * k, r + 16 * k);
+      store_sb<N>(smem, p, c0n, r);
     }
     tmem_wait_st();
   }
@@ -196,6 +213,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
         sDt[r] = d[j];
         sCum[r] = cum;
         sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
+        sE[r] = __expf(cum);
       }
       if (lane == 0) *sDec = __expf(cum_last);
     }
@@ -216,7 +234,8 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       umma_commit(bar_g);
     }
 
-    // ---- meanwhile: S -> bf16 copy (operand of the state term); exp(cum_last) S back into TMEM
+    // ---- meanwhile: the state decays in TMEM, S = exp(cum_last) S (its bf16 copy, made at the end of the
+    // previous chunk, keeps the incoming state for the state term)
     {
       const float dec = *sDec;
 #pragma unroll 1
@@ -225,14 +244,6 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
 #pragma unroll
         for (int k = 0; k < 4; ++k) tmem_ld16_nw(t_lane + T_S + c0n + 16 * k, r + 16 * k);
         tmem_wait();
-        uint8_t* rowp = smem + L::SB_OFF + (c0n >> 6) * 16384;
-#pragma unroll
-        for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(rowp + sw(p, c)) = make_uint4(
-              pack_bf16x2(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1])),
-              pack_bf16x2(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])),
-              pack_bf16x2(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])),
-              pack_bf16x2(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])));
 #pragma unroll
         for (int j = 0; j < 64; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * dec);
 #pragma unroll
@@ -241,7 +252,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       tmem_wait_st();
     }
 
-    // ---- G -> M (masked, decayed, dt-weighted, D on the diagonal); C rows *= exp(cum_t); B rows *= w_s
+    // ---- G -> M (masked, decayed, dt-weighted, D on the diagonal); B rows *= w_s
     ok = mbar_wait(bar_g, par, abort_flag, P.err);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
@@ -272,32 +283,12 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
         }
       }
     }
-    __syncthreads();  // the G MMAs are done with C and B (every thread passed bar_g)
-    if (ok) {
-      // row t = tid / 4 of C and of B, a quarter of its 16-byte chunks each
-      const int t = tid >> 2, part = tid & 3;
-      const float ec = __expf(sCum[t]), wb = sW[t];
-#pragma unroll
-      for (int i = 0; i < L::KB * 2; ++i) {
-        const int cidx = part * (L::KB * 2) + i;  // chunk along n: block cidx / 8, chunk cidx % 8
-        const uint32_t off = (cidx >> 3) * 8192 + sw(t, cidx & 7);
-        uint4* pc = reinterpret_cast<uint4*>(smem + L::C_OFF + off);
-        uint4* pb = reinterpret_cast<uint4*>(smem + L::B_OFF + off);
-        uint4 u = *pc, v = *pb;
-        float2 a0 = unpack_bf16x2(u.x), a1 = unpack_bf16x2(u.y), a2 = unpack_bf16x2(u.z), a3 = unpack_bf16x2(u.w);
-        *pc = make_uint4(pack_bf16x2(a0.x * ec, a0.y * ec), pack_bf16x2(a1.x * ec, a1.y * ec),
-                         pack_bf16x2(a2.x * ec, a2.y * ec), pack_bf16x2(a3.x * ec, a3.y * ec));
-        a0 = unpack_bf16x2(v.x), a1 = unpack_bf16x2(v.y), a2 = unpack_bf16x2(v.z), a3 = unpack_bf16x2(v.w);
-        *pb = make_uint4(pack_bf16x2(a0.x * wb, a0.y * wb), pack_bf16x2(a1.x * wb, a1.y * wb),
-                         pack_bf16x2(a2.x * wb, a2.y * wb), pack_bf16x2(a3.x * wb, a3.y * wb));
-      }
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // M -> tensor core reads
     tc_fence_before();
-    __syncthreads();
+    __syncthreads();  // M built; the G MMAs are done with B (every thread passed bar_g)
     if (*abort_flag) break;
 
-    // ---- y^T = x^T M^T + S C'^T ; S += x^T (w B)
+    // ---- y^T = x^T M^T ; ys^T = S C^T (B is not an operand: it is weighted meanwhile)
     if (tid == 0) {
       tc_fence_after();
       constexpr uint32_t idy_x = umma_idesc_mn(128, 64) | IDESC_A_MN;
@@ -310,9 +301,32 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       for (int kb = 0; kb < L::KB; ++kb)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem + T_Y, umma_desc(sb + L::SB_OFF + kb * 16384 + kk * 32),
-                   umma_desc(sb + L::C_OFF + kb * 8192 + kk * 32), idy, 1);
+          umma_f16(tmem + T_YS, umma_desc(sb + L::SB_OFF + kb * 16384 + kk * 32),
+                   umma_desc(sb + L::C_OFF + kb * 8192 + kk * 32), idy, (kb | kk) != 0);
       umma_commit(bar_y);
+    }
+    if (ok) {
+      // row t = tid / 4 of B, a quarter of its 16-byte chunks each
+      const int t = tid >> 2, part = tid & 3;
+      const float wb = sW[t];
+#pragma unroll
+      for (int i = 0; i < L::KB * 2; ++i) {
+        const int cidx = part * (L::KB * 2) + i;  // chunk along n: block cidx / 8, chunk cidx % 8
+        uint4* pb = reinterpret_cast<uint4*>(smem + L::B_OFF + (cidx >> 3) * 8192 + sw(t, cidx & 7));
+        const uint4 v = *pb;
+        const float2 a0 = unpack_bf16x2(v.x), a1 = unpack_bf16x2(v.y), a2 = unpack_bf16x2(v.z), a3 = unpack_bf16x2(v.w);
+        *pb = make_uint4(pack_bf16x2(a0.x * wb, a0.y * wb), pack_bf16x2(a1.x * wb, a1.y * wb),
+                         pack_bf16x2(a2.x * wb, a2.y * wb), pack_bf16x2(a3.x * wb, a3.y * wb));
+      }
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
+    tc_fence_before();
+    __syncthreads();
+    if (*abort_flag) break;
+
+    // ---- S += x^T (w B)
+    if (tid == 0) {
+      tc_fence_after();
       constexpr uint32_t ids = umma_idesc_mn(128, N) | IDESC_A_MN | IDESC_B_MN;
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
@@ -325,21 +339,35 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
     // staged and stored under them
     ok = mbar_wait(bar_y, par, abort_flag, P.err);
     ok = __all_sync(0xffffffffu, ok);
-    uint32_t yv[32];
+    float yv[32];
     if (ok) {
       tc_fence_after();
-      tmem_ld16_nw(t_lane + T_Y + half * 32, yv);
-      tmem_ld16_nw(t_lane + T_Y + half * 32 + 16, yv + 16);
+      uint32_t yi[32], ys[32];
+      tmem_ld16_nw(t_lane + T_Y + half * 32, yi);
+      tmem_ld16_nw(t_lane + T_Y + half * 32 + 16, yi + 16);
+      tmem_ld16_nw(t_lane + T_YS + half * 32, ys);
+      tmem_ld16_nw(t_lane + T_YS + half * 32 + 16, ys + 16);
       tmem_wait();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) yv[j] = fmaf(sE[half * 32 + j], __uint_as_float(ys[j]), __uint_as_float(yi[j]));
     }
     mbar_wait(bar_s, par, abort_flag, P.err);
     tc_fence_after();
     __syncthreads();  // every MMA of this chunk is done: C, B, x, M and the bf16 S are free
     if (*abort_flag) break;
     if (tid == 0 && c0 + SQ < t_end) issue_loads(c0 + SQ);
+    // bf16 copy of the outgoing state (the next chunk's state term) while the loads are in flight
+#pragma unroll 1
+    for (int c0n = half * (N / 2); c0n < (half + 1) * (N / 2); c0n += 64) {
+      uint32_t r[64];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tmem_ld16_nw(t_lane + T_S + c0n + 16 * k, r + 16 * k);
+      tmem_wait();
+      store_sb<N>(smem, p, c0n, r);
+    }
 #pragma unroll
     for (int j = 0; j < 32; ++j)
-      *reinterpret_cast<bf16*>(smem + L::Y_OFF + (half * 32 + j) * L::YLD + p * 2) = f2bf(__uint_as_float(yv[j]));
+      *reinterpret_cast<bf16*>(smem + L::Y_OFF + (half * 32 + j) * L::YLD + p * 2) = f2bf(yv[j]);
     __syncthreads();
     for (int i = tid; i < SQ * (SP / 8); i += STHR) {
       const int t = i / (SP / 8), c = i % (SP / 8);
