@@ -44,6 +44,8 @@ class Groups:
     device: torch.device
     quad: Coordinator | None = None
     extra: dict = field(default_factory=dict)
+    prebuilt: frozenset = frozenset()  # every pre-built block set (all pairs / quads), the same on every rank
+    created: set = field(default_factory=set)  # sets made by ensure(), the same on every rank
 
     def group_for_ranks(self, ranks: tuple[int, ...]) -> Coordinator | None:
         """The coordinator whose membership equals `ranks`, or None for a single rank."""
@@ -58,14 +60,17 @@ class Groups:
         raise ValueError(f"no communicator for ranks {ranks} (rank {self.rank})")
 
     def ensure(self, rank_sets: list[tuple[int, ...]]) -> None:
-        """Collectively create communicators for `rank_sets` (every rank must call this with the same list)."""
+        """Collectively create communicators for `rank_sets` (every rank must call this with the same list).
+
+        dist.new_group is collective over the whole world, so whether a set is skipped must not depend on the
+        calling rank: sets that were pre-built (any rank's pair or quad) or created earlier are skipped on
+        every rank alike."""
         for rs in rank_sets:
             rs = tuple(rs)
-            if len(rs) <= 1 or len(rs) == self.world_size or rs in self.extra:
-                continue
-            if (self.pair and self.pair.ranks == rs) or (self.quad and self.quad.ranks == rs):
+            if len(rs) <= 1 or len(rs) == self.world_size or rs in self.prebuilt or rs in self.created:
                 continue
             pg = dist.new_group(list(rs))
+            self.created.add(rs)
             if self.rank in rs:
                 self.extra[rs] = Coordinator(rs, pg)
 
@@ -94,15 +99,19 @@ def init_groups(backend: str | None = None, timeout_s: float = 300.0) -> Groups:
         dist.init_process_group(be, rank=rank, world_size=world, timeout=timedelta(seconds=timeout_s), **kw)
     tp = Coordinator(tuple(range(world)), None)
     pair = quad = None
+    prebuilt = set()
     if world >= 4 and world % 2 == 0:
         for rs, pg in _blocks(world, 2, None):
+            prebuilt.add(rs)
             if rank in rs:
                 pair = Coordinator(rs, pg)
     if world >= 8 and world % 4 == 0:
         for rs, pg in _blocks(world, 4, None):
+            prebuilt.add(rs)
             if rank in rs:
                 quad = Coordinator(rs, pg)
-    return Groups(rank=rank, local_rank=local_rank, world_size=world, tp=tp, pair=pair, device=device, quad=quad)
+    return Groups(rank=rank, local_rank=local_rank, world_size=world, tp=tp, pair=pair, device=device, quad=quad,
+                  prebuilt=frozenset(prebuilt))
 
 
 def describe_comm(g: Coordinator | None) -> dict:

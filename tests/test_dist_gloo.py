@@ -149,3 +149,50 @@ def test_sharded_partials_all_reduce_to_the_full_layer(world, mode, dims_name):
         assert err < 1e-5, f"rank {rank}: relative error {err}"
         assert xr == 0.0, f"ranks disagree by {xr}"
         assert tmax == world - 1  # max over ranks
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_group_creation_is_identical_on_every_rank(world, monkeypatch):
+    """dist.new_group is collective over the world: every rank must issue the same calls in the same order,
+    whatever pair or quad it belongs to (a rank-dependent skip deadlocks NCCL at world 4 / 8)."""
+    import torch.distributed as tdist
+
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.dist import Coordinator, Groups
+    from multi_modal_parallelism_b200.config import MODES
+
+    dims7 = preset("falcon_h1_7b_like")
+    modes = [m for m in MODES if not m.startswith("split")] + [f"split{a}{world - a}" for a in range(1, world)]
+    for dims in (dims7, dims7.replace(n_groups=2), DIMS_G2):
+        for mode in modes:
+            try:
+                sets = all_norm_groups(mode, world, dims)
+            except ValueError:
+                continue
+            calls = []
+            for rank in range(world):
+                made = []
+                monkeypatch.setattr(tdist, "new_group", lambda ranks, *a, **k: made.append(tuple(ranks)) or object())
+                pre = set()
+                pair = quad = None
+                if world >= 4:
+                    for i in range(world // 2):
+                        rs = (2 * i, 2 * i + 1)
+                        pre.add(rs)
+                        if rank in rs:
+                            pair = Coordinator(rs, None)
+                if world >= 8:
+                    for i in range(world // 4):
+                        rs = tuple(range(4 * i, 4 * i + 4))
+                        pre.add(rs)
+                        if rank in rs:
+                            quad = Coordinator(rs, None)
+                g = Groups(rank=rank, local_rank=rank, world_size=world, tp=Coordinator(tuple(range(world)), None),
+                           pair=pair, device=torch.device("cpu"), quad=quad, prebuilt=frozenset(pre))
+                g.ensure(sets)
+                g.ensure(sets)  # idempotent
+                calls.append(made)
+                for rs in sets:  # every member finds its communicator
+                    if rank in rs and len(rs) > 1:
+                        assert g.group_for_ranks(tuple(rs)) is not None
+            assert all(c == calls[0] for c in calls), (mode, world, calls)
