@@ -220,9 +220,9 @@ def decode_step(full: dict, dims, h: np.ndarray, k_cache, v_cache, conv_state: n
     k = gemm(xa, f("self_attn.k_proj.weight")).reshape(B, nkv, hd)
     v = gemm(xa, f("self_attn.v_proj.weight")).reshape(B, nkv, hd)
     q, k = rope_qk(q, k, positions, dims.rope_theta, dims.key_mult)
-    rep = nq // nkv
+    rep = nq // nkv if nkv else 0  # a layer without attention heads: the branch contributes zeros
     o = np.zeros((B, nq, hd), dtype=F32)
-    for b in range(B):
+    for b in range(B if nq else 0):
         Kb = np.concatenate([np.asarray(k_cache[b], dtype=F32), k[b][None]], 0)  # [c+1, nkv, hd]
         Vb = np.concatenate([np.asarray(v_cache[b], dtype=F32), v[b][None]], 0)
         Kq, Vq = np.repeat(Kb, rep, axis=1), np.repeat(Vb, rep, axis=1)
