@@ -48,6 +48,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--prefill-seqs", type=int, default=8)
     ap.add_argument("--prefill-len", type=int, default=2048, help="0 skips the prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--workload", choices=["hybrid", "mamba2_sg"], default="hybrid",
+                    help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split)")
+    ap.add_argument("--sg-batch", type=int, default=256, help="mamba2_sg: live requests per step")
     return ap.parse_args()
 
 
@@ -423,9 +426,83 @@ def our_arm(args) -> None:
     destroy()
 
 
+def mamba2_arm(args) -> None:
+    """The pure Mamba-2 layer (hidden 4096, 128 heads x 64, d_state 128, 8 groups) under continuous batching:
+    `--sg-batch` live requests, a quarter restarting as prompts of 64-1024 tokens each step, the rest decoding,
+    rows in a fresh order every step. Layouts: tp at N=1; sg{N/2}{N/2} and tp at even N > 1. One step = one
+    mixed batch through Mamba2Layer.step (eager: the batch shape changes every step); value = tokens / device
+    time, max over ranks. Run e.g. `python bench.py --workload mamba2_sg --steps 20 --warmup 3`."""
+    import torch
+
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
+    from multi_modal_parallelism_b200.mamba2 import Mamba2Layer, alloc_mamba2_states, mixed_ctx
+    from multi_modal_parallelism_b200.sg import continuous_batches, parse_sg, sg_plan
+    from multi_modal_parallelism_b200.sharding import ssm_shard
+    from multi_modal_parallelism_b200.weights import random_layer
+
+    groups = init_groups()
+    world, dev = groups.world_size, groups.device
+    dims = preset("mamba2_sg")
+    full = random_layer(dims, args.seed)
+    batches = list(continuous_batches(args.warmup + args.steps, batch=args.sg_batch, prefill_frac=0.25,
+                                      len_range=(64, 1024), seed=args.seed))
+    tmax = max(b.T for b in batches)
+    ctxs = [mixed_ctx(b, dev) for b in batches]
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    h_all = torch.randn(tmax, dims.hidden, device=dev, generator=g).to(torch.bfloat16)
+    modes = ["tp"] if world == 1 else ([f"sg{world // 2}{world // 2}"] if world % 2 == 0 else []) + ["tp"]
+    results = {}
+    for mode in modes:
+        if parse_sg(mode):
+            plan = sg_plan(mode, groups.rank, world, dims)
+            shard, role = plan.shard, plan.role
+        else:
+            shard, role = ssm_shard(dims, groups.rank, world, tuple(range(world))), "tp"
+        states = alloc_mamba2_states(dims, shard, args.sg_batch + 1, dev) if role != "gate" else None
+        layer = Mamba2Layer(mode, dims, full, groups, states, dev, tmax)
+        for b, c in zip(batches[:args.warmup], ctxs[:args.warmup]):
+            layer.step(h_all[:b.T], c)
+        barrier_sync()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
+        ev[0].record()
+        for i, (b, c) in enumerate(zip(batches[args.warmup:], ctxs[args.warmup:])):
+            layer.step(h_all[:b.T], c)
+            ev[i + 1].record()
+        torch.cuda.synchronize()
+        per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
+        total = max_over_ranks(ev[0].elapsed_time(ev[-1]), groups)
+        tokens = sum(b.T for b in batches[args.warmup:])
+        results[mode] = {"ms_per_step": total / args.steps, "p50_ms": max_over_ranks(statistics.median(per), groups),
+                         "tokens_per_s": tokens / total * 1e3, "tokens_per_step": tokens / args.steps}
+        del layer, states
+        torch.cuda.empty_cache()
+        barrier_sync()
+    if groups.rank == 0:
+        best = max(results, key=lambda m: results[m]["tokens_per_s"])
+        r = results[best]
+        print(json.dumps({
+            "metric": "pure Mamba-2 layer tokens/s under continuous batching (SSM/gate split vs TP)",
+            "value": r["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+            "config": {"workload": f"mamba2_sg layer, {args.sg_batch} requests, 25% prefill U[64,1024], rows "
+                                   "re-ordered every step", "parallelism": best,
+                       "recipes": {m: {k: round(v, 4) for k, v in x.items()} for m, x in results.items()}},
+        }), flush=True)
+    destroy()
+
+
 def main() -> None:
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
+    if args.workload == "mamba2_sg":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "no CPU arm for the mamba2_sg workload"}))
+            return
+        mamba2_arm(args)
+        return
     if args.impl == "reference":
         reference_arm(args, rank)
         return
