@@ -257,6 +257,39 @@ int mmp_paged_attn_prefill(const void* q, int64_t q_t, int64_t q_h,
 int mmp_add(const void* a, int64_t a_b, const void* b, int64_t b_b, const void* c, int64_t c_b,
             void* out, int64_t o_b, int rows, int cols, void* stream);
 
+/* ---- Gated DeltaNet linear attention (the config's gated delta-rule layers) ----------------------------
+ * The reference has no kernel for these layers: configs/qwen35_35b_a3b.yaml:1-22 describes them and
+ * harness/synth.py:114-138 models their bytes. Per value head j (key head j / (nv / nk)), with q, k the
+ * post-conv rows L2-normalised in fp32 (q also scaled by dk^-1/2), g = -exp(A_log[j]) softplus(a + dt_bias[j])
+ * (A_log / dt_bias NULL: factor 1 / bias 0), beta = sigmoid(b):
+ *   S <- exp(g) S (I - beta k k^T) + beta v k^T,   o = S q,
+ * S the [dv, dk] fp32 state of the line. Output: rmsnorm(o) * norm_w * silu(z) over the head's dv values
+ * (norm_w NULL: o itself; z NULL: no gate; eps for the norm). dk == dv == 128.
+ *
+ * Decode: one token per row. q/k [batch, nk, dk], v/z/out [batch, nv, dv], a/b [batch, nv] (raw projections,
+ * heads contiguous), state [lines, nv, dv, dk] fp32, idx[row] its line (NULL: the row index; pad_slot: the
+ * row's output is zero and no state is touched; out-of-range lines set MMP_DEVERR_INDEX in *err).
+ */
+int mmp_gdn_decode(float* state, int64_t s_line, int64_t s_head, int64_t s_row,
+                   const void* q, int64_t q_b, int64_t q_h, const void* k, int64_t k_b, int64_t k_h,
+                   const void* v, int64_t v_b, int64_t v_h, const void* a, int64_t a_b,
+                   const void* b, int64_t b_b, const float* A_log, const float* dt_bias,
+                   const void* z, int64_t z_b, int64_t z_h, const void* norm_w, float eps,
+                   const int32_t* idx, int pad_slot, void* out, int64_t o_b, int64_t o_h,
+                   int batch, int nk, int nv, int dk, int dv, int lines, int* err, void* stream);
+
+/* Chunked prefill (64-token chunks) of variable-length sequences: tokens [cu_seqlens[i], cu_seqlens[i+1]) of
+ * q/k [ntok, nk, dk], v/z/out [ntok, nv, dv], a/b [ntok, nv]; sequence i starts from state line state_idx[i]
+ * when has_init[i] (has_init NULL: from zeros) and leaves its final state there. Rows 16-byte aligned. */
+int mmp_gdn_prefill(const void* q, int64_t q_t, int64_t q_h, const void* k, int64_t k_t, int64_t k_h,
+                    const void* v, int64_t v_t, int64_t v_h, const void* a, int64_t a_t,
+                    const void* b, int64_t b_t, const float* A_log, const float* dt_bias,
+                    const void* z, int64_t z_t, int64_t z_h, const void* norm_w, float eps,
+                    float* state, int64_t s_line, int64_t s_head, int64_t s_row,
+                    const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init,
+                    void* out, int64_t o_t, int64_t o_h,
+                    int nseq, int ntok, int nk, int nv, int dk, int dv, int lines, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

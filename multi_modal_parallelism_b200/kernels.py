@@ -457,3 +457,77 @@ def attn_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Te
               _p(block_table), block_table.stride(0), _p(cu_q), _p(ctx_start), _p(out), out.stride(0), out.stride(1),
               nseq, int(max_q_len), nq, nkv, hd, blk, nb, 1.0 / math.sqrt(hd), _p(error_word(q.device)), _stream(q))
     return out
+
+
+# ----------------------------------------------------------------------------- Gated DeltaNet
+def _gdn_common(name: str, q, k, v, a, b, state, A_log, dt_bias, z, norm_w):
+    _cuda(name, q, k, v, a, b, state, A_log, dt_bias, z, norm_w)
+    for t in (q, k, v, a, b, z, norm_w):
+        _dtype(name, t, BF16)
+    for t in (state, A_log, dt_bias):
+        _dtype(name, t, torch.float32)
+    if q.dim() != 3 or k.shape != q.shape or v.dim() != 3:
+        raise ValueError(f"{name}: q/k [rows, nk, dk] and v [rows, nv, dv] expected")
+    for nm, t in (("q", q), ("k", k), ("v", v), ("z", z)):
+        if t is not None and t.stride(-1) != 1:
+            raise ValueError(f"{name}: {nm} must have a contiguous last dimension")
+    for nm, t in (("a", a), ("b", b)):
+        if t.dim() != 2 or (t.shape[1] > 1 and t.stride(1) != 1):
+            raise ValueError(f"{name}: {nm} must be [rows, nv] with contiguous heads")
+    lines, nv, dv, dk = state.shape
+    if state.stride(3) != 1:
+        raise ValueError(f"{name}: state rows must be contiguous")
+    if v.shape[1] != nv or v.shape[2] != dv or q.shape[2] != dk or a.shape[1] != nv or b.shape[1] != nv:
+        raise ValueError(f"{name}: shapes disagree: q {tuple(q.shape)} v {tuple(v.shape)} a {tuple(a.shape)} "
+                         f"state {tuple(state.shape)}")
+    for nm, t in (("A_log", A_log), ("dt_bias", dt_bias)):
+        if t is not None and (t.numel() != nv or not t.is_contiguous()):
+            raise ValueError(f"{name}: {nm} must be a contiguous fp32 [nv] vector")
+    if norm_w is not None and (norm_w.numel() != dv or not norm_w.is_contiguous()):
+        raise ValueError(f"{name}: norm_w must be a contiguous bf16 [dv] vector")
+    zs = (z.stride(0), z.stride(1)) if z is not None else (0, 0)
+    return lines, nv, dv, dk, zs
+
+
+def gdn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+               state: torch.Tensor, idx: torch.Tensor | None, out: torch.Tensor, z: torch.Tensor | None = None,
+               norm_w: torch.Tensor | None = None, eps: float = 1e-6, A_log: torch.Tensor | None = None,
+               dt_bias: torch.Tensor | None = None, pad_slot: int = PAD_SLOT_ID) -> torch.Tensor:
+    """One gated delta-rule step per row: q/k [B, nk, dk], v/z/out [B, nv, dv], a/b [B, nv] raw projections,
+    state [lines, nv, dv, dk] fp32 updated in place at lines idx [B] int32. out = rmsnorm(o) * norm_w * silu(z)
+    per head (o itself without norm_w)."""
+    lines, nv, dv, dk, zs = _gdn_common("gdn_decode", q, k, v, a, b, state, A_log, dt_bias, z, norm_w)
+    _cuda("gdn_decode", idx, out)
+    _dtype("gdn_decode", out, BF16)
+    if idx is not None:
+        _dtype("gdn_decode", idx, torch.int32)
+    B = q.shape[0]
+    _lib.call("mmp_gdn_decode", _p(state), state.stride(0), state.stride(1), state.stride(2),
+              _p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1), _p(v), v.stride(0), v.stride(1),
+              _p(a), a.stride(0), _p(b), b.stride(0), _p(A_log), _p(dt_bias), _p(z), zs[0], zs[1], _p(norm_w),
+              float(eps), _p(idx), pad_slot, _p(out), out.stride(0), out.stride(1),
+              B, q.shape[1], nv, dk, dv, lines, _p(error_word(q.device)), _stream(q))
+    return out
+
+
+def gdn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
+                state: torch.Tensor, cu_seqlens: torch.Tensor, state_idx: torch.Tensor, has_init: torch.Tensor | None,
+                out: torch.Tensor, z: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
+                eps: float = 1e-6, A_log: torch.Tensor | None = None,
+                dt_bias: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked gated delta rule over variable-length sequences (tokens [cu[i], cu[i+1]) of q/k [T, nk, dk],
+    v/z/out [T, nv, dv], a/b [T, nv]); initial state from state[state_idx[i]] where has_init[i], final state
+    written back there."""
+    lines, nv, dv, dk, zs = _gdn_common("gdn_prefill", q, k, v, a, b, state, A_log, dt_bias, z, norm_w)
+    _cuda("gdn_prefill", cu_seqlens, state_idx, has_init, out)
+    _dtype("gdn_prefill", out, BF16)
+    for t in (cu_seqlens, state_idx, has_init):
+        if t is not None:
+            _dtype("gdn_prefill", t, torch.int32)
+    nseq = cu_seqlens.numel() - 1
+    _lib.call("mmp_gdn_prefill", _p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1),
+              _p(v), v.stride(0), v.stride(1), _p(a), a.stride(0), _p(b), b.stride(0), _p(A_log), _p(dt_bias),
+              _p(z), zs[0], zs[1], _p(norm_w), float(eps), _p(state), state.stride(0), state.stride(1),
+              state.stride(2), _p(cu_seqlens), _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1),
+              nseq, q.shape[0], q.shape[1], nv, dk, dv, lines, _p(error_word(q.device)), _stream(q))
+    return out

@@ -22,7 +22,8 @@ every ratio of decays above is <= 1, so nothing overflows.
 The layer (a Qwen3.5-style block, the config's description: hidden 2048; 16 key heads x 128 shared by 32
 value heads x 128; short conv of width 4 with SiLU over q|k|v; L2-normalised q/k; per-head decay
 g = -softplus(a), beta = sigmoid(b); output RMSNorm per head gated by silu(z); out_proj; residual; then a
-SwiGLU MLP with its own residual).
+SwiGLU MLP with its own residual). Optional per-head `A_log` / `dt_bias` weights give the Qwen3-Next form of the
+decay, g = -exp(A_log) softplus(a + dt_bias).
 """
 from __future__ import annotations
 
@@ -116,12 +117,20 @@ def gdn_random_layer(d: GdnDims, seed: int) -> dict:
     }
 
 
+def gates(a: np.ndarray, b: np.ndarray, A_log: np.ndarray | None = None, dt_bias: np.ndarray | None = None):
+    """Per-head log-decay g = -exp(A_log) softplus(a + dt_bias) and write strength beta = sigmoid(b) from the raw
+    projections a, b [..., n_v]; without A_log / dt_bias (the layer's stated form) g = -softplus(a)."""
+    a = a.astype(F32) + (0 if dt_bias is None else dt_bias.astype(F32))
+    g = -softplus(a) * (1 if A_log is None else np.exp(A_log.astype(F32)))
+    beta = F32(1) / (F32(1) + np.exp(-b.astype(F32)))
+    return g.astype(F32), beta.astype(F32)
+
+
 def _mixer_inputs(w: dict, d: GdnDims, x: np.ndarray):
     qkv = gemm(x, w["in_proj_qkv.weight"])
     z = gemm(x, w["in_proj_z.weight"])
-    g = -softplus(gemm(x, w["in_proj_a.weight"]))
-    beta = 1.0 / (1.0 + np.exp(-gemm(x, w["in_proj_b.weight"])))
-    return qkv, z, g.astype(F32), beta.astype(F32)
+    g, beta = gates(gemm(x, w["in_proj_a.weight"]), gemm(x, w["in_proj_b.weight"]), w.get("A_log"), w.get("dt_bias"))
+    return qkv, z, g, beta
 
 
 def _split_heads(d: GdnDims, c: np.ndarray):
