@@ -48,8 +48,9 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--prefill-seqs", type=int, default=8)
     ap.add_argument("--prefill-len", type=int, default=2048, help="0 skips the prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=20)
-    ap.add_argument("--workload", choices=["hybrid", "mamba2_sg"], default="hybrid",
-                    help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split)")
+    ap.add_argument("--workload", choices=["hybrid", "mamba2_sg", "qwen35"], default="hybrid",
+                    help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split); "
+                         "qwen35: the Gated DeltaNet hybrid block stack (tp and attention data-parallel)")
     ap.add_argument("--sg-batch", type=int, default=256, help="mamba2_sg: live requests per step")
     return ap.parse_args()
 
@@ -493,9 +494,130 @@ def mamba2_arm(args) -> None:
     destroy()
 
 
+def stack_flops(d, lens: list[int]) -> float:
+    """Algorithmic FLOPs of one prefill of the Gated DeltaNet stack over sequences of `lens` tokens: projections
+    and MLPs (2 per multiply-add), causal attention (QK^T and PV over the causal half), the chunked delta rule
+    per token and value head (K K^T, Q K^T, S K^T, S Q^T, T R, Qm U and the state update at chunk C)."""
+    T, H, C = sum(lens), d.hidden, d.chunk
+    mlp = 2 * 3 * H * d.intermediate * T
+    f = 0.0
+    for kind in d.layout:
+        if kind == "G":
+            rows = d.qkv_rows + d.n_v * d.dv + 2 * d.n_v
+            f += 2 * H * rows * T + 2 * d.n_v * d.dv * H * T
+            f += T * d.n_v * (4 * C * d.dk + 6 * d.dk * d.dv + 4 * C * d.dv)
+        else:
+            f += 2 * H * (d.n_q + 2 * d.n_kv) * d.head_dim * T + 2 * d.n_q * d.head_dim * H * T
+            f += sum(2 * L * L * d.n_q * d.head_dim for L in lens)  # 2 contractions x causal half
+        f += mlp
+    return f
+
+
+def qwen35_arm(args) -> None:
+    """The Gated DeltaNet hybrid block stack (qwen35_like: three delta-rule layers of 16 key / 32 value heads x 128
+    and one GQA attention layer of 16 / 2 heads x 128, hidden 2048, SwiGLU 6144, fp32 delta-rule state): decode of
+    --batch sequences at context --ctx (one CUDA-graph replay of the stack per step) and a prefill of
+    --prefill-seqs x --prefill-len fresh sequences (eager), in the tp and attn_dp layouts; value = decode tokens /
+    device time of the faster layout, max over ranks. Run e.g. `python bench.py --workload qwen35 --steps 200
+    --warmup 20 --ctx 4096 --prefill-seqs 4 --prefill-len 4096`."""
+    import torch
+
+    from multi_modal_parallelism_b200 import kernels as K
+    from multi_modal_parallelism_b200.dist import barrier_sync, capture_context, destroy, init_groups
+    from multi_modal_parallelism_b200.qwen35 import GdnLayer, Qwen35Dims, Qwen35Stack, random_stack
+    from multi_modal_parallelism_b200.state import make_decode_ctx, make_prefill_ctx
+
+    groups = init_groups()
+    world, dev = groups.world_size, groups.device
+    d = Qwen35Dims.from_yaml("qwen35_like")
+    ws = random_stack(d, args.seed)
+    B, c = args.batch, args.ctx
+    dc = make_decode_ctx(B, c, 16, dev)
+    lens = [args.prefill_len] * args.prefill_seqs if args.prefill_len > 0 else []
+    pc = make_prefill_ctx(lens, 16, dev) if lens else None
+    nblocks = max(dc.block_table.numel(), pc.block_table.numel() if pc else 0)
+    rows = max(B, sum(lens))
+    g = torch.Generator(device=dev).manual_seed(args.seed)
+    h_dec = torch.randn(B, d.hidden, device=dev, generator=g).to(torch.bfloat16)
+    h_pre = torch.randn(max(1, sum(lens)), d.hidden, device=dev, generator=g).to(torch.bfloat16)
+    hbm, hbm_src = roofline_peak()
+    tf, tf_src = bf16_peak()
+    modes = ["tp"] if world == 1 else ["tp", "attn_dp"]
+    results = {}
+    for mode in modes:
+        stack = Qwen35Stack(d, ws, mode, groups, dev, lines=B + 1, num_blocks=nblocks, kv_block=16, max_tokens=rows)
+        for layer in stack.layers:  # decode from non-zero delta-rule states (their values do not change the work)
+            if isinstance(layer, GdnLayer):
+                layer.ssm_state.normal_(0, 0.05, generator=g)
+        r = {}
+        with capture_context(groups) as cc, torch.cuda.stream(cc.stream):
+            for _ in range(3):
+                stack.step(h_dec, dc)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=cc.stream):
+                stack.step(h_dec, dc)
+        ms, p50 = time_replays(graph.replay, args.steps, args.warmup, groups)
+        r["decode"] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": B / ms * 1e3}
+        # the delta-rule decode kernel alone (first layer): fp32 state read + write per (row, value head)
+        gl = next(x for x in stack.layers if isinstance(x, GdnLayer))
+        nbytes = 2 * B * gl.nv * d.dv * d.dk * 4
+        q = torch.randn(B, gl.nk, d.dk, device=dev).to(torch.bfloat16)
+        vz = torch.randn(B, gl.nv, d.dv, device=dev).to(torch.bfloat16)
+        ab = torch.randn(B, gl.nv, device=dev).to(torch.bfloat16)
+        o = torch.empty(B, gl.nv, d.dv, device=dev, dtype=torch.bfloat16)
+        run = lambda: K.gdn_decode(q, q, vz, ab, ab, gl.ssm_state, dc.state_idx, o, z=vz, norm_w=gl.norm_w)  # noqa: E731
+        for _ in range(5):
+            run()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(50):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / 50
+        r["gdn_decode_kernel"] = {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "frac": nbytes / us / 1e3 / hbm}
+        if pc is not None:
+            ms_p, p50_p = time_replays(lambda: stack.step(h_pre, pc), max(1, args.prefill_steps), 2, groups)
+            fl = stack_flops(d, lens)
+            r["prefill"] = {"ms": ms_p, "p50_ms": p50_p, "tokens_per_s": sum(lens) / ms_p * 1e3,
+                            "tflops": fl / ms_p / 1e9, "frac_of_bf16_peak": fl / ms_p / 1e9 / tf}
+        results[mode] = r
+        del graph, stack
+        torch.cuda.empty_cache()
+        barrier_sync()
+    if groups.rank == 0:
+        best = max(results, key=lambda m: results[m]["decode"]["tokens_per_s"])
+        r = results[best]
+        k = r["gdn_decode_kernel"]
+        print(json.dumps({
+            "metric": "Gated DeltaNet hybrid stack decode tokens/s (attention data-parallel vs TP)",
+            "value": r["decode"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": r["decode"]["ms_per_step"], "p50_ms": r["decode"]["p50_ms"],
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded)",
+            "config": {"workload": f"qwen35_like stack ({d.layout}), decode batch {B} at context {c}; prefill "
+                                   f"{args.prefill_seqs} x {args.prefill_len}", "parallelism": best,
+                       "l2": "delta-rule states 268 MB per layer at batch 64: larger than L2, no flush",
+                       "recipes": results},
+            "roofline": {"bound": "hbm", "kernel": "gdn_decode", "achieved": k["gbs"], "peak": hbm, "unit": "GB/s",
+                         "frac": k["frac"], "peak_source": hbm_src, "traffic": None},
+            "bf16_peak": {"tflops": tf, "source": tf_src},
+        }), flush=True)
+    destroy()
+
+
 def main() -> None:
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
+    if args.workload == "qwen35":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference has no implementation of the "
+                                  "Gated DeltaNet stack (a config description and a byte model only)"}))
+            return
+        qwen35_arm(args)
+        return
     if args.workload == "mamba2_sg":
         if args.impl == "reference":
             if rank == 0:

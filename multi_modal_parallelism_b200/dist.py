@@ -33,6 +33,18 @@ class Coordinator:
             dist.all_reduce(t, group=self.pg)
         return t
 
+    def all_gather_rows(self, out: torch.Tensor, t: torch.Tensor) -> torch.Tensor:
+        """out [world * n, ...] <- every rank's t [n, ...] in rank order (contiguous tensors); returns out."""
+        if self.world_size == 1:
+            if out.data_ptr() != t.data_ptr():
+                out.copy_(t)
+            return out
+        if out.is_cuda:
+            dist.all_gather_into_tensor(out, t, group=self.pg)
+        else:  # gloo: one output view per rank
+            dist.all_gather(list(out.chunk(self.world_size)), t, group=self.pg)
+        return out
+
 
 @dataclass
 class Groups:

@@ -131,3 +131,160 @@ def gated_rmsnorm(y, z, w, eps, group, group_size=None, out=None, sumsq=None):
         r = g * torch.rsqrt(tot / (group.world_size * Dd) + eps)
     out.copy_((r * w.float()).to(out.dtype))
     return out
+
+
+# ---------------------------------------------------------------- the Gated DeltaNet stack's extra kernels
+def rms_norm_residual(x, residual, w, eps, out, sum_out=None):
+    s = x.float() + residual.float()
+    if sum_out is not None:
+        sum_out.copy_(s.to(sum_out.dtype))
+    s = s.to(BF16).float()  # the kernel normalises the bf16 sum it stores
+    out.copy_((s * torch.rsqrt(s.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(out.dtype))
+    return out
+
+
+def silu_mul(gate, up, out, gate_scale=1.0):
+    out.copy_((F.silu(gate.float() * gate_scale) * up.float()).to(out.dtype))
+    return out
+
+
+def _gdn_gates(a, b, A_log, dt_bias):
+    g = -F.softplus(a.float() + (0 if dt_bias is None else dt_bias.float()))
+    if A_log is not None:
+        g = g * torch.exp(A_log.float())
+    return g, torch.sigmoid(b.float())
+
+
+def _gdn_token(q, k, v, g, beta, S):
+    """One token of every value head: q, k [nk, dk]; v [nv, dv]; g, beta [nv]; S [nv, dv, dk] fp32 (in place)."""
+    nv, nk = v.shape[0], q.shape[0]
+    dk = q.shape[1]
+    qn = q.float() / torch.sqrt((q.float() ** 2).sum(-1, keepdim=True) + 1e-6) * dk ** -0.5
+    kn = k.float() / torch.sqrt((k.float() ** 2).sum(-1, keepdim=True) + 1e-6)
+    rep = nv // nk
+    o = torch.empty(nv, v.shape[1])
+    for j in range(nv):
+        kk, qq = kn[j // rep], qn[j // rep]
+        a = torch.exp(g[j])
+        s = S[j]
+        u = beta[j] * (v[j].float() - a * (s @ kk))
+        S[j] = a * s + torch.outer(u, kk)
+        o[j] = S[j] @ qq
+    return o
+
+
+def _gdn_out(o, z, norm_w, eps):
+    if norm_w is not None:
+        o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float()
+    if z is not None:
+        o = o * F.silu(z.float())
+    return o
+
+
+def gdn_decode(q, k, v, a, b, state, idx, out, z=None, norm_w=None, eps=1e-6, A_log=None, dt_bias=None, pad_slot=-1):
+    assert q.stride(-1) == 1 and k.stride(-1) == 1 and v.stride(-1) == 1 and a.stride(-1) == 1
+    assert state.dtype == torch.float32
+    g, beta = _gdn_gates(a, b, A_log, dt_bias)
+    for r in range(q.shape[0]):
+        line = r if idx is None else int(idx[r])
+        if line == pad_slot:
+            out[r].zero_()
+            continue
+        S = state[line].clone()
+        o = _gdn_token(q[r], k[r], v[r], g[r], beta[r], S)
+        state[line].copy_(S)
+        out[r].copy_(_gdn_out(o, None if z is None else z[r], norm_w, eps).to(out.dtype))
+    return out
+
+
+def gdn_prefill(q, k, v, a, b, state, cu_seqlens, state_idx, has_init, out, z=None, norm_w=None, eps=1e-6,
+                A_log=None, dt_bias=None):
+    for t in (q, k, v, out) + (() if z is None else (z,)):
+        assert t.stride(-1) == 1 and (t.stride(0) * 2) % 16 == 0, "rows must be 16-byte aligned"
+    g, beta = _gdn_gates(a, b, A_log, dt_bias)
+    cu = cu_seqlens.tolist()
+    for i in range(len(cu) - 1):
+        line = int(state_idx[i])
+        init = has_init is not None and int(has_init[i])
+        S = state[line].clone() if init else torch.zeros_like(state[line])
+        for t in range(cu[i], cu[i + 1]):
+            o = _gdn_token(q[t], k[t], v[t], g[t], beta[t], S)
+            out[t].copy_(_gdn_out(o, None if z is None else z[t], norm_w, eps).to(out.dtype))
+        state[line].copy_(S)
+    return out
+
+
+def rope_inv_freq(head_dim, theta, device):
+    return 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim)).to(device)
+
+
+def _rope(x, pos, inv):
+    """x [T, heads, hd] fp32, NeoX halves."""
+    ang = pos.float()[:, None] * inv[None, :]
+    c, s = ang.cos()[:, None, :], ang.sin()[:, None, :]
+    h = x.shape[-1] // 2
+    x1, x2 = x[..., :h], x[..., h:]
+    return torch.cat([x1 * c - x2 * s, x2 * c + x1 * s], -1)
+
+
+def qkv_rope_kv_write(qkv, nq, nkv, head_dim, positions, inv_freq, key_mult, q_out, key_cache, value_cache,
+                      slot_mapping):
+    _rows16("qkv_rope_kv_write.qkv", qkv)
+    T = qkv.shape[0]
+    q = qkv[:, :nq * head_dim].float().view(T, nq, head_dim)
+    k = qkv[:, nq * head_dim:(nq + nkv) * head_dim].float().view(T, nkv, head_dim) * key_mult
+    v = qkv[:, (nq + nkv) * head_dim:(nq + 2 * nkv) * head_dim].view(T, nkv, head_dim)
+    q_out.copy_(_rope(q, positions, inv_freq).reshape(T, -1).to(q_out.dtype))
+    k = _rope(k, positions, inv_freq).to(key_cache.dtype)
+    blk = key_cache.shape[1]
+    for t in range(T):
+        s = int(slot_mapping[t])
+        if s < 0:
+            continue
+        key_cache[s // blk, s % blk].copy_(k[t])
+        value_cache[s // blk, s % blk].copy_(v[t])
+    return q_out
+
+
+def _attend(q, key_cache, value_cache, table_row, n_keys):
+    """q [m, nq, hd] queries attending to keys 0 .. limit[i] (inclusive) given as n_keys [m]."""
+    blk = key_cache.shape[1]
+    nkv = key_cache.shape[2]
+    L = int(max(n_keys))
+    pos = torch.arange(L)
+    K = key_cache[table_row[pos // blk].long(), pos % blk].float()  # [L, nkv, hd]
+    V = value_cache[table_row[pos // blk].long(), pos % blk].float()
+    m, nq, hd = q.shape
+    rep = nq // nkv
+    out = torch.empty(m, nq, hd)
+    for hh in range(nq):
+        s = (q[:, hh].float() @ K[:, hh // rep].T) / hd ** 0.5
+        s = s.masked_fill(pos[None, :] >= torch.as_tensor(n_keys)[:, None], float("-inf"))
+        out[:, hh] = torch.softmax(s, -1) @ V[:, hh // rep]
+    return out
+
+
+def attn_prefill(q, key_cache, value_cache, block_table, cu_q, ctx_start, max_q_len, out):
+    cu = cu_q.tolist()
+    for i in range(len(cu) - 1):
+        n = cu[i + 1] - cu[i]
+        if n == 0:
+            continue
+        c0 = int(ctx_start[i])
+        lim = [c0 + j + 1 for j in range(n)]
+        out[cu[i]:cu[i + 1]].copy_(_attend(q[cu[i]:cu[i + 1]], key_cache, value_cache, block_table[i], lim).to(out.dtype))
+    return out
+
+
+def attn_default_splits(batch, nkv, max_seqlen):
+    return 1
+
+
+def attn_workspace(batch, nq, hd, splits, device):
+    return torch.empty(1)
+
+
+def attn_decode(q, key_cache, value_cache, cu_q, seqused_k, max_k, block_table, out, workspace=None, splits=0):
+    for r in range(q.shape[0]):
+        out[r:r + 1].copy_(_attend(q[r:r + 1], key_cache, value_cache, block_table[r], [int(seqused_k[r])]).to(out.dtype))
+    return out
