@@ -90,3 +90,33 @@ def test_four_gpu_prefill(mode):
 @pytest.mark.parametrize("mode", ["split44", "tp4_fused"])
 def test_eight_gpu_prefill(mode):
     run_prefill_check(8, mode)
+
+
+def run_script_check(world, script, tag, mode):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), str(ROOT / "tests" / script), "--mode", mode]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "600", *cmd], cwd=ROOT, env=env, capture_output=True, text=True)
+    out = r.stdout + r.stderr
+    m = re.search(rf"\[{tag}\].*pass=(True|False)", out)
+    assert r.returncode == 0 and m and m.group(1) == "True", out[-3000:]
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world,mode", [(2, "tp"), (2, "attn_dp"), (4, "attn_dp"), (8, "tp"), (8, "attn_dp")])
+def test_gdn_stack_layouts(world, mode):
+    """The Gated DeltaNet stack at N ranks: ranks bitwise equal, within tolerance of one rank."""
+    if ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_script_check(world, "_qwen35_ranks.py", "qwen35-check", mode)
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world,mode", [(2, "sg11"), (2, "tp"), (4, "sg22"), (8, "sg44")])
+def test_mamba2_continuous_batching_layouts(world, mode):
+    """The pure Mamba-2 layer under continuous batching at N ranks (SSM/gate split and tp)."""
+    if ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_script_check(world, "_mamba2_ranks.py", "mamba2-check", mode)
