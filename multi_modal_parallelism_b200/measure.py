@@ -22,6 +22,7 @@ from .config import FalconH1Dims, RunSpec
 from .correctness import compare, cross_rank_max_abs, passes, within_tolerance
 from .dist import Groups, barrier_sync, describe_comm
 from .layer import ParallelHybridLayer
+from .model import BwTables, bytes_per_op, choose_k, predict_rank
 from .sharding import neutral_k, plan_for, swing_width
 from .state import alloc_and_fill, full_states_for_reference, input_hidden, make_decode_ctx
 from .timing import time_eager, time_graph
@@ -40,13 +41,20 @@ def gpu_env(local_rank: int) -> dict:
         return {"sm_clock_mhz": -1, "temp_c": -1, "power_w": -1.0, "util_pct": -1}
 
 
-def resolve_k(spec: RunSpec, dims: FalconH1Dims, world: int) -> tuple[int, int | None, str]:
-    """(w, k, cuts_src) of the swing pool; 'model' (the reference's byte-model choice) falls back to neutral."""
+def resolve_k(spec: RunSpec, dims: FalconH1Dims, world: int, bw: BwTables | None = None) -> tuple[int, int | None, str]:
+    """(w, k, cuts_src) of the swing pool (`harness/measure.py:48-62`): 'model' asks the byte model for the cut
+    with the smallest predicted slowest-rank step under the bandwidth tables `bw` (neutral without tables)."""
     if not spec.mode.startswith("split") or spec.swing <= 0:
         return 0, None, ""
     w = swing_width(spec.swing, dims.intermediate // world)
-    if spec.cuts_src in ("neutral", "model"):
-        return w, neutral_k(w), "neutral" if spec.cuts_src == "neutral" else "neutral(no-model)"
+    if spec.cuts_src == "neutral":
+        return w, neutral_k(w), "neutral"
+    if spec.cuts_src == "model":
+        if bw is None:
+            return w, neutral_k(w), "neutral(no-bw)"
+        variant = "graph" if spec.variant != "eager" else "eager"
+        k, _ = choose_k(dims, spec.batch, spec.ctx, spec.swing, bw, variant, spec.kv_block, mode=spec.mode, world=world)
+        return w, k, "model"
     assert spec.k is not None, "grid/manual needs k"
     return w, int(spec.k), spec.cuts_src
 
@@ -72,8 +80,12 @@ def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, t
             correctness_csv: str, check: bool, bw=None, image_tag: str = "",
             ssm_dtype: torch.dtype = torch.float32) -> list[dict]:
     rank, world, device = groups.rank, groups.world_size, groups.device
-    w, k, cuts_src = resolve_k(spec, dims, world)
+    w, k, cuts_src = resolve_k(spec, dims, world, bw)
     plan = plan_for(spec.mode, rank, world, dims, spec.swing, k)
+    # the byte model's per-op predictions for this rank (filled into the rows' ms_pred / bytes_pred columns)
+    pred = {v: predict_rank(plan, dims, spec.batch, spec.ctx, bw, v, spec.kv_block) for v in ("eager", "graph")} \
+        if bw is not None else {}
+    op_bytes = bytes_per_op(plan, dims, spec.batch, spec.ctx)
     rw = shard_to_device(full, plan, dims, device)
     ctx = make_decode_ctx(spec.batch, spec.ctx, spec.kv_block, device)
     st = alloc_and_fill(plan, dims, ctx, spec.seed, device, ssm_dtype=ssm_dtype)
@@ -115,9 +127,11 @@ def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, t
             fn = time_eager if variant == "eager" else time_graph
             stats, wall = fn(layer, h, spec.n_warm, spec.n_iter, groups)
             rep_id = rep + spec.repeat_offset
+            p = pred.get(variant, {})
             for op, s in stats.items():
                 extra = {"tokens_per_s": spec.batch / s["median_ms"] * 1e3} if op == "step" else {}
-                rows.append(dict(base, variant=variant, repeat=rep_id, rank=rank, op=op, **s, **env, **extra))
+                rows.append(dict(base, variant=variant, repeat=rep_id, rank=rank, op=op, **s, **env, **extra,
+                                 ms_pred=p.get(op, ""), bytes_pred=op_bytes.get(op, "")))
             rows.append(dict(base, variant=variant, repeat=rep_id, rank=rank, op="step_wall", n=spec.n_iter,
                              median_ms=wall, p10_ms=wall, p90_ms=wall, mean_ms=wall, **env))
             barrier_sync()

@@ -4,7 +4,8 @@ correctness check. Same flags as the reference's `harness/run.py:41-70`:
   torchrun --standalone --nproc-per-node=4 -m multi_modal_parallelism_b200.run --mode split22 \\
       --batch 16 --ctx 8192 --variant graph --check --out results/raw/dev.csv
 
-Extensions: any split{a}{m} mode, --ssm-dtype (fp32 default), bundled dims names for --dims-yaml. The
+Extensions: any split{a}{m} mode, --ssm-dtype (fp32 default), bundled dims names for --dims-yaml. `--k model`
+takes the swing cut the byte model (model.py) predicts fastest under the microbench tables in --bw. The
 reference's other templates (parallel-residual, sequential hybrid) are not part of this build.
 """
 from __future__ import annotations
@@ -18,6 +19,7 @@ import torch
 from .config import FalconH1Dims, RunSpec
 from .dist import barrier_sync, destroy, init_groups
 from .measure import measure
+from .model import BwTables
 from .weights import load_layer_from_safetensors, random_layer
 
 
@@ -38,7 +40,8 @@ def add_common_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--random-weights", action="store_true")
     ap.add_argument("--layer-idx", type=int, default=0)
     ap.add_argument("--seed", type=int, default=0)
-    ap.add_argument("--bw", default="", help="accepted for compatibility; the byte model is not part of this build")
+    ap.add_argument("--bw", default="results/raw/microbench.csv",
+                    help="microbench CSV for the byte model (--k model, predicted ms per op); used when it exists")
     ap.add_argument("--out", default="results/raw/dev.csv")
     ap.add_argument("--correctness-out", default="results/raw/correctness.csv")
     ap.add_argument("--tag", default="")
@@ -75,7 +78,8 @@ def main(argv: list[str] | None = None) -> int:
     groups = init_groups()
     dims, full = load_dims_and_weights(args)
     ssm_dtype = torch.float32 if args.ssm_dtype == "fp32" else torch.bfloat16
-    rows = measure(spec, groups, dims, full, args.out, args.correctness_out, args.check, None,
+    bw = BwTables.from_csv(args.bw) if args.bw and os.path.exists(args.bw) else None
+    rows = measure(spec, groups, dims, full, args.out, args.correctness_out, args.check, bw,
                    os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype)
     ok = True
     if args.check and groups.rank == 0:
