@@ -52,6 +52,8 @@ def parse() -> argparse.Namespace:
                     help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split); "
                          "qwen35: the Gated DeltaNet hybrid block stack (tp and attention data-parallel)")
     ap.add_argument("--sg-batch", type=int, default=256, help="mamba2_sg: live requests per step")
+    ap.add_argument("--ar-impl", choices=["nccl", "p2p"], default="nccl",
+                    help="N>1 decode all-reduces: NCCL, or the peer-memory all-reduce fused with residual and norm")
     return ap.parse_args()
 
 
@@ -265,7 +267,7 @@ def build_layer(args, mode, groups, dims, full):
     ctx = make_decode_ctx(args.batch, args.ctx, 16, dev)
     st = alloc_and_fill(plan, dims, ctx, args.seed, dev, ssm_dtype=torch.float32)
     h = input_hidden(args.seed, args.batch, dims.hidden, dev)
-    layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev)
+    layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev, ar_impl=getattr(args, "ar_impl", "nccl"))
     return layer, h
 
 
@@ -413,6 +415,7 @@ def our_arm(args) -> None:
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
             "config": {**workload(args), "parallelism": best,
+                       "allreduce": "nccl" if world == 1 else args.ar_impl,
                        "recipes": {m: {k: round(v, 5) if isinstance(v, float) else v for k, v in x.items()}
                                    for m, x in results.items()}},
             "e2e": {"value": args.batch / e2e_ms * 1e3, "unit": UNIT, "h2d_bytes_per_step": nbytes_io,

@@ -290,6 +290,30 @@ int mmp_gdn_prefill(const void* q, int64_t q_t, int64_t q_h, const void* k, int6
                     void* out, int64_t o_t, int64_t o_h,
                     int nseq, int ntok, int nk, int nv, int dk, int dv, int lines, int* err, void* stream);
 
+/* ---- peer-memory all-reduce fused with the residual add and RMSNorm (decode-sized messages) ------------
+ * Replaces the NCCL all-reduce of the layer's partial sums (`ParallelHybridLayer._ar`, harness/layer.py:175-181)
+ * and the residual / pre-MLP norm after it (harness/layer.py:217-227) on ranks of one node.
+ *
+ * Buffers: every rank allocates mmp_ar_buffer_bytes(world, rows_max, H) bytes of zeroed device memory, exports it
+ * with mmp_ipc_export (MMP_IPC_BLOB_BYTES opaque bytes), exchanges the blobs with the other ranks (any host
+ * channel) and maps theirs with mmp_ipc_import; `bufs` is a device array of the world's buffer addresses in
+ * this process (own at index rank). mmp_ipc_release unmaps an imported buffer.
+ *
+ * mmp_ar_join: sum_out = resid + bf16(sum over ranks of part), and, with norm_w, norm_out = rmsnorm(sum_out) *
+ * norm_w. part / resid / sum_out / norm_out are [rows, H] bf16 with row strides (16-byte aligned rows; sum_out
+ * may alias resid; resid may be NULL). Every rank must make the same sequence of calls on its buffer (a device
+ * epoch counts them); results are bit-identical on every rank. A wait that runs out sets MMP_DEVERR_TIMEOUT in
+ * *err. world <= 8; rows <= rows_max. */
+#define MMP_IPC_BLOB_BYTES 72
+size_t mmp_ar_buffer_bytes(int world, int rows_max, int H);
+int mmp_ipc_export(const void* ptr, void* blob);
+int mmp_ipc_import(const void* blob, void** ptr_out);
+int mmp_ipc_release(void* ptr);
+int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_max,
+                const void* part, int64_t p_b, const void* resid, int64_t r_b,
+                void* sum_out, int64_t s_b, const void* norm_w, float eps, void* norm_out, int64_t n_b,
+                int rows, int H, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

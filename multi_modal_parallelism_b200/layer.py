@@ -246,10 +246,13 @@ class SwingMLP:
 
 class ParallelHybridLayer:
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
-                 ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True):
+                 ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True,
+                 ar_impl: str = "nccl"):
         """overlap_branches: on a rank holding both branches (fused projections), run the attention core on a
         side stream concurrently with the Mamba-2 core. `ctx` is a DecodeCtx (step() is one decode step) or a
-        PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer)."""
+        PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer). ar_impl "p2p": the
+        decode step's [B, H] all-reduces (mixer and MLP; not tp4's per-branch pair) run as the peer-memory
+        all-reduce fused with the residual add and the next norm (p2p.PeerAllReduce); prefill keeps NCCL."""
         self.plan, self.w, self.dims, self.groups, self.ctx = plan, w, dims, groups, ctx
         self.st = st
         self.overlap_branches = overlap_branches
@@ -298,6 +301,15 @@ class ParallelHybridLayer:
         self.h1 = mk() if self.has_mlp else self.out
         self.mix, self.part_a, self.part_s, self.mlp_part = mk(), mk(), mk(), mk()
         self.tp = groups.tp
+        if ar_impl not in ("nccl", "p2p"):
+            raise ValueError(f"ar_impl {ar_impl!r}: nccl or p2p")
+        self.ar_impl = ar_impl
+        self.p2p = None
+        if (ar_impl == "p2p" and world > 1 and collectives and not isinstance(ctx, PrefillCtx)
+                and self.mode != "tp4"):
+            from .p2p import PeerAllReduce
+
+            self.p2p = PeerAllReduce(groups.tp, groups.rank, ctx.rows, dims.hidden, device)  # collective
         self.overlap = self.fused and overlap_branches
         if self.overlap:
             self.s_side = torch.cuda.Stream(device=device)
@@ -340,6 +352,19 @@ class ParallelHybridLayer:
         t.end(name)
         return x
 
+    def _reduce_join(self, h: torch.Tensor, t: OpTimer) -> None:
+        """All-reduce self.mix over the layer's ranks, then h1 = h + mix (and the pre-MLP norm into yn)."""
+        if self.p2p is None:
+            self._ar(self.mix, "ar.mixer", t)
+            self._join(h, self.mix, t)
+            return
+        t.begin("ar.mixer")
+        if self.has_mlp:
+            self.p2p.join(self.mix, h, self.h1, self.w.ff_norm, self.dims.rms_eps, self.yn)
+        else:
+            self.p2p.join(self.mix, h, self.out)
+        t.end("ar.mixer")
+
     def _join(self, h: torch.Tensor, mix: torch.Tensor, t: OpTimer) -> None:
         """h1 = h + mix; with an MLP the sum is fused into the pre-MLP norm, which then writes yn."""
         t.begin("residual")
@@ -380,8 +405,7 @@ class ParallelHybridLayer:
                 K.gemm(self.mid_buf, self.w.w_out_cat, out=self.mix, alpha=dims.attn_out, **seg)
             t.end("mixer.outproj")
             if mode == "tp4_fused":
-                self._ar(self.mix, "ar.mixer", t)
-                self._join(h, self.mix, t)
+                self._reduce_join(h, t)
                 y_ready = self.has_mlp
         elif mode == "tp1":
             self.attn.decode(x, t, out=self.h1, addend=h, x_scale=dims.attn_in)
@@ -395,8 +419,7 @@ class ParallelHybridLayer:
         elif mode == "tp4_fused":
             self.attn.decode(x, t, out=self.mix, x_scale=dims.attn_in)
             self.ssm.decode(x, t, out=self.mix, addend=self.mix, x_scale=dims.ssm_in)
-            self._ar(self.mix, "ar.mixer", t)
-            self._join(h, self.mix, t)
+            self._reduce_join(h, t)
             y_ready = self.has_mlp
         elif mode == "tp4_streams":
             cur = torch.cuda.current_stream(self.device)
@@ -409,16 +432,14 @@ class ParallelHybridLayer:
             cur.wait_stream(self.s_attn)
             cur.wait_stream(self.s_ssm)
             K.add(self.part_a, self.part_s, self.mix)
-            self._ar(self.mix, "ar.mixer", t)
-            self._join(h, self.mix, t)
+            self._reduce_join(h, t)
             y_ready = self.has_mlp
         else:  # split{a}{m}
             if self.attn is not None:
                 self.attn.decode(x, t, out=self.mix, x_scale=dims.attn_in)
             else:
                 self.ssm.decode(x, t, out=self.mix, x_scale=dims.ssm_in)
-            self._ar(self.mix, "ar.mixer", t)
-            self._join(h, self.mix, t)
+            self._reduce_join(h, t)
             y_ready = self.has_mlp
         if not self.has_mlp:
             return self.out
@@ -430,6 +451,11 @@ class ParallelHybridLayer:
             self.mlp.forward(self.yn, t, out=self.out, addend=self.h1)
         else:
             self.mlp.forward(self.yn, t, out=self.mlp_part)
+            if self.p2p is not None:
+                t.begin("ar.mlp")
+                self.p2p.join(self.mlp_part, self.h1, self.out)
+                t.end("ar.mlp")
+                return self.out
             self._ar(self.mlp_part, "ar.mlp", t)
             t.begin("residual2")
             K.add(self.h1, self.mlp_part, self.out)

@@ -1,0 +1,80 @@
+"""Peer-memory all-reduce over NVLink for decode-sized [rows, H] partial sums (libmmp_b200's mmp_ar_join): a
+one-shot all-reduce fused with the residual add and the next RMSNorm, replacing an NCCL all-reduce plus the
+norm kernel after it (the reference's `ParallelHybridLayer._ar`, `harness/layer.py:175-181`, and the residual /
+pre-MLP norm, `harness/layer.py:217-227`).
+
+Setup is collective over the group: every rank allocates a zeroed buffer, exports it as a CUDA IPC blob, the blobs
+are exchanged with `torch.distributed.all_gather_object`, and each rank maps the others'. Calls are then plain
+kernel launches (graph-capturable); every rank must make the same sequence of calls.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .dist import Coordinator
+
+BLOB_BYTES = 72
+
+
+class PeerAllReduce:
+    def __init__(self, group: Coordinator, global_rank: int, rows_max: int, hidden: int, device: torch.device):
+        """Collective over `group` (every member calls it, in the same order as its other collectives)."""
+        if not 1 <= group.world_size <= 8:
+            raise ValueError(f"PeerAllReduce: {group.world_size} ranks (1..8 on one node)")
+        self.world, self.rank = group.world_size, group.ranks.index(global_rank)
+        self.rows_max, self.hidden, self.device = rows_max, hidden, device
+        nbytes = int(_lib.lib().mmp_ar_buffer_bytes(self.world, rows_max, hidden))
+        self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+        torch.cuda.synchronize(device)  # the zeros must be in place before any peer can write
+        blob = ctypes.create_string_buffer(BLOB_BYTES)
+        _lib.call("mmp_ipc_export", self.buf.data_ptr(), blob, kernels=0)
+        blobs: list = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(blobs, blob.raw, group=group.pg)
+        else:
+            blobs = [blob.raw]
+        self._imported: list[int] = []
+        ptrs = []
+        for q, b in enumerate(blobs):
+            if q == self.rank:
+                ptrs.append(self.buf.data_ptr())
+                continue
+            out = ctypes.c_void_p()
+            _lib.call("mmp_ipc_import", ctypes.create_string_buffer(b, BLOB_BYTES), ctypes.byref(out), kernels=0)
+            ptrs.append(int(out.value))
+            self._imported.append(int(out.value))
+        self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        if self.world > 1:
+            dist.barrier(group=group.pg)
+
+    def join(self, part: torch.Tensor, resid: torch.Tensor | None, sum_out: torch.Tensor,
+             norm_w: torch.Tensor | None = None, eps: float = 0.0, norm_out: torch.Tensor | None = None) -> torch.Tensor:
+        """sum_out = resid + all-reduce(part) (bf16); with norm_w also norm_out = rmsnorm(sum_out) * norm_w.
+        Returns norm_out when given, else sum_out."""
+        from .kernels import _rowmajor, _stream, error_word
+
+        rows, H = part.shape
+        if H != self.hidden or rows > self.rows_max:
+            raise ValueError(f"PeerAllReduce.join: [{rows}, {H}] does not fit [{self.rows_max}, {self.hidden}]")
+        for t in (part, resid, sum_out, norm_w, norm_out):
+            if t is not None and (t.dtype != torch.bfloat16 or not t.is_cuda):
+                raise ValueError("PeerAllReduce.join: bf16 CUDA tensors expected")
+        if (norm_w is None) != (norm_out is None):
+            raise ValueError("PeerAllReduce.join: norm_w and norm_out go together")
+        p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        ld = lambda n, t: 0 if t is None else _rowmajor(n, t)  # noqa: E731
+        _lib.call("mmp_ar_join", self.bufs.data_ptr(), self.rank, self.world, self.rows_max,
+                  part.data_ptr(), ld("part", part), p(resid), ld("resid", resid), sum_out.data_ptr(),
+                  ld("sum_out", sum_out), p(norm_w), float(eps), p(norm_out), ld("norm_out", norm_out),
+                  rows, H, error_word(part.device).data_ptr(), _stream(part))
+        return norm_out if norm_out is not None else sum_out
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after the last call has finished on this rank)."""
+        for ptr in self._imported:
+            _lib.call("mmp_ipc_release", ptr, kernels=0)
+        self._imported = []

@@ -4,7 +4,8 @@ correctness check. Same flags as the reference's `harness/run.py:41-70`:
   torchrun --standalone --nproc-per-node=4 -m multi_modal_parallelism_b200.run --mode split22 \\
       --batch 16 --ctx 8192 --variant graph --check --out results/raw/dev.csv
 
-Extensions: any split{a}{m} mode, --ssm-dtype (fp32 default), bundled dims names for --dims-yaml. `--k model`
+Extensions: any split{a}{m} mode, --ssm-dtype (fp32 default), --ar-impl (nccl / p2p), bundled dims names for
+--dims-yaml. `--k model`
 takes the swing cut the byte model (model.py) predicts fastest under the microbench tables in --bw. The
 reference's other templates (parallel-residual, sequential hybrid) are not part of this build.
 """
@@ -65,6 +66,8 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--check", action="store_true")
     ap.add_argument("--no-collectives", action="store_true", help="diagnostic: per-rank compute only (outputs wrong)")
     ap.add_argument("--ssm-dtype", choices=["fp32", "bf16"], default="fp32")
+    ap.add_argument("--ar-impl", choices=["nccl", "p2p"], default="nccl",
+                    help="p2p: decode all-reduces over NVLink peer memory, fused with the residual and norm")
     args = ap.parse_args(argv)
 
     if args.k in ("neutral", "model"):
@@ -80,7 +83,7 @@ def main(argv: list[str] | None = None) -> int:
     ssm_dtype = torch.float32 if args.ssm_dtype == "fp32" else torch.bfloat16
     bw = BwTables.from_csv(args.bw) if args.bw and os.path.exists(args.bw) else None
     rows = measure(spec, groups, dims, full, args.out, args.correctness_out, args.check, bw,
-                   os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype)
+                   os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype, ar_impl=args.ar_impl)
     ok = True
     if args.check and groups.rank == 0:
         with open(args.correctness_out) as f:

@@ -120,3 +120,29 @@ def test_mamba2_continuous_batching_layouts(world, mode):
     if ngpu() < world:
         pytest.skip(f"needs {world} GPUs")
     run_script_check(world, "_mamba2_ranks.py", "mamba2-check", mode)
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_allreduce(world):
+    """The peer-memory all-reduce fused with residual and norm: bit-exact sums, graph replays equal eager."""
+    if ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), str(ROOT / "tests" / "_p2p_ranks.py")]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "30", "300", *cmd], cwd=ROOT, env=env, capture_output=True, text=True)
+    out = r.stdout + r.stderr
+    m = re.search(r"\[p2p-check\].*pass=(True|False)", out)
+    assert r.returncode == 0 and m and m.group(1) == "True", out[-3000:]
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world,mode", [(2, "split11"), (2, "tp4_fused"), (4, "split22"), (8, "split44")])
+def test_layouts_with_peer_allreduce(world, mode, tmp_path):
+    """Every rank of the layer with the peer-memory all-reduce: bitwise equal, within tolerance of fp32."""
+    if ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_check(world, mode, tmp_path, ("--ar-impl", "p2p"))
