@@ -11,6 +11,7 @@ from __future__ import annotations
 
 import json
 import subprocess
+from pathlib import Path
 import time
 import uuid
 
@@ -39,6 +40,40 @@ def gpu_env(local_rank: int) -> dict:
         return {"sm_clock_mhz": int(q[0]), "temp_c": int(q[1]), "power_w": float(q[2]), "util_pct": int(q[3])}
     except Exception:
         return {"sm_clock_mhz": -1, "temp_c": -1, "power_w": -1.0, "util_pct": -1}
+
+
+PEAKS = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def hbm_peak_gbs() -> float:
+    """The measured copy bandwidth of this pool's B200s (MEASURED_PEAKS.json at the repository root), else an
+    earlier measurement on the same pool."""
+    try:
+        return float(json.loads(PEAKS.read_text())["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS
+
+
+def step_hbm_bytes(plan, dims: FalconH1Dims, B: int, c: int, state_bytes: int = 4) -> int:
+    """Algorithmic HBM bytes of one decode step on this rank (its floor at the copy bandwidth): every weight once,
+    the keys and values of all c + 1 positions of its KV heads, its SSM state lines read and written at
+    `state_bytes` per element, its conv state lines read and written."""
+    H, hd, bf = dims.hidden, dims.head_dim, 2
+    total = 0
+    if plan.attn is not None:
+        nq, nkv = len(plan.attn.q_heads), len(plan.attn.kv_heads)
+        total += (nq + 2 * nkv) * hd * H * bf + H * nq * hd * bf  # QKV and o-projection weights
+        total += 2 * B * (c + 1) * nkv * hd * bf  # keys + values
+    if plan.ssm is not None:
+        s = plan.ssm
+        ch = len(s.heads) * dims.mamba_head_dim
+        conv_rows = sum(r.stop - r.start for r in s.conv_rows)
+        total += sum(s.local_in_rows) * H * bf + H * ch * bf  # in- and out-projection weights
+        total += 2 * B * ch * dims.d_state * state_bytes  # state lines read + written
+        total += 2 * B * (dims.d_conv - 1) * conv_rows * bf  # conv lines read + written
+    total += 3 * plan.mlp.active_rows * H * bf  # gate, up, down
+    return total
 
 
 def resolve_k(spec: RunSpec, dims: FalconH1Dims, world: int, bw: BwTables | None = None) -> tuple[int, int | None, str]:
@@ -86,6 +121,8 @@ def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, t
     pred = {v: predict_rank(plan, dims, spec.batch, spec.ctx, bw, v, spec.kv_block) for v in ("eager", "graph")} \
         if bw is not None else {}
     op_bytes = bytes_per_op(plan, dims, spec.batch, spec.ctx)
+    step_bytes = step_hbm_bytes(plan, dims, spec.batch, spec.ctx, 4 if ssm_dtype == torch.float32 else 2)
+    peak = hbm_peak_gbs()
     rw = shard_to_device(full, plan, dims, device)
     ctx = make_decode_ctx(spec.batch, spec.ctx, spec.kv_block, device)
     st = alloc_and_fill(plan, dims, ctx, spec.seed, device, ssm_dtype=ssm_dtype)
@@ -130,7 +167,11 @@ def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, t
             rep_id = rep + spec.repeat_offset
             p = pred.get(variant, {})
             for op, s in stats.items():
-                extra = {"tokens_per_s": spec.batch / s["median_ms"] * 1e3} if op == "step" else {}
+                extra = {}
+                if op == "step":
+                    gbs = step_bytes / (s["median_ms"] * 1e6)
+                    extra = {"tokens_per_s": spec.batch / s["median_ms"] * 1e3, "bytes": step_bytes,
+                             "achieved_gbs": gbs, "roofline_frac": gbs / peak}
                 rows.append(dict(base, variant=variant, repeat=rep_id, rank=rank, op=op, **s, **env, **extra,
                                  ms_pred=p.get(op, ""), bytes_pred=op_bytes.get(op, "")))
             rows.append(dict(base, variant=variant, repeat=rep_id, rank=rank, op="step_wall", n=spec.n_iter,
