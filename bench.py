@@ -52,7 +52,7 @@ def parse() -> argparse.Namespace:
                     help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split); "
                          "qwen35: the Gated DeltaNet hybrid block stack (tp and attention data-parallel)")
     ap.add_argument("--sg-batch", type=int, default=256, help="mamba2_sg: live requests per step")
-    ap.add_argument("--ar-impl", choices=["nccl", "p2p"], default="nccl",
+    ap.add_argument("--ar-impl", choices=["nccl", "p2p", "p2p_fused"], default="nccl",
                     help="N>1 decode all-reduces: NCCL, or the peer-memory all-reduce fused with residual and norm")
     return ap.parse_args()
 

@@ -303,16 +303,25 @@ int mmp_gdn_prefill(const void* q, int64_t q_t, int64_t q_h, const void* k, int6
  * norm_w. part / resid / sum_out / norm_out are [rows, H] bf16 with row strides (16-byte aligned rows; sum_out
  * may alias resid; resid may be NULL). Every rank must make the same sequence of calls on its buffer (a device
  * epoch counts them); results are bit-identical on every rank. A wait that runs out sets MMP_DEVERR_TIMEOUT in
- * *err. world <= 8; rows <= rows_max. */
+ * *err. world <= 8; rows <= rows_max. pushed = 1: the partial was produced by mmp_gemm_bf16_push on every rank
+ * (already in the buffers; `part` is ignored), so this call only waits, sums and normalises.
+ *
+ * mmp_gemm_bf16_push: the decode GEMM (M <= 256 rows; arguments as mmp_gemm_bf16_seg, no addend) whose output
+ * tiles go straight into slot `rank` of every rank's all-reduce buffer instead of a local array, each CTA adding
+ * the number of elements it wrote to its counter on every rank: the transfer over NVLink overlaps the GEMM. The
+ * mmp_ar_join(pushed = 1) that follows on the same buffer completes the all-reduce. N must equal the buffer's H. */
 #define MMP_IPC_BLOB_BYTES 72
 size_t mmp_ar_buffer_bytes(int world, int rows_max, int H);
 int mmp_ipc_export(const void* ptr, void* blob);
 int mmp_ipc_import(const void* blob, void** ptr_out);
 int mmp_ipc_release(void* ptr);
-int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_max,
+int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_max, int pushed,
                 const void* part, int64_t p_b, const void* resid, int64_t r_b,
                 void* sum_out, int64_t s_b, const void* norm_w, float eps, void* norm_out, int64_t n_b,
                 int rows, int H, int* err, void* stream);
+int mmp_gemm_bf16_push(const void* a, int64_t lda, const void* w, int64_t ldw, int M, int N, int K, float alpha,
+                       int k_seg, float alpha2, const float* colscale, const uint64_t* bufs, int rank, int world,
+                       int rows_max, int* err, void* stream);
 
 #ifdef __cplusplus
 }

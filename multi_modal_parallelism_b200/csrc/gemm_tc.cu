@@ -20,6 +20,7 @@
 #include <mutex>
 
 #include "mmp_common.cuh"
+#include "p2p_layout.cuh"
 #include "tc_common.cuh"
 
 namespace cg = cooperative_groups;
@@ -39,6 +40,7 @@ struct TcParams {
   const float* colscale;
   const bf16* addend; int64_t ldd;
   int* err;
+  PeerBufs push;  // decode output pushed into every rank's all-reduce buffer (push.bufs null: written to out)
 };
 
 template <int BN, int STAGES>
@@ -90,13 +92,29 @@ __device__ __forceinline__ void store8(const TcParams& P, int r, int c0, const f
   for (int k = 0; k < n; ++k) dst[k] = f2bf(vals[k] + (add ? bf2f(add[k]) : 0.f));
 }
 
+// The same 8 output elements written into slot `rank` (parity par) of every rank's all-reduce buffer.
+__device__ __forceinline__ void push8(const TcParams& P, int r, int c0, const float* vals, int n, int par) {
+  const PeerBufs& B = P.push;
+  if (n == 8 && (c0 & 7) == 0 && (B.H & 7) == 0) {
+    const uint4 v = make_uint4(pack_bf16x2(vals[0], vals[1]), pack_bf16x2(vals[2], vals[3]), pack_bf16x2(vals[4], vals[5]),
+                               pack_bf16x2(vals[6], vals[7]));
+#pragma unroll 1
+    for (int q = 0; q < B.world; ++q)
+      *reinterpret_cast<uint4*>(ar_slot_elem(B.bufs[q], B, par, B.rank, r, c0)) = v;
+    return;
+  }
+#pragma unroll 1
+  for (int q = 0; q < B.world; ++q)
+    for (int k = 0; k < n; ++k) *reinterpret_cast<bf16*>(ar_slot_elem(B.bufs[q], B, par, B.rank, r, c0 + k)) = f2bf(vals[k]);
+}
+
 // Sum `ns` staged fp32 blocks of tile rows [row0, row0 + nrows) (block q at src + q * src_stride; swapped
 // tiles column-major [BN][ld], plain tiles row-major [nrows][ld]) and write them with the addend. Swapped:
 // 8 consecutive tile rows are 8 consecutive output columns of one output row; plain: 8 consecutive columns of
 // one tile row. Consecutive threads take consecutive chunks: 16-byte, coalesced, bank-conflict-free.
-template <bool TRANS, int BN>
+template <bool TRANS, int BN, bool PUSH = false>
 __device__ __forceinline__ void finish_tile(const TcParams& P, const float* src, int ns, int src_stride, int ld,
-                                            int row0, int nrows, int m0, int n0) {
+                                            int row0, int nrows, int m0, int n0, int par = 0) {
   if (nrows <= 0) return;
   if constexpr (TRANS) {
     // source blocks are column-major [BN][ld]: tile rows g*8 .. g*8+7 of column c are two float4
@@ -115,7 +133,8 @@ __device__ __forceinline__ void finish_tile(const TcParams& P, const float* src,
         const float4 x = b[0], y = b[1];
         v[0] += x.x; v[1] += x.y; v[2] += x.z; v[3] += x.w; v[4] += y.x; v[5] += y.y; v[6] += y.z; v[7] += y.w;
       }
-      store8(P, orow, ocol, v, n);
+      if constexpr (PUSH) push8(P, orow, ocol, v, n, par);
+      else store8(P, orow, ocol, v, n);
     }
   } else {
     constexpr int CH = BN / 8;
@@ -138,7 +157,7 @@ __device__ __forceinline__ void finish_tile(const TcParams& P, const float* src,
   }
 }
 
-template <int BN, int STAGES, bool TRANS, bool CLUSTER>
+template <int BN, int STAGES, bool TRANS, bool CLUSTER, bool PUSH = false>
 __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                                                              const __grid_constant__ CUtensorMap tmB,
                                                              const TcParams P) {
@@ -289,6 +308,16 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
   if (tid == 0 && *abort_flag) {
     for (int i = max(0, issued - STAGES); i < issued; ++i) mbar_drain(full_bar(i % STAGES), (i / STAGES) & 1);
   }
+  // pushed output: this call's parity, from the all-reduce epoch (written by the previous call's join kernel,
+  // which completed before this kernel's dependency wait returned)
+  __shared__ int s_par;
+  if constexpr (PUSH) {
+    if (tid == 0) {
+      const PeerBufs& B = P.push;
+      const uint32_t ep = *reinterpret_cast<volatile const uint32_t*>(B.bufs[B.rank] + ar_epoch_off(B.world, B.rows_max, B.H));
+      s_par = static_cast<int>((ep + 1u) & 1u);
+    }
+  }
   __syncthreads();  // the ring is free: every MMA finished (done barrier), every copy landed (drain)
 
   // Stage the scaled fp32 tile in shared memory (tile row r = this thread's TMEM lane): alpha / alpha2 per K
@@ -357,11 +386,29 @@ __global__ void __launch_bounds__(TTHREADS, 1) gemm_tc_kernel(const __grid_const
       asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
     }
     const bool got = mbar_wait(recv_bar, 0, abort_flag, P.err);
-    if (got) finish_tile<TRANS, BN>(P, recv, ns, BN * rp, rp, own_row0, own_rows, m0, n0);
+    if (got) finish_tile<TRANS, BN, PUSH>(P, recv, ns, BN * rp, rp, own_row0, own_rows, m0, n0, PUSH ? s_par : 0);
     if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");  // our blocks have left
   } else {
     __syncthreads();
-    finish_tile<TRANS, BN>(P, stage, 1, 0, TRANS ? L::TLD : L::SLD, 0, TBM, m0, n0);
+    finish_tile<TRANS, BN, PUSH>(P, stage, 1, 0, TRANS ? L::TLD : L::SLD, 0, TBM, m0, n0, PUSH ? s_par : 0);
+  }
+  if constexpr (PUSH) {
+    // every output element this CTA owns is in every rank's buffer: count them on every rank (release), so
+    // the join kernel that follows knows when this rank's partial has fully arrived
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+      const PeerBufs& B = P.push;
+      const int cols = max(0, min(own_rows, P.a_rows - (m0 + own_row0)));
+      const int rows = max(0, min(BN, P.b_rows - n0));
+      const uint64_t cnt = static_cast<uint64_t>(cols) * static_cast<uint64_t>(rows);
+      if (cnt) {
+        for (int q = 0; q < B.world; ++q) {
+          uint64_t* c = reinterpret_cast<uint64_t*>(B.bufs[q] + ar_counters_off(B.world, B.rows_max, B.H)) + B.rank;
+          asm volatile("red.release.sys.global.add.u64 [%0], %1;\n" ::"l"(c), "l"(cnt) : "memory");
+        }
+      }
+    }
   }
 
   tc_fence_before();
@@ -593,10 +640,10 @@ int make_map(CUtensorMap* map, const void* base, int rows, int K, int64_t ld, in
 
 int g_tc_sms = 0;
 
-template <int BN, int STAGES, bool TRANS, bool CLUSTER>
+template <int BN, int STAGES, bool TRANS, bool CLUSTER, bool PUSH = false>
 int launch_tc(const CUtensorMap& ma, const CUtensorMap& mb, const TcParams& P, dim3 grid, int split, cudaStream_t s) {
   using L = TcLayout<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, TRANS, CLUSTER>;
+  auto kern = gemm_tc_kernel<BN, STAGES, TRANS, CLUSTER, PUSH>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -632,6 +679,40 @@ int launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const TcPara
   cudaError_t e = mmp::launch_kind(1, kern, dim3(grid), dim3(PTHREADS), L::DYN, s, nullptr, 0, ma, mb, P, tiles_n, ntiles);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "gemm_tc: launch failed: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_gemm_bf16_tc");
+}
+
+// Decode (M <= 256): swap-AB, A = weight rows (the 128-row M side of the MMA), B = the activation rows (N);
+// K split over a cluster when the output tiles cannot fill the GPU. PUSH: output tiles go to every rank's
+// all-reduce buffer (P.push) instead of P.out.
+template <bool PUSH>
+int decode_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, int M, int N, int K, TcParams& P, int k_tiles,
+                cudaStream_t s) {
+  int rc;
+  CUtensorMap ma, mb;
+  const int bn = M <= 64 ? 64 : 128;
+  P.a_rows = N;
+  P.b_rows = M;
+  if ((rc = make_map(&ma, w, N, K, ldw, TBM)) || (rc = make_map(&mb, a, M, K, lda, bn))) return rc;
+  const int tiles = (N + TBM - 1) / TBM;
+  const int ntiles_b = (M + bn - 1) / bn;
+  const int slots = (bn == 64 ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
+  int split = 1;
+  if (tiles * ntiles_b < slots) split = std::min(8, std::max(1, std::min(slots / (tiles * ntiles_b), k_tiles / 2)));
+  // the staged and received owner blocks must fit in the ring
+  auto fits = [&](int ns) {
+    return ns == 1 || (bn == 64 ? TcLayout<64, 4>::split_fits(ns) : TcLayout<128, 5>::split_fits(ns));
+  };
+  int ktps = (k_tiles + split - 1) / split;
+  split = (k_tiles + ktps - 1) / ktps;
+  while (split > 1 && !fits(split)) {
+    ktps = (k_tiles + split - 2) / (split - 1);
+    split = (k_tiles + ktps - 1) / ktps;
+  }
+  P.k_tiles_per_split = ktps;
+  dim3 grid(ntiles_b, tiles, split);
+  const bool cl = split > 1;
+  if (bn == 64) return cl ? launch_tc<64, 4, true, true, PUSH>(ma, mb, P, grid, split, s) : launch_tc<64, 4, true, false, PUSH>(ma, mb, P, grid, 1, s);
+  return cl ? launch_tc<128, 5, true, true, PUSH>(ma, mb, P, grid, split, s) : launch_tc<128, 5, true, false, PUSH>(ma, mb, P, grid, 1, s);
 }
 
 }  // namespace
@@ -670,33 +751,7 @@ extern "C" int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int6
   TcParams P{0, 0, K, k_tiles, static_cast<bf16*>(out), ldo, alpha, k_seg_tile, alpha2, colscale,
              static_cast<const bf16*>(addend), ldd, err};
   CUtensorMap ma, mb;
-  if (M <= 256) {
-    // decode: swap-AB, A = weight rows (the 128-row M side of the MMA), B = the activation rows (N)
-    const int bn = M <= 64 ? 64 : 128;
-    P.a_rows = N;
-    P.b_rows = M;
-    if ((rc = make_map(&ma, w, N, K, ldw, TBM)) || (rc = make_map(&mb, a, M, K, lda, bn))) return rc;
-    const int tiles = (N + TBM - 1) / TBM;
-    const int ntiles_b = (M + bn - 1) / bn;
-    const int slots = (bn == 64 ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
-    int split = 1;
-    if (tiles * ntiles_b < slots) split = std::min(8, std::max(1, std::min(slots / (tiles * ntiles_b), k_tiles / 2)));
-    // the staged and received owner blocks must fit in the ring
-    auto fits = [&](int ns) {
-      return ns == 1 || (bn == 64 ? TcLayout<64, 4>::split_fits(ns) : TcLayout<128, 5>::split_fits(ns));
-    };
-    int ktps = (k_tiles + split - 1) / split;
-    split = (k_tiles + ktps - 1) / ktps;
-    while (split > 1 && !fits(split)) {
-      ktps = (k_tiles + split - 2) / (split - 1);
-      split = (k_tiles + ktps - 1) / ktps;
-    }
-    P.k_tiles_per_split = ktps;
-    dim3 grid(ntiles_b, tiles, split);
-    const bool cl = split > 1;
-    if (bn == 64) return cl ? launch_tc<64, 4, true, true>(ma, mb, P, grid, split, s) : launch_tc<64, 4, true, false>(ma, mb, P, grid, 1, s);
-    return cl ? launch_tc<128, 5, true, true>(ma, mb, P, grid, split, s) : launch_tc<128, 5, true, false>(ma, mb, P, grid, 1, s);
-  }
+  if (M <= 256) return decode_gemm<false>(a, lda, w, ldw, M, N, K, P, k_tiles, s);
   // large M (prefill): A = activations, B = weight rows; a persistent CTA per SM over 128 x 256 output tiles
   // (128 x 128 when two K segments need two accumulators per tile)
   P.a_rows = M;
@@ -709,4 +764,30 @@ extern "C" int mmp_gemm_bf16_seg(const void* a, int64_t lda, const void* w, int6
   if (ntiles > (1LL << 30)) return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_tc: M=%d too large", M);
   if (two) return launch_persistent<128, 6, 2>(ma, mb, P, tiles_n, static_cast<int>(ntiles), s);
   return launch_persistent<256, 4, 1>(ma, mb, P, tiles_n, static_cast<int>(ntiles), s);
+}
+
+extern "C" int mmp_gemm_bf16_push(const void* a, int64_t lda, const void* w, int64_t ldw, int M, int N, int K,
+                                  float alpha, int k_seg, float alpha2, const float* colscale, const uint64_t* bufs,
+                                  int rank, int world, int rows_max, int* err, void* stream) {
+  if (M == 0 || N == 0) return MMP_OK;
+  if (!a || !w || !bufs) return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_push: null pointer");
+  if (M < 0 || M > 256 || M > rows_max || N < 0 || N % 8 || K <= 0 || K % 8 || lda % 8 || ldw % 8 || !aligned16(a) ||
+      !aligned16(w) || lda < K || ldw < K || world < 1 || world > 8 || rank < 0 || rank >= world)
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_push: M=%d N=%d K=%d rows_max=%d rank=%d world=%d "
+                         "(decode rows only; multiples of 8; 16-byte aligned)", M, N, K, rows_max, rank, world);
+  if (k_seg < K && (k_seg <= 0 || k_seg % TBK))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_gemm_bf16_push: k_seg %d must be a positive multiple of %d", k_seg, TBK);
+  int rc = get_encoder();
+  if (rc != MMP_OK) return rc;
+  if (g_tc_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_tc_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_tc_sms <= 0) g_tc_sms = 148;
+  }
+  const int k_tiles = (K + TBK - 1) / TBK;
+  const int k_seg_tile = k_seg < K ? k_seg / TBK : k_tiles;
+  TcParams P{0, 0, K, k_tiles, nullptr, N, alpha, k_seg_tile, alpha2, colscale, nullptr, 0, err,
+             PeerBufs{bufs, rank, world, rows_max, N}};
+  return decode_gemm<true>(a, lda, w, ldw, M, N, K, P, k_tiles, static_cast<cudaStream_t>(stream));
 }

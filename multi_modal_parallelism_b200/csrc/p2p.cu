@@ -15,12 +15,18 @@
 // rank order (every rank computes bit-identical results), adds the residual and normalises. The grid is at most
 // one CTA per SM (CTA c owns rows c, c + grid, ...), so all CTAs are resident together.
 // Waits give up after a bounded number of polls: the kernel then sets MMP_DEVERR_TIMEOUT and skips the sum.
+//
+// Fused form (`pushed`): the decode GEMM that produced the partial already wrote its output tiles into slot
+// `rank` of every rank's buffer and added the number of elements it wrote to its counter on every rank
+// (gemm_tc.cu), so the transfer overlapped the GEMM; this kernel then only waits until every source's counter
+// reaches the cumulative target (rows x H per call), sums and normalises.
 #include <cuda.h>
 
 #include <map>
 #include <mutex>
 
 #include "mmp_common.cuh"
+#include "p2p_layout.cuh"
 
 namespace mmp {
 namespace {
@@ -33,6 +39,7 @@ struct ArJoinParams {  // element strides
   const uint64_t* bufs;    // [world] base address of every rank's buffer in this process
   int rank, world;
   int rows, H, rows_max;
+  int pushed;              // 1: the producing GEMM already pushed the partial (wait on the counters)
   const bf16* part; int64_t p_b;      // local partial [rows, H]
   const bf16* resid; int64_t r_b;     // residual [rows, H] or null
   bf16* sum_out; int64_t s_b;         // residual + all-reduced partials [rows, H]
@@ -41,15 +48,22 @@ struct ArJoinParams {  // element strides
   int* err;
 };
 
-__host__ __device__ inline size_t slots_bytes(int world, int rows_max, int H) {
-  return 2ull * world * rows_max * H * sizeof(uint16_t);
-}
-
 __device__ __forceinline__ uint32_t* flag_ptr(uint64_t base, const ArJoinParams& P, int row, int src) {
-  return reinterpret_cast<uint32_t*>(base + slots_bytes(P.world, P.rows_max, P.H)) + row * P.world + src;
+  return reinterpret_cast<uint32_t*>(base + ar_flags_off(P.world, P.rows_max, P.H)) + row * P.world + src;
 }
 __device__ __forceinline__ uint32_t* epoch_ptr(uint64_t base, const ArJoinParams& P) {
-  return reinterpret_cast<uint32_t*>(base + slots_bytes(P.world, P.rows_max, P.H)) + P.rows_max * P.world;
+  return reinterpret_cast<uint32_t*>(base + ar_epoch_off(P.world, P.rows_max, P.H));
+}
+__device__ __forceinline__ uint64_t* counter_ptr(uint64_t base, const ArJoinParams& P, int src) {
+  return reinterpret_cast<uint64_t*>(base + ar_counters_off(P.world, P.rows_max, P.H)) + src;
+}
+__device__ __forceinline__ uint64_t* target_ptr(uint64_t base, const ArJoinParams& P) {
+  return reinterpret_cast<uint64_t*>(base + ar_target_off(P.world, P.rows_max, P.H));
+}
+__device__ __forceinline__ uint64_t ld_acquire_sys64(const uint64_t* p) {
+  uint64_t v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -126,10 +140,14 @@ __global__ void __launch_bounds__(AR_THREADS) ar_join_kernel(const ArJoinParams 
   __shared__ float red[32];
   __shared__ int s_abort;
   __shared__ uint32_t s_epoch;
+  __shared__ uint64_t s_target;
   const int tid = threadIdx.x;
   const uint64_t own = P.bufs[P.rank];
   if (tid == 0) {
     s_epoch = *reinterpret_cast<volatile uint32_t*>(epoch_ptr(own, P)) + 1u;
+    // the pushed calls' cumulative element count per source (plain calls leave it alone)
+    s_target = *reinterpret_cast<volatile uint64_t*>(target_ptr(own, P)) +
+               (P.pushed ? static_cast<uint64_t>(P.rows) * P.H : 0ull);
     s_abort = 0;
   }
   __syncthreads();
@@ -137,19 +155,12 @@ __global__ void __launch_bounds__(AR_THREADS) ar_join_kernel(const ArJoinParams 
   const int par = e & 1;
   const size_t slot_elems = static_cast<size_t>(P.rows_max) * P.H;
 
-  // 1. push this rank's rows into slot `rank` of every rank's buffer (own included)
-  for (int row = blockIdx.x; row < P.rows; row += gridDim.x) push_row(P, row, par, slot_elems);
-  __threadfence_system();
-  __syncthreads();
-  // 2. raise the rows' flags on every rank; 3. wait for every rank's flags of the rows on this rank (bounded)
-  if (tid == 0) {
-    for (int row = blockIdx.x; row < P.rows; row += gridDim.x)
-      for (int q = 0; q < P.world; ++q) st_release_sys(flag_ptr(P.bufs[q], P, row, P.rank), e);
-    for (int row = blockIdx.x; row < P.rows && !s_abort; row += gridDim.x) {
-      for (int q = 0; q < P.world; ++q) {
-        const uint32_t* f = flag_ptr(own, P, row, q);
+  if (P.pushed) {
+    // the GEMM pushed every source's partial: wait until each source's element count reaches the target
+    if (tid == 0) {
+      for (int q = 0; q < P.world && !s_abort; ++q) {
         long long polls = 0;
-        while (static_cast<int>(ld_acquire_sys(f) - e) < 0) {
+        while (static_cast<int64_t>(ld_acquire_sys64(counter_ptr(own, P, q)) - s_target) < 0) {
           if (++polls > AR_MAX_POLLS) {
             s_abort = 1;
             flag_error(P.err, DEVERR_TIMEOUT);
@@ -157,7 +168,31 @@ __global__ void __launch_bounds__(AR_THREADS) ar_join_kernel(const ArJoinParams 
           }
           __nanosleep(128);
         }
-        if (s_abort) break;
+      }
+    }
+  } else {
+    // 1. push this rank's rows into slot `rank` of every rank's buffer (own included)
+    for (int row = blockIdx.x; row < P.rows; row += gridDim.x) push_row(P, row, par, slot_elems);
+    __threadfence_system();
+    __syncthreads();
+    // 2. raise the rows' flags on every rank; 3. wait for every rank's flags of the rows on this rank (bounded)
+    if (tid == 0) {
+      for (int row = blockIdx.x; row < P.rows; row += gridDim.x)
+        for (int q = 0; q < P.world; ++q) st_release_sys(flag_ptr(P.bufs[q], P, row, P.rank), e);
+      for (int row = blockIdx.x; row < P.rows && !s_abort; row += gridDim.x) {
+        for (int q = 0; q < P.world; ++q) {
+          const uint32_t* f = flag_ptr(own, P, row, q);
+          long long polls = 0;
+          while (static_cast<int>(ld_acquire_sys(f) - e) < 0) {
+            if (++polls > AR_MAX_POLLS) {
+              s_abort = 1;
+              flag_error(P.err, DEVERR_TIMEOUT);
+              break;
+            }
+            __nanosleep(128);
+          }
+          if (s_abort) break;
+        }
       }
     }
   }
@@ -182,6 +217,7 @@ __global__ void __launch_bounds__(AR_THREADS) ar_join_kernel(const ArJoinParams 
     __threadfence();
     if (atomicAdd(done, 1u) == gridDim.x - 1) {
       *done = 0;
+      if (P.pushed) *reinterpret_cast<volatile uint64_t*>(target_ptr(own, P)) = s_target;
       *reinterpret_cast<volatile uint32_t*>(epoch_ptr(own, P)) = e;
       __threadfence();
     }
@@ -209,11 +245,7 @@ int get_range_fn() {
 
 using namespace mmp;
 
-extern "C" size_t mmp_ar_buffer_bytes(int world, int rows_max, int H) {
-  // slots, then one flag word per (row, source), the epoch word and the done counter (16-byte padded)
-  const size_t flags = (static_cast<size_t>(rows_max) * world + 2) * sizeof(uint32_t);
-  return slots_bytes(world, rows_max, H) + (flags + 15) / 16 * 16;
-}
+extern "C" size_t mmp_ar_buffer_bytes(int world, int rows_max, int H) { return ar_total_bytes(world, rows_max, H); }
 
 extern "C" int mmp_ipc_export(const void* ptr, void* blob) {
   if (!ptr || !blob) return mmp_set_error(MMP_ERR_INVALID, "mmp_ipc_export: null pointer");
@@ -262,12 +294,12 @@ extern "C" int mmp_ipc_release(void* ptr) {
   return MMP_OK;
 }
 
-extern "C" int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_max,
+extern "C" int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_max, int pushed,
                            const void* part, int64_t p_b, const void* resid, int64_t r_b,
                            void* sum_out, int64_t s_b, const void* norm_w, float eps, void* norm_out, int64_t n_b,
                            int rows, int H, int* err, void* stream) {
   if (rows == 0) return MMP_OK;
-  if (!bufs || !part || !sum_out || (norm_w && !norm_out))
+  if (!bufs || (!pushed && !part) || !sum_out || (norm_w && !norm_out))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_ar_join: null pointer");
   if (world < 1 || world > AR_MAX_WORLD || rank < 0 || rank >= world || rows < 0 || rows > rows_max || H <= 0 || H % 8)
     return mmp_set_error(MMP_ERR_INVALID, "mmp_ar_join: bad sizes rank=%d world=%d rows=%d rows_max=%d H=%d", rank,
@@ -276,7 +308,7 @@ extern "C" int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_m
   if (!rows_ok(part, p_b) || !rows_ok(resid, r_b) || !rows_ok(sum_out, s_b) || !rows_ok(norm_out, n_b) ||
       (norm_w && !aligned16(norm_w)))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_ar_join: rows must be 16-byte aligned");
-  ArJoinParams P{bufs, rank, world, rows, H, rows_max,
+  ArJoinParams P{bufs, rank, world, rows, H, rows_max, pushed ? 1 : 0,
                  static_cast<const bf16*>(part), p_b, static_cast<const bf16*>(resid), r_b,
                  static_cast<bf16*>(sum_out), s_b, static_cast<const bf16*>(norm_w), eps,
                  static_cast<bf16*>(norm_out), n_b, err};

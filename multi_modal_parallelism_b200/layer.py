@@ -86,19 +86,25 @@ class AttentionBranch:
                       ctx.seqused_k, ctx.max_k, ctx.block_table, self.out, workspace=self.ws, splits=self.splits)
         t.end("attn.fa")
 
-    def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
+    def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
+                    push=None) -> torch.Tensor | None:
+        """push: a p2p.PeerAllReduce that receives the partial straight from the GEMM (nothing returned)."""
         t.begin("attn.oproj")
-        out = K.gemm(self.out2d, self.w.wo, out=out, alpha=self.dims.attn_out, addend=addend)
+        if push is not None:
+            push.gemm(self.out2d, self.w.wo, alpha=self.dims.attn_out)
+            out = None
+        else:
+            out = K.gemm(self.out2d, self.w.wo, out=out, alpha=self.dims.attn_out, addend=addend)
         t.end("attn.oproj")
         return out
 
     def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
-               x_scale: float = 1.0) -> torch.Tensor:
+               x_scale: float = 1.0, push=None) -> torch.Tensor | None:
         """x: [B, H] (already multiplied by attn_in unless x_scale carries it). Returns the o_proj partial
-        times attn_out (+ addend), written to `out`."""
+        times attn_out (+ addend), written to `out` (or pushed into `push`)."""
         self.project_in(x, t, x_scale)
         self.core(t)
-        return self.project_out(t, out, addend)
+        return self.project_out(t, out, addend, push)
 
 
 class _LocalOnly:
@@ -191,17 +197,22 @@ class SsmBranch:
                         self.norm_group, self.group_size, out=self.yn, sumsq=self.sumsq)
         t.end("ssm.norm")
 
-    def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None) -> torch.Tensor:
+    def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
+                    push=None) -> torch.Tensor | None:
         t.begin("ssm.outproj")
-        out = K.gemm(self.yn, self.w.wout, out=out, alpha=self.dims.ssm_out, addend=addend)
+        if push is not None:
+            push.gemm(self.yn, self.w.wout, alpha=self.dims.ssm_out)
+            out = None
+        else:
+            out = K.gemm(self.yn, self.w.wout, out=out, alpha=self.dims.ssm_out, addend=addend)
         t.end("ssm.outproj")
         return out
 
     def decode(self, x: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
-               x_scale: float = 1.0) -> torch.Tensor:
+               x_scale: float = 1.0, push=None) -> torch.Tensor | None:
         self.project_in(x, t, x_scale)
         self.core(t)
-        return self.project_out(t, out, addend)
+        return self.project_out(t, out, addend, push)
 
 
 class SwingMLP:
@@ -228,7 +239,7 @@ class SwingMLP:
         return m.n_fixed + (self.k if m.role == "attn" else 2 * m.w - self.k)
 
     def forward(self, y: torch.Tensor, t: OpTimer, out: torch.Tensor | None = None,
-                addend: torch.Tensor | None = None) -> torch.Tensor:
+                addend: torch.Tensor | None = None, push=None) -> torch.Tensor | None:
         w, n, B = self.w, self.n_active, y.shape[0]
         g, u = self.g[:B, :n], self.u[:B, :n]
         t.begin("mlp.gateup")
@@ -239,7 +250,11 @@ class SwingMLP:
         K.silu_mul(g, u, g, self.gm)
         t.end("mlp.act")
         t.begin("mlp.down")
-        out = K.gemm(g, w.mlp_down[:, :n], out=out, alpha=self.dm, addend=addend)
+        if push is not None:
+            push.gemm(g, w.mlp_down[:, :n], alpha=self.dm)
+            out = None
+        else:
+            out = K.gemm(g, w.mlp_down[:, :n], out=out, alpha=self.dm, addend=addend)
         t.end("mlp.down")
         return out
 
@@ -252,7 +267,9 @@ class ParallelHybridLayer:
         side stream concurrently with the Mamba-2 core. `ctx` is a DecodeCtx (step() is one decode step) or a
         PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer). ar_impl "p2p": the
         decode step's [B, H] all-reduces (mixer and MLP; not tp4's per-branch pair) run as the peer-memory
-        all-reduce fused with the residual add and the next norm (p2p.PeerAllReduce); prefill keeps NCCL."""
+        all-reduce fused with the residual add and the next norm (p2p.PeerAllReduce); "p2p_fused": in addition the
+        GEMM producing the partial (out-projection, MLP down) writes it into every rank's buffer itself, where the
+        layout lets it (tp4_fused with fused projections, split{a}{m}, the MLP); prefill keeps NCCL."""
         self.plan, self.w, self.dims, self.groups, self.ctx = plan, w, dims, groups, ctx
         self.st = st
         self.overlap_branches = overlap_branches
@@ -301,15 +318,18 @@ class ParallelHybridLayer:
         self.h1 = mk() if self.has_mlp else self.out
         self.mix, self.part_a, self.part_s, self.mlp_part = mk(), mk(), mk(), mk()
         self.tp = groups.tp
-        if ar_impl not in ("nccl", "p2p"):
-            raise ValueError(f"ar_impl {ar_impl!r}: nccl or p2p")
+        if ar_impl not in ("nccl", "p2p", "p2p_fused"):
+            raise ValueError(f"ar_impl {ar_impl!r}: nccl, p2p or p2p_fused")
         self.ar_impl = ar_impl
         self.p2p = None
-        if (ar_impl == "p2p" and world > 1 and collectives and not isinstance(ctx, PrefillCtx)
+        if (ar_impl != "nccl" and world > 1 and collectives and not isinstance(ctx, PrefillCtx)
                 and self.mode != "tp4"):
             from .p2p import PeerAllReduce
 
             self.p2p = PeerAllReduce(groups.tp, groups.rank, ctx.rows, dims.hidden, device)  # collective
+        # p2p_fused: the GEMM that produces a partial (out-projection, MLP down) writes it into every rank's
+        # buffer as its tiles finish, and the join kernel only waits, sums and normalises
+        self.push = self.p2p if ar_impl == "p2p_fused" else None
         self.overlap = self.fused and overlap_branches
         if self.overlap:
             self.s_side = torch.cuda.Stream(device=device)
@@ -352,17 +372,19 @@ class ParallelHybridLayer:
         t.end(name)
         return x
 
-    def _reduce_join(self, h: torch.Tensor, t: OpTimer) -> None:
-        """All-reduce self.mix over the layer's ranks, then h1 = h + mix (and the pre-MLP norm into yn)."""
+    def _reduce_join(self, h: torch.Tensor, t: OpTimer, pushed: bool = False) -> None:
+        """All-reduce self.mix (pushed: the partial the last GEMM pushed) over the layer's ranks, then
+        h1 = h + mix (and the pre-MLP norm into yn)."""
         if self.p2p is None:
             self._ar(self.mix, "ar.mixer", t)
             self._join(h, self.mix, t)
             return
         t.begin("ar.mixer")
+        part = None if pushed else self.mix
         if self.has_mlp:
-            self.p2p.join(self.mix, h, self.h1, self.w.ff_norm, self.dims.rms_eps, self.yn)
+            self.p2p.join(part, h, self.h1, self.w.ff_norm, self.dims.rms_eps, self.yn)
         else:
-            self.p2p.join(self.mix, h, self.out)
+            self.p2p.join(part, h, self.out)
         t.end("ar.mixer")
 
     def _join(self, h: torch.Tensor, mix: torch.Tensor, t: OpTimer) -> None:
@@ -399,13 +421,16 @@ class ParallelHybridLayer:
                 self.ssm.core(t)
             t.begin("mixer.outproj")
             seg = {} if self.out_ratio is not None else {"k_seg": self.k_seg, "alpha2": dims.ssm_out}
+            pushed = self.push is not None and mode == "tp4_fused"
             if mode == "tp1":
                 K.gemm(self.mid_buf, self.w.w_out_cat, out=self.h1, alpha=dims.attn_out, addend=h, **seg)
+            elif pushed:
+                self.push.gemm(self.mid_buf, self.w.w_out_cat, alpha=dims.attn_out, **seg)
             else:
                 K.gemm(self.mid_buf, self.w.w_out_cat, out=self.mix, alpha=dims.attn_out, **seg)
             t.end("mixer.outproj")
             if mode == "tp4_fused":
-                self._reduce_join(h, t)
+                self._reduce_join(h, t, pushed)
                 y_ready = self.has_mlp
         elif mode == "tp1":
             self.attn.decode(x, t, out=self.h1, addend=h, x_scale=dims.attn_in)
@@ -436,10 +461,10 @@ class ParallelHybridLayer:
             y_ready = self.has_mlp
         else:  # split{a}{m}
             if self.attn is not None:
-                self.attn.decode(x, t, out=self.mix, x_scale=dims.attn_in)
+                self.attn.decode(x, t, out=self.mix, x_scale=dims.attn_in, push=self.push)
             else:
-                self.ssm.decode(x, t, out=self.mix, x_scale=dims.ssm_in)
-            self._reduce_join(h, t)
+                self.ssm.decode(x, t, out=self.mix, x_scale=dims.ssm_in, push=self.push)
+            self._reduce_join(h, t, self.push is not None)
             y_ready = self.has_mlp
         if not self.has_mlp:
             return self.out
@@ -450,10 +475,10 @@ class ParallelHybridLayer:
         if self._local:
             self.mlp.forward(self.yn, t, out=self.out, addend=self.h1)
         else:
-            self.mlp.forward(self.yn, t, out=self.mlp_part)
+            self.mlp.forward(self.yn, t, out=self.mlp_part, push=self.push)
             if self.p2p is not None:
                 t.begin("ar.mlp")
-                self.p2p.join(self.mlp_part, self.h1, self.out)
+                self.p2p.join(None if self.push is not None else self.mlp_part, self.h1, self.out)
                 t.end("ar.mlp")
                 return self.out
             self._ar(self.mlp_part, "ar.mlp", t)

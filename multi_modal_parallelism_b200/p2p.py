@@ -5,7 +5,9 @@ pre-MLP norm, `harness/layer.py:217-227`).
 
 Setup is collective over the group: every rank allocates a zeroed buffer, exports it as a CUDA IPC blob, the blobs
 are exchanged with `torch.distributed.all_gather_object`, and each rank maps the others'. Calls are then plain
-kernel launches (graph-capturable); every rank must make the same sequence of calls.
+kernel launches (graph-capturable); every rank must make the same sequence of calls. `gemm` + `join(None, ...)` is
+the fused form: the producing decode GEMM writes its output tiles into every rank's buffer as they finish, so the
+transfer overlaps the GEMM, and the join kernel only waits, sums and normalises.
 """
 from __future__ import annotations
 
@@ -48,16 +50,41 @@ class PeerAllReduce:
             ptrs.append(int(out.value))
             self._imported.append(int(out.value))
         self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=device)
+        self._pushed_rows = 0
         if self.world > 1:
             dist.barrier(group=group.pg)
 
-    def join(self, part: torch.Tensor, resid: torch.Tensor | None, sum_out: torch.Tensor,
-             norm_w: torch.Tensor | None = None, eps: float = 0.0, norm_out: torch.Tensor | None = None) -> torch.Tensor:
-        """sum_out = resid + all-reduce(part) (bf16); with norm_w also norm_out = rmsnorm(sum_out) * norm_w.
-        Returns norm_out when given, else sum_out."""
+    def gemm(self, x: torch.Tensor, w: torch.Tensor, alpha: float = 1.0, colscale: torch.Tensor | None = None,
+             k_seg: int | None = None, alpha2: float | None = None) -> None:
+        """This rank's partial alpha * colscale * (x @ w^T) (x: [rows <= 256, K] decode rows; w: [hidden, K]),
+        written by the GEMM straight into every rank's buffer; complete it with join(None, ..., pushed rows)."""
         from .kernels import _rowmajor, _stream, error_word
 
-        rows, H = part.shape
+        M, K = x.shape
+        if w.shape[0] != self.hidden or w.shape[1] != K or M > self.rows_max:
+            raise ValueError(f"PeerAllReduce.gemm: x {tuple(x.shape)} w {tuple(w.shape)} for [{self.rows_max}, "
+                             f"{self.hidden}]")
+        for t in (x, w):
+            if t.dtype != torch.bfloat16 or not t.is_cuda:
+                raise ValueError("PeerAllReduce.gemm: bf16 CUDA tensors expected")
+        if colscale is not None and (colscale.dtype != torch.float32 or colscale.numel() != self.hidden):
+            raise ValueError("PeerAllReduce.gemm: colscale must be fp32 [hidden]")
+        ks = K if k_seg is None else int(k_seg)
+        a2 = float(alpha if alpha2 is None else alpha2)
+        _lib.call("mmp_gemm_bf16_push", x.data_ptr(), _rowmajor("x", x), w.data_ptr(), _rowmajor("w", w), M,
+                  self.hidden, K, float(alpha), ks, a2, None if colscale is None else colscale.data_ptr(),
+                  self.bufs.data_ptr(), self.rank, self.world, self.rows_max, error_word(x.device).data_ptr(),
+                  _stream(x))
+        self._pushed_rows = M
+
+    def join(self, part: torch.Tensor | None, resid: torch.Tensor | None, sum_out: torch.Tensor,
+             norm_w: torch.Tensor | None = None, eps: float = 0.0, norm_out: torch.Tensor | None = None) -> torch.Tensor:
+        """sum_out = resid + all-reduce(part) (bf16); with norm_w also norm_out = rmsnorm(sum_out) * norm_w.
+        part None: the partial is the one the last gemm() pushed. Returns norm_out when given, else sum_out."""
+        from .kernels import _rowmajor, _stream, error_word
+
+        pushed = part is None
+        rows, H = (self._pushed_rows, self.hidden) if pushed else part.shape
         if H != self.hidden or rows > self.rows_max:
             raise ValueError(f"PeerAllReduce.join: [{rows}, {H}] does not fit [{self.rows_max}, {self.hidden}]")
         for t in (part, resid, sum_out, norm_w, norm_out):
@@ -67,10 +94,12 @@ class PeerAllReduce:
             raise ValueError("PeerAllReduce.join: norm_w and norm_out go together")
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         ld = lambda n, t: 0 if t is None else _rowmajor(n, t)  # noqa: E731
-        _lib.call("mmp_ar_join", self.bufs.data_ptr(), self.rank, self.world, self.rows_max,
-                  part.data_ptr(), ld("part", part), p(resid), ld("resid", resid), sum_out.data_ptr(),
+        if sum_out.shape[0] != rows:
+            raise ValueError(f"PeerAllReduce.join: sum_out has {sum_out.shape[0]} rows, the partial {rows}")
+        _lib.call("mmp_ar_join", self.bufs.data_ptr(), self.rank, self.world, self.rows_max, 1 if pushed else 0,
+                  p(part), ld("part", part), p(resid), ld("resid", resid), sum_out.data_ptr(),
                   ld("sum_out", sum_out), p(norm_w), float(eps), p(norm_out), ld("norm_out", norm_out),
-                  rows, H, error_word(part.device).data_ptr(), _stream(part))
+                  rows, H, error_word(sum_out.device).data_ptr(), _stream(sum_out))
         return norm_out if norm_out is not None else sum_out
 
     def close(self) -> None:

@@ -66,7 +66,7 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--check", action="store_true")
     ap.add_argument("--no-collectives", action="store_true", help="diagnostic: per-rank compute only (outputs wrong)")
     ap.add_argument("--ssm-dtype", choices=["fp32", "bf16"], default="fp32")
-    ap.add_argument("--ar-impl", choices=["nccl", "p2p"], default="nccl",
+    ap.add_argument("--ar-impl", choices=["nccl", "p2p", "p2p_fused"], default="nccl",
                     help="p2p: decode all-reduces over NVLink peer memory, fused with the residual and norm")
     args = ap.parse_args(argv)
 

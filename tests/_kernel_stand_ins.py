@@ -28,7 +28,10 @@ def gemm(x, w, out=None, alpha=1.0, colscale=None, addend=None, k_seg=None, alph
     _rows16("gemm.x", x)
     _rows16("gemm.w", w)
     assert x.shape[1] == w.shape[1] and x.shape[1] % 8 == 0
-    r = (x.float() @ w.float().T) * alpha
+    ks = x.shape[1] if k_seg is None else int(k_seg)
+    r = (x[:, :ks].float() @ w[:, :ks].float().T) * alpha
+    if ks < x.shape[1]:
+        r = r + (x[:, ks:].float() @ w[:, ks:].float().T) * (alpha if alpha2 is None else alpha2)
     if colscale is not None:
         r = r * colscale.reshape(1, -1).float()
     if addend is not None:
@@ -288,3 +291,36 @@ def attn_decode(q, key_cache, value_cache, cu_q, seqused_k, max_k, block_table, 
     for r in range(q.shape[0]):
         out[r:r + 1].copy_(_attend(q[r:r + 1], key_cache, value_cache, block_table[r], [int(seqused_k[r])]).to(out.dtype))
     return out
+
+
+class PeerAllReduceStandIn:
+    """Stands in for p2p.PeerAllReduce on CPU ranks: same methods and results (rank-order fp32 sum of the bf16
+    partials, rounded to bf16, plus the residual, optional RMSNorm), through a gloo all-gather."""
+
+    calls: list = []
+
+    def __init__(self, group, global_rank, rows_max, hidden, device):
+        self.group, self.rows_max, self.hidden = group, rows_max, hidden
+        self.pending = None
+
+    def gemm(self, x, w, alpha=1.0, colscale=None, k_seg=None, alpha2=None):
+        self.pending = gemm(x, w, alpha=alpha, colscale=colscale, k_seg=k_seg, alpha2=alpha2)
+        PeerAllReduceStandIn.calls.append("gemm")
+
+    def join(self, part, resid, sum_out, norm_w=None, eps=0.0, norm_out=None):
+        import torch.distributed as dist
+
+        PeerAllReduceStandIn.calls.append("join-pushed" if part is None else "join")
+        part = self.pending if part is None else part
+        parts = [torch.empty_like(part) for _ in range(self.group.world_size)]
+        dist.all_gather(parts, part.contiguous(), group=self.group.pg)
+        acc = torch.zeros(part.shape)
+        for q in parts:
+            acc = acc + q.float()
+        s = acc.to(BF16).float() + (0 if resid is None else resid.float())
+        sum_out.copy_(s.to(BF16))
+        if norm_w is not None:
+            sf = sum_out.float()
+            norm_out.copy_((sf * torch.rsqrt(sf.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float()).to(BF16))
+            return norm_out
+        return sum_out

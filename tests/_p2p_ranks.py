@@ -2,8 +2,9 @@
 tests/test_multigpu.py: every rank makes the same calls on seeded per-rank partials (decode-sized rows), with
 and without the fused RMSNorm and with fewer rows than the buffer holds (the epoch parity flips every call); the
 residual-plus-sum must equal, bit for bit, h + bf16(sum of the all-gathered partials in rank order), the norm
-output must be within tolerance of fp32 math, and a CUDA graph of two calls replayed three times must match the
-same calls made eagerly. Prints one `[p2p-check] pass=...` line."""
+output must be within tolerance of fp32 math; the fused form (the decode GEMM pushing its tiles, interleaved with
+plain calls on the same buffer) must match the sum of the ranks' GEMM outputs; and a CUDA graph of two calls
+replayed three times must match the same calls made eagerly. Prints one `[p2p-check] pass=...` line."""
 import sys
 from pathlib import Path
 
@@ -55,6 +56,31 @@ def main():
             ok &= within_tolerance(m)
             msgs.append(f"norm {m['rel_l2']:.2e}")
         outs.append(s_out)
+    # fused form: the decode GEMM pushes its output tiles; plain and pushed calls interleave on one buffer
+    K_in = 1024
+    for call, norm in enumerate([True, False, True]):
+        x = (torch.randn(ROWS, K_in, device=dev, generator=g) * 0.5).to(torch.bfloat16)
+        wt = (torch.randn(H, K_in, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+        h = torch.randn(ROWS, H, device=dev, generator=g).to(torch.bfloat16)
+        s_out, y_out = torch.empty_like(h), torch.empty_like(h)
+        ar.gemm(x, wt, alpha=0.75)
+        ar.join(None, h, s_out, w if norm else None, EPS, y_out if norm else None)
+        torch.cuda.synchronize()
+        part = ((x.float() @ wt.float().T) * 0.75).to(torch.bfloat16)  # this rank's partial as the GEMM rounds it
+        s_ref, y_ref = reference(part, h, w, world)
+        m = compare(s_out.float().cpu(), s_ref.float().cpu())
+        ok &= within_tolerance(m)
+        msgs.append(f"pushed call {call} sum {m['rel_l2']:.2e}")
+        if norm:
+            m = compare(y_out.float().cpu(), y_ref.float().cpu())
+            ok &= within_tolerance(m)
+        outs.append(s_out)
+        # a plain call between pushed ones
+        part = torch.randn(ROWS, H, device=dev, generator=g).to(torch.bfloat16)
+        s_out = torch.empty_like(h)
+        ar.join(part, h, s_out)
+        torch.cuda.synchronize()
+        ok &= torch.equal(s_out, reference(part, h, w, world)[0])
     # graph capture: two calls per replay, three replays, against the same calls made eagerly
     part = torch.randn(ROWS, H, device=dev, generator=g).to(torch.bfloat16)
     h = torch.randn(ROWS, H, device=dev, generator=g).to(torch.bfloat16)

@@ -140,9 +140,12 @@ def test_peer_allreduce(world):
 
 @pytest.mark.run_last
 @pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("impl", ["p2p", "p2p_fused"])
 @pytest.mark.parametrize("world,mode", [(2, "split11"), (2, "tp4_fused"), (4, "split22"), (8, "split44")])
-def test_layouts_with_peer_allreduce(world, mode, tmp_path):
-    """Every rank of the layer with the peer-memory all-reduce: bitwise equal, within tolerance of fp32."""
+def test_layouts_with_peer_allreduce(world, mode, impl, tmp_path):
+    """Every rank of the layer with the peer-memory all-reduce (and with the GEMMs pushing their tiles): bitwise
+    equal across ranks, within tolerance of fp32."""
     if ngpu() < world:
         pytest.skip(f"needs {world} GPUs")
-    run_check(world, mode, tmp_path, ("--ar-impl", "p2p"))
+    run_check(world, mode, tmp_path, ("--ar-impl", impl, "--dims-yaml", "falcon_h1_7b", "--swing", "0.2")
+              if mode.startswith("split") else ("--ar-impl", impl))
