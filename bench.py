@@ -64,6 +64,30 @@ def workload(args) -> dict:
 
 
 # ------------------------------------------------------------------------------------------- CPU layer
+def cpu_prefill_tokens_per_s(args, positions: int = 64) -> dict:
+    """The reference defines no prefill; its fp32 layer runs a sequence as one decode step per position. Time
+    the oracle's port of that (prefill_sequential) over the first `positions` positions of one fresh sequence and
+    report tokens/s: an extrapolation to the bench's prefill (later positions attend to more keys, so it is an
+    upper bound on the CPU's rate)."""
+    import numpy as np
+
+    import oracle
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.weights import random_layer
+
+    dims = preset(args.dims)
+    full = {k: oracle.to_numpy(v) for k, v in random_layer(dims, args.seed).items()}
+    g = np.random.default_rng(args.seed + 1)
+    h = g.standard_normal((positions, dims.hidden)).astype(np.float32)
+    oracle.prefill_sequential(full, dims, [h[:2]])  # warm
+    t0 = time.perf_counter()
+    oracle.prefill_sequential(full, dims, [h])
+    dt = time.perf_counter() - t0
+    return {"value": positions / dt, "unit": UNIT, "kind": "port", "cores": os.cpu_count(),
+            "sample": f"first {positions} positions of one sequence as sequential fp32 decode steps of the numpy "
+                      f"layer ({dt:.2f} s); extrapolated to the prefill workload"}
+
+
 def cpu_layer_tokens_per_s(args, budget_s: float, max_steps: int | None = None) -> dict:
     """Time the oracle's fp32 layer (a numpy port of the reference's harness/reference.py:decode_step) on
     this host's cores, full batch, on the same seeded inputs."""
@@ -400,6 +424,8 @@ def our_arm(args) -> None:
     cpu = None
     if groups.rank == 0 and world == 1 and args.cpu_s > 0:
         cpu = cpu_layer_tokens_per_s(args, args.cpu_s)
+        if prefill is not None:
+            prefill["cpu_baseline"] = cpu_prefill_tokens_per_s(args)
     if groups.rank == 0:
         peak, peak_src = roofline_peak()
         roof = None
