@@ -323,6 +323,17 @@ int mmp_gemm_bf16_push(const void* a, int64_t lda, const void* w, int64_t ldw, i
                        int k_seg, float alpha2, const float* colscale, const uint64_t* bufs, int rank, int world,
                        int rows_max, int* err, void* stream);
 
+/* Gated RMSNorm whose row statistic spans a norm group's ranks (replaces the tensor-parallel path of
+ * kernels.gated_rmsnorm, harness/kernels.py:47-52: local sums of squares, an all-reduce of [rows, 1] over the
+ * norm group, the normalisation) in one kernel over peer memory: out = w * g * rsqrt(sum over ranks of
+ * sum(g^2) / (world * D) + eps), g = y * silu(z), each rank holding D columns of every row. Buffers as above with
+ * mmp_gn_buffer_bytes(world, rows_max) bytes per rank (zeroed, shared with mmp_ipc_export / mmp_ipc_import).
+ * y, z, out: [rows, D] bf16 with row strides; w: [D] bf16. Every rank of the group makes the same calls. */
+size_t mmp_gn_buffer_bytes(int world, int rows_max);
+int mmp_gated_rmsnorm_p2p(const uint64_t* bufs, int rank, int world, int rows_max,
+                          const void* y, int64_t y_b, const void* z, int64_t z_b, const void* w,
+                          void* out, int64_t o_b, int rows, int D, float eps, int* err, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

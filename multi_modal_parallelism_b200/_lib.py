@@ -51,6 +51,8 @@ SIGNATURES: dict[str, tuple] = {
     "mmp_ipc_release": (I32, [P]),
     "mmp_ar_join": (I32, [P, I32, I32, I32, I32, P, I64, P, I64, P, I64, P, F32, P, I64, I32, I32, P, P]),
     "mmp_gemm_bf16_push": (I32, [P, I64, P, I64, I32, I32, I32, F32, I32, F32, P, P, I32, I32, I32, P, P]),
+    "mmp_gn_buffer_bytes": (SZ, [I32, I32]),
+    "mmp_gated_rmsnorm_p2p": (I32, [P, I32, I32, I32, P, I64, P, I64, P, P, I64, I32, I32, F32, P, P]),
     "mmp_gdn_decode": (I32, [P, I64, I64, I64, P, I64, I64, P, I64, I64, P, I64, I64, P, I64, P, I64, P, P,
                              P, I64, I64, P, F32, P, I32, P, I64, I64, I32, I32, I32, I32, I32, I32, P, P]),
     "mmp_gdn_prefill": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, P, I64, P, P, P, I64, I64, P, F32,

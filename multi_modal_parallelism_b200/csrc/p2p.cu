@@ -224,6 +224,124 @@ __global__ void __launch_bounds__(AR_THREADS) ar_join_kernel(const ArJoinParams 
   }
 }
 
+// ---- gated RMSNorm whose row statistic spans the ranks of a norm group (the Mamba-2 norm under tensor
+// parallelism): each rank holds D columns of every row; the row's sum of squares of g = y * silu(z) is the sum
+// of the ranks' partial sums. One kernel: partial sums pushed into every rank's buffer (slot [parity][rank][row],
+// fp32), per-row flags as in the all-reduce, bounded waits, rank-order sum, then out = w * g * rsqrt(total /
+// (world * D) + eps). Buffer: slots [2][world][rows_max] fp32, flags [rows_max][world] u32, epoch, done.
+struct GnJoinParams {
+  const uint64_t* bufs;
+  int rank, world, rows_max, rows, D;
+  const bf16* y; int64_t y_b;
+  const bf16* z; int64_t z_b;
+  const bf16* w;
+  bf16* out; int64_t o_b;
+  float eps;
+  int* err;
+};
+
+__host__ __device__ inline size_t gn_flags_off(int world, int rows_max) { return 2ull * world * rows_max * 4; }
+__host__ __device__ inline size_t gn_epoch_off(int world, int rows_max) {
+  return gn_flags_off(world, rows_max) + static_cast<size_t>(rows_max) * world * 4;
+}
+
+__device__ __forceinline__ float gated(float y, float z) { return y * silu(z); }
+
+__global__ void __launch_bounds__(AR_THREADS) gnorm_join_kernel(const GnJoinParams P) {
+  __shared__ float red[32];
+  __shared__ int s_abort;
+  __shared__ uint32_t s_epoch;
+  const int tid = threadIdx.x;
+  const uint64_t own = P.bufs[P.rank];
+  uint32_t* own_epoch = reinterpret_cast<uint32_t*>(own + gn_epoch_off(P.world, P.rows_max));
+  if (tid == 0) {
+    s_epoch = *reinterpret_cast<volatile uint32_t*>(own_epoch) + 1u;
+    s_abort = 0;
+  }
+  __syncthreads();
+  const uint32_t e = s_epoch;
+  const int par = e & 1;
+  const int nvec = P.D / 8;
+  // 1. each row's partial sum of squares, pushed to every rank (thread 0) with the row's flag
+  for (int row = blockIdx.x; row < P.rows; row += gridDim.x) {
+    float ss = 0.f;
+    for (int v = tid; v < nvec; v += AR_THREADS) {
+      const uint4 yu = reinterpret_cast<const uint4*>(P.y + row * P.y_b)[v];
+      const uint4 zu = reinterpret_cast<const uint4*>(P.z + row * P.z_b)[v];
+      const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w}, zw[4] = {zu.x, zu.y, zu.z, zu.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = unpack_bf16x2(yw[i]), b = unpack_bf16x2(zw[i]);
+        const float g0 = gated(a.x, b.x), g1 = gated(a.y, b.y);
+        ss = fmaf(g0, g0, fmaf(g1, g1, ss));
+      }
+    }
+    const float tot = block_sum(ss, red);
+    if (tid == 0) {
+      for (int q = 0; q < P.world; ++q) {
+        float* slot = reinterpret_cast<float*>(P.bufs[q]) + (static_cast<size_t>(par) * P.world + P.rank) * P.rows_max + row;
+        *slot = tot;
+      }
+      __threadfence_system();
+      for (int q = 0; q < P.world; ++q)
+        st_release_sys(reinterpret_cast<uint32_t*>(P.bufs[q] + gn_flags_off(P.world, P.rows_max)) + row * P.world + P.rank, e);
+    }
+    __syncthreads();  // red is reused by the next row
+  }
+  // 2. wait for every rank's partial of this CTA's rows (bounded)
+  if (tid == 0) {
+    const uint32_t* flags = reinterpret_cast<const uint32_t*>(own + gn_flags_off(P.world, P.rows_max));
+    for (int row = blockIdx.x; row < P.rows && !s_abort; row += gridDim.x) {
+      for (int q = 0; q < P.world; ++q) {
+        long long polls = 0;
+        while (static_cast<int>(ld_acquire_sys(flags + row * P.world + q) - e) < 0) {
+          if (++polls > AR_MAX_POLLS) {
+            s_abort = 1;
+            flag_error(P.err, DEVERR_TIMEOUT);
+            break;
+          }
+          __nanosleep(128);
+        }
+        if (s_abort) break;
+      }
+    }
+  }
+  __syncthreads();
+  __threadfence();
+  // 3. total in rank order, apply
+  const float* slots = reinterpret_cast<const float*>(own) + static_cast<size_t>(par) * P.world * P.rows_max;
+  for (int row = blockIdx.x; row < P.rows; row += gridDim.x) {
+    float total = 0.f;
+    if (!s_abort)
+      for (int q = 0; q < P.world; ++q) total += __ldcg(slots + q * P.rows_max + row);
+    const float r = rsqrtf(total / (static_cast<float>(P.world) * P.D) + P.eps);
+    for (int v = tid; v < nvec; v += AR_THREADS) {
+      const uint4 yu = reinterpret_cast<const uint4*>(P.y + row * P.y_b)[v];
+      const uint4 zu = reinterpret_cast<const uint4*>(P.z + row * P.z_b)[v];
+      const uint4 wu = reinterpret_cast<const uint4*>(P.w)[v];
+      const uint32_t yw[4] = {yu.x, yu.y, yu.z, yu.w}, zw[4] = {zu.x, zu.y, zu.z, zu.w}, ww[4] = {wu.x, wu.y, wu.z, wu.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 a = unpack_bf16x2(yw[i]), b = unpack_bf16x2(zw[i]), c = unpack_bf16x2(ww[i]);
+        o[i] = pack_bf16x2(c.x * gated(a.x, b.x) * r, c.y * gated(a.y, b.y) * r);
+      }
+      reinterpret_cast<uint4*>(P.out + row * P.o_b)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  // 4. the last CTA advances the epoch
+  __syncthreads();
+  if (tid == 0) {
+    uint32_t* done = own_epoch + 1;
+    __threadfence();
+    if (atomicAdd(done, 1u) == gridDim.x - 1) {
+      *done = 0;
+      *reinterpret_cast<volatile uint32_t*>(own_epoch) = e;
+      __threadfence();
+    }
+  }
+}
+
 // ---- CUDA IPC: export / import a device pointer as (allocation handle, offset)
 using PFN_range = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
 PFN_range g_range = nullptr;
@@ -325,4 +443,36 @@ extern "C" int mmp_ar_join(const uint64_t* bufs, int rank, int world, int rows_m
   cudaError_t e = cudaLaunchKernelEx(&cfg, ar_join_kernel, P);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_ar_join: launch failed: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_ar_join");
+}
+
+
+extern "C" size_t mmp_gn_buffer_bytes(int world, int rows_max) {
+  return (gn_epoch_off(world, rows_max) + 8 + 15) / 16 * 16;
+}
+
+extern "C" int mmp_gated_rmsnorm_p2p(const uint64_t* bufs, int rank, int world, int rows_max,
+                                     const void* y, int64_t y_b, const void* z, int64_t z_b, const void* w,
+                                     void* out, int64_t o_b, int rows, int D, float eps, int* err, void* stream) {
+  if (rows == 0) return MMP_OK;
+  if (!bufs || !y || !z || !w || !out) return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm_p2p: null pointer");
+  if (world < 1 || world > AR_MAX_WORLD || rank < 0 || rank >= world || rows < 0 || rows > rows_max || D <= 0 || D % 8)
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm_p2p: bad sizes rank=%d world=%d rows=%d rows_max=%d D=%d",
+                         rank, world, rows, rows_max, D);
+  auto rows_ok = [](const void* p, int64_t ld) { return aligned16(p) && ld % 8 == 0; };
+  if (!rows_ok(y, y_b) || !rows_ok(z, z_b) || !rows_ok(out, o_b) || !aligned16(w))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm_p2p: rows must be 16-byte aligned");
+  GnJoinParams P{bufs, rank, world, rows_max, rows, D, static_cast<const bf16*>(y), y_b, static_cast<const bf16*>(z),
+                 z_b, static_cast<const bf16*>(w), static_cast<bf16*>(out), o_b, eps, err};
+  static int sms[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm_p2p: device %d", dev);
+  if (!sms[dev]) cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(rows < sms[dev] || sms[dev] <= 0 ? rows : sms[dev]);
+  cfg.blockDim = dim3(AR_THREADS);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, gnorm_join_kernel, P);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_gated_rmsnorm_p2p: launch failed: %s", cudaGetErrorString(e));
+  return mmp_check_launch("mmp_gated_rmsnorm_p2p");
 }

@@ -122,13 +122,15 @@ class SsmBranch:
 
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
                  device: torch.device, norm_group, zxbcdt: torch.Tensor | None = None, yn: torch.Tensor | None = None,
-                 norm_w: torch.Tensor | None = None):
+                 norm_w: torch.Tensor | None = None, norm_peer=None):
         """zxbcdt / yn: optional [B, in rows] and [B, nhr*p] views into buffers shared with the other branch;
-        norm_w: the gated norm's weight when it carries an extra output scale (default w.norm_w)."""
+        norm_w: the gated norm's weight when it carries an extra output scale (default w.norm_w); norm_peer: a
+        p2p.PeerRowNorm that replaces the norm group's all-reduce of the row statistic."""
         s = plan.ssm
         assert s is not None
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
         self.norm_group = norm_group
+        self.norm_peer = norm_peer
         self.norm_w = w.norm_w if norm_w is None else norm_w
         z, x, b, c, dt = s.local_in_rows
         self.sizes = (z, x + b + c, dt)
@@ -193,6 +195,10 @@ class SsmBranch:
 
     def _norm(self, t: OpTimer) -> None:
         t.begin("ssm.norm")
+        if self.norm_peer is not None:
+            self.norm_peer(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.norm_w, self.dims.rms_eps, self.yn)
+            t.end("ssm.norm")
+            return
         K.gated_rmsnorm(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.norm_w, self.dims.rms_eps,
                         self.norm_group, self.group_size, out=self.yn, sumsq=self.sumsq)
         t.end("ssm.norm")
@@ -309,7 +315,14 @@ class ParallelHybridLayer:
         norm_w = None
         if self.fused and self.out_ratio is not None:
             norm_w = (w.norm_w.float() * self.out_ratio).to(BF16)
-        self.ssm = SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w) if plan.ssm is not None else None
+        norm_peer = None
+        if (ar_impl != "nccl" and world > 1 and collectives and not isinstance(ctx, PrefillCtx)
+                and plan.ssm is not None and len(plan.ssm.norm_ranks) > 1):
+            from .p2p import PeerRowNorm
+
+            norm_peer = PeerRowNorm(norm_group, groups.rank, ctx.rows, device)  # collective over the norm group
+        self.ssm = (SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w, norm_peer)
+                    if plan.ssm is not None else None)
         self.has_mlp = dims.intermediate > 0
         self.mlp = SwingMLP(plan, w, dims, ctx.rows, device) if self.has_mlp else None
         B, H = ctx.rows, dims.hidden

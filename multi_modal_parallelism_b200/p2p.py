@@ -22,14 +22,14 @@ from .dist import Coordinator
 BLOB_BYTES = 72
 
 
-class PeerAllReduce:
-    def __init__(self, group: Coordinator, global_rank: int, rows_max: int, hidden: int, device: torch.device):
-        """Collective over `group` (every member calls it, in the same order as its other collectives)."""
+class _PeerBuffer:
+    """A zeroed device buffer of `nbytes` on every rank of `group`, mapped into every rank (CUDA IPC). Collective
+    over `group` (every member constructs it, in the same order as its other collectives)."""
+
+    def __init__(self, group: Coordinator, global_rank: int, nbytes: int, device: torch.device):
         if not 1 <= group.world_size <= 8:
-            raise ValueError(f"PeerAllReduce: {group.world_size} ranks (1..8 on one node)")
-        self.world, self.rank = group.world_size, group.ranks.index(global_rank)
-        self.rows_max, self.hidden, self.device = rows_max, hidden, device
-        nbytes = int(_lib.lib().mmp_ar_buffer_bytes(self.world, rows_max, hidden))
+            raise ValueError(f"{type(self).__name__}: {group.world_size} ranks (1..8 on one node)")
+        self.world, self.rank, self.device = group.world_size, group.ranks.index(global_rank), device
         self.buf = torch.zeros(nbytes, dtype=torch.uint8, device=device)
         torch.cuda.synchronize(device)  # the zeros must be in place before any peer can write
         blob = ctypes.create_string_buffer(BLOB_BYTES)
@@ -50,9 +50,23 @@ class PeerAllReduce:
             ptrs.append(int(out.value))
             self._imported.append(int(out.value))
         self.bufs = torch.tensor(ptrs, dtype=torch.int64, device=device)
-        self._pushed_rows = 0
         if self.world > 1:
             dist.barrier(group=group.pg)
+
+    def close(self) -> None:
+        """Unmap the peers' buffers (after the last call has finished on this rank)."""
+        for ptr in self._imported:
+            _lib.call("mmp_ipc_release", ptr, kernels=0)
+        self._imported = []
+
+
+class PeerAllReduce(_PeerBuffer):
+    def __init__(self, group: Coordinator, global_rank: int, rows_max: int, hidden: int, device: torch.device):
+        """Collective over `group` (every member calls it, in the same order as its other collectives)."""
+        self.rows_max, self.hidden = rows_max, hidden
+        nbytes = int(_lib.lib().mmp_ar_buffer_bytes(group.world_size, rows_max, hidden))
+        super().__init__(group, global_rank, nbytes, device)
+        self._pushed_rows = 0
 
     def gemm(self, x: torch.Tensor, w: torch.Tensor, alpha: float = 1.0, colscale: torch.Tensor | None = None,
              k_seg: int | None = None, alpha2: float | None = None) -> None:
@@ -102,8 +116,22 @@ class PeerAllReduce:
                   rows, H, error_word(sum_out.device).data_ptr(), _stream(sum_out))
         return norm_out if norm_out is not None else sum_out
 
-    def close(self) -> None:
-        """Unmap the peers' buffers (after the last call has finished on this rank)."""
-        for ptr in self._imported:
-            _lib.call("mmp_ipc_release", ptr, kernels=0)
-        self._imported = []
+
+class PeerRowNorm(_PeerBuffer):
+    """The Mamba-2 gated RMSNorm whose row statistic spans the ranks of a norm group (mmp_gated_rmsnorm_p2p): the
+    partial sums of squares go straight to every rank's buffer, with no separate all-reduce launch."""
+
+    def __init__(self, group: Coordinator, global_rank: int, rows_max: int, device: torch.device):
+        self.rows_max = rows_max
+        super().__init__(group, global_rank, int(_lib.lib().mmp_gn_buffer_bytes(group.world_size, rows_max)), device)
+
+    def __call__(self, y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
+        from .kernels import _rowmajor, _stream, error_word
+
+        rows, D = y.shape
+        if rows > self.rows_max or z.shape != y.shape or out.shape != y.shape or w.numel() != D:
+            raise ValueError(f"PeerRowNorm: y {tuple(y.shape)} z {tuple(z.shape)} out {tuple(out.shape)} w {w.numel()}")
+        _lib.call("mmp_gated_rmsnorm_p2p", self.bufs.data_ptr(), self.rank, self.world, self.rows_max, y.data_ptr(),
+                  _rowmajor("y", y), z.data_ptr(), _rowmajor("z", z), w.data_ptr(), out.data_ptr(),
+                  _rowmajor("out", out), rows, D, float(eps), error_word(y.device).data_ptr(), _stream(y))
+        return out

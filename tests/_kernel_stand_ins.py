@@ -324,3 +324,20 @@ class PeerAllReduceStandIn:
             norm_out.copy_((sf * torch.rsqrt(sf.pow(2).mean(-1, keepdim=True) + eps) * norm_w.float()).to(BF16))
             return norm_out
         return sum_out
+
+
+class PeerRowNormStandIn:
+    """Stands in for p2p.PeerRowNorm on CPU ranks: the row statistic summed over the norm group (gloo)."""
+
+    def __init__(self, group, global_rank, rows_max, device):
+        self.group = group
+
+    def __call__(self, y, z, w, eps, out):
+        import torch.distributed as dist
+
+        PeerAllReduceStandIn.calls.append("norm")
+        g = y.float() * F.silu(z.float())
+        tot = g.pow(2).sum(-1, keepdim=True)
+        dist.all_reduce(tot, group=self.group.pg)
+        out.copy_((g * torch.rsqrt(tot / (self.group.world_size * g.shape[1]) + eps) * w.float()).to(out.dtype))
+        return out

@@ -3,7 +3,8 @@ tests/test_multigpu.py: every rank makes the same calls on seeded per-rank parti
 and without the fused RMSNorm and with fewer rows than the buffer holds (the epoch parity flips every call); the
 residual-plus-sum must equal, bit for bit, h + bf16(sum of the all-gathered partials in rank order), the norm
 output must be within tolerance of fp32 math; the fused form (the decode GEMM pushing its tiles, interleaved with
-plain calls on the same buffer) must match the sum of the ranks' GEMM outputs; and a CUDA graph of two calls
+plain calls on the same buffer) must match the sum of the ranks' GEMM outputs; the gated RMSNorm with its row
+statistic exchanged over peer memory must match the NCCL-reduced fp32 norm; and a CUDA graph of two calls
 replayed three times must match the same calls made eagerly. Prints one `[p2p-check] pass=...` line."""
 import sys
 from pathlib import Path
@@ -16,7 +17,7 @@ sys.path.insert(0, str(Path(__file__).resolve().parents[1]))
 from multi_modal_parallelism_b200 import kernels as K  # noqa: E402
 from multi_modal_parallelism_b200.correctness import compare, cross_rank_max_abs, within_tolerance  # noqa: E402
 from multi_modal_parallelism_b200.dist import destroy, init_groups  # noqa: E402
-from multi_modal_parallelism_b200.p2p import PeerAllReduce  # noqa: E402
+from multi_modal_parallelism_b200.p2p import PeerAllReduce, PeerRowNorm  # noqa: E402
 
 ROWS, H, EPS = 64, 3072, 1e-5
 
@@ -81,6 +82,25 @@ def main():
         ar.join(part, h, s_out)
         torch.cuda.synchronize()
         ok &= torch.equal(s_out, reference(part, h, w, world)[0])
+    # the gated norm's row statistic over peer memory (each rank holds D columns of every row)
+    D = 1536
+    gn = PeerRowNorm(groups.tp, rank, ROWS, dev)
+    wn = (1 + 0.1 * torch.randn(D, device=dev, generator=torch.Generator(device=dev).manual_seed(9))).to(torch.bfloat16)
+    for call, rows in enumerate([ROWS, 5, ROWS]):
+        y = torch.randn(rows, D, device=dev, generator=g).to(torch.bfloat16)
+        z = torch.randn(rows, D, device=dev, generator=g).to(torch.bfloat16)
+        out = torch.empty_like(y)
+        gn(y, z, wn, EPS, out)
+        torch.cuda.synchronize()
+        gg = y.float() * torch.nn.functional.silu(z.float())
+        tot = gg.pow(2).sum(-1, keepdim=True)
+        dist.all_reduce(tot)
+        ref = (gg * torch.rsqrt(tot / (world * D) + EPS) * wn.float()).to(torch.bfloat16)
+        m = compare(out.float().cpu(), ref.float().cpu())
+        ok &= within_tolerance(m)
+        msgs.append(f"gated norm call {call} {m['rel_l2']:.2e}")
+        outs.append(out)
+    gn.close()
     # graph capture: two calls per replay, three replays, against the same calls made eagerly
     part = torch.randn(ROWS, H, device=dev, generator=g).to(torch.bfloat16)
     h = torch.randn(ROWS, H, device=dev, generator=g).to(torch.bfloat16)

@@ -2,7 +2,8 @@
 with ar_impl "nccl", "p2p" and "p2p_fused" on the same weights and states, the kernel wrappers and
 p2p.PeerAllReduce replaced by torch stand-ins (tests/_kernel_stand_ins.py). The three give the same output
 within bf16 tolerance, every rank holds the same output, and the fused form really routes the out-projection
-and MLP-down GEMMs through the all-reduce (pushed joins) where the layout allows it."""
+and MLP-down GEMMs through the all-reduce (pushed joins) where the layout allows it; where the Mamba-2 heads span
+ranks, the gated norm's row statistic is exchanged over peer memory as well."""
 import multiprocessing as mp
 import os
 import socket
@@ -39,6 +40,7 @@ def _worker(rank, world, port, mode, q):
 
         L.K = S
         P2P.PeerAllReduce = S.PeerAllReduceStandIn
+        P2P.PeerRowNorm = S.PeerRowNormStandIn
         groups = init_groups(backend="gloo", timeout_s=120)
         cpu = torch.device("cpu")
         plan = plan_for(mode, rank, world, DIMS)
@@ -80,5 +82,7 @@ def test_peer_allreduce_orchestration(mode):
             rel = np.linalg.norm(out - ref) / np.linalg.norm(ref)
             assert rel < 1e-2, (rank, impl, rel)
             assert np.array_equal(out, res[0][1][impl][0]), (rank, impl)
-        assert r["p2p"][1] == ["join", "join"]  # mixer and MLP all-reduces, the partials pushed by the join
-        assert r["p2p_fused"][1] == ["gemm", "join-pushed", "gemm", "join-pushed"]
+        # tp4_fused holds the Mamba-2 heads on both ranks: its gated norm's row statistic goes over peer memory too
+        norm = ["norm"] if mode == "tp4_fused" else []
+        assert r["p2p"][1] == norm + ["join", "join"]  # mixer and MLP all-reduces, the partials pushed by the join
+        assert r["p2p_fused"][1] == norm + ["gemm", "join-pushed", "gemm", "join-pushed"]
