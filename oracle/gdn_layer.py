@@ -1,9 +1,11 @@
 """CPU fp32 restatement of a Gated DeltaNet (gated delta rule) linear-attention layer: test infrastructure only.
 
 The reference has no implementation of this layer (its config for the model family is a description,
-`configs/qwen35_35b_a3b.yaml:1-22`, and a byte model, `harness/synth.py:114-138`): parity is unpinned. The
-algorithm restated here is the published gated delta rule (Yang, Kautz, Hatamizadeh, "Gated Delta Networks:
-Improving Mamba2 with Delta Rule", 2024). Per value head, with a d_v x d_k state S:
+`configs/qwen35_35b_a3b.yaml:1-22`, and a byte model, `harness/synth.py:114-138`): parity against the reference is
+unpinned. The algorithm restated here is the published gated delta rule (Yang, Kautz, Hatamizadeh, "Gated Delta
+Networks: Improving Mamba2 with Delta Rule", 2024); the recurrence and the chunked form are cross-checked against
+flash-linear-attention's pure-PyTorch reference functions (fla 0.5.1) through tests/golden/gdn_fla_golden.npz.
+Per value head, with a d_v x d_k state S:
 
     S_t = a_t S_{t-1} (I - b_t k_t k_t^T) + b_t v_t k_t^T,    o_t = S_t q_t
 
