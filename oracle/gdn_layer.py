@@ -4,7 +4,9 @@ The reference has no implementation of this layer (its config for the model fami
 `configs/qwen35_35b_a3b.yaml:1-22`, and a byte model, `harness/synth.py:114-138`): parity against the reference is
 unpinned. The algorithm restated here is the published gated delta rule (Yang, Kautz, Hatamizadeh, "Gated Delta
 Networks: Improving Mamba2 with Delta Rule", 2024); the recurrence and the chunked form are cross-checked against
-flash-linear-attention's pure-PyTorch reference functions (fla 0.5.1) through tests/golden/gdn_fla_golden.npz.
+flash-linear-attention's pure-PyTorch reference functions (fla 0.5.1) through tests/golden/gdn_fla_golden.npz, and
+the mixer (gdn_mixer_prefill) against transformers' Qwen3-Next Gated DeltaNet module through
+tests/golden/qwen3next_golden.npz.
 Per value head, with a d_v x d_k state S:
 
     S_t = a_t S_{t-1} (I - b_t k_t k_t^T) + b_t v_t k_t^T,    o_t = S_t q_t
@@ -152,6 +154,28 @@ def _finish(w: dict, d: GdnDims, h: np.ndarray, o: np.ndarray, z: np.ndarray) ->
     y = rmsnorm(h1, w["post_attention_layernorm.weight"], d.rms_eps)
     mlp = gemm(silu(gemm(y, w["mlp.gate_proj.weight"])) * gemm(y, w["mlp.up_proj.weight"]), w["mlp.down_proj.weight"])
     return h1 + mlp
+
+
+def gdn_mixer_prefill(w: dict, d: GdnDims, x: np.ndarray, conv0=None, S0=None, chunked: bool = True):
+    """The delta-rule mixer alone on one normalised sequence x [L, hidden]: out_proj of the gated-normed outputs
+    (before the residual). Returns (mix [L, hidden], final conv state, final states [n_v, dv, dk])."""
+    qkv, z, g, beta = _mixer_inputs(w, d, x.astype(F32))
+    c, conv_fin = conv1d_prefill(qkv, w["conv1d.weight"], w["conv1d.bias"], conv0)
+    q, k, v = _split_heads(d, c)
+    rep = d.n_v // d.n_k
+    L = x.shape[0]
+    o = np.zeros((L, d.n_v, d.dv), F32)
+    S_fin = np.zeros((d.n_v, d.dv, d.dk), F32)
+    for j in range(d.n_v):
+        kh = j // rep
+        s0 = None if S0 is None else S0[j]
+        if chunked:
+            o[:, j], S_fin[j] = gdn_chunked(q[:, kh], k[:, kh], v[:, j], g[:, j], beta[:, j], d.chunk, s0)
+        else:
+            o[:, j], S_fin[j] = gdn_recurrent(q[:, kh], k[:, kh], v[:, j], g[:, j], beta[:, j], s0)
+    oz = rmsnorm(o.reshape(L * d.n_v, d.dv), w["norm.weight"], d.rms_eps).reshape(L, d.n_v, d.dv)
+    oz = oz * silu(z.reshape(L, d.n_v, d.dv))
+    return gemm(oz.reshape(L, -1), w["out_proj.weight"]), conv_fin, S_fin
 
 
 def gdn_layer_prefill(w: dict, d: GdnDims, h: np.ndarray, conv0=None, S0=None, chunked: bool = True):

@@ -27,3 +27,18 @@ def test_oracle_matches_published_gated_delta_rule(form, head):
     for ref_o, ref_s in ((G["o_recurrent"][:, head], G["s_recurrent"][head]), (G["o_chunk"][:, head], G["s_chunk"][head])):
         assert rel(o, ref_o) < 1e-5
         assert rel(S, ref_s.T) < 1e-5
+
+
+def test_oracle_mixer_matches_public_qwen3_next_gated_deltanet():
+    """The whole delta-rule mixer (projections, causal conv + SiLU, L2-normalised q/k, decay -exp(A_log)
+    softplus(a + dt_bias), beta, chunked rule, norm-before-gate RMSNorm, out_proj) against transformers'
+    Qwen3-Next Gated DeltaNet module on the same weights (fixture: tests/golden/make_qwen3next_golden.py)."""
+    import oracle
+    from oracle.gdn_layer import gdn_mixer_prefill
+    from tests.golden.make_qwen3next_golden import dims, layer_input, layer_weights
+
+    d = dims()
+    w = {k: oracle.to_numpy(v) for k, v in layer_weights(d).items()}
+    mix, _, _ = gdn_mixer_prefill(w, d, layer_input(d).numpy())
+    ref = np.load(Path(__file__).resolve().parent / "golden" / "qwen3next_golden.npz")["out"]
+    assert rel(mix, ref) < 1e-5
