@@ -70,7 +70,8 @@ def gdn_chunked(q, k, v, g, beta, chunk: int, S0=None):
         b = beta[sl].astype(F32)
         cum = np.cumsum(g[sl].astype(F32))
         n = K.shape[0]
-        ratio = np.exp(cum[:, None] - cum[None, :])  # gamma_i / gamma_j
+        causal = np.tril(np.ones((n, n), bool))
+        ratio = np.exp(np.where(causal, cum[:, None] - cum[None, :], 0)).astype(F32)  # gamma_i / gamma_j for j <= i
         lower = np.tril(np.ones((n, n), bool), -1)
         Lm = np.where(lower, ratio * (K @ K.T), 0).astype(F32)
         A = np.eye(n, dtype=F32) + b[:, None] * Lm
