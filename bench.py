@@ -355,6 +355,21 @@ def ssu_roofline(layer, n: int = 50) -> dict | None:
     return {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
 
 
+def layout_candidates(dims, world: int, batch: int, ctx: int) -> list[str]:
+    """The decode layouts timed at `world` ranks (the fastest is reported): one rank runs tp1; more run the even
+    branch split, the split whose busiest rank moves the fewest step bytes (more ranks on the Mamba-2 branch when
+    its state dominates), and tensor parallelism with fused projections. Every rank derives the same list."""
+    from multi_modal_parallelism_b200.measure import split_by_bytes
+
+    if world == 1:
+        return ["tp1"]
+    modes = [f"split{world // 2}{world // 2}"]
+    by_bytes = split_by_bytes(dims, world, batch, ctx)
+    if by_bytes not in modes:
+        modes.append(by_bytes)
+    return modes + ["tp4_fused"]
+
+
 def our_arm(args) -> None:
     import torch
 
@@ -370,7 +385,7 @@ def our_arm(args) -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     dims = preset(args.dims)
     full = random_layer(dims, args.seed)
-    modes = ["tp1"] if world == 1 else [f"split{world // 2}{world // 2}", "tp4_fused"]
+    modes = layout_candidates(dims, world, args.batch, args.ctx)
     results = {}
     keep = {}
     for mode in modes:

@@ -76,6 +76,25 @@ def step_hbm_bytes(plan, dims: FalconH1Dims, B: int, c: int, state_bytes: int = 
     return total
 
 
+def split_by_bytes(dims: FalconH1Dims, world: int, B: int, c: int, state_bytes: int = 4) -> str:
+    """The branch split split{a}{world - a} whose busiest rank has the fewest algorithmic decode-step bytes
+    (`step_hbm_bytes`) at batch B and context c: the layout a bandwidth-bound decode step favours when every rank
+    streams at the same rate. Splits the dimensions do not divide (`plan_for` refuses them) are skipped; ties go
+    to the split with more attention ranks."""
+    best = None
+    for a in range(world - 1, 0, -1):
+        mode = f"split{a}{world - a}"
+        try:
+            worst = max(step_hbm_bytes(plan_for(mode, r, world, dims), dims, B, c, state_bytes) for r in range(world))
+        except ValueError:
+            continue
+        if best is None or worst < best[0]:
+            best = (worst, mode)
+    if best is None:
+        raise ValueError(f"split_by_bytes: no split{{a}}{{m}} divides these dimensions over {world} ranks")
+    return best[1]
+
+
 def resolve_k(spec: RunSpec, dims: FalconH1Dims, world: int, bw: BwTables | None = None) -> tuple[int, int | None, str]:
     """(w, k, cuts_src) of the swing pool (`harness/measure.py:48-62`): 'model' asks the byte model for the cut
     with the smallest predicted slowest-rank step under the bandwidth tables `bw` (neutral without tables)."""

@@ -141,6 +141,7 @@ def run_world(world, mode, dims_name="g1"):
 @pytest.mark.parametrize("world,mode,dims_name", [
     (2, "split11", "g1"), (2, "tp4", "g1"), (2, "tp4_fused", "g2"),
     (4, "split13", "g1"), (4, "split22", "g1"), (4, "tp4", "g2"), (4, "split22", "g2"),
+    (8, "split26", "g1"),
 ])
 def test_sharded_partials_all_reduce_to_the_full_layer(world, mode, dims_name):
     res = run_world(world, mode, dims_name)

@@ -24,3 +24,53 @@ def test_branch_splits_add_only_the_replicated_group_rows(mode, world, ssm_ranks
     per_extra_rank = 2 * gn * d.hidden * 2 + 2 * B * (d.d_conv - 1) * 2 * gn * 2
     total = sum(step_hbm_bytes(plan_for(mode, r, world, d), d, B, c) for r in range(world))
     assert total - one == (ssm_ranks - 1) * per_extra_rank
+
+
+@pytest.mark.parametrize("world,expected", [(2, "split11"), (4, "split13"), (8, "split26")])
+def test_split_by_bytes_puts_the_state_heavy_branch_on_more_ranks(world, expected):
+    """At batch 64, context 2048 the fp32 SSM state (402.7 MB) outweighs keys and values (134.3 MB), so the split
+    with the lightest busiest rank gives the Mamba-2 branch more ranks; it is the minimum over every split the
+    dimensions divide."""
+    from multi_modal_parallelism_b200.measure import split_by_bytes
+
+    d = preset("falcon_h1_7b_like")
+    pick = split_by_bytes(d, world, 64, 2048)
+    assert pick == expected
+    worst = {}
+    for a in range(1, world):
+        mode = f"split{a}{world - a}"
+        try:
+            worst[mode] = max(step_hbm_bytes(plan_for(mode, r, world, d), d, 64, 2048) for r in range(world))
+        except ValueError:
+            pass
+    assert worst[pick] == min(worst.values())
+
+
+def test_split_by_bytes_follows_the_keys_when_context_is_long():
+    """At context 32768 the keys and values (about 2.1 GB at batch 64) outweigh the state: the pick moves toward
+    more attention ranks."""
+    from multi_modal_parallelism_b200.measure import split_by_bytes
+
+    d = preset("falcon_h1_7b_like")
+    short, long = split_by_bytes(d, 8, 64, 2048), split_by_bytes(d, 8, 64, 32768)
+    assert int(long[5]) > int(short[5])  # attention ranks: split{a}{m}
+
+
+def test_bench_layout_candidates_are_valid_and_rank_independent():
+    """bench.py's N>1 list: the even split, the byte-model split when it differs, tp4_fused; every entry plans on
+    every rank (a layout that fails on one rank would leave the others waiting in a collective)."""
+    import importlib.util
+    from pathlib import Path
+
+    spec = importlib.util.spec_from_file_location("bench_mod", Path(__file__).resolve().parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    d = preset("falcon_h1_7b_like")
+    assert bench.layout_candidates(d, 1, 64, 2048) == ["tp1"]
+    assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split13", "tp4_fused"]
+    for world in (2, 4, 8):
+        modes = bench.layout_candidates(d, world, 64, 2048)
+        assert len(set(modes)) == len(modes)
+        for mode in modes:
+            for r in range(world):
+                plan_for(mode, r, world, d)

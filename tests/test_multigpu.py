@@ -57,7 +57,7 @@ def test_four_gpu_layouts(mode, tmp_path):
 
 
 @pytest.mark.skipif(ngpu() < 8, reason="needs 8 GPUs")
-@pytest.mark.parametrize("mode", ["split44", "tp4_fused"])
+@pytest.mark.parametrize("mode", ["split44", "split26", "tp4_fused"])
 def test_eight_gpu_layouts(mode, tmp_path):
     run_check(8, mode, tmp_path)
 
