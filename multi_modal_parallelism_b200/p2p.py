@@ -72,15 +72,15 @@ class PeerAllReduce(_PeerBuffer):
              k_seg: int | None = None, alpha2: float | None = None) -> None:
         """This rank's partial alpha * colscale * (x @ w^T) (x: [rows <= 256, K] decode rows; w: [hidden, K]),
         written by the GEMM straight into every rank's buffer; complete it with join(None, ..., pushed rows)."""
-        from .kernels import _rowmajor, _stream, error_word
+        from .kernels import _cuda, _dtype, _rowmajor, _stream, error_word
 
         M, K = x.shape
         if w.shape[0] != self.hidden or w.shape[1] != K or M > self.rows_max:
             raise ValueError(f"PeerAllReduce.gemm: x {tuple(x.shape)} w {tuple(w.shape)} for [{self.rows_max}, "
                              f"{self.hidden}]")
+        _cuda("PeerAllReduce.gemm", x, w, colscale)
         for t in (x, w):
-            if t.dtype != torch.bfloat16 or not t.is_cuda:
-                raise ValueError("PeerAllReduce.gemm: bf16 CUDA tensors expected")
+            _dtype("PeerAllReduce.gemm", t, torch.bfloat16)
         if colscale is not None and (colscale.dtype != torch.float32 or colscale.numel() != self.hidden):
             raise ValueError("PeerAllReduce.gemm: colscale must be fp32 [hidden]")
         ks = K if k_seg is None else int(k_seg)
@@ -95,15 +95,15 @@ class PeerAllReduce(_PeerBuffer):
              norm_w: torch.Tensor | None = None, eps: float = 0.0, norm_out: torch.Tensor | None = None) -> torch.Tensor:
         """sum_out = resid + all-reduce(part) (bf16); with norm_w also norm_out = rmsnorm(sum_out) * norm_w.
         part None: the partial is the one the last gemm() pushed. Returns norm_out when given, else sum_out."""
-        from .kernels import _rowmajor, _stream, error_word
+        from .kernels import _cuda, _dtype, _rowmajor, _stream, error_word
 
         pushed = part is None
         rows, H = (self._pushed_rows, self.hidden) if pushed else part.shape
         if H != self.hidden or rows > self.rows_max:
             raise ValueError(f"PeerAllReduce.join: [{rows}, {H}] does not fit [{self.rows_max}, {self.hidden}]")
+        _cuda("PeerAllReduce.join", part, resid, sum_out, norm_w, norm_out)
         for t in (part, resid, sum_out, norm_w, norm_out):
-            if t is not None and (t.dtype != torch.bfloat16 or not t.is_cuda):
-                raise ValueError("PeerAllReduce.join: bf16 CUDA tensors expected")
+            _dtype("PeerAllReduce.join", t, torch.bfloat16)
         if (norm_w is None) != (norm_out is None):
             raise ValueError("PeerAllReduce.join: norm_w and norm_out go together")
         p = lambda t: None if t is None else t.data_ptr()  # noqa: E731
@@ -126,11 +126,14 @@ class PeerRowNorm(_PeerBuffer):
         super().__init__(group, global_rank, int(_lib.lib().mmp_gn_buffer_bytes(group.world_size, rows_max)), device)
 
     def __call__(self, y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
-        from .kernels import _rowmajor, _stream, error_word
+        from .kernels import _cuda, _dtype, _rowmajor, _stream, error_word
 
         rows, D = y.shape
         if rows > self.rows_max or z.shape != y.shape or out.shape != y.shape or w.numel() != D:
             raise ValueError(f"PeerRowNorm: y {tuple(y.shape)} z {tuple(z.shape)} out {tuple(out.shape)} w {w.numel()}")
+        _cuda("PeerRowNorm", y, z, w, out)
+        for t in (y, z, w, out):
+            _dtype("PeerRowNorm", t, torch.bfloat16)
         _lib.call("mmp_gated_rmsnorm_p2p", self.bufs.data_ptr(), self.rank, self.world, self.rows_max, y.data_ptr(),
                   _rowmajor("y", y), z.data_ptr(), _rowmajor("z", z), w.data_ptr(), out.data_ptr(),
                   _rowmajor("out", out), rows, D, float(eps), error_word(y.device).data_ptr(), _stream(y))
