@@ -277,7 +277,9 @@ def profiled_traffic(name: str) -> float | None:
     return None
 
 
-def build_layer(args, mode, groups, dims, full):
+def build_layer(args, label, groups, dims, full, single_rank: bool = False):
+    """The decode layer of recipe `label` on this rank, with its seeded states and input. single_rank: the whole
+    layer on this GPU alone (tp1, no collectives), the agreement check's reference at any world size."""
     import torch
 
     from multi_modal_parallelism_b200.layer import ParallelHybridLayer
@@ -286,12 +288,16 @@ def build_layer(args, mode, groups, dims, full):
     from multi_modal_parallelism_b200.weights import shard_to_device
 
     dev = groups.device
-    plan = plan_for(mode, groups.rank, groups.world_size, dims)
+    mode, chains = parse_recipe(label)
+    plan = plan_for("tp1", 0, 1, dims) if single_rank else plan_for(mode, groups.rank, groups.world_size, dims)
     rw = shard_to_device(full, plan, dims, dev)
     ctx = make_decode_ctx(args.batch, args.ctx, 16, dev)
     st = alloc_and_fill(plan, dims, ctx, args.seed, dev, ssm_dtype=torch.float32)
     h = input_hidden(args.seed, args.batch, dims.hidden, dev)
-    layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev, ar_impl=getattr(args, "ar_impl", "nccl"))
+    if single_rank:
+        return ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev, collectives=False), h
+    layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev, ar_impl=getattr(args, "ar_impl", "nccl"),
+                                branch_chains=chains)
     return layer, h
 
 
@@ -355,19 +361,26 @@ def ssu_roofline(layer, n: int = 50) -> dict | None:
     return {"us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3}
 
 
-def layout_candidates(dims, world: int, batch: int, ctx: int) -> list[str]:
-    """The decode layouts timed at `world` ranks (the fastest is reported): one rank runs tp1; more run the even
-    branch split, the split whose busiest rank moves the fewest step bytes (more ranks on the Mamba-2 branch when
-    its state dominates), and tensor parallelism with fused projections. Every rank derives the same list."""
+def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nccl") -> list[str]:
+    """The decode recipes timed at `world` ranks (the fastest that agrees with a single-rank step is reported):
+    one rank runs tp1 with fused projections and tp1 with the branch-chains schedule (`_chains`: each branch's
+    whole chain on its own stream); more run the even branch split, the split whose busiest rank moves the fewest
+    step bytes (more ranks on the Mamba-2 branch when its state dominates), and tp4_fused in both schedules (the
+    chains schedule is not combined with a pushed out-projection). Every rank derives the same list."""
     from multi_modal_parallelism_b200.measure import split_by_bytes
 
     if world == 1:
-        return ["tp1"]
+        return ["tp1", "tp1_chains"]
     modes = [f"split{world // 2}{world // 2}"]
     by_bytes = split_by_bytes(dims, world, batch, ctx)
     if by_bytes not in modes:
         modes.append(by_bytes)
-    return modes + ["tp4_fused"]
+    return modes + ["tp4_fused"] + ([] if ar_impl == "p2p_fused" else ["tp4_fused_chains"])
+
+
+def parse_recipe(label: str) -> tuple[str, bool]:
+    """(layout, branch_chains) of a recipe label such as "tp4_fused_chains"."""
+    return (label[:-len("_chains")], True) if label.endswith("_chains") else (label, False)
 
 
 def our_arm(args) -> None:
@@ -375,6 +388,7 @@ def our_arm(args) -> None:
 
     from multi_modal_parallelism_b200 import _lib
     from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.correctness import compare, within_tolerance
     from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
     from multi_modal_parallelism_b200.timing import GraphedStep
     from multi_modal_parallelism_b200.weights import random_layer
@@ -385,21 +399,32 @@ def our_arm(args) -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     dims = preset(args.dims)
     full = random_layer(dims, args.seed)
-    modes = layout_candidates(dims, world, args.batch, args.ctx)
+    modes = layout_candidates(dims, world, args.batch, args.ctx, args.ar_impl)
     results = {}
     keep = {}
+    # every recipe's first decode step is checked against the whole layer on one GPU (same seeded weights,
+    # states and input; bf16 tolerance); a recipe that disagrees on any rank is timed but never reported
+    ref_layer, h_ref = build_layer(args, "tp1", groups, dims, full, single_rank=True)
+    ref_out = ref_layer.step(h_ref).clone()
+    del ref_layer, h_ref
+    torch.cuda.empty_cache()
     for mode in modes:
         layer, h = build_layer(args, mode, groups, dims, full)
-        layer.step(h)  # eager warm-up (allocations, library init)
+        m = compare(layer.step(h), ref_out)  # also the eager warm-up (allocations, library init)
+        agrees = max_over_ranks(0.0 if within_tolerance(m) else 1.0, groups) == 0.0
         n0 = _lib.LAUNCHES[0]
         layer.step(h)
         launches_per_step = _lib.LAUNCHES[0] - n0
         gs = GraphedStep(layer, groups, h)
         ms, p50 = time_replays(gs.replay, args.steps, args.warmup, groups)
         results[mode] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": args.batch / ms * 1e3,
-                         "launches_per_step": launches_per_step}
+                         "launches_per_step": launches_per_step, "agrees_with_single_gpu": agrees,
+                         "rel_l2_vs_single_gpu": max_over_ranks(m["rel_l2"], groups)}
         keep[mode] = (layer, h, gs)
-    best = min(results, key=lambda m: results[m]["ms_per_step"])
+    valid = [m for m in modes if results[m]["agrees_with_single_gpu"]]
+    if not valid:
+        raise SystemExit(f"no decode recipe agrees with the single-GPU layer step: {results}")
+    best = min(valid, key=lambda m: results[m]["ms_per_step"])
     layer, h, gs = keep[best]
     for m in modes:
         if m != best:

@@ -268,9 +268,13 @@ class SwingMLP:
 class ParallelHybridLayer:
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
                  ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True,
-                 ar_impl: str = "nccl"):
+                 ar_impl: str = "nccl", branch_chains: bool = False):
         """overlap_branches: on a rank holding both branches (fused projections), run the attention core on a
-        side stream concurrently with the Mamba-2 core. `ctx` is a DecodeCtx (step() is one decode step) or a
+        side stream concurrently with the Mamba-2 core. branch_chains (decode, tp1 / tp4_fused, a rank holding
+        both branches, no pushed GEMM): instead of fused projections, the attention branch's whole chain (QKV
+        GEMM, RoPE + KV write, attention, o-projection) runs on the side stream while the Mamba-2 chain runs on
+        this one, and the Mamba-2 out-projection adds the attention partial as its addend; the attention GEMMs'
+        latency (first loads, epilogue) then hides under the Mamba-2 chain instead of lying on the step's path. `ctx` is a DecodeCtx (step() is one decode step) or a
         PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer). ar_impl "p2p": the
         decode step's [B, H] all-reduces (mixer and MLP; not tp4's per-branch pair) run as the peer-memory
         all-reduce fused with the residual add and the next norm (p2p.PeerAllReduce); "p2p_fused": in addition the
@@ -292,8 +296,10 @@ class ParallelHybridLayer:
         # A rank holding both branches runs their input projections as one GEMM (shared input) and their
         # output projections as one two-segment GEMM (shared output), except in tp4 / tp4_streams, whose point
         # is separate branch outputs.
-        self.fused = (plan.attn is not None and plan.ssm is not None and w.w_in_cat is not None
-                      and self.mode in ("tp1", "tp4_fused"))
+        both = plan.attn is not None and plan.ssm is not None and self.mode in ("tp1", "tp4_fused")
+        self.chains = (branch_chains and both and not isinstance(ctx, PrefillCtx)
+                       and not (ar_impl == "p2p_fused" and self.mode == "tp4_fused"))
+        self.fused = both and w.w_in_cat is not None and not self.chains
         qkv = zx = ao = yn = None
         self.out_ratio = None
         B = ctx.rows
@@ -344,7 +350,7 @@ class ParallelHybridLayer:
         # buffer as its tiles finish, and the join kernel only waits, sums and normalises
         self.push = self.p2p if ar_impl == "p2p_fused" else None
         self.overlap = self.fused and overlap_branches
-        if self.overlap:
+        if self.overlap or self.chains:
             self.s_side = torch.cuda.Stream(device=device)
         if self.mode == "tp4_streams":
             self.s_attn = torch.cuda.Stream(device=device)
@@ -444,6 +450,22 @@ class ParallelHybridLayer:
             t.end("mixer.outproj")
             if mode == "tp4_fused":
                 self._reduce_join(h, t, pushed)
+                y_ready = self.has_mlp
+        elif self.chains:
+            # attention chain on the side stream (h + its partial in tp1), Mamba-2 chain here; they meet at the
+            # Mamba-2 out-projection, which adds the attention partial
+            cur = torch.cuda.current_stream(self.device)
+            self.s_side.wait_stream(cur)
+            with torch.cuda.stream(self.s_side):
+                self.attn.decode(x, t, out=self.part_a, addend=h if mode == "tp1" else None, x_scale=dims.attn_in)
+            self.ssm.project_in(x, t, dims.ssm_in)
+            self.ssm.core(t)
+            cur.wait_stream(self.s_side)
+            if mode == "tp1":
+                self.ssm.project_out(t, out=self.h1, addend=self.part_a)
+            else:
+                self.ssm.project_out(t, out=self.mix, addend=self.part_a)
+                self._reduce_join(h, t)
                 y_ready = self.has_mlp
         elif mode == "tp1":
             self.attn.decode(x, t, out=self.h1, addend=h, x_scale=dims.attn_in)

@@ -4,8 +4,9 @@ CUDA-graph step timing, CSV rows.
 Same flow as the reference's `harness/measure.py:65-158`: build the rank's plan, weights, metadata and
 seeded states; with `check`, run one step, require bitwise-identical outputs across ranks and compare rank
 0's output with the fp32 layer (`reference.decode_step` on the full weights and states); restore the states;
-time eager and/or graph steps; gather rows and record the max over ranks. The byte-model predictions of the
-reference (`harness/model.py`) are not part of this build; the rows carry tokens/s instead.
+time eager and/or graph steps; gather rows and record the max over ranks. Each row also carries the byte model's
+per-op prediction for the rank (`model.py`, when bandwidth tables are given), the step's algorithmic HBM bytes and
+the fraction of the measured copy bandwidth they reach.
 """
 from __future__ import annotations
 
@@ -132,7 +133,7 @@ def check_against_reference(spec: RunSpec, dims: FalconH1Dims, full: dict, out: 
 
 def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, torch.Tensor], out_csv: str,
             correctness_csv: str, check: bool, bw=None, image_tag: str = "",
-            ssm_dtype: torch.dtype = torch.float32, ar_impl: str = "nccl") -> list[dict]:
+            ssm_dtype: torch.dtype = torch.float32, ar_impl: str = "nccl", branch_chains: bool = False) -> list[dict]:
     rank, world, device = groups.rank, groups.world_size, groups.device
     w, k, cuts_src = resolve_k(spec, dims, world, bw)
     plan = plan_for(spec.mode, rank, world, dims, spec.swing, k)
@@ -147,7 +148,7 @@ def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, t
     st = alloc_and_fill(plan, dims, ctx, spec.seed, device, ssm_dtype=ssm_dtype)
     h = input_hidden(spec.seed, spec.batch, dims.hidden, device)
     layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, device, collectives=spec.collectives,
-                                ar_impl=ar_impl)
+                                ar_impl=ar_impl, branch_chains=branch_chains)
     barrier_sync()
 
     run_id = uuid.uuid4().hex[:8]

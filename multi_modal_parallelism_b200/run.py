@@ -68,6 +68,8 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--ssm-dtype", choices=["fp32", "bf16"], default="fp32")
     ap.add_argument("--ar-impl", choices=["nccl", "p2p", "p2p_fused"], default="nccl",
                     help="p2p: decode all-reduces over NVLink peer memory, fused with the residual and norm")
+    ap.add_argument("--branch-chains", action="store_true",
+                    help="tp1 / tp4_fused: each branch's whole chain (projections included) on its own stream")
     args = ap.parse_args(argv)
 
     if args.k in ("neutral", "model"):
@@ -83,7 +85,8 @@ def main(argv: list[str] | None = None) -> int:
     ssm_dtype = torch.float32 if args.ssm_dtype == "fp32" else torch.bfloat16
     bw = BwTables.from_csv(args.bw) if args.bw and os.path.exists(args.bw) else None
     rows = measure(spec, groups, dims, full, args.out, args.correctness_out, args.check, bw,
-                   os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype, ar_impl=args.ar_impl)
+                   os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype, ar_impl=args.ar_impl,
+                   branch_chains=args.branch_chains)
     ok = True
     if args.check and groups.rank == 0:
         with open(args.correctness_out) as f:

@@ -57,8 +57,9 @@ def test_split_by_bytes_follows_the_keys_when_context_is_long():
 
 
 def test_bench_layout_candidates_are_valid_and_rank_independent():
-    """bench.py's N>1 list: the even split, the byte-model split when it differs, tp4_fused; every entry plans on
-    every rank (a layout that fails on one rank would leave the others waiting in a collective)."""
+    """bench.py's recipe lists: tp1 in both schedules at N=1; at N>1 the even split, the byte-model split when it
+    differs, tp4_fused in both schedules (one with a pushed out-projection); every layout plans on every rank (a
+    layout that fails on one rank would leave the others waiting in a collective)."""
     import importlib.util
     from pathlib import Path
 
@@ -66,11 +67,15 @@ def test_bench_layout_candidates_are_valid_and_rank_independent():
     bench = importlib.util.module_from_spec(spec)
     spec.loader.exec_module(bench)
     d = preset("falcon_h1_7b_like")
-    assert bench.layout_candidates(d, 1, 64, 2048) == ["tp1"]
-    assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split13", "tp4_fused"]
-    for world in (2, 4, 8):
-        modes = bench.layout_candidates(d, world, 64, 2048)
-        assert len(set(modes)) == len(modes)
-        for mode in modes:
+    assert bench.layout_candidates(d, 1, 64, 2048) == ["tp1", "tp1_chains"]
+    assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split13", "tp4_fused", "tp4_fused_chains"]
+    assert bench.layout_candidates(d, 4, 64, 2048, "p2p_fused") == ["split22", "split13", "tp4_fused"]
+    assert bench.parse_recipe("tp4_fused_chains") == ("tp4_fused", True)
+    assert bench.parse_recipe("split26") == ("split26", False)
+    for world in (1, 2, 4, 8):
+        labels = bench.layout_candidates(d, world, 64, 2048)
+        assert len(set(labels)) == len(labels)
+        for label in labels:
+            mode, _ = bench.parse_recipe(label)
             for r in range(world):
                 plan_for(mode, r, world, d)

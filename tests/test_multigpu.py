@@ -149,3 +149,15 @@ def test_layouts_with_peer_allreduce(world, mode, impl, tmp_path):
         pytest.skip(f"needs {world} GPUs")
     run_check(world, mode, tmp_path, ("--ar-impl", impl, "--dims-yaml", "falcon_h1_7b", "--swing", "0.2")
               if mode.startswith("split") else ("--ar-impl", impl))
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 1, reason="needs a GPU")
+@pytest.mark.parametrize("world,mode,extra", [(1, "tp1", ()), (2, "tp4_fused", ()), (2, "tp4_fused", ("--ar-impl", "p2p")),
+                                              (4, "tp4_fused", ())])
+def test_branch_chains_schedule(world, mode, extra, tmp_path):
+    """The branch-chains decode schedule (the attention chain on a side stream, the Mamba-2 out-projection adding
+    its partial) through run.py --check: within tolerance of the fp32 layer, ranks bitwise equal."""
+    if ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_check(world, mode, tmp_path, ("--branch-chains", *extra))
