@@ -257,6 +257,12 @@ __global__ void __launch_bounds__(ATHR, 2) attn_prefill_kernel(const AttnPrefill
 }
 
 }  // namespace
+
+int attn_prefill_tc(const void* q, int64_t q_t, int64_t q_h, const void* key_cache, const void* value_cache,
+                    int64_t c_block, int64_t c_tok, int64_t c_head, const int32_t* block_table, int64_t bt_stride,
+                    const int32_t* cu_q, const int32_t* ctx_start, void* out, int64_t o_t, int64_t o_h, int nseq,
+                    int max_q_len, int nq, int nkv, int hd, int block_size, int num_blocks, float scale, int* err,
+                    cudaStream_t stream);
 }  // namespace mmp
 
 using namespace mmp;
@@ -277,12 +283,18 @@ extern "C" int mmp_paged_attn_prefill(const void* q, int64_t q_t, int64_t q_h,
   if (!aligned16(q) || !aligned16(key_cache) || !aligned16(value_cache) || q_t % 8 || q_h % 8 || c_block % 8 ||
       c_tok % 8 || c_head % 8 || (o_t | o_h) & 1 || (reinterpret_cast<uintptr_t>(out) & 3))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_paged_attn_prefill: q and cache rows must be 16-byte aligned");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  {
+    const int rc = attn_prefill_tc(q, q_t, q_h, key_cache, value_cache, c_block, c_tok, c_head, block_table, bt_stride,
+                                   cu_q, ctx_start, out, o_t, o_h, nseq, max_q_len, nq, nkv, hd, block_size, num_blocks,
+                                   scale, err, s);
+    if (rc != MMP_ERR_UNSUPPORTED) return rc;  // ran on the tensor cores (or failed there)
+  }
   AttnPrefillParams P{static_cast<const bf16*>(q), q_t, q_h, static_cast<const bf16*>(key_cache),
                       static_cast<const bf16*>(value_cache), c_block, c_tok, c_head, block_table, bt_stride, cu_q,
                       ctx_start, static_cast<bf16*>(out), o_t, o_h, nq, nkv, block_size, num_blocks,
                       (block_size & (block_size - 1)) == 0 ? __builtin_ctz(block_size) : -1,
                       scale * 1.4426950408889634f, err};
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -445,6 +445,12 @@ def ssd_prefill(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Ten
     return out
 
 
+def set_attn_prefill_tc(enable: bool) -> bool:
+    """Select the tcgen05/TMEM kernel for attn_prefill (True) or the mma.sync kernel (False, the default);
+    process-wide. Returns the previous setting."""
+    return bool(_lib.lib().mmp_set_attn_prefill_tc(1 if enable else 0))
+
+
 def attn_prefill(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor,
                  cu_q: torch.Tensor, ctx_start: torch.Tensor, max_q_len: int, out: torch.Tensor) -> torch.Tensor:
     """Causal GQA attention of new tokens q [T, nq, hd] over the paged cache (which already holds them)."""
