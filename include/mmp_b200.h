@@ -235,6 +235,25 @@ int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const void* dt, int
                     void* out, int64_t o_t, int64_t o_h,
                     int nseq, int ntok, int nh, int p, int N, int ngroups, int lines, int* err, void* stream);
 
+/* ---- prefill: the chunked SSD scan with balanced walks ---------------------------------------------------
+ * Same result as mmp_ssd_prefill (up to rounding) for head dim 128. The host cuts each sequence at 64-token chunk
+ * boundaries into segments (vcu: [nvirt + 1] packed-row offsets; sequence i owns segments [seg0[i], seg0[i + 1]));
+ * the scan runs them as independent sequences with their states in `scratch` ([scratch_lines][nh][128][N] fp32,
+ * contiguous; vline[v] = v, vinit[v] = has_init of a sequence's first segment, else 0), so more, shorter walks
+ * fill the SMs; then one kernel per (head, sequence) chains the segment states, adds exp(cum_t) S_in C_t to the
+ * later segments' outputs and writes the final state to line state_idx[i]. A sequence that continues
+ * (has_init[i]) first has its line copied to its first segment's scratch line. Other arguments as
+ * mmp_ssd_prefill (cu_seqlens of the sequences is implied by vcu and seg0).
+ */
+int mmp_ssd_prefill_seg(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h,
+                        const float* A, const float* D, const float* dt_bias,
+                        const void* B, int64_t B_t, int64_t B_g, const void* C, int64_t C_t, int64_t C_g,
+                        void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
+                        const int32_t* state_idx, const int32_t* has_init, void* out, int64_t o_t, int64_t o_h,
+                        const int32_t* vcu, const int32_t* vline, const int32_t* vinit, const int32_t* seg0,
+                        float* scratch, int scratch_lines, int nvirt, int nseq, int ntok, int nh, int p, int N,
+                        int ngroups, int lines, int* err, void* stream);
+
 /* ---- prefill: causal GQA attention over the paged KV cache ----------------------------------------------
  * The prefill counterpart of mmp_paged_attn_decode (FlashAttention-2 varlen, causal). Query token j of
  * sequence i (rows [cu_q[i], cu_q[i+1]) of q) sits at position ctx_start[i] + j and attends to cache positions

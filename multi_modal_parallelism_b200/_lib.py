@@ -43,6 +43,8 @@ SIGNATURES: dict[str, tuple] = {
     "mmp_conv1d_prefill": (I32, [P, I64, P, I64, P, I64, I64, P, P, P, P, P, I32, I32, I32, I32, I32, I32, P, P]),
     "mmp_ssd_prefill": (I32, [P, I64, I64, P, I64, I64, P, P, P, P, I64, I64, P, I64, I64, P, I32, I64, I64, I64,
                               P, P, P, P, I64, I64, I32, I32, I32, I32, I32, I32, I32, P, P]),
+    "mmp_ssd_prefill_seg": (I32, [P, I64, I64, P, I64, I64, P, P, P, P, I64, I64, P, I64, I64, P, I32, I64, I64, I64,
+                                  P, P, P, I64, I64, P, P, P, P, P, I32, I32, I32, I32, I32, I32, I32, I32, I32, P, P]),
     "mmp_paged_attn_prefill": (I32, [P, I64, I64, P, P, I64, I64, I64, P, I64, P, P, P, I64, I64, I32, I32, I32, I32,
                                      I32, I32, I32, F32, P, P]),
     "mmp_add": (I32, [P, I64, P, I64, P, I64, P, I64, I32, I32, P]),

@@ -445,6 +445,27 @@ def ssd_prefill(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Ten
     return out
 
 
+def ssd_prefill_segmented(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B: torch.Tensor, C: torch.Tensor,
+                          D: torch.Tensor | None, dt_bias: torch.Tensor | None, state: torch.Tensor,
+                          state_idx: torch.Tensor, has_init: torch.Tensor | None, out: torch.Tensor, segs) -> torch.Tensor:
+    """ssd_prefill with the sequences cut into the segments of `segs` (segments.SsdSegments): the same outputs and
+    final states (up to rounding), the scan's walks balanced over the SMs."""
+    _cuda("ssd_prefill_segmented", x, dt, A, B, C, D, dt_bias, state, state_idx, has_init, out, segs.vcu, segs.scratch)
+    T, nh, p = x.shape
+    lines, _, _, N = state.shape
+    sc = segs.scratch
+    if sc.shape[1:] != (nh, p, N) or not sc.is_contiguous() or sc.dtype != torch.float32:
+        raise ValueError(f"ssd_prefill_segmented: scratch {tuple(sc.shape)} for [*, {nh}, {p}, {N}] fp32, contiguous")
+    nseq = segs.seg0.numel() - 1
+    _lib.call("mmp_ssd_prefill_seg", _p(x), x.stride(0), x.stride(1), _p(dt), dt.stride(0), dt.stride(1), _p(A), _p(D),
+              _p(dt_bias), _p(B), B.stride(0), B.stride(1), _p(C), C.stride(0), C.stride(1), _p(state),
+              MMP_F32 if state.dtype == torch.float32 else MMP_BF16, state.stride(0), state.stride(1), state.stride(2),
+              _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1), _p(segs.vcu), _p(segs.vline),
+              _p(segs.vinit), _p(segs.seg0), _p(sc), sc.shape[0], segs.nvirt, nseq, T, nh, p, N, B.shape[1], lines,
+              _p(error_word(x.device)), _stream(x), kernels=3)
+    return out
+
+
 def set_attn_prefill_tc(enable: bool) -> bool:
     """Select the tcgen05/TMEM kernel for attn_prefill (True) or the mma.sync kernel (False, the default);
     process-wide. Returns the previous setting."""

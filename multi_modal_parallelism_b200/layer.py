@@ -122,10 +122,11 @@ class SsmBranch:
 
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
                  device: torch.device, norm_group, zxbcdt: torch.Tensor | None = None, yn: torch.Tensor | None = None,
-                 norm_w: torch.Tensor | None = None, norm_peer=None):
+                 norm_w: torch.Tensor | None = None, norm_peer=None, ssd_segments: bool = False):
         """zxbcdt / yn: optional [B, in rows] and [B, nhr*p] views into buffers shared with the other branch;
         norm_w: the gated norm's weight when it carries an extra output scale (default w.norm_w); norm_peer: a
-        p2p.PeerRowNorm that replaces the norm group's all-reduce of the row statistic."""
+        p2p.PeerRowNorm that replaces the norm group's all-reduce of the row statistic; ssd_segments (prefill):
+        run the chunked scan with the sequences cut into balanced segments (segments.py) where that helps."""
         s = plan.ssm
         assert s is not None
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
@@ -159,6 +160,11 @@ class SsmBranch:
             self.xs_c = self.xBCc[:, :x].view(B, self.nhr, self.p)
             self.Bm_c = self.xBCc[:, x:x + b].view(B, self.ng, self.N)
             self.Cm_c = self.xBCc[:, x + b:].view(B, self.ng, self.N)
+        self.segs = None
+        if self.prefill and ssd_segments:
+            from .segments import build_segments
+
+            self.segs = build_segments(ctx.lens, ctx.has_init.tolist(), self.nhr, self.p, self.N, device)
         self.y = torch.empty(B, self.nhr, self.p, device=device, dtype=BF16)
         self.yn = yn if yn is not None else torch.empty(B, self.nhr * self.p, device=device, dtype=BF16)
         self.sumsq = torch.empty(B, 1, device=device, dtype=torch.float32)
@@ -180,8 +186,12 @@ class SsmBranch:
                            ctx.has_init, self.xBCc)
             t.end("ssm.conv")
             t.begin("ssm.ssd")
-            K.ssd_prefill(self.xs_c, self.dt, w.A, self.Bm_c, self.Cm_c, w.D, w.dt_bias, self.st.ssm_state,
-                          ctx.cu_seqlens, ctx.state_idx, ctx.has_init, self.y)
+            if self.segs is not None:
+                K.ssd_prefill_segmented(self.xs_c, self.dt, w.A, self.Bm_c, self.Cm_c, w.D, w.dt_bias,
+                                        self.st.ssm_state, ctx.state_idx, ctx.has_init, self.y, self.segs)
+            else:
+                K.ssd_prefill(self.xs_c, self.dt, w.A, self.Bm_c, self.Cm_c, w.D, w.dt_bias, self.st.ssm_state,
+                              ctx.cu_seqlens, ctx.state_idx, ctx.has_init, self.y)
             t.end("ssm.ssd")
             self._norm(t)
             return
@@ -268,13 +278,14 @@ class SwingMLP:
 class ParallelHybridLayer:
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
                  ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True,
-                 ar_impl: str = "nccl", branch_chains: bool = False):
+                 ar_impl: str = "nccl", branch_chains: bool = False, ssd_segments: bool = False):
         """overlap_branches: on a rank holding both branches (fused projections), run the attention core on a
         side stream concurrently with the Mamba-2 core. branch_chains (decode, tp1 / tp4_fused, a rank holding
         both branches, no pushed GEMM): instead of fused projections, the attention branch's whole chain (QKV
         GEMM, RoPE + KV write, attention, o-projection) runs on the side stream while the Mamba-2 chain runs on
         this one, and the Mamba-2 out-projection adds the attention partial as its addend; the attention GEMMs'
-        latency (first loads, epilogue) then hides under the Mamba-2 chain instead of lying on the step's path. `ctx` is a DecodeCtx (step() is one decode step) or a
+        latency (first loads, epilogue) then hides under the Mamba-2 chain instead of lying on the step's path.
+        ssd_segments: prefill() runs the Mamba-2 chunked scan with balanced walks (segments.py). `ctx` is a DecodeCtx (step() is one decode step) or a
         PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer). ar_impl "p2p": the
         decode step's [B, H] all-reduces (mixer and MLP; not tp4's per-branch pair) run as the peer-memory
         all-reduce fused with the residual add and the next norm (p2p.PeerAllReduce); "p2p_fused": in addition the
@@ -283,6 +294,7 @@ class ParallelHybridLayer:
         self.plan, self.w, self.dims, self.groups, self.ctx = plan, w, dims, groups, ctx
         self.st = st
         self.overlap_branches = overlap_branches
+        self.ssd_segments = ssd_segments
         self._prefill_twins: dict[int, ParallelHybridLayer] = {}
         self.collectives = collectives
         self.device = device
@@ -327,7 +339,7 @@ class ParallelHybridLayer:
             from .p2p import PeerRowNorm
 
             norm_peer = PeerRowNorm(norm_group, groups.rank, ctx.rows, device)  # collective over the norm group
-        self.ssm = (SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w, norm_peer)
+        self.ssm = (SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w, norm_peer, ssd_segments)
                     if plan.ssm is not None else None)
         self.has_mlp = dims.intermediate > 0
         self.mlp = SwingMLP(plan, w, dims, ctx.rows, device) if self.has_mlp else None
@@ -372,7 +384,7 @@ class ParallelHybridLayer:
         twin = self._prefill_twins.get(ctx.T)
         if twin is None:
             twin = ParallelHybridLayer(self.plan, self.w, self.dims, self.groups, self.st, ctx, self.device,
-                                       self.collectives, self.overlap_branches)
+                                       self.collectives, self.overlap_branches, ssd_segments=self.ssd_segments)
             self._prefill_twins[ctx.T] = twin
         twin._bind(ctx)
         if self.mlp is not None:
