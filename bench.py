@@ -48,6 +48,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--prefill-seqs", type=int, default=8)
     ap.add_argument("--prefill-len", type=int, default=2048, help="0 skips the prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=20)
+    ap.add_argument("--prefill-new", action="store_true",
+                    help="time the prefill with the tcgen05 attention kernel and the balanced-walk SSD scan")
     ap.add_argument("--workload", choices=["hybrid", "mamba2_sg", "qwen35"], default="hybrid",
                     help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split); "
                          "qwen35: the Gated DeltaNet hybrid block stack (tp and attention data-parallel)")
@@ -242,6 +244,19 @@ def time_prefill(args, layer, groups) -> dict | None:
     pc = make_prefill_ctx([L] * nseq, 16, dev, block_table=layer.ctx.block_table[:nseq].cpu(), reserve=0)
     g = torch.Generator().manual_seed(args.seed + 1)
     h = torch.randn(pc.T, layer.dims.hidden, generator=g).to(dev, torch.bfloat16)
+    kernels = "attention mma.sync, SSD scan tcgen05"
+    agrees = None
+    if args.prefill_new:
+        # the tcgen05 attention kernel and the balanced-walk scan, checked against the default kernels first
+        from multi_modal_parallelism_b200 import kernels as K
+        from multi_modal_parallelism_b200.correctness import compare, within_tolerance
+
+        ref = layer.prefill(h, pc).clone()
+        K.set_attn_prefill_tc(True)
+        layer.set_prefill_options(ssd_segments=True)
+        m = compare(layer.prefill(h, pc), ref)
+        agrees = max_over_ranks(0.0 if within_tolerance(m) else 1.0, groups) == 0.0
+        kernels = "attention tcgen05, SSD scan tcgen05 with balanced walks"
     for _ in range(3):
         layer.prefill(h, pc)
     barrier_sync()
@@ -254,13 +269,17 @@ def time_prefill(args, layer, groups) -> dict | None:
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.prefill_steps)]
     ms = max_over_ranks(statistics.median(per), groups)
     barrier_sync()
+    if args.prefill_new:
+        K.set_attn_prefill_tc(False)
+        layer.set_prefill_options(ssd_segments=False)
     fl = prefill_flops(layer.dims, [L] * nseq)
     peak, src = bf16_peak()
     tfs = fl["total"] / ms / 1e9
     return {"workload": f"{nseq} fresh sequences x {L} tokens", "tokens": pc.T, "ms_per_step": ms,
             "tokens_per_s": pc.T / ms * 1e3, "alg_tflop": {k: round(v / 1e12, 4) for k, v in fl.items()},
             "achieved_tflops": tfs, "peak_tflops": peak, "frac": tfs / peak, "peak_source": f"{src} bf16_tflops",
-            "timing": "eager, median of device-timed steps, max over ranks"}
+            "timing": "eager, median of device-timed steps, max over ranks", "kernels": kernels,
+            "agrees_with_default_kernels": agrees}
 
 
 def profiled_traffic(name: str) -> float | None:

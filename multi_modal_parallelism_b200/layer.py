@@ -374,6 +374,12 @@ class ParallelHybridLayer:
             if br is not None:
                 br.ctx = ctx
 
+    def set_prefill_options(self, ssd_segments: bool) -> None:
+        """Change how later prefills run (the balanced-walk SSD scan on or off); drops the per-shape prefill
+        layers built so far."""
+        self.ssd_segments = ssd_segments
+        self._prefill_twins.clear()
+
     def prefill(self, h: torch.Tensor, ctx: PrefillCtx, t: OpTimer = NULL) -> torch.Tensor:
         """Prefill of ctx.nseq ragged sequences packed into h [T, H]: the layer output [T, H], with every new
         token's key/value written to the paged cache and each sequence's final conv and SSM state written to
