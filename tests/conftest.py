@@ -11,12 +11,20 @@ if str(ROOT) not in sys.path:
 
 def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a B200 (CUDA sm_100a) and the built libmmp_b200.so")
-    config.addinivalue_line("markers", "run_last: collected after every other test, so that under -x a failure "
-                                       "there cannot hide the results of the rest of the suite")
+    config.addinivalue_line("markers", "run_last(order=0): collected after every other test, so that under -x a "
+                                       "failure there cannot hide the results of the rest of the suite; among "
+                                       "them, higher orders run later")
+
+
+def _run_last_key(it) -> tuple[int, int]:
+    m = it.get_closest_marker("run_last")
+    if m is None:
+        return (0, 0)
+    return (1, int(m.kwargs.get("order", m.args[0] if m.args else 0)))
 
 
 def pytest_collection_modifyitems(config, items):
-    items.sort(key=lambda it: 1 if "run_last" in it.keywords else 0)  # stable: file order otherwise kept
+    items.sort(key=_run_last_key)  # stable: file order otherwise kept
     # GPU tests are skipped, not failed, where no GPU is visible (the CPU suite runs everything else).
     try:
         import torch

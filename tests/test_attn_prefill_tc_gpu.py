@@ -11,7 +11,7 @@ import torch
 from multi_modal_parallelism_b200 import kernels as K
 from tests.test_prefill_kernels_gpu import BF, DEV, close, cu, npf, paged_reference
 
-pytestmark = [pytest.mark.gpu, pytest.mark.run_last]
+pytestmark = [pytest.mark.gpu, pytest.mark.run_last(order=2)]  # the newest kernels: after the rest
 
 
 @pytest.fixture(autouse=True)

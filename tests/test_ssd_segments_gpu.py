@@ -12,7 +12,7 @@ from multi_modal_parallelism_b200 import kernels as K
 from multi_modal_parallelism_b200.segments import build_segments
 from tests.test_prefill_kernels_gpu import BF, DEV, close, cu, npf
 
-pytestmark = [pytest.mark.gpu, pytest.mark.run_last]
+pytestmark = [pytest.mark.gpu, pytest.mark.run_last(order=1)]  # the newest kernels: after the rest
 
 
 @pytest.fixture(autouse=True)
