@@ -384,9 +384,10 @@ def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nc
     """The decode recipes timed at `world` ranks (the fastest that agrees with a single-rank step is reported):
     one rank runs tp1 with fused projections and tp1 with the branch-chains schedule (`_chains`: each branch's
     whole chain on its own stream); more run the even branch split, the split whose busiest rank moves the fewest
-    step bytes (more ranks on the Mamba-2 branch when its state dominates), and tp4_fused in both schedules (the
-    chains schedule is not combined with a pushed out-projection). Every rank derives the same list."""
-    from multi_modal_parallelism_b200.measure import split_by_bytes
+    step bytes (more ranks on the Mamba-2 branch when its state dominates), at two ranks the byte-balanced
+    mix{k} layouts, and tp4_fused in both schedules (the chains schedule is not combined with a pushed
+    out-projection). Every rank derives the same list."""
+    from multi_modal_parallelism_b200.measure import mix_by_bytes, split_by_bytes
 
     if world == 1:
         return ["tp1", "tp1_chains"]
@@ -394,7 +395,25 @@ def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nc
     by_bytes = split_by_bytes(dims, world, batch, ctx)
     if by_bytes not in modes:
         modes.append(by_bytes)
+    if world == 2:
+        # two ranks: the uneven layout with the busier rank's bytes balanced, and one with two heads fewer on
+        # the rank that also runs the attention chain (its kernels' fixed costs)
+        k = mix_by_bytes(dims, batch, ctx)
+        if k is not None:
+            modes += [f"mix{kk}" for kk in sorted({k, max(1, k - 2)}, reverse=True)
+                      if plan_ok(f"mix{kk}", dims, world)]
     return modes + ["tp4_fused"] + ([] if ar_impl == "p2p_fused" else ["tp4_fused_chains"])
+
+
+def plan_ok(mode: str, dims, world: int) -> bool:
+    from multi_modal_parallelism_b200.sharding import plan_for
+
+    try:
+        for r in range(world):
+            plan_for(mode, r, world, dims)
+        return True
+    except ValueError:
+        return False
 
 
 def parse_recipe(label: str) -> tuple[str, bool]:

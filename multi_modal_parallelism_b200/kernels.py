@@ -121,11 +121,13 @@ def silu_and_mul(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tens
 
 
 def gated_rmsnorm(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float, group, group_size: int | None = None,
-                  out: torch.Tensor | None = None, sumsq: torch.Tensor | None = None) -> torch.Tensor:
+                  out: torch.Tensor | None = None, sumsq: torch.Tensor | None = None,
+                  total_width: int | None = None) -> torch.Tensor:
     """Mamba-2 gated RMSNorm, gate before the norm. group=None: local norm over groups of `group_size`
     columns (None -> the whole row). Otherwise the row is one group spread over `group`'s ranks: the
     [T, 1] fp32 sum of squares is all-reduced over `group` (an object with `all_reduce(t) -> t` and
-    `world_size`, like the reference's coordinator) and the mean is taken over world_size * D."""
+    `world_size`, like the reference's coordinator) and the mean is taken over the group's full width,
+    `total_width` (default world_size * D: every rank holding D columns of it)."""
     _cuda("gated_rmsnorm", y, z, w, out)
     for t in (y, z, w, out):
         _dtype("gated_rmsnorm", t, BF16)
@@ -144,8 +146,9 @@ def gated_rmsnorm(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float,
     _lib.call("mmp_gated_rmsnorm", _p(y), ys, _p(z), zs, _p(w), _p(out), os_, _p(sumsq), rows, D, D, 1, 0.0,
               float(eps), st)
     total = group.all_reduce(sumsq)
+    width = group.world_size * D if total_width is None else int(total_width)
     _lib.call("mmp_gated_rmsnorm", _p(y), ys, _p(z), zs, _p(w), _p(out), os_, _p(total), rows, D, D, 2,
-              float(group.world_size * D), float(eps), st)
+              float(width), float(eps), st)
     return out
 
 

@@ -14,8 +14,10 @@ Prefill (`ParallelHybridLayer.prefill`) runs the same per-layout order over T pa
 with the prefill cores: causal paged GQA attention over the cache, and the varlen causal conv followed by
 the chunked SSD scan, each reading and writing the sequence's state line.
 Modes: tp1, tp4 (one all-reduce per branch), tp4_fused (one all-reduce of the summed branches),
-tp4_streams (branches on two streams, one all-reduce), and any branch split split{a}{m} (attention on
-ranks 0..a-1, Mamba-2 on a..a+m-1, one all-reduce); the "tp4" names work at any world size.
+tp4_streams (branches on two streams, one all-reduce), any branch split split{a}{m} (attention on
+ranks 0..a-1, Mamba-2 on a..a+m-1, one all-reduce), and mix{k} on two ranks (rank 0: the attention branch and
+Mamba-2 heads 0..k-1 with fused projections, rank 1: the other heads; one all-reduce), which balances the two
+ranks' bytes when the Mamba-2 state outweighs the KV cache; the "tp4" names work at any world size.
 """
 from __future__ import annotations
 
@@ -24,7 +26,7 @@ import torch
 from . import kernels as K
 from .config import FalconH1Dims
 from .dist import Groups
-from .sharding import RankPlan, all_norm_groups, parse_split
+from .sharding import RankPlan, all_norm_groups, parse_mix, parse_split
 from .state import DecodeCtx, PrefillCtx, RankStates
 from .timing import NULL, OpTimer
 from .weights import RankWeights
@@ -170,6 +172,8 @@ class SsmBranch:
         self.sumsq = torch.empty(B, 1, device=device, dtype=torch.float32)
         self.conv_state_T = st.conv_state.transpose(-1, -2)  # [lines, rows, d_conv-1] view
         self.group_size = (self.nhr * self.p) // self.ng if self.ng > 1 else None
+        # a norm row spread over ranks is one B/C group's heads: its full width divides the sum of squares
+        self.norm_width = (dims.n_mamba_heads // dims.n_groups) * self.p
 
     def project_in(self, x: torch.Tensor, t: OpTimer, x_scale: float = 1.0) -> None:
         t.begin("ssm.inproj")
@@ -210,7 +214,7 @@ class SsmBranch:
             t.end("ssm.norm")
             return
         K.gated_rmsnorm(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.norm_w, self.dims.rms_eps,
-                        self.norm_group, self.group_size, out=self.yn, sumsq=self.sumsq)
+                        self.norm_group, self.group_size, out=self.yn, sumsq=self.sumsq, total_width=self.norm_width)
         t.end("ssm.norm")
 
     def project_out(self, t: OpTimer, out: torch.Tensor | None = None, addend: torch.Tensor | None = None,
@@ -299,7 +303,8 @@ class ParallelHybridLayer:
         self.collectives = collectives
         self.device = device
         self.mode = plan.mode
-        if not (self.mode in ("tp1", "tp4", "tp4_fused", "tp4_streams") or parse_split(self.mode)):
+        mixed = parse_mix(self.mode) is not None
+        if not (self.mode in ("tp1", "tp4", "tp4_fused", "tp4_streams") or parse_split(self.mode) or mixed):
             raise ValueError(self.mode)
         self.B, self.H = ctx.rows, dims.hidden
         world = groups.world_size
@@ -308,9 +313,9 @@ class ParallelHybridLayer:
         # A rank holding both branches runs their input projections as one GEMM (shared input) and their
         # output projections as one two-segment GEMM (shared output), except in tp4 / tp4_streams, whose point
         # is separate branch outputs.
-        both = plan.attn is not None and plan.ssm is not None and self.mode in ("tp1", "tp4_fused")
+        both = plan.attn is not None and plan.ssm is not None and (self.mode in ("tp1", "tp4_fused") or mixed)
         self.chains = (branch_chains and both and not isinstance(ctx, PrefillCtx)
-                       and not (ar_impl == "p2p_fused" and self.mode == "tp4_fused"))
+                       and not (ar_impl == "p2p_fused" and self.mode != "tp1"))
         self.fused = both and w.w_in_cat is not None and not self.chains
         qkv = zx = ao = yn = None
         self.out_ratio = None
@@ -335,7 +340,8 @@ class ParallelHybridLayer:
             norm_w = (w.norm_w.float() * self.out_ratio).to(BF16)
         norm_peer = None
         if (ar_impl != "nccl" and world > 1 and collectives and not isinstance(ctx, PrefillCtx)
-                and plan.ssm is not None and len(plan.ssm.norm_ranks) > 1):
+                and plan.ssm is not None and len(plan.ssm.norm_ranks) > 1 and not mixed):
+            # (the peer-memory row norm divides by world x local width: equal widths only)
             from .p2p import PeerRowNorm
 
             norm_peer = PeerRowNorm(norm_group, groups.rank, ctx.rows, device)  # collective over the norm group
@@ -458,7 +464,7 @@ class ParallelHybridLayer:
                 self.ssm.core(t)
             t.begin("mixer.outproj")
             seg = {} if self.out_ratio is not None else {"k_seg": self.k_seg, "alpha2": dims.ssm_out}
-            pushed = self.push is not None and mode == "tp4_fused"
+            pushed = self.push is not None and mode != "tp1"
             if mode == "tp1":
                 K.gemm(self.mid_buf, self.w.w_out_cat, out=self.h1, alpha=dims.attn_out, addend=h, **seg)
             elif pushed:
@@ -466,7 +472,7 @@ class ParallelHybridLayer:
             else:
                 K.gemm(self.mid_buf, self.w.w_out_cat, out=self.mix, alpha=dims.attn_out, **seg)
             t.end("mixer.outproj")
-            if mode == "tp4_fused":
+            if mode != "tp1":  # tp4_fused, or the rank of mix{k} holding both branches
                 self._reduce_join(h, t, pushed)
                 y_ready = self.has_mlp
         elif self.chains:

@@ -96,6 +96,20 @@ def split_by_bytes(dims: FalconH1Dims, world: int, B: int, c: int, state_bytes: 
     return best[1]
 
 
+def mix_by_bytes(dims: FalconH1Dims, B: int, c: int, state_bytes: int = 4) -> int | None:
+    """The k of the two-rank layout mix{k} whose busier rank moves the fewest decode-step bytes, or None when no
+    cut is valid (several B/C groups and no group boundary helps)."""
+    best = None
+    for k in range(1, dims.n_mamba_heads):
+        try:
+            worst = max(step_hbm_bytes(plan_for(f"mix{k}", r, 2, dims), dims, B, c, state_bytes) for r in range(2))
+        except ValueError:
+            continue
+        if best is None or worst < best[0]:
+            best = (worst, k)
+    return None if best is None else best[1]
+
+
 def resolve_k(spec: RunSpec, dims: FalconH1Dims, world: int, bw: BwTables | None = None) -> tuple[int, int | None, str]:
     """(w, k, cuts_src) of the swing pool (`harness/measure.py:48-62`): 'model' asks the byte model for the cut
     with the smallest predicted slowest-rank step under the bandwidth tables `bw` (neutral without tables)."""

@@ -18,7 +18,7 @@ from dataclasses import dataclass, field
 from pathlib import Path
 
 from .config import FalconH1Dims
-from .sharding import RankPlan, k_grid, parse_split, plan_for, swing_width
+from .sharding import RankPlan, k_grid, parse_mix, parse_split, plan_for, swing_width
 
 BF16 = 2
 LAUNCH_US = {"eager": 4.0, "graph": 1.0}  # per-kernel launch overhead the model adds (reference values)
@@ -176,7 +176,7 @@ COLLECTIVES = {
 def collectives(mode: str) -> list[tuple[str, str]]:
     if mode in COLLECTIVES:
         return COLLECTIVES[mode]
-    if parse_split(mode):
+    if parse_split(mode) or parse_mix(mode) is not None:
         return _SUMMED
     raise KeyError(mode)
 

@@ -206,6 +206,34 @@ def ssm_shard(dims: FalconH1Dims, group_rank: int, group_size: int, group_world_
     )
 
 
+def ssm_shard_heads(dims: FalconH1Dims, heads: range, norm_ranks: tuple[int, ...], group_rank: int,
+                    group_size: int) -> SsmShard:
+    """Mamba-2 shard of an arbitrary contiguous head range (the uneven layouts): the B/C groups of those heads are
+    held locally; `norm_ranks` are the world ranks whose heads share the gated-norm reduction."""
+    p, N, G, nh, d = dims.mamba_head_dim, dims.d_state, dims.n_groups, dims.n_mamba_heads, dims.d_ssm
+    _require(0 <= heads.start < heads.stop <= nh, f"heads {heads} outside 0..{nh}")
+    hpg = nh // G
+    groups = range(heads.start // hpg, (heads.stop - 1) // hpg + 1)
+    ng, per = len(groups), len(heads)
+    b_base, c_base, dt_base = 2 * d, 2 * d + G * N, 2 * d + 2 * G * N
+    return SsmShard(
+        heads=heads, groups=groups,
+        z_rows=_rows(heads.start * p, per * p),
+        x_rows=_rows(d + heads.start * p, per * p),
+        b_rows=_rows(b_base + groups.start * N, ng * N),
+        c_rows=_rows(c_base + groups.start * N, ng * N),
+        dt_rows=_rows(dt_base + heads.start, per),
+        conv_rows=(
+            _rows(heads.start * p, per * p),
+            _rows(d + groups.start * N, ng * N),
+            _rows(d + G * N + groups.start * N, ng * N),
+        ),
+        out_cols=_rows(heads.start * p, per * p),
+        norm_cols=_rows(heads.start * p, per * p),
+        group_rank=group_rank, group_size=group_size, norm_ranks=norm_ranks,
+    )
+
+
 def swing_width(S: float, cols_per_rank: int, granule: int = SWING_GRANULE) -> int:
     if S <= 0:
         return 0
@@ -251,6 +279,17 @@ def parse_split(mode: str) -> tuple[int, int] | None:
     return (int(m.group(1)), int(m.group(2))) if m else None
 
 
+_MIX = re.compile(r"^mix(\d+)$")
+
+
+def parse_mix(mode: str) -> int | None:
+    """``mix{k}`` -> k; None for other modes. Two ranks: rank 0 holds the whole attention branch and Mamba-2
+    heads [0, k), rank 1 heads [k, nh): a branch split whose byte loads can be balanced when one branch
+    outweighs the other (an extension beyond the reference's layouts)."""
+    m = _MIX.match(mode)
+    return int(m.group(1)) if m else None
+
+
 def plan_for(mode: str, rank: int, world: int, dims: FalconH1Dims, swing: float = 0.0, k: int | None = None) -> RankPlan:
     everyone = tuple(range(world))
     if mode == "tp1":
@@ -279,6 +318,24 @@ def plan_for(mode: str, rank: int, world: int, dims: FalconH1Dims, swing: float 
             ssm=None if is_attn else ssm_shard(dims, rank - a, m, ssm_ranks),
             mlp=mlp_shard(dims, rank, world, swing if even else 0.0, k, role if even else "tp", partner),
             attn_ranks=attn_ranks, ssm_ranks=ssm_ranks, combine="sum_then_allreduce",
+        )
+    k = parse_mix(mode)
+    if k is not None:
+        _require(world == 2, f"{mode} runs on 2 ranks")
+        nh, G = dims.n_mamba_heads, dims.n_groups
+        _require(1 <= k < nh, f"{mode}: rank 0 takes 1..{nh - 1} Mamba-2 heads")
+        hpg = nh // G
+        # one B/C group: the gated norm's row spans both ranks; several: the cut must fall on a group boundary,
+        # so each rank normalises its own whole groups
+        _require(G == 1 or k % hpg == 0, f"{mode}: with {G} groups the cut must be a multiple of {hpg} heads")
+        norm = (0, 1) if G == 1 else (rank,)
+        heads = range(0, k) if rank == 0 else range(k, nh)
+        return RankPlan(
+            mode=mode, rank=rank, world=world,
+            attn=attn_shard(dims, 0, 1) if rank == 0 else None,
+            ssm=ssm_shard_heads(dims, heads, norm, rank, 2),
+            mlp=mlp_shard(dims, rank, world, 0.0, None), attn_ranks=(0,), ssm_ranks=(0, 1),
+            combine="sum_then_allreduce",
         )
     raise ValueError(f"unknown mode {mode}")
 

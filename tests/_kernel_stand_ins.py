@@ -121,7 +121,7 @@ def ssd_prefill(x, dt, A, B, C, D, dt_bias, state, cu_seqlens, state_idx, has_in
     return out
 
 
-def gated_rmsnorm(y, z, w, eps, group, group_size=None, out=None, sumsq=None):
+def gated_rmsnorm(y, z, w, eps, group, group_size=None, out=None, sumsq=None, total_width=None):
     g = y.float() * F.silu(z.float())
     rows, Dd = g.shape
     if group is None:
@@ -131,7 +131,8 @@ def gated_rmsnorm(y, z, w, eps, group, group_size=None, out=None, sumsq=None):
     else:
         tot = g.pow(2).sum(-1, keepdim=True)
         group.all_reduce(tot)
-        r = g * torch.rsqrt(tot / (group.world_size * Dd) + eps)
+        width = group.world_size * Dd if total_width is None else total_width
+        r = g * torch.rsqrt(tot / width + eps)
     out.copy_((r * w.float()).to(out.dtype))
     return out
 

@@ -71,7 +71,7 @@ def test_hybrid_layer_calls_validate(validating_library, dims_name, mode):
 
 
 @pytest.mark.parametrize("mode,world", [("split13", 4), ("split22", 4), ("tp4", 4), ("tp4_fused", 4),
-                                        ("split26", 8), ("split44", 8)])
+                                        ("split26", 8), ("split44", 8), ("mix8", 2), ("mix6", 2)])
 def test_every_rank_of_the_multi_gpu_layouts_validates(validating_library, mode, world):
     """Each rank's share of the 7B-like layer (its heads, channel slices, MLP rows) at that rank's real shapes: the
     per-rank kernel calls of the layouts the scaling bench and the multi-GPU checks run. The layer is built without
@@ -150,7 +150,8 @@ def test_a_misaligned_request_is_caught(validating_library):
 
 
 @pytest.mark.parametrize("ar_impl", ["p2p", "p2p_fused"])
-@pytest.mark.parametrize("mode,world", [("split13", 4), ("tp4_fused", 4), ("split26", 8), ("split44", 8)])
+@pytest.mark.parametrize("mode,world", [("split13", 4), ("tp4_fused", 4), ("split26", 8), ("split44", 8),
+                                        ("mix8", 2)])
 def test_peer_memory_calls_of_every_rank_validate(validating_library, monkeypatch, mode, world, ar_impl):
     """The decode step with the peer-memory all-reduce on every rank of a layout: the pushing GEMM
     (mmp_gemm_bf16_push), the join (mmp_ar_join) and the gated norm's cross-rank statistic (mmp_gated_rmsnorm_p2p)
@@ -194,4 +195,5 @@ def test_peer_memory_calls_of_every_rank_validate(validating_library, monkeypatc
     names = {n for n, _ in validating_library}
     assert "mmp_ar_join" in names
     assert ("mmp_gemm_bf16_push" in names) == (ar_impl == "p2p_fused")
-    assert "mmp_gated_rmsnorm_p2p" in names  # one B/C group: the norm statistic spans the SSM ranks
+    # one B/C group: the norm statistic spans the SSM ranks (mix{k}: unequal widths, the NCCL statistic instead)
+    assert ("mmp_gated_rmsnorm_p2p" in names) == (not mode.startswith("mix"))

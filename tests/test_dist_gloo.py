@@ -80,7 +80,8 @@ def rank_partials(plan, dims, groups, h):
         if len(s.norm_ranks) > 1:  # one group spread over ranks: all-reduce the sum of squares
             tot = g.pow(2).sum(-1, keepdim=True)
             groups.group_for_ranks(s.norm_ranks).all_reduce(tot)
-            g = g * torch.rsqrt(tot / (len(s.norm_ranks) * g.shape[1]) + dims.rms_eps)
+            width = (dims.n_mamba_heads // dims.n_groups) * p  # the group's full width (ranks may hold unequal parts)
+            g = g * torch.rsqrt(tot / width + dims.rms_eps)
         else:  # local groups
             gg = g.view(B, ng, -1)
             g = (gg * torch.rsqrt(gg.pow(2).mean(-1, keepdim=True) + dims.rms_eps)).view(B, -1)
@@ -141,7 +142,7 @@ def run_world(world, mode, dims_name="g1"):
 @pytest.mark.parametrize("world,mode,dims_name", [
     (2, "split11", "g1"), (2, "tp4", "g1"), (2, "tp4_fused", "g2"),
     (4, "split13", "g1"), (4, "split22", "g1"), (4, "tp4", "g2"), (4, "split22", "g2"),
-    (8, "split26", "g1"),
+    (8, "split26", "g1"), (2, "mix4", "g1"), (2, "mix1", "g1"), (2, "mix6", "g2"),
 ])
 def test_sharded_partials_all_reduce_to_the_full_layer(world, mode, dims_name):
     res = run_world(world, mode, dims_name)
@@ -163,7 +164,8 @@ def test_group_creation_is_identical_on_every_rank(world, monkeypatch):
     from multi_modal_parallelism_b200.config import MODES
 
     dims7 = preset("falcon_h1_7b_like")
-    modes = [m for m in MODES if not m.startswith("split")] + [f"split{a}{world - a}" for a in range(1, world)]
+    modes = [m for m in MODES if not m.startswith("split")] + [f"split{a}{world - a}" for a in range(1, world)] + \
+        ([f"mix{k}" for k in (1, 8, 12, 23)] if world == 2 else [])
     for dims in (dims7, dims7.replace(n_groups=2), DIMS_G2):
         for mode in modes:
             try:

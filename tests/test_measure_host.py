@@ -69,6 +69,7 @@ def test_bench_layout_candidates_are_valid_and_rank_independent():
     d = preset("falcon_h1_7b_like")
     assert bench.layout_candidates(d, 1, 64, 2048) == ["tp1", "tp1_chains"]
     assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split13", "tp4_fused", "tp4_fused_chains"]
+    assert bench.layout_candidates(d, 2, 64, 2048) == ["split11", "mix8", "mix6", "tp4_fused", "tp4_fused_chains"]
     assert bench.layout_candidates(d, 4, 64, 2048, "p2p_fused") == ["split22", "split13", "tp4_fused"]
     assert bench.parse_recipe("tp4_fused_chains") == ("tp4_fused", True)
     assert bench.parse_recipe("split26") == ("split26", False)
@@ -79,3 +80,16 @@ def test_bench_layout_candidates_are_valid_and_rank_independent():
             mode, _ = bench.parse_recipe(label)
             for r in range(world):
                 plan_for(mode, r, world, d)
+
+
+def test_mix_by_bytes_balances_the_two_ranks():
+    """7B-like layer, batch 64, context 2048: attention (156 MB) plus 8 Mamba-2 heads on rank 0, 16 heads on rank 1:
+    314 / 311 MB, against split11's 156 / 465 MB."""
+    from multi_modal_parallelism_b200.measure import mix_by_bytes
+
+    d = preset("falcon_h1_7b_like")
+    assert mix_by_bytes(d, 64, 2048) == 8
+    per = [step_hbm_bytes(plan_for("mix8", r, 2, d), d, 64, 2048) for r in range(2)]
+    assert abs(per[0] - per[1]) < 0.01 * sum(per)
+    assert sum(per) - step_hbm_bytes(plan_for("tp1", 0, 1, d), d, 64, 2048) < 0.01 * sum(per)  # only B/C replicated
+    assert mix_by_bytes(d.replace(n_groups=24), 64, 2048) is not None

@@ -161,3 +161,11 @@ def test_branch_chains_schedule(world, mode, extra, tmp_path):
     if ngpu() < world:
         pytest.skip(f"needs {world} GPUs")
     run_check(world, mode, tmp_path, ("--branch-chains", *extra))
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("extra", [(), ("--ar-impl", "p2p"), ("--ar-impl", "p2p_fused"), ("--branch-chains",)])
+def test_two_gpu_mix_layout(extra, tmp_path):
+    """mix8: rank 0 the attention branch and 8 Mamba-2 heads (fused projections), rank 1 the other 16 heads."""
+    run_check(2, "mix8", tmp_path, extra)
