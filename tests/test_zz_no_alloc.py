@@ -16,7 +16,7 @@ import torch
 from multi_modal_parallelism_b200 import _lib
 from multi_modal_parallelism_b200 import kernels as K
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.run_last(order=99)]  # collected after every other test
 DEV = torch.device("cuda", 0)
 BF = torch.bfloat16
 
