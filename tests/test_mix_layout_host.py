@@ -3,7 +3,8 @@ projections; rank 1: the other heads; one all-reduce) through ParallelHybridLaye
 kernel wrappers replaced by torch stand-ins (tests/_kernel_stand_ins.py): every rank's output equals the whole
 layer run on one rank within bf16 tolerance, for one and two B/C groups (two: the cut on a group boundary, each
 rank normalising its own groups; one: the gated norm's statistic spans both ranks and is divided by the group's
-full width), with the NCCL-style and peer-memory all-reduce and with the branch-chains schedule on rank 0."""
+full width), with the NCCL-style and peer-memory all-reduce and with the branch-chains schedule on rank 0; and
+the prefill of ragged sequences in the same layouts against the single-rank prefill."""
 import multiprocessing as mp
 import os
 import socket
@@ -63,6 +64,21 @@ def _worker(rank, world, port, cases, q):
                                           alloc_and_fill(plan, dims, ctx, SEED, cpu), ctx, cpu, overlap_branches=False,
                                           ar_impl=impl, branch_chains=chains)
             res[(groups_n, mode, impl, chains)] = (layer.step(h).float().numpy().copy(), ref)
+        # prefill of two fresh ragged sequences in the same layouts (NCCL-style collectives, as prefill runs)
+        from multi_modal_parallelism_b200.state import alloc_states, decode_ctx_after, make_prefill_ctx
+
+        pc = make_prefill_ctx([40, 17], 16, cpu)
+        hp = input_hidden(SEED + 1, pc.T, DIMS.hidden, cpu)
+        for groups_n, mode in ((1, "mix3"), (2, "mix4")):
+            dims = DIMS.replace(n_groups=groups_n)
+            full = random_layer(dims, SEED)
+            outs = []
+            for plan, g in ((plan_for("tp1", 0, 1, dims), single), (plan_for(mode, rank, world, dims), groups)):
+                st = alloc_states(plan, dims, 3, pc.block_table.numel(), 16, cpu, torch.float32)
+                lay = L.ParallelHybridLayer(plan, shard_to_device(full, plan, dims, cpu), dims, g, st,
+                                            decode_ctx_after(pc), cpu, overlap_branches=False)
+                outs.append(lay.prefill(hp, pc).float().numpy().copy())
+            res[("prefill", groups_n, mode)] = (outs[1], outs[0])
         q.put((rank, res, None))
         destroy()
     except Exception as e:  # pragma: no cover - reported to the parent
@@ -87,7 +103,7 @@ def test_mix_layout_matches_the_single_rank_layer():
         p.join(timeout=60)
     for rank, _, err in res:
         assert err is None, f"rank {rank}: {err}"
-    for case in cases:
+    for case in cases + [("prefill", 1, "mix3"), ("prefill", 2, "mix4")]:
         outs = [r[case][0] for _, r, _ in res]
         ref = res[0][1][case][1]
         scale = max(1.0, float(np.abs(ref).max()))

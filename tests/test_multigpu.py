@@ -169,3 +169,10 @@ def test_branch_chains_schedule(world, mode, extra, tmp_path):
 def test_two_gpu_mix_layout(extra, tmp_path):
     """mix8: rank 0 the attention branch and 8 Mamba-2 heads (fused projections), rank 1 the other 16 heads."""
     run_check(2, "mix8", tmp_path, extra)
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+def test_two_gpu_mix_prefill():
+    """Prefill (and the decode step after it) in mix8 equals the single-rank prefill."""
+    run_prefill_check(2, "mix8")
