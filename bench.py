@@ -307,7 +307,7 @@ def build_layer(args, label, groups, dims, full, single_rank: bool = False):
     from multi_modal_parallelism_b200.weights import shard_to_device
 
     dev = groups.device
-    mode, chains = parse_recipe(label)
+    mode, chains, defer = parse_recipe(label)
     plan = plan_for("tp1", 0, 1, dims) if single_rank else plan_for(mode, groups.rank, groups.world_size, dims)
     rw = shard_to_device(full, plan, dims, dev)
     ctx = make_decode_ctx(args.batch, args.ctx, 16, dev)
@@ -316,7 +316,7 @@ def build_layer(args, label, groups, dims, full, single_rank: bool = False):
     if single_rank:
         return ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev, collectives=False), h
     layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, dev, ar_impl=getattr(args, "ar_impl", "nccl"),
-                                branch_chains=chains)
+                                branch_chains=chains, defer_norm=defer)
     return layer, h
 
 
@@ -385,8 +385,9 @@ def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nc
     one rank runs tp1 with fused projections and tp1 with the branch-chains schedule (`_chains`: each branch's
     whole chain on its own stream); more run the even branch split, the split whose busiest rank moves the fewest
     step bytes (more ranks on the Mamba-2 branch when its state dominates), at two ranks the byte-balanced
-    mix{k} layouts, and tp4_fused in both schedules (the chains schedule is not combined with a pushed
-    out-projection). Every rank derives the same list."""
+    mix{k} layouts, each also with the deferred norm statistic (`_dn`) where some rank would defer it, and
+    tp4_fused in both schedules (the chains schedule is not combined with a pushed out-projection). Every rank
+    derives the same list."""
     from multi_modal_parallelism_b200.measure import mix_by_bytes, split_by_bytes
 
     if world == 1:
@@ -402,7 +403,20 @@ def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nc
         if k is not None:
             modes += [f"mix{kk}" for kk in sorted({k, max(1, k - 2)}, reverse=True)
                       if plan_ok(f"mix{kk}", dims, world)]
+    if ar_impl == "nccl":  # the deferred norm statistic where some rank would defer it
+        modes = [x for m in modes for x in ([m, f"{m}_dn"] if defers(m, dims, world) else [m])]
     return modes + ["tp4_fused"] + ([] if ar_impl == "p2p_fused" else ["tp4_fused_chains"])
+
+
+def defers(mode: str, dims, world: int) -> bool:
+    """Some rank of the layout holds only the Mamba-2 branch and shares its gated norm's row with other ranks."""
+    from multi_modal_parallelism_b200.sharding import plan_for
+
+    for r in range(world):
+        pl = plan_for(mode, r, world, dims)
+        if pl.attn is None and pl.ssm is not None and len(pl.ssm.norm_ranks) > 1:
+            return True
+    return False
 
 
 def plan_ok(mode: str, dims, world: int) -> bool:
@@ -416,9 +430,16 @@ def plan_ok(mode: str, dims, world: int) -> bool:
         return False
 
 
-def parse_recipe(label: str) -> tuple[str, bool]:
-    """(layout, branch_chains) of a recipe label such as "tp4_fused_chains"."""
-    return (label[:-len("_chains")], True) if label.endswith("_chains") else (label, False)
+def parse_recipe(label: str) -> tuple[str, bool, bool]:
+    """(layout, branch_chains, defer_norm) of a recipe label such as "tp4_fused_chains" or "split13_dn"."""
+    chains = defer = False
+    while True:
+        if label.endswith("_chains"):
+            label, chains = label[:-len("_chains")], True
+        elif label.endswith("_dn"):
+            label, defer = label[:-len("_dn")], True
+        else:
+            return label, chains, defer
 
 
 def our_arm(args) -> None:

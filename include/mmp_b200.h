@@ -101,11 +101,20 @@ int mmp_rmsnorm(const void* x, int64_t x_b, const void* residual, int64_t r_b, v
  * mode 1 (partial): write each row's per-group sum of squares to sumsq [rows, D/group_size] fp32 and
  *   nothing else — the caller reduces it across the ranks of the norm group.
  * mode 2 (apply): use the reduced sums in sumsq with `count` elements per group.
+ * mode 3 (deferred): write the partial sums as mode 1 and out = w * g unnormalised; once the sums are reduced,
+ *   mmp_scale_rows applies the normalisation to any product linear in the rows of out (the out-projection), so
+ *   the reduction can run while that product is computed.
  * y, z, out: [rows, D] bf16 with row strides; w: [D] bf16.
  */
 int mmp_gated_rmsnorm(const void* y, int64_t y_b, const void* z, int64_t z_b, const void* w,
                       void* out, int64_t o_b, float* sumsq, int rows, int D, int group_size,
                       int mode, float count, float eps, void* stream);
+
+/* x[r, :] *= rsqrt(sumsq[r] / count + eps), in place: the normalisation deferred by mmp_gated_rmsnorm mode 3, applied
+ * to the rows of a product of the unnormalised values (one group per row: sumsq [rows] fp32, reduced over the norm
+ * group's ranks; count = the group's full width). x: [rows, cols] bf16, row stride ld, cols % 8 == 0, 16-byte
+ * aligned rows. No counterpart in the reference: its tensor-parallel norm always reduces before the projection. */
+int mmp_scale_rows(void* x, int64_t ld, const float* sumsq, int rows, int cols, float count, float eps, void* stream);
 
 /* ---- RoPE + key multiplier + paged KV write --------------------------------------------------------
  * Replaces kernels.apply_rope and kernels.write_kv (harness/kernels.py:56-66,112-115) and the layer's

@@ -81,7 +81,8 @@ struct GnParams {
   float count, eps;
 };
 
-// grid: (groups, rows). mode 0 = local, 1 = write partial sums, 2 = apply given sums.
+// grid: (groups, rows). mode 0 = local, 1 = write partial sums, 2 = apply given sums, 3 = write partial sums and
+// the gated, weighted values unnormalised (the caller scales the rows once the sums are complete).
 template <int MAXV>
 __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const GnParams P) {
   pdl_trigger();
@@ -111,13 +112,13 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const GnParams P) {
     total = P.sumsq[row * ngroups + grp];
   } else {
     total = block_sum(ss, red);
-    if (P.mode == 1) {
+    if (P.mode == 1 || P.mode == 3) {
       if (threadIdx.x == 0) P.sumsq[row * ngroups + grp] = total;
-      return;
+      if (P.mode == 1) return;
     }
   }
   const float cnt = P.mode == 2 ? P.count : static_cast<float>(P.group_size);
-  const float inv = rsqrtf(total / cnt + P.eps);
+  const float inv = P.mode == 3 ? 1.f : rsqrtf(total / cnt + P.eps);
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
@@ -128,6 +129,24 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_kernel(const GnParams P) {
       for (int j = 0; j < 8; ++j) o[j] = g[i][j] * inv * w[j];
       st16(P.out + row * P.o_b + base + vi * 8, pack8(o));
     }
+  }
+}
+
+// x[r, :] *= rsqrt(sumsq[r] / count + eps), in place (bf16 rows, fp32 sums): the deferred normalisation of a
+// partial product computed from unnormalised gated values. grid: rows; 16-byte vectors.
+__global__ void __launch_bounds__(256) scale_rows_kernel(bf16* x, int64_t ld, const float* sumsq, int cols,
+                                                         float count, float eps) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x;
+  const float s = rsqrtf(sumsq[row] / count + eps);
+  bf16* xr = x + row * ld;
+  for (int v = threadIdx.x; v < cols / 8; v += blockDim.x) {
+    float f[8];
+    unpack8(ld16(xr + v * 8), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) f[j] *= s;
+    st16(xr + v * 8, pack8(f));
   }
 }
 
@@ -163,7 +182,7 @@ extern "C" int mmp_gated_rmsnorm(const void* y, int64_t y_b, const void* z, int6
   if (!y || !z || (mode != 1 && (!w || !out)) || (mode != 0 && !sumsq))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm: null pointer");
   if (rows < 0 || rows > 65535 || D <= 0 || group_size <= 0 || D % group_size || group_size % 8 || group_size > 256 * 8 * 4 ||
-      mode < 0 || mode > 2 || (mode == 2 && !(count > 0.f)))
+      mode < 0 || mode > 3 || (mode == 2 && !(count > 0.f)))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm: bad sizes rows=%d D=%d group=%d mode=%d", rows, D, group_size, mode);
   if (!rows_ok(y, y_b) || !rows_ok(z, z_b) || (mode != 1 && (!rows_ok(out, o_b) || !aligned16(w))))
     return mmp_set_error(MMP_ERR_INVALID, "mmp_gated_rmsnorm: rows must be 16-byte aligned");
@@ -253,4 +272,17 @@ extern "C" int mmp_add(const void* a, int64_t a_b, const void* b, int64_t b_b, c
                               o_b, cols);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_add: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_add");
+}
+
+extern "C" int mmp_scale_rows(void* x, int64_t ld, const float* sumsq, int rows, int cols, float count, float eps,
+                              void* stream) {
+  if (rows == 0 || cols == 0) return MMP_OK;
+  if (!x || !sumsq) return mmp_set_error(MMP_ERR_INVALID, "mmp_scale_rows: null pointer");
+  if (rows < 0 || rows > 65535 || cols < 0 || cols % 8 || !(count > 0.f) || !rows_ok(x, ld))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_scale_rows: rows=%d cols=%d (multiple of 8), 16-byte aligned rows", rows,
+                         cols);
+  cudaError_t e = mmp::launch(scale_rows_kernel, dim3(rows), dim3(256), 0, static_cast<cudaStream_t>(stream), nullptr, 0,
+                              static_cast<bf16*>(x), ld, sumsq, cols, count, eps);
+  if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_scale_rows: %s", cudaGetErrorString(e));
+  return mmp_check_launch("mmp_scale_rows");
 }

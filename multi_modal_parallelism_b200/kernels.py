@@ -152,6 +152,35 @@ def gated_rmsnorm(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, eps: float,
     return out
 
 
+def gated_rmsnorm_deferred(y: torch.Tensor, z: torch.Tensor, w: torch.Tensor, out: torch.Tensor,
+                           sumsq: torch.Tensor) -> torch.Tensor:
+    """The first half of a gated RMSNorm whose row spans several ranks, with the normalisation deferred: writes
+    this rank's [rows, 1] fp32 sum of squares of g = y * silu(z) and out = w * g unnormalised. After the sums are
+    reduced over the norm group, scale_rows(p, sums, width, eps) normalises any product p linear in out's rows."""
+    _cuda("gated_rmsnorm_deferred", y, z, w, out, sumsq)
+    for t in (y, z, w, out):
+        _dtype("gated_rmsnorm_deferred", t, BF16)
+    _dtype("gated_rmsnorm_deferred", sumsq, torch.float32)
+    rows, D = y.shape
+    if sumsq.numel() != rows or not sumsq.is_contiguous():
+        raise ValueError("gated_rmsnorm_deferred: sumsq must be a contiguous fp32 [rows, 1]")
+    _lib.call("mmp_gated_rmsnorm", _p(y), _rowmajor("y", y), _p(z), _rowmajor("z", z), _p(w), _p(out),
+              _rowmajor("out", out), _p(sumsq), rows, D, D, 3, 0.0, 0.0, _stream(y))
+    return out
+
+
+def scale_rows(x: torch.Tensor, sumsq: torch.Tensor, count: int, eps: float) -> torch.Tensor:
+    """In place: x[r, :] *= rsqrt(sumsq[r] / count + eps) (x bf16 [rows, cols], sumsq fp32 [rows, 1])."""
+    _cuda("scale_rows", x, sumsq)
+    _dtype("scale_rows", x, BF16)
+    _dtype("scale_rows", sumsq, torch.float32)
+    rows, cols = x.shape
+    if sumsq.numel() != rows or not sumsq.is_contiguous():
+        raise ValueError("scale_rows: sumsq must be a contiguous fp32 [rows, 1]")
+    _lib.call("mmp_scale_rows", _p(x), _rowmajor("x", x), _p(sumsq), rows, cols, float(count), float(eps), _stream(x))
+    return x
+
+
 # ----------------------------------------------------------------------------- rope / kv
 def rope_inv_freq(head_dim: int, theta: float, device: torch.device) -> torch.Tensor:
     """[hd/2] fp32 inverse frequencies theta^(-2i/hd), computed in fp32 as the fp32 layer does."""

@@ -124,11 +124,16 @@ class SsmBranch:
 
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, st: RankStates, ctx: DecodeCtx,
                  device: torch.device, norm_group, zxbcdt: torch.Tensor | None = None, yn: torch.Tensor | None = None,
-                 norm_w: torch.Tensor | None = None, norm_peer=None, ssd_segments: bool = False):
+                 norm_w: torch.Tensor | None = None, norm_peer=None, ssd_segments: bool = False,
+                 defer_norm: bool = False):
         """zxbcdt / yn: optional [B, in rows] and [B, nhr*p] views into buffers shared with the other branch;
         norm_w: the gated norm's weight when it carries an extra output scale (default w.norm_w); norm_peer: a
         p2p.PeerRowNorm that replaces the norm group's all-reduce of the row statistic; ssd_segments (prefill):
-        run the chunked scan with the sequences cut into balanced segments (segments.py) where that helps."""
+        run the chunked scan with the sequences cut into balanced segments (segments.py) where that helps;
+        defer_norm (decode, a norm row spread over ranks, output projection without addend or push): project the
+        unnormalised gated values while the row statistic is all-reduced on a side stream, then scale the
+        projected rows (the projection is linear and the norm is one scale per row), taking that all-reduce's
+        latency off the step's path."""
         s = plan.ssm
         assert s is not None
         self.plan, self.w, self.dims, self.st, self.ctx = plan, w, dims, st, ctx
@@ -174,6 +179,10 @@ class SsmBranch:
         self.group_size = (self.nhr * self.p) // self.ng if self.ng > 1 else None
         # a norm row spread over ranks is one B/C group's heads: its full width divides the sum of squares
         self.norm_width = (dims.n_mamba_heads // dims.n_groups) * self.p
+        self.defer = (defer_norm and not self.prefill and norm_group is not None and norm_peer is None
+                      and norm_group.world_size > 1)
+        if self.defer:
+            self.s_norm = torch.cuda.Stream(device=device)
 
     def project_in(self, x: torch.Tensor, t: OpTimer, x_scale: float = 1.0) -> None:
         t.begin("ssm.inproj")
@@ -209,6 +218,15 @@ class SsmBranch:
 
     def _norm(self, t: OpTimer) -> None:
         t.begin("ssm.norm")
+        if self.defer:
+            K.gated_rmsnorm_deferred(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.norm_w, self.yn,
+                                     self.sumsq)
+            cur = torch.cuda.current_stream(self.yn.device)
+            self.s_norm.wait_stream(cur)
+            with torch.cuda.stream(self.s_norm):  # overlaps the out-projection, joined in project_out
+                self.norm_group.all_reduce(self.sumsq)
+            t.end("ssm.norm")
+            return
         if self.norm_peer is not None:
             self.norm_peer(self.y.view(self.ctx.rows, self.nhr * self.p), self.z, self.norm_w, self.dims.rms_eps, self.yn)
             t.end("ssm.norm")
@@ -225,6 +243,11 @@ class SsmBranch:
             out = None
         else:
             out = K.gemm(self.yn, self.w.wout, out=out, alpha=self.dims.ssm_out, addend=addend)
+        if self.defer:
+            if push is not None or addend is not None:
+                raise ValueError("SsmBranch: a deferred norm scales the projected rows: no addend, no push")
+            torch.cuda.current_stream(out.device).wait_stream(self.s_norm)
+            K.scale_rows(out, self.sumsq, self.norm_width, self.dims.rms_eps)
         t.end("ssm.outproj")
         return out
 
@@ -282,14 +305,17 @@ class SwingMLP:
 class ParallelHybridLayer:
     def __init__(self, plan: RankPlan, w: RankWeights, dims: FalconH1Dims, groups: Groups, st: RankStates,
                  ctx: DecodeCtx, device: torch.device, collectives: bool = True, overlap_branches: bool = True,
-                 ar_impl: str = "nccl", branch_chains: bool = False, ssd_segments: bool = False):
+                 ar_impl: str = "nccl", branch_chains: bool = False, ssd_segments: bool = False,
+                 defer_norm: bool = False):
         """overlap_branches: on a rank holding both branches (fused projections), run the attention core on a
         side stream concurrently with the Mamba-2 core. branch_chains (decode, tp1 / tp4_fused, a rank holding
         both branches, no pushed GEMM): instead of fused projections, the attention branch's whole chain (QKV
         GEMM, RoPE + KV write, attention, o-projection) runs on the side stream while the Mamba-2 chain runs on
         this one, and the Mamba-2 out-projection adds the attention partial as its addend; the attention GEMMs'
         latency (first loads, epilogue) then hides under the Mamba-2 chain instead of lying on the step's path.
-        ssd_segments: prefill() runs the Mamba-2 chunked scan with balanced walks (segments.py). `ctx` is a DecodeCtx (step() is one decode step) or a
+        ssd_segments: prefill() runs the Mamba-2 chunked scan with balanced walks (segments.py). defer_norm
+        (decode, ranks holding only the Mamba-2 branch, a norm row spread over ranks, NCCL or peer-memory join
+        without pushed GEMMs): the norm's row-statistic all-reduce overlaps the out-projection (SsmBranch). `ctx` is a DecodeCtx (step() is one decode step) or a
         PrefillCtx (step() is that prefill; the usual entry is prefill() on the decode layer). ar_impl "p2p": the
         decode step's [B, H] all-reduces (mixer and MLP; not tp4's per-branch pair) run as the peer-memory
         all-reduce fused with the residual add and the next norm (p2p.PeerAllReduce); "p2p_fused": in addition the
@@ -345,7 +371,10 @@ class ParallelHybridLayer:
             from .p2p import PeerRowNorm
 
             norm_peer = PeerRowNorm(norm_group, groups.rank, ctx.rows, device)  # collective over the norm group
-        self.ssm = (SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w, norm_peer, ssd_segments)
+        defer = (defer_norm and plan.attn is None and world > 1 and collectives and ar_impl != "p2p_fused")
+        self.defer_norm = defer_norm
+        self.ssm = (SsmBranch(plan, w, dims, st, ctx, device, norm_group, zx, yn, norm_w, norm_peer, ssd_segments,
+                              defer)
                     if plan.ssm is not None else None)
         self.has_mlp = dims.intermediate > 0
         self.mlp = SwingMLP(plan, w, dims, ctx.rows, device) if self.has_mlp else None

@@ -147,7 +147,8 @@ def check_against_reference(spec: RunSpec, dims: FalconH1Dims, full: dict, out: 
 
 def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, torch.Tensor], out_csv: str,
             correctness_csv: str, check: bool, bw=None, image_tag: str = "",
-            ssm_dtype: torch.dtype = torch.float32, ar_impl: str = "nccl", branch_chains: bool = False) -> list[dict]:
+            ssm_dtype: torch.dtype = torch.float32, ar_impl: str = "nccl", branch_chains: bool = False,
+            defer_norm: bool = False) -> list[dict]:
     rank, world, device = groups.rank, groups.world_size, groups.device
     w, k, cuts_src = resolve_k(spec, dims, world, bw)
     plan = plan_for(spec.mode, rank, world, dims, spec.swing, k)
@@ -162,7 +163,7 @@ def measure(spec: RunSpec, groups: Groups, dims: FalconH1Dims, full: dict[str, t
     st = alloc_and_fill(plan, dims, ctx, spec.seed, device, ssm_dtype=ssm_dtype)
     h = input_hidden(spec.seed, spec.batch, dims.hidden, device)
     layer = ParallelHybridLayer(plan, rw, dims, groups, st, ctx, device, collectives=spec.collectives,
-                                ar_impl=ar_impl, branch_chains=branch_chains)
+                                ar_impl=ar_impl, branch_chains=branch_chains, defer_norm=defer_norm)
     barrier_sync()
 
     run_id = uuid.uuid4().hex[:8]

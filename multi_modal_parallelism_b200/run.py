@@ -70,6 +70,8 @@ def main(argv: list[str] | None = None) -> int:
                     help="p2p: decode all-reduces over NVLink peer memory, fused with the residual and norm")
     ap.add_argument("--branch-chains", action="store_true",
                     help="tp1 / tp4_fused: each branch's whole chain (projections included) on its own stream")
+    ap.add_argument("--defer-norm", action="store_true",
+                    help="Mamba-2-only ranks: the gated norm's cross-rank statistic overlaps the out-projection")
     args = ap.parse_args(argv)
 
     if args.k in ("neutral", "model"):
@@ -86,7 +88,7 @@ def main(argv: list[str] | None = None) -> int:
     bw = BwTables.from_csv(args.bw) if args.bw and os.path.exists(args.bw) else None
     rows = measure(spec, groups, dims, full, args.out, args.correctness_out, args.check, bw,
                    os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype, ar_impl=args.ar_impl,
-                   branch_chains=args.branch_chains)
+                   branch_chains=args.branch_chains, defer_norm=args.defer_norm)
     ok = True
     if args.check and groups.rank == 0:
         with open(args.correctness_out) as f:

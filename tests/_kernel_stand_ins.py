@@ -137,6 +137,18 @@ def gated_rmsnorm(y, z, w, eps, group, group_size=None, out=None, sumsq=None, to
     return out
 
 
+def gated_rmsnorm_deferred(y, z, w, out, sumsq):
+    g = y.float() * F.silu(z.float())
+    sumsq.copy_(g.pow(2).sum(-1, keepdim=True).reshape(sumsq.shape))
+    out.copy_((g * w.float()).to(out.dtype))
+    return out
+
+
+def scale_rows(x, sumsq, count, eps):
+    x.copy_((x.float() * torch.rsqrt(sumsq.reshape(-1, 1).float() / count + eps)).to(x.dtype))
+    return x
+
+
 # ---------------------------------------------------------------- the Gated DeltaNet stack's extra kernels
 def rms_norm_residual(x, residual, w, eps, out, sum_out=None):
     s = x.float() + residual.float()

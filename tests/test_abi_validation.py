@@ -197,3 +197,45 @@ def test_peer_memory_calls_of_every_rank_validate(validating_library, monkeypatc
     assert ("mmp_gemm_bf16_push" in names) == (ar_impl == "p2p_fused")
     # one B/C group: the norm statistic spans the SSM ranks (mix{k}: unequal widths, the NCCL statistic instead)
     assert ("mmp_gated_rmsnorm_p2p" in names) == (not mode.startswith("mix"))
+
+
+@pytest.mark.parametrize("mode,world", [("split13", 4), ("split26", 8), ("mix8", 2)])
+def test_deferred_norm_calls_of_every_rank_validate(validating_library, monkeypatch, mode, world):
+    """The deferred gated-norm statistic (defer_norm) at the 7B-like layer's per-rank shapes: the norm kernel's
+    deferred mode and the row scaling of the out-projection's output. Communicators and streams are host
+    stand-ins; only the arguments the library checks are tested."""
+    from multi_modal_parallelism_b200 import dist as D
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.layer import ParallelHybridLayer
+    from multi_modal_parallelism_b200.sharding import plan_for
+    from multi_modal_parallelism_b200.state import alloc_states, make_decode_ctx
+    from multi_modal_parallelism_b200.weights import shard_to_device
+    from tests.test_branch_chains_host import _FakeStreams
+
+    def fake_ensure(self, rank_sets):
+        for rs in rank_sets:
+            rs = tuple(rs)
+            if 1 < len(rs) < self.world_size and self.rank in rs:
+                self.extra[rs] = D.Coordinator(rs, None)
+
+    fs = _FakeStreams([])
+    monkeypatch.setattr(torch.cuda, "Stream", fs.Stream)
+    monkeypatch.setattr(torch.cuda, "current_stream", fs.current_stream)
+    monkeypatch.setattr(torch.cuda, "stream", fs.stream)
+    monkeypatch.setattr(D.Groups, "ensure", fake_ensure)
+    monkeypatch.setattr(D.Coordinator, "all_reduce", lambda self, t: t)
+    dims = preset("falcon_h1_7b_like")
+    full = {k: torch.zeros(v.shape, dtype=v.dtype) for k, v in _layer_shapes(dims).items()}
+    B, deferring = 64, 0
+    for r in range(world):
+        plan = plan_for(mode, r, world, dims)
+        ctx = make_decode_ctx(B, 40, 16, CPU)
+        st = alloc_states(plan, dims, B, ctx.block_table.numel(), 16, CPU, torch.float32)
+        g = D.Groups(rank=r, local_rank=r, world_size=world, tp=D.Coordinator(tuple(range(world)), None), pair=None,
+                     device=CPU)
+        layer = ParallelHybridLayer(plan, shard_to_device(full, plan, dims, CPU), dims, g, st, ctx, CPU,
+                                    overlap_branches=False, defer_norm=True)
+        deferring += int(layer.ssm is not None and layer.ssm.defer)
+        layer.step(torch.zeros(B, dims.hidden, dtype=torch.bfloat16))
+    names = {n for n, _ in validating_library}
+    assert "mmp_scale_rows" in names and deferring > 0

@@ -68,16 +68,19 @@ def test_bench_layout_candidates_are_valid_and_rank_independent():
     spec.loader.exec_module(bench)
     d = preset("falcon_h1_7b_like")
     assert bench.layout_candidates(d, 1, 64, 2048) == ["tp1", "tp1_chains"]
-    assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split13", "tp4_fused", "tp4_fused_chains"]
-    assert bench.layout_candidates(d, 2, 64, 2048) == ["split11", "mix8", "mix6", "tp4_fused", "tp4_fused_chains"]
+    assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split22_dn", "split13", "split13_dn", "tp4_fused",
+                                                       "tp4_fused_chains"]
+    assert bench.layout_candidates(d, 2, 64, 2048) == ["split11", "mix8", "mix8_dn", "mix6", "mix6_dn", "tp4_fused",
+                                                       "tp4_fused_chains"]
     assert bench.layout_candidates(d, 4, 64, 2048, "p2p_fused") == ["split22", "split13", "tp4_fused"]
-    assert bench.parse_recipe("tp4_fused_chains") == ("tp4_fused", True)
-    assert bench.parse_recipe("split26") == ("split26", False)
+    assert bench.parse_recipe("tp4_fused_chains") == ("tp4_fused", True, False)
+    assert bench.parse_recipe("split26") == ("split26", False, False)
+    assert bench.parse_recipe("mix8_dn") == ("mix8", False, True)
     for world in (1, 2, 4, 8):
         labels = bench.layout_candidates(d, world, 64, 2048)
         assert len(set(labels)) == len(labels)
         for label in labels:
-            mode, _ = bench.parse_recipe(label)
+            mode, _, _ = bench.parse_recipe(label)
             for r in range(world):
                 plan_for(mode, r, world, d)
 

@@ -176,3 +176,13 @@ def test_two_gpu_mix_layout(extra, tmp_path):
 def test_two_gpu_mix_prefill():
     """Prefill (and the decode step after it) in mix8 equals the single-rank prefill."""
     run_prefill_check(2, "mix8")
+
+
+@pytest.mark.run_last
+@pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world,mode", [(2, "mix8"), (4, "split13"), (4, "split22"), (8, "split26")])
+def test_deferred_norm_statistic(world, mode, tmp_path):
+    """Mamba-2-only ranks overlap the gated norm's row-statistic all-reduce with their out-projection."""
+    if ngpu() < world:
+        pytest.skip(f"needs {world} GPUs")
+    run_check(world, mode, tmp_path, ("--defer-norm",))
