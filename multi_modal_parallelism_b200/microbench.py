@@ -6,6 +6,8 @@ prefill kernels, which the reference does not have.
     torchrun --standalone --nproc_per_node=4 -m multi_modal_parallelism_b200.microbench --out microbench.csv
     python -m multi_modal_parallelism_b200.microbench --only gemm --shape 4096,8728,3072 --iters 3
     python -m multi_modal_parallelism_b200.microbench --only ssd_prefill --nseq 2 --len 2048 --iters 3
+    python -m multi_modal_parallelism_b200.microbench --only ssd_prefill --segments --nseq 8 --len 2048 --iters 3
+    python -m multi_modal_parallelism_b200.microbench --only attn_prefill --tc --nseq 2 --len 2048 --iters 3
     python -m multi_modal_parallelism_b200.microbench --only attn_prefill --nseq 2 --len 2048 --iters 3
     python -m multi_modal_parallelism_b200.microbench --only decode_step --iters 3
 
@@ -205,7 +207,18 @@ def only(args, g) -> dict:
             Cm = torch.randn_like(Bm)
             st = torch.zeros(args.nseq + 1, nh, p, N, device=dev)
             y = torch.empty_like(x)
-            ms = timed(lambda: K.ssd_prefill(x, dt, A, Bm, Cm, D, dtb, st, pc.cu_seqlens, pc.state_idx, pc.has_init, y))
+            if args.segments:  # balanced walks: the planner's cuts (3 per sequence when it would not cut)
+                from .segments import build_segments
+
+                lens = [args.len] * args.nseq
+                segs = build_segments(lens, [0] * args.nseq, nh, p, N, dev) or \
+                    build_segments(lens, [0] * args.nseq, nh, p, N, dev, counts=[3] * args.nseq)
+                ms = timed(lambda: K.ssd_prefill_segmented(x, dt, A, Bm, Cm, D, dtb, st, pc.state_idx, pc.has_init, y,
+                                                           segs))
+                res.update(segments=segs.counts)
+            else:
+                ms = timed(lambda: K.ssd_prefill(x, dt, A, Bm, Cm, D, dtb, st, pc.cu_seqlens, pc.state_idx,
+                                                 pc.has_init, y))
             res.update(tokens=T, ms=ms, tokens_per_s=T / ms * 1e3)
         elif args.only == "attn_prefill":
             nq, nkv, hd = 12, 2, 128
@@ -213,7 +226,10 @@ def only(args, g) -> dict:
             kv.normal_(generator=gen)
             q = torch.randn(T, nq, hd, device=dev, dtype=BF, generator=gen)
             out = torch.empty_like(q)
+            prev = K.set_attn_prefill_tc(args.tc)
             ms = timed(lambda: K.attn_prefill(q, kc, vc, pc.block_table, pc.cu_seqlens, pc.ctx_start, pc.max_len, out))
+            K.set_attn_prefill_tc(prev)
+            res.update(kernel_variant="tcgen05" if args.tc else "mma.sync")
             flops = 4 * args.nseq * (args.len * (args.len + 1) / 2) * hd * nq
             res.update(tokens=T, ms=ms, tflops=flops / ms / 1e9)
         else:
@@ -257,6 +273,8 @@ def main() -> None:
     ap.add_argument("--nseq", type=int, default=2)
     ap.add_argument("--len", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--tc", action="store_true", help="attn_prefill: the tcgen05/TMEM kernel")
+    ap.add_argument("--segments", action="store_true", help="ssd_prefill: balanced walks (segments + join)")
     args = ap.parse_args()
     g = init_groups()
     if args.only:
