@@ -430,6 +430,18 @@ def plan_ok(mode: str, dims, world: int) -> bool:
         return False
 
 
+def device_error_flagged(device) -> bool:
+    """Whether a library kernel flagged an error on this device since the last look (the word is then cleared);
+    unlike kernels.check_device_errors this does not raise, so every rank can take part in the same decision."""
+    from multi_modal_parallelism_b200 import kernels as K
+
+    w = K.error_word(device)
+    flagged = int(w.item()) != 0
+    if flagged:
+        w.zero_()
+    return flagged
+
+
 def state_tensors(layer) -> list:
     """The layer's mutable decode state (paged KV buffer, conv and SSM state lines)."""
     st = layer.st
@@ -468,8 +480,8 @@ def our_arm(args) -> None:
     results = {}
     keep = {}
     # every recipe's first decode step, eager and as the replayed graph that is timed, is checked against the whole
-    # layer on one GPU (same seeded weights, states and input; bf16 tolerance); a recipe that disagrees on any rank
-    # is timed but never reported
+    # layer on one GPU (same seeded weights, states and input; bf16 tolerance) and against the device error word;
+    # a recipe that fails on any rank is neither timed nor reported
     ref_layer, h_ref = build_layer(args, "tp1", groups, dims, full, single_rank=True)
     ref_out = ref_layer.step(h_ref).clone()
     del ref_layer, h_ref
@@ -487,11 +499,21 @@ def our_arm(args) -> None:
             t.copy_(t0)
         mg = compare(gs.replay(), ref_out)  # the replayed graph: what is timed
         del snap
-        agrees = max_over_ranks(0.0 if within_tolerance(m) and within_tolerance(mg) else 1.0, groups) == 0.0
+        flagged = device_error_flagged(groups.device)  # an index error or a wait that ran out of its budget
+        ok = within_tolerance(m) and within_tolerance(mg) and not flagged
+        agrees = max_over_ranks(0.0 if ok else 1.0, groups) == 0.0  # the same decision on every rank
+        rel = max_over_ranks(max(m["rel_l2"], mg["rel_l2"]), groups)
+        if not agrees:  # never timed: a recipe whose waits run out would stall the bench for every replay
+            results[mode] = {"ms_per_step": None, "tokens_per_s": None, "launches_per_step": launches_per_step,
+                             "agrees_with_single_gpu": False, "rel_l2_vs_single_gpu": rel,
+                             "device_error": flagged}
+            gs.release()
+            keep[mode] = (layer, h, gs)
+            continue
         ms, p50 = time_replays(gs.replay, args.steps, args.warmup, groups)
         results[mode] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": args.batch / ms * 1e3,
                          "launches_per_step": launches_per_step, "agrees_with_single_gpu": agrees,
-                         "rel_l2_vs_single_gpu": max_over_ranks(max(m["rel_l2"], mg["rel_l2"]), groups)}
+                         "rel_l2_vs_single_gpu": rel}
         keep[mode] = (layer, h, gs)
     valid = [m for m in modes if results[m]["agrees_with_single_gpu"]]
     if not valid:
