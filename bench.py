@@ -492,27 +492,32 @@ def our_arm(args) -> None:
     del ref_layer, h_ref
     torch.cuda.empty_cache()
     for mode in modes:
-        layer, h = build_layer(args, mode, groups, dims, full)
-        # the recipe's seeded states, so that the captured step can be checked from the same starting point
-        snap = [t.clone() for t in state_tensors(layer)]
-        m = compare(layer.step(h), ref_out)  # also the eager warm-up (allocations, library init)
-        n0 = _lib.LAUNCHES[0]
-        layer.step(h)
-        launches_per_step = _lib.LAUNCHES[0] - n0
-        gs = GraphedStep(layer, groups, h)
-        for t, t0 in zip(state_tensors(layer), snap):
-            t.copy_(t0)
-        mg = compare(gs.replay(), ref_out)  # the replayed graph: what is timed
-        del snap
-        flagged = device_error_flagged(groups.device)  # an index error or a wait that ran out of its budget
-        ok = within_tolerance(m) and within_tolerance(mg) and not flagged
+        gs, layer, h, m, mg, launches_per_step, flagged, err = None, None, None, None, None, None, False, None
+        try:
+            layer, h = build_layer(args, mode, groups, dims, full)
+            # the recipe's seeded states, so that the captured step can be checked from the same starting point
+            snap = [t.clone() for t in state_tensors(layer)]
+            m = compare(layer.step(h), ref_out)  # also the eager warm-up (allocations, library init)
+            n0 = _lib.LAUNCHES[0]
+            layer.step(h)
+            launches_per_step = _lib.LAUNCHES[0] - n0
+            gs = GraphedStep(layer, groups, h)
+            for t, t0 in zip(state_tensors(layer), snap):
+                t.copy_(t0)
+            mg = compare(gs.replay(), ref_out)  # the replayed graph: what is timed
+            del snap
+            flagged = device_error_flagged(groups.device)  # an index error or a wait that ran out of its budget
+            ok = within_tolerance(m) and within_tolerance(mg) and not flagged
+        except Exception as e:  # a recipe that cannot be built, stepped or captured here is dropped, not fatal
+            ok, err = False, f"{type(e).__name__}: {e}"[:300]
         agrees = max_over_ranks(0.0 if ok else 1.0, groups) == 0.0  # the same decision on every rank
-        rel = max_over_ranks(max(m["rel_l2"], mg["rel_l2"]), groups)
+        rel = max_over_ranks(max(m["rel_l2"], mg["rel_l2"]) if m and mg else 1.0, groups)
         if not agrees:  # never timed: a recipe whose waits run out would stall the bench for every replay
             results[mode] = {"ms_per_step": None, "tokens_per_s": None, "launches_per_step": launches_per_step,
                              "agrees_with_single_gpu": False, "rel_l2_vs_single_gpu": rel,
-                             "device_error": flagged}
-            gs.release()
+                             "device_error": flagged, "error": err}
+            if gs is not None:
+                gs.release()
             keep[mode] = (layer, h, gs)
             continue
         ms, p50 = time_replays(gs.replay, args.steps, args.warmup, groups)
@@ -526,7 +531,7 @@ def our_arm(args) -> None:
     best = min(valid, key=lambda m: results[m]["ms_per_step"])
     layer, h, gs = keep[best]
     for m in modes:
-        if m != best:
+        if m != best and keep[m][2] is not None:
             keep[m][2].release()
 
     # clocks over a soak plus a second timed pass of the headline recipe
@@ -556,7 +561,8 @@ def our_arm(args) -> None:
         roof_local = max(cands, key=lambda r: r["us"]) if cands else None
     gs.release()
     for m in modes:
-        keep[m][2].release()
+        if keep[m][2] is not None:
+            keep[m][2].release()
     barrier_sync()
     prefill = time_prefill(args, layer, groups)
 
