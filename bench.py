@@ -564,7 +564,10 @@ def our_arm(args) -> None:
         if keep[m][2] is not None:
             keep[m][2].release()
     barrier_sync()
-    prefill = time_prefill(args, layer, groups)
+    try:
+        prefill = time_prefill(args, layer, groups)
+    except Exception as e:  # the prefill figure is secondary: its failure must not cost the decode line
+        prefill = {"error": f"{type(e).__name__}: {e}"[:300]}
 
     cpu = None
     if groups.rank == 0 and world == 1 and args.cpu_s > 0:
