@@ -1,0 +1,198 @@
+"""Discrete-event model of the synchronisation of attn_prefill_tc_kernel (csrc/attn_prefill_tc.cu), test
+infrastructure. mbarriers keep arrival counts, transaction bytes and a phase counter, with try_wait.parity's
+meaning (true once the phase of that parity has completed; parity 1 passes before the first phase). The copy
+engine completes each page box at a random time; the tensor pipe completes MMAs in issue order at random times
+and a commit arrives once everything issued before it has completed. The producer (copies), the MMA thread and W
+softmax warps run the kernel's sequence of waits, arrivals, issues, reads and writes. Every access is checked:
+an MMA may only read a buffer holding the version it needs with no copy or thread writing it, a copy may only
+overwrite a stage nothing is still reading, threads may only read scores the MMA has finished and write P or O
+while no MMA uses them. A run also fails if every actor waits and nothing is in flight (a deadlock)."""
+from __future__ import annotations
+
+import random
+
+
+class Bar:
+    def __init__(self, count: int):
+        self.count, self.pending, self.tx, self.phase = count, count, 0, 0
+
+    def _check(self):
+        if self.pending == 0 and self.tx == 0:
+            self.phase += 1
+            self.pending = self.count
+
+    def arrive(self):
+        assert self.pending > 0
+        self.pending -= 1
+        self._check()
+
+    def expect_tx(self, n):
+        self.tx += n
+        self.arrive()
+
+    def complete_tx(self, n):
+        self.tx -= n
+        self._check()
+
+    def passed(self, parity: int) -> bool:
+        return (self.phase & 1) != parity
+
+
+class Sim:
+    def __init__(self, nkt: int, warps: int, nb: int, seed: int, tail: bool, rescale_p: float, bug: str = ""):
+        self.rng = random.Random(seed)
+        self.nkt, self.warps, self.nb, self.tail, self.rescale_p, self.bug = nkt, warps, nb, tail, rescale_p, bug
+        self.bars = {"Q": Bar(warps), "K0": Bar(1), "K1": Bar(1), "V0": Bar(1), "V1": Bar(1), "E0": Bar(1),
+                     "E1": Bar(1), "S0": Bar(1), "S1": Bar(1), "P": Bar(warps), "O": Bar(1), "DONE": Bar(1)}
+        self.version = {"K0": None, "K1": None, "V0": None, "V1": None, "S0": None, "S1": None, "P": None, "O": -1}
+        self.readers = {k: 0 for k in self.version}   # MMAs in flight reading the buffer
+        self.writers = {k: 0 for k in self.version}   # copies or MMAs in flight writing it
+        self.s_read = {"S0": None, "S1": None}         # last score tile every warp has read
+        self.warp_read = [{"S0": None, "S1": None} for _ in range(warps)]
+        self.p_rows = [None] * warps                   # P tile each warp's rows hold
+        self.copies: list = []                          # in flight: (bar, bytes, buffer, tile)
+        self.mma_q: list = []                           # in order: ("mma", reads, writes, tile) / ("commit", bar)
+        self.errors: list[str] = []
+        self.q_written = 0
+
+    def err(self, msg):
+        self.errors.append(msg)
+
+    # ---------------------------------------------------------------- the engines
+    def issue_copy(self, buf, tile):
+        if self.readers[buf]:
+            self.err(f"copy of tile {tile} into {buf} while an MMA still reads it")
+        self.writers[buf] += self.nb
+        for _ in range(self.nb):
+            self.copies.append((buf[0] + buf[1], 32768 // self.nb, buf, tile))
+
+    def complete_copy(self, i):
+        bar, n, buf, tile = self.copies.pop(i)
+        self.writers[buf] -= 1
+        if self.writers[buf] == 0:
+            self.version[buf] = tile
+        self.bars[bar].complete_tx(n)
+
+    def issue_mma(self, reads: dict, writes: dict, what: str):
+        for buf, ver in reads.items():
+            if self.writers[buf] or self.version[buf] != ver:
+                self.err(f"{what} reads {buf}: holds {self.version[buf]} (writers {self.writers[buf]}), needs {ver}")
+            self.readers[buf] += 1
+        for buf in writes:
+            if buf in ("S0", "S1") and self.version[buf] is not None and any(
+                    w[buf] != self.version[buf] for w in self.warp_read):
+                self.err(f"{what} overwrites {buf} before every warp read tile {self.version[buf]}")
+            self.writers[buf] += 1
+        self.mma_q.append(("mma", reads, writes, what))
+
+    def commit(self, bar):
+        self.mma_q.append(("commit", bar))
+
+    def complete_mma_head(self):
+        item = self.mma_q.pop(0)
+        if item[0] == "commit":
+            self.bars[item[1]].arrive()
+            return
+        _, reads, writes, _ = item
+        for buf in reads:
+            self.readers[buf] -= 1
+        for buf, ver in writes.items():
+            self.writers[buf] -= 1
+            self.version[buf] = ver
+
+    # ---------------------------------------------------------------- the roles
+    def producer(self):
+        for j in range(self.nkt):
+            s = j & 1
+            if j >= 2:
+                yield ("E" + str(s), ((j >> 1) - 1) & 1)
+            self.bars["K" + str(s)].expect_tx(32768)
+            self.issue_copy("K" + str(s), j)
+            self.bars["V" + str(s)].expect_tx(32768)
+            self.issue_copy("V" + str(s), j)
+
+    def mma(self):
+        yield ("Q", 0)
+        yield ("K0", 0)
+        self.issue_mma({"K0": 0}, {"S0": 0}, "S(0)")
+        self.commit("S0")
+        for j in range(self.nkt):
+            if j + 1 < self.nkt:
+                b = (j + 1) & 1
+                yield ("K" + str(b), ((j + 1) >> 1) & 1)
+                self.issue_mma({"K" + str(b): j + 1}, {"S" + str(b): j + 1}, f"S({j + 1})")
+                self.commit("S" + str(b))
+            yield ("P", j & 1)
+            if self.bug != "pv_before_v":
+                yield ("V" + str(j & 1), (j >> 1) & 1)
+            self.issue_mma({"P": j, "V" + str(j & 1): j}, {"O": j}, f"PV({j})")
+            self.commit("O")
+            self.commit("E" + str(j & 1))
+        self.commit("DONE")
+
+    def softmax(self, w):
+        self.q_written += 1
+        self.bars["Q"].arrive()
+        for j in range(self.nkt):
+            sb = "S" + str(j & 1)
+            yield (sb, (j >> 1) & 1)
+            if self.writers[sb] or self.version[sb] != j:
+                self.err(f"warp {w} reads {sb} holding {self.version[sb]} (writers {self.writers[sb]}) for tile {j}")
+            self.warp_read[w][sb] = j
+            o_ready = j == 0
+            if j > 0 and self.rng.random() < self.rescale_p:  # a row maximum grew: rescale O
+                yield ("O", (j - 1) & 1)
+                o_ready = True
+                if self.writers["O"] or self.version["O"] != j - 1:
+                    self.err(f"warp {w} rescales O holding {self.version['O']} while PV runs (tile {j})")
+            if not o_ready and self.bug != "p_before_pv":
+                yield ("O", (j - 1) & 1)
+            if self.tail and j == self.nkt - 1:
+                vb = "V" + str(j & 1)
+                yield (vb, (j >> 1) & 1)
+                if self.writers[vb] or self.readers[vb] or self.version[vb] != j:
+                    self.err(f"warp {w} zeroes the tail of {vb} holding {self.version[vb]} (tile {j})")
+            if self.readers["P"]:
+                self.err(f"warp {w} writes P({j}) while PV reads P")
+            self.p_rows[w] = j
+            if all(p == j for p in self.p_rows):
+                self.version["P"] = j
+            self.bars["P"].arrive()
+        yield ("O", (self.nkt - 1) & 1)
+        if self.writers["O"] or self.version["O"] != self.nkt - 1:
+            self.err(f"warp {w} reads the output holding {self.version['O']}")
+
+    # ---------------------------------------------------------------- the scheduler
+    def run(self) -> list[str]:
+        actors = [self.producer(), self.mma()] + [self.softmax(w) for w in range(self.warps)]
+        waiting = [None] * len(actors)
+        live = list(range(len(actors)))
+        steps = 0
+        while live or self.copies or self.mma_q:
+            steps += 1
+            if steps > 100000:
+                return self.errors + ["no progress"]
+            choices = []
+            for a in live:
+                wt = waiting[a]
+                if wt is None or self.bars[wt[0]].passed(wt[1]):
+                    choices.append(("actor", a))
+            choices += [("copy", i) for i in range(len(self.copies))]
+            if self.mma_q:
+                choices.append(("mma", 0))
+            if not choices:
+                return self.errors + [f"deadlock: waits {[waiting[a] for a in live]}"]
+            kind, i = self.rng.choice(choices)
+            if kind == "copy":
+                self.complete_copy(i)
+            elif kind == "mma":
+                self.complete_mma_head()
+            else:
+                try:
+                    waiting[i] = next(actors[i])
+                except StopIteration:
+                    live.remove(i)
+                    waiting[i] = None
+        if not self.bars["DONE"].passed(0):
+            self.errors.append("the final commit never arrived")
+        return self.errors
