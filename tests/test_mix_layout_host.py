@@ -10,7 +10,6 @@ import os
 import socket
 
 import numpy as np
-import pytest
 import torch
 
 from multi_modal_parallelism_b200.config import preset

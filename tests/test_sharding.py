@@ -2,7 +2,7 @@
 reference holds the same expectations), plus the generalised split{a}{m} layouts."""
 import pytest
 
-from multi_modal_parallelism_b200.config import MODES, FalconH1Dims, preset
+from multi_modal_parallelism_b200.config import MODES, preset
 from multi_modal_parallelism_b200.sharding import (
     all_norm_groups, attn_shard, build_mup_vector, k_grid, kv_replication_map, mlp_shard, parse_split, plan_for,
     ssm_shard, swing_width,

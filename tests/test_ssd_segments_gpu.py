@@ -3,7 +3,6 @@ and final states against the oracle's sequential recurrence, for head dim 128 wi
 128 and 256 (tcgen05 scan), fp32 and bf16 state lines, fresh and continuing sequences, cuts chosen by the planner
 and forced ones; lines no sequence owns stay untouched. And the hybrid layer's prefill with the option against the
 same layer without it. Tolerance as the other prefill tests."""
-import numpy as np
 import pytest
 import torch
 

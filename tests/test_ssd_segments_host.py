@@ -5,8 +5,6 @@ scans segments from zero in fp64, joins them the way the join kernel does (S_in 
 correction product, y rounded to bf16 before and after), and must reproduce the unsegmented recurrence within the
 bf16 tolerance, for fresh and continuing sequences. Plus the C library's argument checks for the segmented call
 at the 7B-like layer's prefill shapes."""
-import math
-
 import numpy as np
 import pytest
 import torch
