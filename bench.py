@@ -127,6 +127,79 @@ def cpu_layer_tokens_per_s(args, budget_s: float, max_steps: int | None = None) 
             "ms_per_step": med * 1e3, "steps_timed": len(times)}
 
 
+def cpu_mamba2_tokens_per_s(args, dims, full, budget_s: float) -> dict:
+    """The oracle's fp32 pure Mamba-2 layer (numpy mixed step) on this host's cores: a bounded sample of the same
+    workload, 16 live requests with a quarter restarting as prompts of 64-1024 tokens each step, tokens/s."""
+    import numpy as np
+
+    import oracle
+    from multi_modal_parallelism_b200.sg import continuous_batches
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # pragma: no cover
+        threads = os.cpu_count()
+    fn = {k: oracle.to_numpy(v) for k, v in full.items()}
+    req = 16
+    conv = np.zeros((req + 1, dims.d_conv - 1, dims.d_ssm + 2 * dims.n_groups * dims.d_state), np.float32)
+    ssm = np.zeros((req + 1, dims.n_mamba_heads, dims.mamba_head_dim, dims.d_state), np.float32)
+    rng = np.random.default_rng(args.seed)
+    tokens, t_total, steps = 0, 0.0, 0
+    for b in continuous_batches(1000, batch=req, prefill_frac=0.25, len_range=(64, 1024), seed=args.seed):
+        h = rng.standard_normal((b.T, dims.hidden)).astype(np.float32)
+        t0 = time.perf_counter()
+        oracle.mamba2_mixed_step(fn, dims, h, b.dec_lines, b.pre_lens, b.pre_lines, [0] * len(b.pre_req), conv, ssm)
+        t_total += time.perf_counter() - t0
+        tokens += b.T
+        steps += 1
+        if t_total >= budget_s:
+            break
+    return {"value": tokens / t_total, "unit": "tokens/s", "cores": int(threads), "kind": "port",
+            "sample": f"{steps} mixed steps of {req} requests ({tokens} tokens) of the numpy fp32 layer, "
+                      f"{threads} BLAS threads"}
+
+
+def cpu_qwen35_tokens_per_s(args, d, ws, budget_s: float) -> dict:
+    """The oracle's fp32 Gated DeltaNet stack (numpy) decoding on this host's cores: a bounded sample of up to 4
+    rows at the bench's context (delta-rule and conv states and cached keys/values seeded directly), tokens/s."""
+    import numpy as np
+
+    import oracle
+
+    try:
+        from threadpoolctl import threadpool_info
+
+        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
+    except Exception:  # pragma: no cover
+        threads = os.cpu_count()
+    rng = np.random.default_rng(args.seed)
+    rows = min(args.batch, 4)
+    wn = [{k: oracle.to_numpy(v) for k, v in w.items()} for w in ws]
+    f32 = np.float32
+    state = []
+    for kind in d.layout:
+        if kind == "G":
+            state.append([((rng.standard_normal((d.d_conv - 1, d.qkv_rows)) * 0.1).astype(f32),
+                           (rng.standard_normal((d.n_v, d.dv, d.dk)) * 0.05).astype(f32)) for _ in range(rows)])
+        else:
+            state.append([(rng.standard_normal((args.ctx, d.n_kv, d.head_dim)).astype(f32),
+                           rng.standard_normal((args.ctx, d.n_kv, d.head_dim)).astype(f32)) for _ in range(rows)])
+    h = rng.standard_normal((rows, d.hidden)).astype(f32)
+    _, state = oracle.qwen35_stack_decode(wn, d, h, state)  # warm
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while not times or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        _, state = oracle.qwen35_stack_decode(wn, d, h, state)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"value": rows / med, "unit": "tokens/s", "cores": int(threads), "kind": "port",
+            "sample": f"{len(times)} decode steps of {rows} rows at context {args.ctx} of the numpy fp32 stack, median "
+                      f"{med * 1e3:.1f} ms/step, {threads} BLAS threads"}
+
+
 def reference_arm(args, rank: int) -> None:
     if rank != 0:
         return
@@ -612,6 +685,7 @@ def mamba2_arm(args) -> None:
     time, max over ranks. Run e.g. `python bench.py --workload mamba2_sg --steps 20 --warmup 3`."""
     import torch
 
+    from multi_modal_parallelism_b200 import _lib
     from multi_modal_parallelism_b200.config import preset
     from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
     from multi_modal_parallelism_b200.mamba2 import Mamba2Layer, alloc_mamba2_states, mixed_ctx
@@ -631,6 +705,7 @@ def mamba2_arm(args) -> None:
     h_all = torch.randn(tmax, dims.hidden, device=dev, generator=g).to(torch.bfloat16)
     modes = ["tp"] if world == 1 else ([f"sg{world // 2}{world // 2}"] if world % 2 == 0 else []) + ["tp"]
     results = {}
+    clocks_by_mode = {}
     for mode in modes:
         if parse_sg(mode):
             plan = sg_plan(mode, groups.rank, world, dims)
@@ -642,24 +717,49 @@ def mamba2_arm(args) -> None:
         for b, c in zip(batches[:args.warmup], ctxs[:args.warmup]):
             layer.step(h_all[:b.T], c)
         barrier_sync()
+        n0 = _lib.LAUNCHES[0]
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps + 1)]
-        ev[0].record()
-        for i, (b, c) in enumerate(zip(batches[args.warmup:], ctxs[args.warmup:])):
-            layer.step(h_all[:b.T], c)
-            ev[i + 1].record()
-        torch.cuda.synchronize()
+        with Clocks(groups.local_rank) as clk:
+            ev[0].record()
+            for i, (b, c) in enumerate(zip(batches[args.warmup:], ctxs[args.warmup:])):
+                layer.step(h_all[:b.T], c)
+                ev[i + 1].record()
+            torch.cuda.synchronize()
+        launches = _lib.LAUNCHES[0] - n0
         per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.steps)]
         total = max_over_ranks(ev[0].elapsed_time(ev[-1]), groups)
         tokens = sum(b.T for b in batches[args.warmup:])
+        # end to end: each step's rows from pinned host memory, the step, its output rows back to pinned host memory
+        h_host = h_all.detach().cpu().pin_memory()
+        o_host = torch.empty(h_all.shape, dtype=h_all.dtype).pin_memory()
+        barrier_sync()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for b, c in zip(batches[args.warmup:], ctxs[args.warmup:]):
+            h_all[:b.T].copy_(h_host[:b.T], non_blocking=True)
+            out = layer.step(h_all[:b.T], c)
+            if out is not None:
+                o_host[:b.T].copy_(out, non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), groups)
         results[mode] = {"ms_per_step": total / args.steps, "p50_ms": max_over_ranks(statistics.median(per), groups),
-                         "tokens_per_s": tokens / total * 1e3, "tokens_per_step": tokens / args.steps}
+                         "tokens_per_s": tokens / total * 1e3, "tokens_per_step": tokens / args.steps,
+                         "launches": launches, "e2e_tokens_per_s": tokens / e2e_ms * 1e3,
+                         "io_bytes": tokens * dims.hidden * 2}
+        clocks_by_mode[mode] = clk.summary()
         del layer, states
         torch.cuda.empty_cache()
         barrier_sync()
     if groups.rank == 0:
         best = max(results, key=lambda m: results[m]["tokens_per_s"])
         r = results[best]
+        cpu = cpu_mamba2_tokens_per_s(args, dims, full, args.cpu_s) if world == 1 and args.cpu_s > 0 else None
+        io = r["io_bytes"] / args.steps
         print(json.dumps({
+            "e2e": {"value": r["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": io,
+                    "d2h_bytes_per_step": io},
+            "gpu_launches": r["launches"], "clocks": clocks_by_mode[best], "cpu_baseline": cpu,
             "metric": "pure Mamba-2 layer tokens/s under continuous batching (SSM/gate split vs TP)",
             "value": r["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "higher_is_better": True,
@@ -699,6 +799,7 @@ def qwen35_arm(args) -> None:
     --warmup 20 --ctx 4096 --prefill-seqs 4 --prefill-len 4096`."""
     import torch
 
+    from multi_modal_parallelism_b200 import _lib
     from multi_modal_parallelism_b200 import kernels as K
     from multi_modal_parallelism_b200.dist import barrier_sync, capture_context, destroy, init_groups
     from multi_modal_parallelism_b200.qwen35 import GdnLayer, Qwen35Dims, Qwen35Stack, random_stack
@@ -730,11 +831,29 @@ def qwen35_arm(args) -> None:
         with capture_context(groups) as cc, torch.cuda.stream(cc.stream):
             for _ in range(3):
                 stack.step(h_dec, dc)
+            n0 = _lib.LAUNCHES[0]
+            stack.step(h_dec, dc)
+            launches = _lib.LAUNCHES[0] - n0
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph, stream=cc.stream):
-                stack.step(h_dec, dc)
-        ms, p50 = time_replays(graph.replay, args.steps, args.warmup, groups)
-        r["decode"] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": B / ms * 1e3}
+                out_dec = stack.step(h_dec, dc)
+        with Clocks(groups.local_rank) as clk:
+            ms, p50 = time_replays(graph.replay, args.steps, args.warmup, groups)
+        # end to end: this step's input from pinned host memory, the replay, the output back to pinned host memory
+        h_host = h_dec.detach().cpu().pin_memory()
+        o_host = torch.empty(out_dec.shape, dtype=out_dec.dtype).pin_memory()
+
+        def e2e_step():
+            h_dec.copy_(h_host, non_blocking=True)
+            graph.replay()
+            o_host.copy_(out_dec, non_blocking=True)
+
+        e2e_ms, _ = time_replays(e2e_step, args.steps, max(3, args.warmup // 10), groups)
+        r["decode"] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": B / ms * 1e3, "launches_per_step": launches,
+                       "clocks": clk.summary(), "e2e": {"value": B / e2e_ms * 1e3, "unit": "tokens/s",
+                                                        "h2d_bytes_per_step": h_dec.numel() * 2,
+                                                        "d2h_bytes_per_step": out_dec.numel() * 2,
+                                                        "ms_per_step": e2e_ms}}
         # the delta-rule decode kernel alone (first layer): fp32 state read + write per (row, value head)
         gl = next(x for x in stack.layers if isinstance(x, GdnLayer))
         nbytes = 2 * B * gl.nv * d.dv * d.dk * 4
@@ -767,6 +886,7 @@ def qwen35_arm(args) -> None:
         best = max(results, key=lambda m: results[m]["decode"]["tokens_per_s"])
         r = results[best]
         k = r["gdn_decode_kernel"]
+        cpu = cpu_qwen35_tokens_per_s(args, d, ws, args.cpu_s) if world == 1 and args.cpu_s > 0 else None
         print(json.dumps({
             "metric": "Gated DeltaNet hybrid stack decode tokens/s (attention data-parallel vs TP)",
             "value": r["decode"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
@@ -780,6 +900,8 @@ def qwen35_arm(args) -> None:
             "roofline": {"bound": "hbm", "kernel": "gdn_decode", "achieved": k["gbs"], "peak": hbm, "unit": "GB/s",
                          "frac": k["frac"], "peak_source": hbm_src, "traffic": None},
             "bf16_peak": {"tflops": tf, "source": tf_src},
+            "e2e": r["decode"]["e2e"], "gpu_launches": r["decode"]["launches_per_step"] * args.steps,
+            "clocks": r["decode"]["clocks"], "cpu_baseline": cpu,
         }), flush=True)
     destroy()
 
