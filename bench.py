@@ -90,7 +90,7 @@ def cpu_prefill_tokens_per_s(args, positions: int = 64) -> dict:
                       f"layer ({dt:.2f} s); extrapolated to the prefill workload"}
 
 
-def cpu_layer_tokens_per_s(args, budget_s: float, max_steps: int | None = None) -> dict:
+def cpu_layer_tokens_per_s(args, budget_s: float, max_steps: int | None = None, warmup: int = 1) -> dict:
     """Time the oracle's fp32 layer (a numpy port of the reference's harness/reference.py:decode_step) on
     this host's cores, full batch, on the same seeded inputs."""
     import numpy as np
@@ -101,30 +101,30 @@ def cpu_layer_tokens_per_s(args, budget_s: float, max_steps: int | None = None) 
     from multi_modal_parallelism_b200.state import full_states_for_reference, input_hidden
     from multi_modal_parallelism_b200.weights import random_layer
 
-    try:
-        from threadpoolctl import threadpool_info
-
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:  # pragma: no cover
-        threads = os.cpu_count()
+    threads = os.cpu_count()  # numpy's BLAS runs on every core (_all_cores)
     dims = preset(args.dims)
     cpu = torch.device("cpu")
     full = {k: oracle.to_numpy(v) for k, v in random_layer(dims, args.seed).items()}
     kc, vc, conv, ssm = full_states_for_reference(dims, args.batch, args.ctx, args.seed, cpu)
     kc, vc, conv, ssm = (oracle.to_numpy(t) for t in (kc, vc, conv, ssm))
     h = oracle.to_numpy(input_hidden(args.seed, args.batch, dims.hidden, cpu))
-    oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx)  # warm
     times = []
-    t_end = time.perf_counter() + budget_s
-    while (not times or time.perf_counter() < t_end) and (max_steps is None or len(times) < max_steps):
-        t0 = time.perf_counter()
-        oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx)
-        times.append(time.perf_counter() - t0)
+    with _all_cores():
+        t_end = time.perf_counter() + budget_s
+        for _ in range(max(1, warmup)):  # warm-up calls, bounded by the budget
+            oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx)
+            if time.perf_counter() > t_end - 0.5 * budget_s:
+                break
+        t_end = time.perf_counter() + budget_s
+        while (not times or time.perf_counter() < t_end) and (max_steps is None or len(times) < max_steps):
+            t0 = time.perf_counter()
+            oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx)
+            times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": args.batch / med, "unit": UNIT, "cores": int(threads), "kind": "port",
             "sample": f"{len(times)} full decode steps (batch {args.batch}, context {args.ctx}) of the numpy fp32 "
                       f"layer, median {med * 1e3:.1f} ms/step, {threads} BLAS threads on {os.cpu_count()} host cores",
-            "ms_per_step": med * 1e3, "steps_timed": len(times)}
+            "ms_per_step": med * 1e3, "steps_timed": len(times), "warmup": warmup}
 
 
 def cpu_mamba2_tokens_per_s(args, dims, full, budget_s: float) -> dict:
@@ -135,27 +135,24 @@ def cpu_mamba2_tokens_per_s(args, dims, full, budget_s: float) -> dict:
     import oracle
     from multi_modal_parallelism_b200.sg import continuous_batches
 
-    try:
-        from threadpoolctl import threadpool_info
-
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:  # pragma: no cover
-        threads = os.cpu_count()
+    threads = os.cpu_count()  # numpy's BLAS runs on every core (_all_cores)
     fn = {k: oracle.to_numpy(v) for k, v in full.items()}
     req = 16
     conv = np.zeros((req + 1, dims.d_conv - 1, dims.d_ssm + 2 * dims.n_groups * dims.d_state), np.float32)
     ssm = np.zeros((req + 1, dims.n_mamba_heads, dims.mamba_head_dim, dims.d_state), np.float32)
     rng = np.random.default_rng(args.seed)
     tokens, t_total, steps = 0, 0.0, 0
-    for b in continuous_batches(1000, batch=req, prefill_frac=0.25, len_range=(64, 1024), seed=args.seed):
-        h = rng.standard_normal((b.T, dims.hidden)).astype(np.float32)
-        t0 = time.perf_counter()
-        oracle.mamba2_mixed_step(fn, dims, h, b.dec_lines, b.pre_lens, b.pre_lines, [0] * len(b.pre_req), conv, ssm)
-        t_total += time.perf_counter() - t0
-        tokens += b.T
-        steps += 1
-        if t_total >= budget_s:
-            break
+    with _all_cores():
+        for b in continuous_batches(1000, batch=req, prefill_frac=0.25, len_range=(64, 1024), seed=args.seed):
+            h = rng.standard_normal((b.T, dims.hidden)).astype(np.float32)
+            t0 = time.perf_counter()
+            oracle.mamba2_mixed_step(fn, dims, h, b.dec_lines, b.pre_lens, b.pre_lines, [0] * len(b.pre_req), conv,
+                                     ssm)
+            t_total += time.perf_counter() - t0
+            tokens += b.T
+            steps += 1
+            if t_total >= budget_s:
+                break
     return {"value": tokens / t_total, "unit": "tokens/s", "cores": int(threads), "kind": "port",
             "sample": f"{steps} mixed steps of {req} requests ({tokens} tokens) of the numpy fp32 layer, "
                       f"{threads} BLAS threads"}
@@ -168,12 +165,7 @@ def cpu_qwen35_tokens_per_s(args, d, ws, budget_s: float) -> dict:
 
     import oracle
 
-    try:
-        from threadpoolctl import threadpool_info
-
-        threads = max((i.get("num_threads", 1) for i in threadpool_info()), default=os.cpu_count())
-    except Exception:  # pragma: no cover
-        threads = os.cpu_count()
+    threads = os.cpu_count()  # numpy's BLAS runs on every core (_all_cores)
     rng = np.random.default_rng(args.seed)
     rows = min(args.batch, 4)
     wn = [{k: oracle.to_numpy(v) for k, v in w.items()} for w in ws]
@@ -187,13 +179,14 @@ def cpu_qwen35_tokens_per_s(args, d, ws, budget_s: float) -> dict:
             state.append([(rng.standard_normal((args.ctx, d.n_kv, d.head_dim)).astype(f32),
                            rng.standard_normal((args.ctx, d.n_kv, d.head_dim)).astype(f32)) for _ in range(rows)])
     h = rng.standard_normal((rows, d.hidden)).astype(f32)
-    _, state = oracle.qwen35_stack_decode(wn, d, h, state)  # warm
     times = []
-    t_end = time.perf_counter() + budget_s
-    while not times or time.perf_counter() < t_end:
-        t0 = time.perf_counter()
-        _, state = oracle.qwen35_stack_decode(wn, d, h, state)
-        times.append(time.perf_counter() - t0)
+    with _all_cores():
+        _, state = oracle.qwen35_stack_decode(wn, d, h, state)  # warm
+        t_end = time.perf_counter() + budget_s
+        while not times or time.perf_counter() < t_end:
+            t0 = time.perf_counter()
+            _, state = oracle.qwen35_stack_decode(wn, d, h, state)
+            times.append(time.perf_counter() - t0)
     med = statistics.median(times)
     return {"value": rows / med, "unit": "tokens/s", "cores": int(threads), "kind": "port",
             "sample": f"{len(times)} decode steps of {rows} rows at context {args.ctx} of the numpy fp32 stack, median "
@@ -204,9 +197,9 @@ def reference_arm(args, rank: int) -> None:
     if rank != 0:
         return
     budget = min(120.0, max(10.0, 0.05 * (args.steps + args.warmup)))
-    r = cpu_layer_tokens_per_s(args, budget, max_steps=max(1, args.steps))
+    r = cpu_layer_tokens_per_s(args, budget, max_steps=max(1, args.steps), warmup=args.warmup)
     line = {"metric": METRIC, "value": r["value"], "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": r["steps_timed"], "warmup": 1, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "steps": r["steps_timed"], "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
             "config": {**workload(args), "parallelism": "cpu"},
             "cpu_baseline": {k: r[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -263,6 +256,75 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+# ------------------------------------------------------------------------------------------- run guards
+_T0 = time.perf_counter()
+NCCL_TIMEOUT_S = 120.0  # eager collectives that wait longer end the job (NCCL's watchdog)
+
+
+def log(msg: str) -> None:
+    """One progress line on stderr, tagged with the rank and the seconds since start (the last lines of a job
+    that failed name the recipe and phase it was in)."""
+    print(f"[bench r{os.environ.get('RANK', '0')} {time.perf_counter() - _T0:7.1f}s] {msg}", file=sys.stderr,
+          flush=True)
+
+
+class Watchdog:
+    """Host-side bound on each phase of the run. NCCL's watchdog does not see collectives replayed from a CUDA
+    graph, so a rank whose peers never join a replayed all-reduce would wait forever; here a phase that outlives
+    its limit ends the process (torchrun then ends the other ranks) with a line naming the phase."""
+
+    def __init__(self):
+        import threading
+
+        self.deadline = None
+        self.name = ""
+        self.lock = threading.Lock()
+        t = threading.Thread(target=self._run, daemon=True)
+        t.start()
+
+    def _run(self) -> None:
+        while True:
+            time.sleep(0.5)
+            with self.lock:
+                d, name = self.deadline, self.name
+            if d is not None and time.perf_counter() > d:
+                log(f"phase '{name}' exceeded its time limit: ending the job")
+                os._exit(3)
+
+    def phase(self, name: str, limit_s: float):
+        wd = self
+
+        class _P:
+            def __enter__(self):
+                with wd.lock:
+                    wd.deadline, wd.name = time.perf_counter() + limit_s, name
+                log(f"{name}: start")
+
+            def __exit__(self, *exc):
+                with wd.lock:
+                    wd.deadline = None
+                return False
+
+        return _P()
+
+
+def fatal(where: str, e: BaseException) -> None:
+    """An exception inside a phase that issues collectives: this rank cannot rejoin its peers' collective
+    sequence, so the job ends here (torchrun ends the other ranks) rather than leaving them waiting."""
+    import traceback
+
+    log(f"{where}: {type(e).__name__}: {e}; ending the job")
+    traceback.print_exc(file=sys.stderr)
+    sys.stderr.flush()
+    sys.stdout.flush()
+    os._exit(2)
+
+
+def agree(ok: bool, groups) -> bool:
+    """True on every rank iff `ok` on every rank (one all-reduce)."""
+    return max_over_ranks(0.0 if ok else 1.0, groups) == 0.0
+
+
 # ------------------------------------------------------------------------------------------- our arm
 def roofline_peak() -> tuple[float, str]:
     p = ROOT / "MEASURED_PEAKS.json"
@@ -302,9 +364,11 @@ def prefill_flops(dims, lens: list[int], chunk: int = 256) -> dict:
     return {"gemm": gemm, "attn": attn, "ssd": ssd, "total": gemm + attn + ssd}
 
 
-def time_prefill(args, layer, groups) -> dict | None:
+def time_prefill(args, layer, groups, wd: "Watchdog | None" = None) -> dict | None:
     """Prefill of args.prefill_seqs fresh sequences of args.prefill_len tokens on the decode layer's own
-    cache blocks and state lines (the decode timing is over), device-timed, max over ranks."""
+    cache blocks and state lines (the decode timing is over), device-timed, max over ranks. Building the
+    inputs issues no collective and its outcome is agreed on every rank; an exception inside the prefill steps
+    (which all-reduce) ends the job."""
     import torch
 
     from multi_modal_parallelism_b200.dist import barrier_sync
@@ -313,10 +377,18 @@ def time_prefill(args, layer, groups) -> dict | None:
     nseq, L = args.prefill_seqs, args.prefill_len
     if L <= 0 or nseq <= 0 or nseq > args.batch or L > args.ctx:
         return None
+    wd = wd or Watchdog()
     dev = groups.device
-    pc = make_prefill_ctx([L] * nseq, 16, dev, block_table=layer.ctx.block_table[:nseq].cpu(), reserve=0)
-    g = torch.Generator().manual_seed(args.seed + 1)
-    h = torch.randn(pc.T, layer.dims.hidden, generator=g).to(dev, torch.bfloat16)
+    world = groups.world_size
+    err = None
+    try:
+        pc = make_prefill_ctx([L] * nseq, 16, dev, block_table=layer.ctx.block_table[:nseq].cpu(), reserve=0)
+        g = torch.Generator().manual_seed(args.seed + 1)
+        h = torch.randn(pc.T, layer.dims.hidden, generator=g).to(dev, torch.bfloat16)
+    except Exception as e:
+        err = f"{type(e).__name__}: {e}"[:300]
+    if not agree(err is None, groups):
+        return {"error": err or "another rank could not build the prefill inputs"}
     kernels = "attention mma.sync, SSD scan tcgen05"
     agrees = None
     if args.prefill_new:
@@ -324,26 +396,34 @@ def time_prefill(args, layer, groups) -> dict | None:
         from multi_modal_parallelism_b200 import kernels as K
         from multi_modal_parallelism_b200.correctness import compare, within_tolerance
 
-        ref = layer.prefill(h, pc).clone()
-        K.set_attn_prefill_tc(True)
-        layer.set_prefill_options(ssd_segments=True)
-        m = compare(layer.prefill(h, pc), ref)
-        ok = within_tolerance(m) and not device_error_flagged(groups.device)
-        agrees = max_over_ranks(0.0 if ok else 1.0, groups) == 0.0
+        with wd.phase("prefill: new kernels check", 300):
+            try:
+                ref = layer.prefill(h, pc).clone()
+                K.set_attn_prefill_tc(True)
+                layer.set_prefill_options(ssd_segments=True)
+                m = compare(layer.prefill(h, pc), ref)
+                ok = within_tolerance(m) and not device_error_flagged(groups.device)
+            except Exception as e:
+                fatal("prefill: new kernels check", e)
+        agrees = agree(ok, groups)
         kernels = "attention tcgen05, SSD scan tcgen05 with balanced walks"
         if not agrees:  # time the default kernels instead
             K.set_attn_prefill_tc(False)
             layer.set_prefill_options(ssd_segments=False)
             kernels = "attention mma.sync, SSD scan tcgen05 (the new kernels disagreed: not timed)"
-    for _ in range(3):
-        layer.prefill(h, pc)
-    barrier_sync()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.prefill_steps + 1)]
-    ev[0].record()
-    for i in range(args.prefill_steps):
-        layer.prefill(h, pc)
-        ev[i + 1].record()
-    torch.cuda.synchronize()
+    with wd.phase("prefill: timing", 300):
+        try:
+            for _ in range(3):
+                layer.prefill(h, pc)
+            barrier_sync()
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(args.prefill_steps + 1)]
+            ev[0].record()
+            for i in range(args.prefill_steps):
+                layer.prefill(h, pc)
+                ev[i + 1].record()
+            torch.cuda.synchronize()
+        except Exception as e:
+            fatal("prefill: timing", e)
     per = [ev[i].elapsed_time(ev[i + 1]) for i in range(args.prefill_steps)]
     ms = max_over_ranks(statistics.median(per), groups)
     barrier_sync()
@@ -355,7 +435,8 @@ def time_prefill(args, layer, groups) -> dict | None:
     tfs = fl["total"] / ms / 1e9
     return {"workload": f"{nseq} fresh sequences x {L} tokens", "tokens": pc.T, "ms_per_step": ms,
             "tokens_per_s": pc.T / ms * 1e3, "alg_tflop": {k: round(v / 1e12, 4) for k, v in fl.items()},
-            "achieved_tflops": tfs, "peak_tflops": peak, "frac": tfs / peak, "peak_source": f"{src} bf16_tflops",
+            "achieved_tflops": tfs, "peak_tflops": peak, "frac": tfs / (world * peak),
+            "peak_source": f"{src} bf16_tflops per GPU; frac = achieved / ({world} x peak)",
             "timing": "eager, median of device-timed steps, max over ranks", "kernels": kernels,
             "agrees_with_default_kernels": agrees}
 
@@ -538,6 +619,52 @@ def parse_recipe(label: str) -> tuple[str, bool, bool]:
             return label, chains, defer
 
 
+def oracle_check(args, outs: dict) -> dict:
+    """Each recipe's first decode step (rank 0's copy of the layer output) against the fp32 oracle layer on the
+    same seeded weights, states and input, on this host's cores: max-abs and rel-L2 per recipe."""
+    import torch
+
+    import oracle
+    from multi_modal_parallelism_b200.config import preset
+    from multi_modal_parallelism_b200.correctness import ABS_MAX, compare, within_tolerance
+    from multi_modal_parallelism_b200.state import full_states_for_reference, input_hidden
+    from multi_modal_parallelism_b200.weights import random_layer
+
+    dims = preset(args.dims)
+    cpu = torch.device("cpu")
+    with _all_cores():
+        full = {k: oracle.to_numpy(v) for k, v in random_layer(dims, args.seed).items()}
+        kc, vc, conv, ssm = (oracle.to_numpy(t) for t in full_states_for_reference(dims, args.batch, args.ctx,
+                                                                                     args.seed, cpu))
+        h = oracle.to_numpy(input_hidden(args.seed, args.batch, dims.hidden, cpu))
+        ref = torch.from_numpy(oracle.decode_step(full, dims, h, kc, vc, conv, ssm, args.ctx).out)
+    res = {}
+    for mode, o in outs.items():
+        m = compare(o, ref)
+        res[mode] = {"max_abs": round(m["max_abs"], 5), "rel_l2": round(m["rel_l2"], 6),
+                     "ref_max_abs": round(m["ref_max_abs"], 4), "within_tolerance": within_tolerance(m),
+                     "max_abs_within_absolute_2e-2": m["max_abs"] <= ABS_MAX}
+    return res
+
+
+class _all_cores:
+    """numpy's BLAS on every host core for the duration (torchrun sets OMP_NUM_THREADS=1 per rank)."""
+
+    def __enter__(self):
+        try:
+            from threadpoolctl import threadpool_limits
+
+            self.ctl = threadpool_limits(limits=os.cpu_count())
+        except Exception:  # pragma: no cover
+            self.ctl = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.ctl is not None:
+            self.ctl.unregister()
+        return False
+
+
 def our_arm(args) -> None:
     import torch
 
@@ -545,55 +672,85 @@ def our_arm(args) -> None:
     from multi_modal_parallelism_b200.config import preset
     from multi_modal_parallelism_b200.correctness import compare, within_tolerance
     from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
+    from multi_modal_parallelism_b200.sharding import all_norm_groups
     from multi_modal_parallelism_b200.timing import GraphedStep
     from multi_modal_parallelism_b200.weights import random_layer
 
-    groups = init_groups()
+    wd = Watchdog()
+    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
     world = groups.world_size
     if args.gpus != world:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     dims = preset(args.dims)
     full = random_layer(dims, args.seed)
     modes = layout_candidates(dims, world, args.batch, args.ctx, args.ar_impl)
+    log(f"recipes: {modes}")
+    # every communicator any recipe needs, created up front on every rank in the same order: building a recipe's
+    # layer then issues no collective (with the NCCL all-reduce)
+    with wd.phase("communicators", 300):
+        for mode in modes:
+            groups.ensure(all_norm_groups(parse_recipe(mode)[0], world, dims))
+    build_has_collectives = args.ar_impl != "nccl"  # peer-memory buffers are registered collectively
     results = {}
     keep = {}
+    first_out = {}
     # every recipe's first decode step, eager and as the replayed graph that is timed, is checked against the whole
     # layer on one GPU (same seeded weights, states and input; bf16 tolerance) and against the device error word;
     # a recipe that fails on any rank is neither timed nor reported
-    ref_layer, h_ref = build_layer(args, "tp1", groups, dims, full, single_rank=True)
-    ref_out = ref_layer.step(h_ref).clone()
-    del ref_layer, h_ref
-    torch.cuda.empty_cache()
+    with wd.phase("single-GPU reference step", 300):
+        ref_layer, h_ref = build_layer(args, "tp1", groups, dims, full, single_rank=True)
+        ref_out = ref_layer.step(h_ref).clone()
+        del ref_layer, h_ref
+        torch.cuda.empty_cache()
     for mode in modes:
         gs, layer, h, m, mg, launches_per_step, flagged, err = None, None, None, None, None, None, False, None
-        try:
-            layer, h = build_layer(args, mode, groups, dims, full)
-            # the recipe's seeded states, so that the captured step can be checked from the same starting point
-            snap = [t.clone() for t in state_tensors(layer)]
-            m = compare(layer.step(h), ref_out)  # also the eager warm-up (allocations, library init)
-            n0 = _lib.LAUNCHES[0]
-            layer.step(h)
-            launches_per_step = _lib.LAUNCHES[0] - n0
-            gs = GraphedStep(layer, groups, h)
-            for t, t0 in zip(state_tensors(layer), snap):
-                t.copy_(t0)
-            mg = compare(gs.replay(), ref_out)  # the replayed graph: what is timed
-            del snap
-            flagged = device_error_flagged(groups.device)  # an index error or a wait that ran out of its budget
-            ok = within_tolerance(m) and within_tolerance(mg) and not flagged
-        except Exception as e:  # a recipe that cannot be built, stepped or captured here is dropped, not fatal
-            ok, err = False, f"{type(e).__name__}: {e}"[:300]
-        agrees = max_over_ranks(0.0 if ok else 1.0, groups) == 0.0  # the same decision on every rank
-        rel = max_over_ranks(max(m["rel_l2"], mg["rel_l2"]) if m and mg else 1.0, groups)
+        with wd.phase(f"{mode}: build", 300):
+            try:
+                layer, h = build_layer(args, mode, groups, dims, full)
+                # the recipe's seeded states, so that the captured step can be checked from the same starting point
+                snap = [t.clone() for t in state_tensors(layer)]
+            except Exception as e:
+                if build_has_collectives:
+                    fatal(f"{mode}: build", e)
+                err = f"{type(e).__name__}: {e}"[:300]
+        if not agree(err is None, groups):  # the same decision on every rank, before any collective of the recipe
+            results[mode] = {"ms_per_step": None, "tokens_per_s": None, "agrees_with_single_gpu": False,
+                             "error": err or "another rank could not build this recipe"}
+            log(f"{mode}: not built ({results[mode]['error']})")
+            layer = h = None
+            torch.cuda.empty_cache()
+            continue
+        with wd.phase(f"{mode}: check", 300):
+            try:
+                out0 = layer.step(h)  # also the eager warm-up (allocations, library init)
+                m = compare(out0, ref_out)
+                if groups.rank == 0:
+                    first_out[mode] = out0.float().cpu()
+                n0 = _lib.LAUNCHES[0]
+                layer.step(h)
+                launches_per_step = _lib.LAUNCHES[0] - n0
+                gs = GraphedStep(layer, groups, h)
+                for t, t0 in zip(state_tensors(layer), snap):
+                    t.copy_(t0)
+                mg = compare(gs.replay(), ref_out)  # the replayed graph: what is timed
+                del snap
+                flagged = device_error_flagged(groups.device)  # an index error or a wait that ran out of its budget
+                ok = within_tolerance(m) and within_tolerance(mg) and not flagged
+            except Exception as e:
+                fatal(f"{mode}: check", e)
+        agrees = agree(ok, groups)
+        rel = max_over_ranks(max(m["rel_l2"], mg["rel_l2"]), groups)
         if not agrees:  # never timed: a recipe whose waits run out would stall the bench for every replay
             results[mode] = {"ms_per_step": None, "tokens_per_s": None, "launches_per_step": launches_per_step,
                              "agrees_with_single_gpu": False, "rel_l2_vs_single_gpu": rel,
-                             "device_error": flagged, "error": err}
-            if gs is not None:
-                gs.release()
-            keep[mode] = (layer, h, gs)
+                             "device_error": flagged}
+            log(f"{mode}: disagrees with the single-GPU step (rel-L2 {rel:.3g}, device error {flagged})")
+            gs.release()
+            keep[mode] = (layer, h, None)
             continue
-        ms, p50 = time_replays(gs.replay, args.steps, args.warmup, groups)
+        with wd.phase(f"{mode}: timing", 300):
+            ms, p50 = time_replays(gs.replay, args.steps, args.warmup, groups)
+        log(f"{mode}: {ms * 1e3:.1f} us per step")
         results[mode] = {"ms_per_step": ms, "p50_ms": p50, "tokens_per_s": args.batch / ms * 1e3,
                          "launches_per_step": launches_per_step, "agrees_with_single_gpu": agrees,
                          "rel_l2_vs_single_gpu": rel}
@@ -604,59 +761,68 @@ def our_arm(args) -> None:
     best = min(valid, key=lambda m: results[m]["ms_per_step"])
     layer, h, gs = keep[best]
     for m in modes:
-        if m != best and keep[m][2] is not None:
+        if m != best and m in keep and keep[m][2] is not None:
             keep[m][2].release()
 
     # clocks over a soak plus a second timed pass of the headline recipe
-    with Clocks(groups.local_rank) as clk:
-        t_end = time.perf_counter() + args.soak_s
-        while time.perf_counter() < t_end:
-            for _ in range(50):
-                gs.replay()
-            torch.cuda.synchronize()
-        ms2, p50_2 = time_replays(gs.replay, args.steps, 0, groups)
+    with wd.phase(f"{best}: soak and clocks", 300):
+        with Clocks(groups.local_rank) as clk:
+            t_end = time.perf_counter() + args.soak_s
+            while time.perf_counter() < t_end:
+                for _ in range(50):
+                    gs.replay()
+                torch.cuda.synchronize()
+            ms2, p50_2 = time_replays(gs.replay, args.steps, 0, groups)
     clocks = clk.summary()
     results[best]["ms_per_step_under_clock_sampling"] = ms2
 
     # end to end through the public call: pinned host input -> device, replay, output -> pinned host
-    h_host = h.detach().cpu().pin_memory()
-    out_host = torch.empty(layer.out.shape, dtype=layer.out.dtype).pin_memory()
-    e2e_ms, _ = time_replays(lambda: gs(h_host, out_host), args.steps, max(3, args.warmup // 10), groups)
+    with wd.phase(f"{best}: end to end", 300):
+        h_host = h.detach().cpu().pin_memory()
+        out_host = torch.empty(layer.out.shape, dtype=layer.out.dtype).pin_memory()
+        e2e_ms, _ = time_replays(lambda: gs(h_host, out_host), args.steps, max(3, args.warmup // 10), groups)
     nbytes_io = h.numel() * h.element_size()
 
-    roof_local = ssu_roofline(layer)
-    if world > 1:
-        import torch.distributed as dist
+    with wd.phase("ssu roofline", 300):
+        roof_local = ssu_roofline(layer)
+        if world > 1:
+            import torch.distributed as dist
 
-        allr = [None] * world
-        dist.all_gather_object(allr, roof_local)
-        cands = [r for r in allr if r is not None]
-        roof_local = max(cands, key=lambda r: r["us"]) if cands else None
+            allr = [None] * world
+            dist.all_gather_object(allr, roof_local)
+            cands = [r for r in allr if r is not None]
+            roof_local = max(cands, key=lambda r: r["us"]) if cands else None
     gs.release()
     for m in modes:
-        if keep[m][2] is not None:
+        if m in keep and keep[m][2] is not None:
             keep[m][2].release()
     barrier_sync()
-    try:
-        prefill = time_prefill(args, layer, groups)
-    except Exception as e:  # the prefill figure is secondary: its failure must not cost the decode line
-        prefill = {"error": f"{type(e).__name__}: {e}"[:300]}
+    prefill = time_prefill(args, layer, groups, wd)
 
     cpu = None
-    if groups.rank == 0 and world == 1 and args.cpu_s > 0:
-        cpu = cpu_layer_tokens_per_s(args, args.cpu_s)
-        if prefill is not None:
-            prefill["cpu_baseline"] = cpu_prefill_tokens_per_s(args)
+    oracle_cmp = None
+    if groups.rank == 0:
+        with wd.phase("oracle check and CPU baseline", 600):
+            oracle_cmp = oracle_check(args, first_out)
+            if world == 1 and args.cpu_s > 0:
+                cpu = cpu_layer_tokens_per_s(args, args.cpu_s)
+                if prefill is not None:
+                    prefill["cpu_baseline"] = cpu_prefill_tokens_per_s(args)
     if groups.rank == 0:
         peak, peak_src = roofline_peak()
         roof = None
         if roof_local is not None:
+            # DRAM traffic from the committed ncu capture only where it profiled this launch shape (one rank
+            # holding all 24 heads at this batch)
+            traffic = profiled_traffic(f"ssu_decode_{args.dims}_b{args.batch}.md") if world == 1 else None
             roof = {"kernel": "ssu_decode (mmp_ssu_decode, fp32 state)", "bound": "hbm",
                     "achieved": roof_local["gbs"], "peak": peak, "unit": "GB/s",
                     "frac": roof_local["gbs"] / peak, "peak_source": f"{peak_src} hbm_gbs",
                     "bytes_per_launch": roof_local["bytes"], "us_per_launch": roof_local["us"],
-                    "traffic": profiled_traffic(f"ssu_decode_{args.dims}_b{args.batch}.md")}
+                    "traffic": traffic}
         r = results[best]
+        for mode, c in (oracle_cmp or {}).items():
+            results[mode]["vs_oracle"] = c
         line = {
             "metric": METRIC, "value": r["tokens_per_s"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "higher_is_better": True,
@@ -693,7 +859,8 @@ def mamba2_arm(args) -> None:
     from multi_modal_parallelism_b200.sharding import ssm_shard
     from multi_modal_parallelism_b200.weights import random_layer
 
-    groups = init_groups()
+    wd = Watchdog()
+    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
     world, dev = groups.world_size, groups.device
     dims = preset("mamba2_sg")
     full = random_layer(dims, args.seed)
@@ -707,6 +874,7 @@ def mamba2_arm(args) -> None:
     results = {}
     clocks_by_mode = {}
     for mode in modes:
+        wd.phase(f"mamba2_sg {mode}", 600).__enter__()
         if parse_sg(mode):
             plan = sg_plan(mode, groups.rank, world, dims)
             shard, role = plan.shard, plan.role
@@ -805,7 +973,8 @@ def qwen35_arm(args) -> None:
     from multi_modal_parallelism_b200.qwen35 import GdnLayer, Qwen35Dims, Qwen35Stack, random_stack
     from multi_modal_parallelism_b200.state import make_decode_ctx, make_prefill_ctx
 
-    groups = init_groups()
+    wd = Watchdog()
+    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
     world, dev = groups.world_size, groups.device
     d = Qwen35Dims.from_yaml("qwen35_like")
     ws = random_stack(d, args.seed)
@@ -823,6 +992,7 @@ def qwen35_arm(args) -> None:
     modes = ["tp"] if world == 1 else ["tp", "attn_dp"]
     results = {}
     for mode in modes:
+        wd.phase(f"qwen35 {mode}", 600).__enter__()
         stack = Qwen35Stack(d, ws, mode, groups, dev, lines=B + 1, num_blocks=nblocks, kv_block=16, max_tokens=rows)
         for layer in stack.layers:  # decode from non-zero delta-rule states (their values do not change the work)
             if isinstance(layer, GdnLayer):

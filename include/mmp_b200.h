@@ -171,7 +171,9 @@ int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
  * the library, held by every GPU that loads it until the process exits. Same arguments and results as
  * mmp_paged_attn_decode without the workspace; returns MMP_ERR_INVALID when batch x nq x splits x
  * (hd + 2) x 4 bytes exceeds the array. The first call on a device looks up the array's address there:
- * make it before any stream capture. Calls share the array: calls that overlap on the GPU race.
+ * make it before any stream capture. The address is kept for the life of the process, so do not call
+ * this entry point on a device after cudaDeviceReset there. Calls share the array: calls that overlap on
+ * the GPU race.
  */
 #define MMP_PAGED_ATTN_NOALLOC_SCRATCH_BYTES (8u * 1024u * 1024u)
 int mmp_paged_attn_decode_noalloc(const void* q, int64_t q_b, int64_t q_h,

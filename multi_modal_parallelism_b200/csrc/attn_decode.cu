@@ -418,6 +418,7 @@ extern "C" int mmp_paged_attn_decode(const void* q, int64_t q_b, int64_t q_h,
 // allocator. For them the split-K partials live in the fixed array below, which every GPU that loads this
 // library holds until the process exits. Its device address is looked up once per device with that device
 // current (cudaGetSymbolAddress) on the first call there; make that first call before any stream capture.
+// The address is kept until the process exits: after cudaDeviceReset on a device it is stale there.
 // All calls share the array, so calls that overlap on the GPU (two streams, two threads) race on it; every
 // partial slot the merge reads is rewritten by the same call, so nothing needs clearing between calls.
 #include <mutex>

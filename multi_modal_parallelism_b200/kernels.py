@@ -284,13 +284,18 @@ def attn_decode(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Ten
 
 
 def attn_decode_noalloc(q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor, seqused_k: torch.Tensor,
-                        max_k: int, block_table: torch.Tensor, out: torch.Tensor, splits: int = 0) -> torch.Tensor:
+                        max_k: int, block_table: torch.Tensor, out: torch.Tensor, splits: int = 0,
+                        err: torch.Tensor | None = None) -> torch.Tensor:
     """attn_decode for callers that cannot allocate device memory (an engine that has reserved the free HBM
     for its own pools, code that must not call cudaFree, hosts that only bind the C ABI): the split-K
     partials go to a fixed 8 MiB array inside the library instead of a workspace. This wrapper allocates
     nothing either. Calls share that array, so calls that overlap on the GPU race; the first call on a device
     sets the array up and should come before any stream capture. Raises ValueError when the request needs more
-    scratch than the array holds."""
+    scratch than the array holds.
+
+    err: the int32 device error word that out-of-range block-table entries are reported to. When omitted, the
+    device's word is used if `error_word(device)` has created it already; otherwise (the word would have to be
+    allocated) bad entries are still skipped but not reported."""
     _cuda("attn_decode_noalloc", q, key_cache, value_cache, seqused_k, block_table, out)
     _dtype("attn_decode_noalloc", block_table, torch.int32)
     _dtype("attn_decode_noalloc", seqused_k, torch.int32)
@@ -300,7 +305,11 @@ def attn_decode_noalloc(q: torch.Tensor, key_cache: torch.Tensor, value_cache: t
     if q.stride(2) != 1 or out.stride(2) != 1:
         raise ValueError("attn_decode_noalloc: head dimension must be contiguous")
     eff = int(splits) if splits > 0 else attn_default_splits(T, nkv, int(max_k))
-    err = _err_words.get(q.device.index or 0)
+    if err is not None:
+        _cuda("attn_decode_noalloc", err)
+        _dtype("attn_decode_noalloc", err, torch.int32)
+    else:
+        err = _err_words.get(q.device.index or 0)
     _lib.call("mmp_paged_attn_decode_noalloc", _p(q), q.stride(0), q.stride(1), _p(key_cache), _p(value_cache), cb,
               ct, ch, _p(block_table), block_table.stride(0), _p(seqused_k), _p(out), out.stride(0), out.stride(1),
               T, nq, nkv, hd, blk, nb, int(max_k), 1.0 / math.sqrt(hd), int(splits), _p(err), _stream(q),

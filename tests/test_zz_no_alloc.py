@@ -3,9 +3,10 @@
 It exists for callers that cannot allocate device memory — an engine whose pools already hold the free HBM,
 code that must not call cudaFree because it synchronises the device, a host that binds only the C ABI —
 and keeps its split-K partials in a fixed array inside the library. Its output must match the workspace
-entry point (mmp_paged_attn_decode) within the suite's tolerance, on two calls in a row (the second call sees
-the first call's leftovers in the shared array). This file is collected last, and it also passes when run
-alone in a fresh process (its first call then performs the per-device set-up)."""
+entry point (mmp_paged_attn_decode) and the CPU oracle's paged attention within the suite's tolerance, on two
+calls in a row (the second call sees the first call's leftovers in the shared array). This file is collected
+last, and it also passes when run alone in a fresh process (its first call then performs the per-device
+set-up)."""
 import ctypes
 import math
 
@@ -13,6 +14,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from multi_modal_parallelism_b200 import _lib
 from multi_modal_parallelism_b200 import kernels as K
 
@@ -59,6 +61,11 @@ def call_workspace(q, kc, vc, table, lens, max_k, out, splits=0):
     K.attn_decode(q, kc, vc, None, lens, max_k, table, out, workspace=ws, splits=s)
 
 
+def oracle_out(q, kc, vc, table, lens):
+    f = lambda t: t.float().cpu().numpy()  # noqa: E731
+    return torch.from_numpy(oracle.paged_attn_decode(f(q), f(kc), f(vc), table.cpu().numpy(), lens.cpu().numpy()))
+
+
 def test_noalloc_matches_workspace_entry_point_twice():
     for seed, splits in ((1, 0), (2, 7)):  # two calls in a row, different inputs and split counts
         q, kc, vc, table, lens, ctx = make_case(seed)
@@ -68,6 +75,21 @@ def test_noalloc_matches_workspace_entry_point_twice():
         call_workspace(q, kc, vc, table, lens, ctx, ref, splits)
         torch.cuda.synchronize()
         close(got, ref)
+        close(got, oracle_out(q, kc, vc, table, lens))
+
+
+def test_noalloc_python_wrapper_matches_oracle():
+    """The package's wrapper (kernels.attn_decode_noalloc) allocates nothing either; with an error word passed
+    in, the call leaves it clear on valid block tables."""
+    err = K.error_word(DEV)
+    err.zero_()
+    for seed in (4, 5):
+        q, kc, vc, table, lens, ctx = make_case(seed, T=16)
+        out = torch.empty_like(q)
+        K.attn_decode_noalloc(q, kc, vc, lens, ctx, table, out, err=err)
+        torch.cuda.synchronize()
+        close(out, oracle_out(q, kc, vc, table, lens))
+    assert int(err.item()) == 0
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
