@@ -54,6 +54,9 @@ def parse() -> argparse.Namespace:
                     help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split); "
                          "qwen35: the Gated DeltaNet hybrid block stack (tp and attention data-parallel)")
     ap.add_argument("--sg-batch", type=int, default=256, help="mamba2_sg: live requests per step")
+    ap.add_argument("--configs", action=argparse.BooleanOptionalAction, default=True,
+                    help="also measure the 34B-like layer (config 2), the pure Mamba-2 layer under continuous batching "
+                         "(config 3) and the Gated DeltaNet stack (config 4) as sub-objects of the line")
     ap.add_argument("--ar-impl", choices=["nccl", "p2p", "p2p_fused"], default="nccl",
                     help="N>1 decode all-reduces: NCCL, or the peer-memory all-reduce fused with residual and norm")
     return ap.parse_args()
@@ -290,6 +293,10 @@ class Watchdog:
             if d is not None and time.perf_counter() > d:
                 log(f"phase '{name}' exceeded its time limit: ending the job")
                 os._exit(3)
+
+    def clear(self) -> None:
+        with self.lock:
+            self.deadline = None
 
     def phase(self, name: str, limit_s: float):
         wd = self
@@ -665,26 +672,27 @@ class _all_cores:
         return False
 
 
-def our_arm(args) -> None:
+def run_hybrid(args, groups, wd, modes: list[str] | None = None, oracle: bool = True,
+               cpu_batch: int | None = None) -> dict | None:
+    """The hybrid layer's decode recipes (and its prefill) at args.dims / args.batch / args.ctx on every rank; the
+    result object on rank 0 (None elsewhere). modes: the recipes to time (default: layout_candidates). oracle: check
+    each recipe's first step against the fp32 oracle layer. cpu_batch: rows of the CPU baseline's bounded sample
+    (default: the whole batch)."""
     import torch
 
     from multi_modal_parallelism_b200 import _lib
     from multi_modal_parallelism_b200.config import preset
     from multi_modal_parallelism_b200.correctness import compare, within_tolerance
-    from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
+    from multi_modal_parallelism_b200.dist import barrier_sync
     from multi_modal_parallelism_b200.sharding import all_norm_groups
     from multi_modal_parallelism_b200.timing import GraphedStep
     from multi_modal_parallelism_b200.weights import random_layer
 
-    wd = Watchdog()
-    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
     world = groups.world_size
-    if args.gpus != world:
-        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
     dims = preset(args.dims)
     full = random_layer(dims, args.seed)
-    modes = layout_candidates(dims, world, args.batch, args.ctx, args.ar_impl)
-    log(f"recipes: {modes}")
+    modes = modes or layout_candidates(dims, world, args.batch, args.ctx, args.ar_impl)
+    log(f"{args.dims}: recipes {modes}")
     # every communicator any recipe needs, created up front on every rank in the same order: building a recipe's
     # layer then issues no collective (with the NCCL all-reduce)
     with wd.phase("communicators", 300):
@@ -757,7 +765,12 @@ def our_arm(args) -> None:
         keep[mode] = (layer, h, gs)
     valid = [m for m in modes if results[m]["agrees_with_single_gpu"]]
     if not valid:
-        raise SystemExit(f"no decode recipe agrees with the single-GPU layer step: {results}")
+        for m in keep.values():
+            if m[2] is not None:
+                m[2].release()
+        if groups.rank == 0:
+            return {"error": "no decode recipe agrees with the single-GPU layer step", "recipes": results}
+        return None
     best = min(valid, key=lambda m: results[m]["ms_per_step"])
     layer, h, gs = keep[best]
     for m in modes:
@@ -799,14 +812,18 @@ def our_arm(args) -> None:
     barrier_sync()
     prefill = time_prefill(args, layer, groups, wd)
 
+    del keep, layer, gs
+    torch.cuda.empty_cache()
     cpu = None
     oracle_cmp = None
     if groups.rank == 0:
         with wd.phase("oracle check and CPU baseline", 600):
-            oracle_cmp = oracle_check(args, first_out)
+            if oracle:
+                oracle_cmp = oracle_check(args, first_out)
             if world == 1 and args.cpu_s > 0:
-                cpu = cpu_layer_tokens_per_s(args, args.cpu_s)
-                if prefill is not None:
+                ca = argparse.Namespace(**{**vars(args), "batch": cpu_batch or args.batch})
+                cpu = cpu_layer_tokens_per_s(ca, args.cpu_s)
+                if prefill is not None and isinstance(prefill, dict) and "error" not in prefill:
                     prefill["cpu_baseline"] = cpu_prefill_tokens_per_s(args)
     if groups.rank == 0:
         peak, peak_src = roofline_peak()
@@ -839,11 +856,49 @@ def our_arm(args) -> None:
             "clocks": clocks,
             "prefill": prefill,
         }
+        return line
+    return None
+
+
+def config2_modes(world: int) -> list[str]:
+    """The 34B-like layer's recipes: tp1 on one GPU; the even branch split against tp4_fused on more."""
+    return ["tp1"] if world == 1 else [f"split{world // 2}{world // 2}", "tp4_fused"]
+
+
+def our_arm(args) -> None:
+    from multi_modal_parallelism_b200.dist import destroy, init_groups
+
+    wd = Watchdog()
+    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
+    world = groups.world_size
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    line = run_hybrid(args, groups, wd)
+    if groups.rank == 0 and (line is None or "error" in line):
+        raise SystemExit(f"no decode recipe agrees with the single-GPU layer step: {line}")
+    extra = {}
+    if args.configs:
+        # the other configurations, each a bounded sub-measurement with its own roofline, CPU baseline and e2e
+        a2 = argparse.Namespace(**{**vars(args), "dims": "falcon_h1_34b_like", "batch": 128, "ctx": 4096,
+                                   "prefill_seqs": 4, "prefill_len": 4096, "prefill_new": False,
+                                   "steps": min(args.steps, 50), "warmup": max(3, min(args.warmup, 10)),
+                                   "prefill_steps": min(args.prefill_steps, 10), "soak_s": 0.5,
+                                   "cpu_s": min(args.cpu_s, 10.0)})
+        extra["config2"] = run_hybrid(a2, groups, wd, modes=config2_modes(world), oracle=False, cpu_batch=4)
+        a3 = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 20), "warmup": 3,
+                                   "cpu_s": min(args.cpu_s, 10.0)})
+        extra["config3"] = run_mamba2(a3, groups, wd)
+        a4 = argparse.Namespace(**{**vars(args), "batch": 64, "ctx": 4096, "prefill_seqs": 4, "prefill_len": 4096,
+                                   "steps": min(args.steps, 50), "warmup": max(3, min(args.warmup, 10)),
+                                   "prefill_steps": min(args.prefill_steps, 5), "cpu_s": min(args.cpu_s, 10.0)})
+        extra["config4"] = run_qwen35(a4, groups, wd)
+    if groups.rank == 0:
+        line.update(extra)
         print(json.dumps(line), flush=True)
     destroy()
 
 
-def mamba2_arm(args) -> None:
+def run_mamba2(args, groups, wd) -> dict | None:
     """The pure Mamba-2 layer (hidden 4096, 128 heads x 64, d_state 128, 8 groups) under continuous batching:
     `--sg-batch` live requests, a quarter restarting as prompts of 64-1024 tokens each step, the rest decoding,
     rows in a fresh order every step. Layouts: tp at N=1; sg{N/2}{N/2} and tp at even N > 1. One step = one
@@ -853,14 +908,12 @@ def mamba2_arm(args) -> None:
 
     from multi_modal_parallelism_b200 import _lib
     from multi_modal_parallelism_b200.config import preset
-    from multi_modal_parallelism_b200.dist import barrier_sync, destroy, init_groups
+    from multi_modal_parallelism_b200.dist import barrier_sync
     from multi_modal_parallelism_b200.mamba2 import Mamba2Layer, alloc_mamba2_states, mixed_ctx
     from multi_modal_parallelism_b200.sg import continuous_batches, parse_sg, sg_plan
     from multi_modal_parallelism_b200.sharding import ssm_shard
     from multi_modal_parallelism_b200.weights import random_layer
 
-    wd = Watchdog()
-    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
     world, dev = groups.world_size, groups.device
     dims = preset("mamba2_sg")
     full = random_layer(dims, args.seed)
@@ -911,23 +964,40 @@ def mamba2_arm(args) -> None:
         e1.record()
         torch.cuda.synchronize()
         e2e_ms = max_over_ranks(e0.elapsed_time(e1), groups)
+        # algorithmic HBM bytes of the timed steps on this rank: its weights once per step, the state lines it
+        # reads and writes (decode rows: read + write; prefill sequences: the final state written, a line read
+        # when it continues), conv lines, activations in and out
+        nbytes = 0.0
+        if states is not None:
+            line_b = states.ssm_state[0].numel() * states.ssm_state.element_size()
+            for b in batches[args.warmup:]:
+                nbytes += (2 * len(b.dec_lines) + len(b.pre_lens)) * line_b + 2 * b.T * dims.hidden * 2
+        nbytes += args.steps * sum(t.numel() * t.element_size() for t in vars(layer.w).values()
+                                   if isinstance(t, torch.Tensor))
         results[mode] = {"ms_per_step": total / args.steps, "p50_ms": max_over_ranks(statistics.median(per), groups),
                          "tokens_per_s": tokens / total * 1e3, "tokens_per_step": tokens / args.steps,
                          "launches": launches, "e2e_tokens_per_s": tokens / e2e_ms * 1e3,
-                         "io_bytes": tokens * dims.hidden * 2}
+                         "io_bytes": tokens * dims.hidden * 2,
+                         "hbm_gbs_busiest_rank": max_over_ranks(nbytes / total / 1e6, groups)}
         clocks_by_mode[mode] = clk.summary()
         del layer, states
         torch.cuda.empty_cache()
         barrier_sync()
+    wd.clear()
     if groups.rank == 0:
         best = max(results, key=lambda m: results[m]["tokens_per_s"])
         r = results[best]
         cpu = cpu_mamba2_tokens_per_s(args, dims, full, args.cpu_s) if world == 1 and args.cpu_s > 0 else None
         io = r["io_bytes"] / args.steps
-        print(json.dumps({
+        hbm, hbm_src = roofline_peak()
+        return {
             "e2e": {"value": r["e2e_tokens_per_s"], "unit": "tokens/s", "h2d_bytes_per_step": io,
                     "d2h_bytes_per_step": io},
             "gpu_launches": r["launches"], "clocks": clocks_by_mode[best], "cpu_baseline": cpu,
+            "roofline": {"bound": "hbm", "kernel": "whole mixed step (busiest rank)",
+                         "achieved": r["hbm_gbs_busiest_rank"], "peak": hbm, "unit": "GB/s",
+                         "frac": r["hbm_gbs_busiest_rank"] / hbm, "peak_source": f"{hbm_src} hbm_gbs",
+                         "traffic": None},
             "metric": "pure Mamba-2 layer tokens/s under continuous batching (SSM/gate split vs TP)",
             "value": r["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["ms_per_step"], "p50_ms": r["p50_ms"], "higher_is_better": True,
@@ -935,7 +1005,19 @@ def mamba2_arm(args) -> None:
             "config": {"workload": f"mamba2_sg layer, {args.sg_batch} requests, 25% prefill U[64,1024], rows "
                                    "re-ordered every step", "parallelism": best,
                        "recipes": {m: {k: round(v, 4) for k, v in x.items()} for m, x in results.items()}},
-        }), flush=True)
+        }
+    return None
+
+
+def mamba2_arm(args) -> None:
+    """`--workload mamba2_sg` alone: the pure Mamba-2 layer's line (run_mamba2)."""
+    from multi_modal_parallelism_b200.dist import destroy, init_groups
+
+    wd = Watchdog()
+    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
+    r = run_mamba2(args, groups, wd)
+    if groups.rank == 0:
+        print(json.dumps(r), flush=True)
     destroy()
 
 
@@ -958,7 +1040,7 @@ def stack_flops(d, lens: list[int]) -> float:
     return f
 
 
-def qwen35_arm(args) -> None:
+def run_qwen35(args, groups, wd) -> dict | None:
     """The Gated DeltaNet hybrid block stack (qwen35_like: three delta-rule layers of 16 key / 32 value heads x 128
     and one GQA attention layer of 16 / 2 heads x 128, hidden 2048, SwiGLU 6144, fp32 delta-rule state): decode of
     --batch sequences at context --ctx (one CUDA-graph replay of the stack per step) and a prefill of
@@ -969,12 +1051,10 @@ def qwen35_arm(args) -> None:
 
     from multi_modal_parallelism_b200 import _lib
     from multi_modal_parallelism_b200 import kernels as K
-    from multi_modal_parallelism_b200.dist import barrier_sync, capture_context, destroy, init_groups
+    from multi_modal_parallelism_b200.dist import barrier_sync, capture_context
     from multi_modal_parallelism_b200.qwen35 import GdnLayer, Qwen35Dims, Qwen35Stack, random_stack
     from multi_modal_parallelism_b200.state import make_decode_ctx, make_prefill_ctx
 
-    wd = Watchdog()
-    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
     world, dev = groups.world_size, groups.device
     d = Qwen35Dims.from_yaml("qwen35_like")
     ws = random_stack(d, args.seed)
@@ -1052,12 +1132,13 @@ def qwen35_arm(args) -> None:
         del graph, stack
         torch.cuda.empty_cache()
         barrier_sync()
+    wd.clear()
     if groups.rank == 0:
         best = max(results, key=lambda m: results[m]["decode"]["tokens_per_s"])
         r = results[best]
         k = r["gdn_decode_kernel"]
         cpu = cpu_qwen35_tokens_per_s(args, d, ws, args.cpu_s) if world == 1 and args.cpu_s > 0 else None
-        print(json.dumps({
+        return ({
             "metric": "Gated DeltaNet hybrid stack decode tokens/s (attention data-parallel vs TP)",
             "value": r["decode"]["tokens_per_s"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": r["decode"]["ms_per_step"], "p50_ms": r["decode"]["p50_ms"],
@@ -1072,8 +1153,22 @@ def qwen35_arm(args) -> None:
             "bf16_peak": {"tflops": tf, "source": tf_src},
             "e2e": r["decode"]["e2e"], "gpu_launches": r["decode"]["launches_per_step"] * args.steps,
             "clocks": r["decode"]["clocks"], "cpu_baseline": cpu,
-        }), flush=True)
+        })
+    return None
+
+
+def qwen35_arm(args) -> None:
+    """`--workload qwen35` alone: the Gated DeltaNet stack's line (run_qwen35)."""
+    from multi_modal_parallelism_b200.dist import destroy, init_groups
+
+    wd = Watchdog()
+    groups = init_groups(timeout_s=NCCL_TIMEOUT_S)
+    r = run_qwen35(args, groups, wd)
+    if groups.rank == 0:
+        print(json.dumps(r), flush=True)
     destroy()
+
+
 
 
 def main() -> None:

@@ -3,15 +3,20 @@
 // the reference measures), selected with mmp_set_attn_prefill_tc.
 //
 // Query token j of sequence i sits at position ctx_start[i] + j and sees cache positions [0, ctx_start[i] + j]
-// of that sequence. One CTA (6 warps) owns 128 query tokens of one query head:
-//   * warps 0-3 (one query row per thread = one TMEM lane) load the Q tile with plain 16-byte loads into the
-//     128-byte-swizzled K-major operand layout, then run the online softmax of every key tile and the epilogue;
+// of that sequence. One CTA (6 warps) owns 128 query tokens of TWO query heads that read the same key/value
+// head (a head pair; the last pair of a key/value head holds one head when the group size is odd), so every
+// key/value tile it loads serves both, and the tensor pipe works on one head while the threads run the softmax
+// of the other:
+//   * warps 0-3 (one query row per thread = one TMEM lane) load both Q tiles with plain 16-byte loads into the
+//     128-byte-swizzled K-major operand layout, then, for every key tile, run the online softmax of head A and
+//     then of head B, and finally the epilogue;
 //   * warp 4 gathers each tile of 128 keys page by page with 4-D TMA boxes [block_size keys x 64 dims] straight
 //     from the paged K and V caches into a two-stage ring (pages past the sequence, or with a bad block id, are
 //     requested at an out-of-range block coordinate and arrive as zeros);
-//   * warp 5 (one thread) issues S = Q K^T (M = 128 queries, N = 128 keys, K = 128 dims) into one of two TMEM
-//     score buffers, and O += P V (M = 128, N = 128 dims, K = 128 keys) into the TMEM output, with P read from
-//     shared memory (K-major) and V as an MN-major operand straight from its TMA boxes.
+//   * warp 5 (one thread) issues, per key tile j, S_A(j+1) = Q_A K_{j+1}^T as soon as the threads have read
+//     S_A(j), O_A += P_A(j) V_j once they have written P_A(j), then the same for head B. Each head has one
+//     score buffer and one output accumulator in TMEM (4 x 128 of the 512 columns); P goes through one shared
+//     bf16 buffer in shared memory (K-major), V is an MN-major operand straight from its TMA boxes.
 // The softmax keeps its running maximum lazily: O (in TMEM) and the row sum are rescaled only when a row's
 // maximum grows by more than 2^8, so most tiles need no correction pass; P is rounded to bf16 as in the
 // mma.sync kernel. Scores of keys a row may not see are replaced (not added to) by -inf, and value rows past
@@ -33,23 +38,23 @@ constexpr int TQ = 128, TK = 128, THD = 128;
 constexpr int TTHR = 192;  // warps 0-3 softmax and epilogue, warp 4 copies, warp 5 MMAs
 
 struct AttnTcSmem {
-  static constexpr int Q_OFF = 0;                  // Q: 2 blocks [128 q][64 dims] (128 B rows, swizzled)
-  static constexpr int K_OFF = Q_OFF + 32768;      // K ring: 2 stages x 2 blocks [128 keys][64 dims]
+  static constexpr int Q_OFF = 0;                  // Q: 2 heads x 2 blocks [128 q][64 dims] (128 B rows, swizzled)
+  static constexpr int K_OFF = Q_OFF + 65536;      // K ring: 2 stages x 2 blocks [128 keys][64 dims]
   static constexpr int V_OFF = K_OFF + 65536;      // V ring: same
-  static constexpr int P_OFF = V_OFF + 65536;      // P: 2 blocks [128 q][64 keys]
+  static constexpr int P_OFF = V_OFF + 65536;      // P: 2 blocks [128 q][64 keys], shared by the two heads
   static constexpr int BAR_OFF = P_OFF + 32768;    // mbarriers (8 bytes each)
-  static constexpr int NBAR = 12;
+  static constexpr int NBAR = 16;
   static constexpr int FLAG_OFF = BAR_OFF + 8 * NBAR;
   static constexpr int USED = FLAG_OFF + 16;
   static constexpr int DYN = USED + 1024;          // + alignment of the base to 1024 bytes
-  static constexpr int OST = THD * 2 + 16;         // output staging row (bytes), in the K ring after the last MMA
+  static constexpr int OST = THD * 2 + 16;         // output staging row (bytes): head A in the K ring, B in the V ring
 };
 static_assert(AttnTcSmem::DYN <= 232448, "shared memory per CTA");
-static_assert(TQ * AttnTcSmem::OST <= 65536, "output staging fits the K ring");
+static_assert(TQ * AttnTcSmem::OST <= 65536, "output staging of one head fits one ring");
 
-// mbarrier slots
-constexpr int B_Q = 0, B_K = 1, B_V = 3, B_EMPTY = 5, B_S = 7, B_P = 9, B_O = 10, B_DONE = 11;
-// TMEM columns: two score buffers and the output accumulator
+// mbarrier slots: per head h (0 = A, 1 = B) S ready, S read (free), P written, O updated (PV done)
+constexpr int B_Q = 0, B_K = 1, B_V = 3, B_EMPTY = 5, B_S = 7, B_F = 9, B_P = 11, B_O = 13, B_DONE = 15;
+// TMEM columns: head h's score buffer at T_S + 128 h, its output accumulator at T_O + 128 h
 constexpr uint32_t T_S = 0, T_O = 256;
 
 struct AttnTcParams {
@@ -58,7 +63,8 @@ struct AttnTcParams {
   const int32_t* cu_q; const int32_t* ctx_start;
   bf16* out; int64_t o_t, o_h;
   int nq, nkv, block_size, num_blocks, q_tiles;
-  int tok_inner;  // the cache maps list the token dimension before the head dimension (smaller stride first)
+  int pairs_per_kv;  // head pairs per key/value head: ceil((nq / nkv) / 2)
+  int tok_inner;     // the cache maps list the token dimension before the head dimension (smaller stride first)
   float scale_log2;
   int* err;
 };
@@ -90,8 +96,9 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t saddr, uint32_t mn_block) {
 }
 constexpr uint32_t IDESC_B_MN_MAJOR = 1u << 16;
 
-// grid (nq * nseq, q tiles): x = head + nq * sequence; y counts query tiles from the last, so the CTAs with the
-// longest key ranges are dispatched first and the short ones fill the tail
+// grid (head pairs * nseq, q tiles): x = pair + pairs * sequence, pair = key/value head * pairs_per_kv + p; y counts
+// query tiles from the last, so the CTAs with the longest key ranges are dispatched first and the short ones fill
+// the tail
 __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap mapK,
                                                                   const __grid_constant__ CUtensorMap mapV,
                                                                   const AttnTcParams P) {
@@ -100,7 +107,12 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
   pdl_trigger();
   pdl_wait();
-  const int head = blockIdx.x % P.nq, seq = blockIdx.x / P.nq;
+  const int npairs = P.nkv * P.pairs_per_kv;
+  const int pair = blockIdx.x % npairs, seq = blockIdx.x / npairs;
+  const int rep = P.nq / P.nkv;
+  const int kh = pair / P.pairs_per_kv;
+  const int head_a = kh * rep + 2 * (pair % P.pairs_per_kv);
+  const int nh = head_a + 1 < (kh + 1) * rep ? 2 : 1;  // heads this CTA serves
   const int q0 = (P.q_tiles - 1 - static_cast<int>(blockIdx.y)) * TQ;
   const int qbase = P.cu_q[seq], qlen = P.cu_q[seq + 1] - qbase;
   if (q0 >= qlen) return;  // whole CTA: nothing initialised yet
@@ -109,7 +121,6 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
   const int total = start + qlen;           // keys of the sequence
   const int kend = start + q0 + rows;       // keys any row of this tile can see
   const int nkt = (kend + TK - 1) / TK;     // >= 1
-  const int kh = head / (P.nq / P.nkv);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sb = smem_addr(smem);
   auto bar = [&](int i) { return sb + L::BAR_OFF + 8 * i; };
@@ -123,9 +134,10 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
       mbar_init(bar(B_V + s), 1);
       mbar_init(bar(B_EMPTY + s), 1);
       mbar_init(bar(B_S + s), 1);
+      mbar_init(bar(B_F + s), 128);
+      mbar_init(bar(B_P + s), 128);
+      mbar_init(bar(B_O + s), 1);
     }
-    mbar_init(bar(B_P), 128);
-    mbar_init(bar(B_O), 1);
     mbar_init(bar(B_DONE), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -197,36 +209,44 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_mn(TQ, TK);
       constexpr uint32_t id_o = umma_idesc_mn(TQ, THD) | IDESC_B_MN_MAJOR;
-      auto issue_s = [&](int j) {  // S(j) = Q K_j^T into score buffer j & 1
+      auto issue_s = [&](int h, int j) {  // S_h(j) = Q_h K_j^T into head h's score buffer
         const uint32_t kst = sb + L::K_OFF + (j & 1) * 32768;
 #pragma unroll
         for (int kk = 0; kk < THD / 16; ++kk) {
           const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_f16(tmem + T_S + (j & 1) * TK, umma_desc(sb + L::Q_OFF + off), umma_desc(kst + off), id_s, kk != 0);
+          umma_f16(tmem + T_S + h * TK, umma_desc(sb + L::Q_OFF + h * 32768 + off), umma_desc(kst + off), id_s,
+                   kk != 0);
         }
-        umma_commit(bar(B_S + (j & 1)));
+        umma_commit(bar(B_S + h));
+      };
+      auto issue_pv = [&](int h, int j) {  // O_h += P V_j, K = keys
+        const uint32_t vst = sb + L::V_OFF + (j & 1) * 32768;
+#pragma unroll
+        for (int kk = 0; kk < TK / 16; ++kk)
+          umma_f16(tmem + T_O + h * THD, umma_desc(sb + L::P_OFF + (kk >> 2) * 16384 + (kk & 3) * 32),
+                   desc_mn(vst + kk * 2048, 16384), id_o, (j | kk) != 0);
+        umma_commit(bar(B_O + h));  // PV_h(j) done: O_h stable, P free
       };
       bool ok = mbar_wait(bar(B_Q), 0, abort_flag, P.err) && mbar_wait(bar(B_K), 0, abort_flag, P.err);
       if (ok) {
         tc_fence_after();
-        issue_s(0);
+        for (int h = 0; h < nh; ++h) issue_s(h, 0);
       }
       for (int j = 0; ok && j < nkt; ++j) {
-        if (j + 1 < nkt) {  // the other score buffer was released with P(j - 1), waited for below last time
-          if (!(ok = mbar_wait(bar(B_K + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, P.err))) break;
+        const bool next = j + 1 < nkt;
+        for (int h = 0; ok && h < nh; ++h) {
+          if (next) {  // S_h(j + 1) once the threads have read S_h(j) and K_{j+1} has landed
+            if (!(ok = mbar_wait(bar(B_F + h), j & 1, abort_flag, P.err))) break;
+            if (h == 0 && !(ok = mbar_wait(bar(B_K + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, P.err))) break;
+            tc_fence_after();
+            issue_s(h, j + 1);
+          }
+          if (!(ok = mbar_wait(bar(B_P + h), j & 1, abort_flag, P.err))) break;  // P_h(j) written
+          if (h == 0 && !(ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err))) break;
           tc_fence_after();
-          issue_s(j + 1);
+          issue_pv(h, j);
         }
-        if (!(ok = mbar_wait(bar(B_P), j & 1, abort_flag, P.err))) break;  // P(j) written, S(j) read
-        if (!(ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err))) break;
-        tc_fence_after();
-        const uint32_t vst = sb + L::V_OFF + (j & 1) * 32768;
-#pragma unroll
-        for (int kk = 0; kk < TK / 16; ++kk)  // O += P V_j, K = keys
-          umma_f16(tmem + T_O, umma_desc(sb + L::P_OFF + (kk >> 2) * 16384 + (kk & 3) * 32),
-                   desc_mn(vst + kk * 2048, 16384), id_o, (j | kk) != 0);
-        umma_commit(bar(B_O));              // PV(j) done: O stable, P free
-        umma_commit(bar(B_EMPTY + (j & 1)));  // K_j, V_j free
+        if (ok) umma_commit(bar(B_EMPTY + (j & 1)));  // every MMA reading K_j and V_j has been issued
       }
       umma_commit(bar(B_DONE));  // arrives once every MMA issued above has completed
     }
@@ -235,12 +255,16 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
     // ---------------------------------------------------------------- warps 0-3: Q, softmax, epilogue
     const int r = tid;  // query row = TMEM lane
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    // Q tile: thread i copies 16-byte chunk i % 16 of rows i / 16 + 8 n (rows past the sequence: zeros)
-    for (int i = tid; i < TQ * 16; i += 128) {
-      const int qr = i >> 4, c = i & 15;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (qr < rows) v = ld16(P.q + static_cast<int64_t>(qbase + q0 + qr) * P.q_t + head * P.q_h + c * 8);
-      *reinterpret_cast<uint4*>(smem + L::Q_OFF + (c >> 3) * 16384 + swz128(qr, c & 7)) = v;
+    // Q tiles: thread i copies 16-byte chunk i % 16 of rows i / 16 + 8 n of each head (rows past the sequence:
+    // zeros)
+    for (int h = 0; h < nh; ++h) {
+      for (int i = tid; i < TQ * 16; i += 128) {
+        const int qr = i >> 4, c = i & 15;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (qr < rows)
+          v = ld16(P.q + static_cast<int64_t>(qbase + q0 + qr) * P.q_t + (head_a + h) * P.q_h + c * 8);
+        *reinterpret_cast<uint4*>(smem + L::Q_OFF + h * 32768 + (c >> 3) * 16384 + swz128(qr, c & 7)) = v;
+      }
     }
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> tensor core reads
     mbar_arrive(bar(B_Q));
@@ -248,124 +272,135 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
     const int qpos = start + q0 + r;          // this row's position (rows >= `rows` are padding)
     const int vis = min(qpos, total - 1);     // last key this row sees
     const float sl = P.scale_log2;
-    float m_used = -INFINITY;                 // running maximum in the exp2 domain (lazy)
-    float lsum = 0.f;
+    float m_used[2] = {-INFINITY, -INFINITY};  // running maxima in the exp2 domain (lazy)
+    float lsum[2] = {0.f, 0.f};
+    bool ok = true;
     int j = 0;
-    for (; j < nkt; ++j) {
-      bool ok = mbar_wait(bar(B_S + (j & 1)), (j >> 1) & 1, abort_flag, P.err);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      uint32_t s[TK];
-#pragma unroll
-      for (int c = 0; c < TK / 16; ++c) tmem_ld16_nw(t_lane + T_S + (j & 1) * TK + c * 16, s + c * 16);
-      tmem_wait();
+    for (; ok && j < nkt; ++j) {
       const int k0 = j * TK;
       const int lim = vis - k0;  // keys k0 + c with c <= lim are visible
-      float mx = -INFINITY;
+      for (int h = 0; h < nh; ++h) {
+        ok = mbar_wait(bar(B_S + h), j & 1, abort_flag, P.err);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        tc_fence_after();
+        uint32_t s[TK];
 #pragma unroll
-      for (int c = 0; c < TK; ++c) {
-        const float v = c <= lim ? __uint_as_float(s[c]) : -INFINITY;
-        s[c] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
-      }
-      const float m_new = mx * sl;
-      const bool need = m_new > m_used + 8.f;  // false for -inf / NaN maxima
-      bool o_ready = j == 0;                    // no PV issued yet
-      if (__any_sync(0xffffffffu, need)) {
-        const float alpha = need ? ex2f(m_used - m_new) : 1.f;  // 0 on the first visible tile
-        if (need) {
-          m_used = m_new;
-          lsum *= alpha;
-        }
-        if (j > 0) {  // O holds PV(0 .. j-1): wait for the last, then rescale this row in TMEM
-          ok = mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, P.err);
-          if (!__all_sync(0xffffffffu, ok)) break;
-          tc_fence_after();
-          o_ready = true;
-#pragma unroll 1
-          for (int c = 0; c < THD; c += 32) {
-            uint32_t o[32];
-            tmem_ld16_nw(t_lane + T_O + c, o);
-            tmem_ld16_nw(t_lane + T_O + c + 16, o + 16);
-            tmem_wait();
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-            tmem_st16(t_lane + T_O + c, o);
-            tmem_st16(t_lane + T_O + c + 16, o + 16);
-          }
-          tmem_wait_st();
-        }
-      }
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      float part = 0.f;
-#pragma unroll
-      for (int c = 0; c < TK; ++c) {
-        const float p = ex2f(fmaf(__uint_as_float(s[c]), sl, -base));
-        s[c] = __float_as_uint(p);
-        part += p;
-      }
-      lsum += part;
-      if (!o_ready) {  // the single P buffer is free once PV(j - 1) is done
-        ok = mbar_wait(bar(B_O), (j - 1) & 1, abort_flag, P.err);
-        if (!__all_sync(0xffffffffu, ok)) break;
-      }
-      if (k0 + TK > total) {
-        // value rows past the sequence's last key (the tail of its last page) may hold anything: zero them
-        // once the tile has landed, before PV(j) reads them
-        ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err);
-        if (!__all_sync(0xffffffffu, ok)) break;
-        if (r >= total - k0) {
-          uint8_t* vrow = smem + L::V_OFF + (j & 1) * 32768 + r * 128;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(vrow + 16384 + c * 16) = make_uint4(0, 0, 0, 0);
-          }
-        }
-      }
-      // P row r (bf16) into the K-major operand layout: keys 0-63 in block 0, 64-127 in block 1
-#pragma unroll
-      for (int c8 = 0; c8 < TK / 8; ++c8) {
-        const uint32_t* pv = s + c8 * 8;
-        *reinterpret_cast<uint4*>(smem + L::P_OFF + (c8 >> 3) * 16384 + swz128(r, c8 & 7)) = make_uint4(
-            pack_bf16x2(__uint_as_float(pv[0]), __uint_as_float(pv[1])),
-            pack_bf16x2(__uint_as_float(pv[2]), __uint_as_float(pv[3])),
-            pack_bf16x2(__uint_as_float(pv[4]), __uint_as_float(pv[5])),
-            pack_bf16x2(__uint_as_float(pv[6]), __uint_as_float(pv[7])));
-      }
-      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-      tc_fence_before();  // this thread's score reads and O writes precede the MMAs issued after the arrive
-      mbar_arrive(bar(B_P));
-    }
-    // epilogue: wait for the last PV, normalise, stage bf16 rows in the (now idle) K ring, store coalesced
-    bool ok = j == nkt && !*abort_flag;
-    if (ok) ok = mbar_wait(bar(B_O), (nkt - 1) & 1, abort_flag, P.err);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      tc_fence_after();
-      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
-      uint8_t* orow = smem + L::K_OFF + r * L::OST;
-#pragma unroll 1
-      for (int c = 0; c < THD; c += 32) {
-        uint32_t o[32];
-        tmem_ld16_nw(t_lane + T_O + c, o);
-        tmem_ld16_nw(t_lane + T_O + c + 16, o + 16);
+        for (int c = 0; c < TK / 16; ++c) tmem_ld16_nw(t_lane + T_S + h * TK + c * 16, s + c * 16);
         tmem_wait();
+        tc_fence_before();  // the score reads precede the next S MMA into this buffer
+        mbar_arrive(bar(B_F + h));
+        float mx = -INFINITY;
 #pragma unroll
-        for (int e = 0; e < 32; e += 8)
-          *reinterpret_cast<uint4*>(orow + (c + e) * 2) = make_uint4(
-              pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
-              pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
-              pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
-              pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+        for (int c = 0; c < TK; ++c) {
+          const float v = c <= lim ? __uint_as_float(s[c]) : -INFINITY;
+          s[c] = __float_as_uint(v);
+          mx = fmaxf(mx, v);
+        }
+        const float m_new = mx * sl;
+        const bool need = m_new > m_used[h] + 8.f;  // false for -inf / NaN maxima
+        if (__any_sync(0xffffffffu, need)) {
+          const float alpha = need ? ex2f(m_used[h] - m_new) : 1.f;  // 0 on the first visible tile
+          if (need) {
+            m_used[h] = m_new;
+            lsum[h] *= alpha;
+          }
+          if (j > 0) {  // O_h holds PV_h(0 .. j-1): wait for the last, then rescale this row in TMEM
+            ok = mbar_wait(bar(B_O + h), (j - 1) & 1, abort_flag, P.err);
+            if (!(ok = __all_sync(0xffffffffu, ok))) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < THD; c += 32) {
+              uint32_t o[32];
+              tmem_ld16_nw(t_lane + T_O + h * THD + c, o);
+              tmem_ld16_nw(t_lane + T_O + h * THD + c + 16, o + 16);
+              tmem_wait();
+#pragma unroll
+              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+              tmem_st16(t_lane + T_O + h * THD + c, o);
+              tmem_st16(t_lane + T_O + h * THD + c + 16, o + 16);
+            }
+            tmem_wait_st();
+          }
+        }
+        const float base = m_used[h] == -INFINITY ? 0.f : m_used[h];
+        float part = 0.f;
+#pragma unroll
+        for (int c = 0; c < TK; ++c) {
+          const float p = ex2f(fmaf(__uint_as_float(s[c]), sl, -base));
+          s[c] = __float_as_uint(p);
+          part += p;
+        }
+        lsum[h] += part;
+        // the shared P buffer is free once the PV that read it last is done: head B's of the previous tile
+        // before head A writes (head A's own with a single head), head A's of this tile before head B writes
+        const int ph = h == 1 ? 0 : nh - 1, pj = h == 1 ? j : j - 1;
+        if (pj >= 0) {
+          ok = mbar_wait(bar(B_O + ph), pj & 1, abort_flag, P.err);
+          if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        }
+        if (h == 0 && k0 + TK > total) {
+          // value rows past the sequence's last key (the tail of its last page) may hold anything: zero them
+          // once the tile has landed, before PV_A(j), their first reader
+          ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err);
+          if (!(ok = __all_sync(0xffffffffu, ok))) break;
+          if (r >= total - k0) {
+            uint8_t* vrow = smem + L::V_OFF + (j & 1) * 32768 + r * 128;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
+              *reinterpret_cast<uint4*>(vrow + 16384 + c * 16) = make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+        // P row r (bf16) into the K-major operand layout: keys 0-63 in block 0, 64-127 in block 1
+#pragma unroll
+        for (int c8 = 0; c8 < TK / 8; ++c8) {
+          const uint32_t* pv = s + c8 * 8;
+          *reinterpret_cast<uint4*>(smem + L::P_OFF + (c8 >> 3) * 16384 + swz128(r, c8 & 7)) = make_uint4(
+              pack_bf16x2(__uint_as_float(pv[0]), __uint_as_float(pv[1])),
+              pack_bf16x2(__uint_as_float(pv[2]), __uint_as_float(pv[3])),
+              pack_bf16x2(__uint_as_float(pv[4]), __uint_as_float(pv[5])),
+              pack_bf16x2(__uint_as_float(pv[6]), __uint_as_float(pv[7])));
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        tc_fence_before();  // this thread's O writes precede the MMAs issued after the arrive
+        mbar_arrive(bar(B_P + h));
+      }
+    }
+    // epilogue per head: wait for its last PV, normalise, stage bf16 rows in an idle ring, store coalesced
+    bool fin = ok && j == nkt && !*abort_flag;
+    for (int h = 0; h < nh; ++h) {
+      bool okh = fin && mbar_wait(bar(B_O + h), (nkt - 1) & 1, abort_flag, P.err);
+      okh = __all_sync(0xffffffffu, okh);
+      if (okh) {
+        tc_fence_after();
+        const float inv = lsum[h] > 0.f ? 1.f / lsum[h] : 0.f;
+        uint8_t* orow = smem + (h ? L::V_OFF : L::K_OFF) + r * L::OST;
+#pragma unroll 1
+        for (int c = 0; c < THD; c += 32) {
+          uint32_t o[32];
+          tmem_ld16_nw(t_lane + T_O + h * THD + c, o);
+          tmem_ld16_nw(t_lane + T_O + h * THD + c + 16, o + 16);
+          tmem_wait();
+#pragma unroll
+          for (int e = 0; e < 32; e += 8)
+            *reinterpret_cast<uint4*>(orow + (c + e) * 2) = make_uint4(
+                pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
+                pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
+                pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
+                pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
+        }
       }
     }
     asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the four softmax warps only
     if (!*abort_flag) {
-      for (int i = tid; i < rows * (THD / 8); i += 128) {
-        const int qr = i / (THD / 8), c = i % (THD / 8);
-        st16(P.out + static_cast<int64_t>(qbase + q0 + qr) * P.o_t + head * P.o_h + c * 8,
-             *reinterpret_cast<const uint4*>(smem + L::K_OFF + qr * L::OST + c * 16));
+      for (int h = 0; h < nh; ++h) {
+        const uint8_t* stage = smem + (h ? L::V_OFF : L::K_OFF);
+        for (int i = tid; i < rows * (THD / 8); i += 128) {
+          const int qr = i / (THD / 8), c = i % (THD / 8);
+          st16(P.out + static_cast<int64_t>(qbase + q0 + qr) * P.o_t + (head_a + h) * P.o_h + c * 8,
+               *reinterpret_cast<const uint4*>(stage + qr * L::OST + c * 16));
+        }
       }
     }
   }
@@ -415,7 +450,7 @@ int attn_prefill_tc(const void* q, int64_t q_t, int64_t q_h, const void* key_cac
                     cudaStream_t stream) {
   if (!g_attn_prefill_tc) return MMP_ERR_UNSUPPORTED;
   if (hd != THD || block_size < 8 || block_size > TK || (block_size & (block_size - 1)) || o_t % 8 || o_h % 8 ||
-      !aligned16(out) || static_cast<int64_t>(nq) * nseq > 0x7fffffff)
+      !aligned16(out) || nq % nkv || static_cast<int64_t>(nq) * nseq > 0x7fffffff)
     return MMP_ERR_UNSUPPORTED;
   const int q_tiles = (max_q_len + TQ - 1) / TQ;
   if (q_tiles > 65535) return MMP_ERR_UNSUPPORTED;
@@ -426,9 +461,10 @@ int attn_prefill_tc(const void* q, int64_t q_t, int64_t q_h, const void* key_cac
   if ((rc = make_cache_map(&mk, key_cache, nkv, block_size, num_blocks, c_head, c_tok, c_block, tok_inner)) ||
       (rc = make_cache_map(&mv, value_cache, nkv, block_size, num_blocks, c_head, c_tok, c_block, tok_inner)))
     return rc;
+  const int pairs_per_kv = (nq / nkv + 1) / 2;
   AttnTcParams P{static_cast<const bf16*>(q), q_t, q_h, block_table, bt_stride, cu_q, ctx_start,
-                 static_cast<bf16*>(out), o_t, o_h, nq, nkv, block_size, num_blocks, q_tiles, tok_inner ? 1 : 0,
-                 scale * 1.4426950408889634f, err};
+                 static_cast<bf16*>(out), o_t, o_h, nq, nkv, block_size, num_blocks, q_tiles, pairs_per_kv,
+                 tok_inner ? 1 : 0, scale * 1.4426950408889634f, err};
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -438,8 +474,8 @@ int attn_prefill_tc(const void* q, int64_t q_t, int64_t q_h, const void* key_cac
     if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_prefill: smem attribute: %s", cudaGetErrorString(e));
     attr[dev] = true;
   }
-  cudaError_t e = mmp::launch(attn_prefill_tc_kernel, dim3(nq * nseq, q_tiles), dim3(TTHR), AttnTcSmem::DYN, stream,
-                              nullptr, 0, mk, mv, P);
+  cudaError_t e = mmp::launch(attn_prefill_tc_kernel, dim3(nkv * pairs_per_kv * nseq, q_tiles), dim3(TTHR),
+                              AttnTcSmem::DYN, stream, nullptr, 0, mk, mv, P);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_paged_attn_prefill: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_paged_attn_prefill");
 }

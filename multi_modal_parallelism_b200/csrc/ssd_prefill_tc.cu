@@ -2,23 +2,24 @@
 // d_state 128 or 256; the restated algorithm and its reference citations are in ssd_prefill.cu, which keeps
 // the other shapes.
 //
-// One CTA (8 warps) owns one head of one sequence and walks its chunks of 64 tokens in order. The fp32 state
-// S [p = 128, N] lives in TMEM for the whole walk (lane = p, column = n). Per chunk, with cum the running sum
-// of dt' A inside the chunk:
-//   * TMA brings C, B [64 x N] and x [64 x 128] (128-byte swizzle, K-major boxes); the next chunk's boxes are
-//     prefetched into L2 meanwhile;
-//   * G = C B^T (tcgen05.mma M=64, N=64, K=N) into TMEM; meanwhile the threads write the bf16 copy of S to
-//     shared memory and exp(cum_last) S back to TMEM;
-//   * the threads turn G into M[t][s] = G exp(cum_t - cum_s) dt_s (s <= t), plus D on the diagonal (so the
-//     intra-chunk product carries the D x skip term), and scale B rows by w_s = exp(cum_last - cum_s) dt_s
-//     in place;
-//   * y^T = x^T M^T and ys^T = S C^T into two TMEM accumulators (M=128 over p, N=64 over t), combined as
-//     y = y + exp(cum_t) ys in the epilogue; S += x^T (w B) (M=128, N=N); x and B are read as MN-major
-//     operands straight from their TMA boxes, M, C and the bf16 S as K-major ones;
-//   * once the MMAs are done the next chunk's loads go out, and the y tile is staged and written (16-byte
-//     stores) under them.
-// Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out of budget flags the error word, leaves
-// its state line untouched, drains its copies and frees TMEM.
+// One CTA owns one head of one sequence and walks its chunks of 64 tokens in order. The fp32 state S [p = 128, N]
+// lives in TMEM for the whole walk (lane = p, column = n). Per chunk, with cum the running sum of dt' A inside the
+// chunk, the work is split over warp roles that run concurrently:
+//   * warp 8 (one thread) streams C, B [64 x N] and x [64 x 128] of each chunk through a two-stage ring of
+//     128-byte-swizzled TMA boxes, a chunk ahead of the math;
+//   * warp 9 (one thread) issues the MMAs: G = C B^T (M = 64 t, N = 64 s, K = N) into TMEM; then
+//     Y = x^T M^T + S_bf C'^T (M = 128 p, N = 64 t; the second term reads the bf16 copy of the incoming state
+//     straight from TMEM as its A operand, and C' = exp(cum_t) C_t carries the state term's decay) and
+//     S += x^T (w B) (M = 128 p, N = N); then the next chunk's G;
+//   * warps 0-3 (one state row p per thread) run the state pass once the previous chunk's update is done: the
+//     bf16 copy of S into TMEM for Y's state term and exp(cum_last) S back into the fp32 columns;
+//   * warps 4-7 run the per-chunk scan of dt (softplus, running sum, weights), turn G into M[t][s] =
+//     G exp(cum_t - cum_s) dt_s (s <= t, D on the diagonal, so the product also carries the D x skip term),
+//     scale C's rows by exp(cum_t) and B's rows by w_s = exp(cum_last - cum_s) dt_s in place, and finally read
+//     Y out of TMEM, stage the bf16 y tile and store it with 16-byte writes.
+// The critical path per chunk is the update MMA, the state pass and the next Y and update MMAs; loads, the M
+// build and the y stores run under them. Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out
+// of budget flags the error word, leaves its state line untouched, drains its copies and MMAs and frees TMEM.
 #include <algorithm>
 
 #include "mmp_common.cuh"
@@ -29,7 +30,7 @@ namespace {
 
 constexpr int SQ = 64;     // tokens per chunk
 constexpr int SP = 128;    // head dim handled by this kernel
-constexpr int STHR = 256;  // 8 warps
+constexpr int STHR = 320;  // warps 0-3 state pass, 4-7 scan / M / y, 8 copies, 9 MMAs
 
 struct SsdTcParams {
   const bf16* dt; int64_t dt_t, dt_h;
@@ -44,22 +45,33 @@ struct SsdTcParams {
 template <int N>
 struct TcSsdSmem {
   static constexpr int KB = N / 64;                   // 64-wide k-blocks along n
-  static constexpr int C_OFF = 0;                     // C chunk: KB blocks [64 t x 128 B]
-  static constexpr int B_OFF = C_OFF + KB * 8192;     // B chunk: same
-  static constexpr int X_OFF = B_OFF + KB * 8192;     // x chunk: 2 blocks [64 t x 128 B] (p 0-63, 64-127)
-  static constexpr int M_OFF = X_OFF + 2 * 8192;      // M: [64 t x 128 B] (s)
-  static constexpr int SB_OFF = M_OFF + 8192;         // bf16 S: KB blocks [128 p x 128 B]
+  static constexpr int STAGE = 2 * KB * 8192 + 2 * 8192;  // one chunk's C, B and x boxes
+  static constexpr int C_OFF = 0;                     // stage 0 C chunk: KB blocks [64 t x 128 B]
+  static constexpr int B_OFF = C_OFF + KB * 8192;     // stage 0 B chunk: same
+  static constexpr int X_OFF = B_OFF + KB * 8192;     // stage 0 x chunk: 2 blocks [64 t x 128 B] (p 0-63, 64-127)
+  static constexpr int M_OFF = 2 * STAGE;             // M: [64 t x 128 B] (s)
   static constexpr int YLD = SP * 2 + 16;             // y tile row bytes (padded)
-  static constexpr int Y_OFF = SB_OFF + KB * 16384;   // y tile [64 t][128 p] bf16
-  static constexpr int CUM_OFF = Y_OFF + SQ * YLD;    // cum[64], dt[64], w[64], exp(cum)[64] fp32
-  static constexpr int BAR_OFF = CUM_OFF + 4 * SQ * 4 + 16;
-  static constexpr int USED = BAR_OFF + 8 * 4 + 16;
+  static constexpr int Y_OFF = M_OFF + 8192;          // y tile [64 t][128 p] bf16
+  static constexpr int CUM_OFF = Y_OFF + SQ * YLD;    // per chunk parity: cum, dt, w, exp(cum) [64] fp32 + decay
+  static constexpr int CUM_BYTES = 4 * SQ * 4 + 16;
+  static constexpr int BAR_OFF = CUM_OFF + 2 * CUM_BYTES;
+  static constexpr int NBAR = 16;
+  static constexpr int USED = BAR_OFF + 8 * NBAR + 16;
   static constexpr int DYN = USED + 1024;
-  static constexpr uint32_t LOAD_BYTES = 2 * KB * 8192 + 2 * 8192;
+  static constexpr uint32_t LOAD_BYTES = STAGE;
 };
+static_assert(TcSsdSmem<256>::DYN <= 232448, "shared memory per CTA");
 
-// TMEM columns
-constexpr uint32_t T_S = 0, T_Y = 256, T_G = 320, T_YS = 384;
+// TMEM columns: fp32 state [N], bf16 state copy [N / 2] (two values per column), Y [64], G [64]
+template <int N>
+struct TcSsdTmem {
+  static constexpr uint32_t S = 0, SBF = N, Y = N + N / 2, G = N + N / 2 + 64;
+};
+static_assert(TcSsdTmem<256>::G + 64 <= 512, "TMEM columns");
+
+// mbarriers
+constexpr int B_FULL = 0, B_EMPTY = 2, B_G = 4, B_MB = 5, B_SP = 6, B_YFREE = 7, B_Y = 8, B_S = 9, B_SCAN = 10,
+              B_DONE = 11;
 
 // byte offset of 16-byte chunk c of row r in a 128-byte-swizzled block of 128-byte rows
 __device__ __forceinline__ uint32_t sw(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -78,17 +90,28 @@ __device__ __forceinline__ uint64_t umma_desc_mn(uint32_t saddr, uint32_t mn_blo
 }
 constexpr uint32_t IDESC_A_MN = 1u << 15, IDESC_B_MN = 1u << 16;
 
-// bf16 copy of 64 state columns (this thread's row p) into the K-major operand blocks of the state term
-template <int N>
-__device__ __forceinline__ void store_sb(uint8_t* smem, int p, int c0n, const uint32_t* r) {
-  uint8_t* rowp = smem + TcSsdSmem<N>::SB_OFF + (c0n >> 6) * 16384;
+// MMA with the A operand in TMEM (K-major, two bf16 per 32-bit column, lane = row)
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+// AND of `v` over the `nthreads` threads of named barrier `id` (a barrier for them too): a decision every warp of
+// a group takes alike, so that none leaves a loop while the others wait at the group's next barrier
+__device__ __forceinline__ bool bar_and(int id, int nthreads, bool v) {
+  int r;
+  asm volatile("{\n.reg .pred p, q;\nsetp.ne.s32 p, %1, 0;\nbar.red.and.pred q, %2, %3, p;\nselp.s32 %0, 1, 0, q;\n}\n"
+               : "=r"(r) : "r"(v ? 1 : 0), "r"(id), "r"(nthreads) : "memory");
+  return r != 0;
+}
+// 64 consecutive TMEM columns of this thread's lane
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t* r) {
 #pragma unroll
-  for (int c = 0; c < 8; ++c)
-    *reinterpret_cast<uint4*>(rowp + sw(p, c)) = make_uint4(
-        pack_bf16x2(__uint_as_float(r[8 * c + 0]), __uint_as_float(r[8 * c + 1])),
-        pack_bf16x2(__uint_as_float(r[8 * c + 2]), __uint_as_float(r[8 * c + 3])),
-        pack_bf16x2(__uint_as_float(r[8 * c + 4]), __uint_as_float(r[8 * c + 5])),
-        pack_bf16x2(__uint_as_float(r[8 * c + 6]), __uint_as_float(r[8 * c + 7])));
+  for (int k = 0; k < 4; ++k) tmem_ld16_nw(taddr + 16 * k, r + 16 * k);
 }
 
 template <typename ST, int N>
@@ -97,6 +120,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
                                                                 const __grid_constant__ CUtensorMap mapC,
                                                                 const SsdTcParams P) {
   using L = TcSsdSmem<N>;
+  using TM = TcSsdTmem<N>;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
   pdl_trigger();
@@ -104,30 +128,35 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   const uint32_t sb = smem_addr(smem);
   const int h = blockIdx.x, seq = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int q = warp & 3, half = warp >> 2;
   const int t_begin = P.cu_seqlens[seq], t_end = P.cu_seqlens[seq + 1];
   const int line = P.state_idx[seq];
   if (line < 0 || line >= P.lines) {
     if (tid == 0) flag_error(P.err, DEVERR_INDEX);
     return;
   }
+  const int nchunks = (t_end - t_begin + SQ - 1) / SQ;
   const int grp = h / (P.nh / P.ngroups);
   const float A = P.A[h], Dh = P.D ? P.D[h] : 0.f, dtb = P.dt_bias ? P.dt_bias[h] : 0.f;
-  float* sCum = reinterpret_cast<float*>(smem + L::CUM_OFF);
-  float* sDt = sCum + SQ;
-  float* sW = sDt + SQ;
-  float* sE = sW + SQ;    // exp(cum_t)
-  float* sDec = sE + SQ;  // exp(cum_last)
-  const uint32_t bar_load = sb + L::BAR_OFF, bar_g = bar_load + 8, bar_y = bar_load + 16, bar_s = bar_load + 24;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 32);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 36);
+  auto bar = [&](int i) { return sb + L::BAR_OFF + 8 * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 8 * L::NBAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 8 * L::NBAR + 4);
   ST* gstate = reinterpret_cast<ST*>(P.state) + line * P.s_line + h * P.s_head;
+  // per-chunk scan results, double-buffered by chunk parity
+  auto cum_buf = [&](int c) { return reinterpret_cast<float*>(smem + L::CUM_OFF + (c & 1) * L::CUM_BYTES); };
 
   if (tid == 0) {
-    mbar_init(bar_load, 1);
-    mbar_init(bar_g, 1);
-    mbar_init(bar_y, 1);
-    mbar_init(bar_s, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(B_FULL + s), 1);
+      mbar_init(bar(B_EMPTY + s), 1);
+    }
+    mbar_init(bar(B_G), 1);
+    mbar_init(bar(B_MB), 128);
+    mbar_init(bar(B_SP), 128);
+    mbar_init(bar(B_YFREE), 128);
+    mbar_init(bar(B_Y), 1);
+    mbar_init(bar(B_S), 1);
+    mbar_init(bar(B_SCAN), 128);
+    mbar_init(bar(B_DONE), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     asm volatile("prefetch.tensormap [%0];\n" ::"l"(reinterpret_cast<uint64_t>(&mapX)) : "memory");
@@ -142,257 +171,265 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // this thread's TMEM lane (= state / output row p) and its half of the columns
-  const int p = q * 32 + lane;
-  const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
 
-  // ---- initial state into TMEM (or zeros) and its bf16 copy for the first chunk's state term
-  {
-    const bool init = P.has_init && P.has_init[seq];
-#pragma unroll 1
-    for (int c0n = half * (N / 2); c0n < (half + 1) * (N / 2); c0n += 64) {
-      uint32_t r[64];
+  if (warp == 8) {
+    // ------------------------------------------------------------------ copies: one chunk's boxes per stage
+    if (lane == 0) {
+      int issued = 0;
+      for (int c = 0; c < nchunks; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(bar(B_EMPTY + s), ((c >> 1) - 1) & 1, abort_flag, P.err)) break;
+        if (*abort_flag) break;
+        const int c0 = t_begin + c * SQ;
+        const uint32_t st = sb + s * L::STAGE;
+        mbar_expect_tx(bar(B_FULL + s), L::LOAD_BYTES);
 #pragma unroll
-      for (int j = 0; j < 64; ++j)
-        r[j] = __float_as_uint(init ? static_cast<float>(gstate[p * P.s_p + c0n + j]) : 0.f);
-#pragma unroll
-      for (int k = 0; k < 4; ++k) tmem_st16(t_lane + T_S + c0n + 16 * k, r + 16 * k);
-      store_sb<N>(smem, p, c0n, r);
-    }
-    tmem_wait_st();
-  }
-
-  auto issue_loads = [&](int c0) {
-    mbar_expect_tx(bar_load, L::LOAD_BYTES);
-#pragma unroll
-    for (int kb = 0; kb < L::KB; ++kb) {
-      tma_load_3d(sb + L::C_OFF + kb * 8192, &mapC, bar_load, kb * 64, grp, c0);
-      tma_load_3d(sb + L::B_OFF + kb * 8192, &mapB, bar_load, kb * 64, grp, c0);
-    }
-    tma_load_3d(sb + L::X_OFF, &mapX, bar_load, 0, h, c0);
-    tma_load_3d(sb + L::X_OFF + 8192, &mapX, bar_load, 64, h, c0);
-    if (c0 + SQ < t_end) {  // the chunk after into L2
-#pragma unroll
-      for (int kb = 0; kb < L::KB; ++kb) {
-        tma_prefetch_3d(&mapC, kb * 64, grp, c0 + SQ);
-        tma_prefetch_3d(&mapB, kb * 64, grp, c0 + SQ);
+        for (int kb = 0; kb < L::KB; ++kb) {
+          tma_load_3d(st + L::C_OFF + kb * 8192, &mapC, bar(B_FULL + s), kb * 64, grp, c0);
+          tma_load_3d(st + L::B_OFF + kb * 8192, &mapB, bar(B_FULL + s), kb * 64, grp, c0);
+        }
+        tma_load_3d(st + L::X_OFF, &mapX, bar(B_FULL + s), 0, h, c0);
+        tma_load_3d(st + L::X_OFF + 8192, &mapX, bar(B_FULL + s), 64, h, c0);
+        issued = c + 1;
       }
-      tma_prefetch_3d(&mapX, 0, h, c0 + SQ);
-      tma_prefetch_3d(&mapX, 64, h, c0 + SQ);
+      // copies in flight may still land after an abort: wait (bounded) for the last chunk of each stage
+      for (int c = max(0, issued - 2); c < issued; ++c) mbar_drain(bar(B_FULL + (c & 1)), (c >> 1) & 1);
     }
-  };
-  if (tid == 0 && t_begin < t_end) issue_loads(t_begin);
-
-  bool ok = true;  // warp-uniform: this warp's last wait succeeded (loop exits follow the CTA's abort flag)
-  int it = 0;
-  for (int c0 = t_begin; c0 < t_end; c0 += SQ, ++it) {
-    const int qn = min(SQ, t_end - c0);
-    const uint32_t par = it & 1;
-    if (warp == 1) {
-      // dt' = softplus(dt + bias), inclusive running sum of dt' A, state-update weights, chunk decay
-      float d[2], cs[2];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = lane * 2 + j;
-        d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) + dtb) : 0.f;
-      }
-      cs[0] = d[0] * A;
-      cs[1] = cs[0] + d[1] * A;
-      float run = cs[1];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float v = __shfl_up_sync(0xffffffffu, run, o);
-        if (lane >= o) run += v;
-      }
-      const float excl = run - cs[1];
-      const float cum_last = __shfl_sync(0xffffffffu, run, 31);  // tokens past qn add nothing
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = lane * 2 + j;
-        const float cum = excl + cs[j];
-        sDt[r] = d[j];
-        sCum[r] = cum;
-        sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
-        sE[r] = __expf(cum);
-      }
-      if (lane == 0) *sDec = __expf(cum_last);
-    }
-    mbar_wait(bar_load, par, abort_flag, P.err);
-    __syncthreads();  // scan results visible; a thread whose wait ran out raised the flag before arriving
-    if (*abort_flag) break;
-
-    // ---- G = C B^T (M = 64 tokens t, N = 64 tokens s, K = n)
-    if (tid == 0) {
-      tc_fence_after();
+    __syncwarp();
+  } else if (warp == 9) {
+    // ------------------------------------------------------------------ MMAs (one thread)
+    if (lane == 0) {
       constexpr uint32_t idg = umma_idesc_mn(64, 64);
+      constexpr uint32_t idy_x = umma_idesc_mn(128, 64) | IDESC_A_MN;
+      constexpr uint32_t idy_s = umma_idesc_mn(128, 64);
+      constexpr uint32_t ids = umma_idesc_mn(128, N) | IDESC_A_MN | IDESC_B_MN;
+      auto issue_g = [&](int c) {  // G = C B^T (M = 64 tokens t, N = 64 tokens s, K = n)
+        const uint32_t st = sb + (c & 1) * L::STAGE;
 #pragma unroll
-      for (int kb = 0; kb < L::KB; ++kb)
+        for (int kb = 0; kb < L::KB; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + TM::G, umma_desc(st + L::C_OFF + kb * 8192 + kk * 32),
+                     umma_desc(st + L::B_OFF + kb * 8192 + kk * 32), idg, (kb | kk) != 0);
+        umma_commit(bar(B_G));
+      };
+      bool ok = nchunks > 0 && mbar_wait(bar(B_FULL), 0, abort_flag, P.err);
+      if (ok) {
+        tc_fence_after();
+        issue_g(0);
+      }
+      for (int c = 0; ok && c < nchunks; ++c) {
+        const uint32_t par = c & 1;
+        const uint32_t st = sb + (c & 1) * L::STAGE;
+        // M, C' and w B built; the state pass done; the previous Y read out
+        if (!(ok = mbar_wait(bar(B_MB), par, abort_flag, P.err))) break;
+        if (!(ok = mbar_wait(bar(B_SP), par, abort_flag, P.err))) break;
+        if (c > 0 && !(ok = mbar_wait(bar(B_YFREE), par ^ 1, abort_flag, P.err))) break;
+        tc_fence_after();
+        // Y = x^T M^T (K = s) + S_bf C'^T (K = n)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem + T_G, umma_desc(sb + L::C_OFF + kb * 8192 + kk * 32),
-                   umma_desc(sb + L::B_OFF + kb * 8192 + kk * 32), idg, (kb | kk) != 0);
-      umma_commit(bar_g);
-    }
-
-    // ---- meanwhile: the state decays in TMEM, S = exp(cum_last) S (its bf16 copy, made at the end of the
-    // previous chunk, keeps the incoming state for the state term)
-    {
-      const float dec = *sDec;
-#pragma unroll 1
-      for (int c0n = half * (N / 2); c0n < (half + 1) * (N / 2); c0n += 64) {
-        uint32_t r[64];
+          umma_f16(tmem + TM::Y, umma_desc_mn(st + L::X_OFF + kk * 2048, 8192), umma_desc(sb + L::M_OFF + kk * 32),
+                   idy_x, kk != 0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tmem_ld16_nw(t_lane + T_S + c0n + 16 * k, r + 16 * k);
+        for (int kb = 0; kb < L::KB; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16_ts(tmem + TM::Y, tmem + TM::SBF + kb * 32 + kk * 8,
+                        umma_desc(st + L::C_OFF + kb * 8192 + kk * 32), idy_s, 1);
+        umma_commit(bar(B_Y));
+        // S += x^T (w B) (K = t)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          umma_f16(tmem + TM::S, umma_desc_mn(st + L::X_OFF + kk * 2048, 8192),
+                   umma_desc_mn(st + L::B_OFF + kk * 2048, 8192), ids, 1);
+        umma_commit(bar(B_S));
+        umma_commit(bar(B_EMPTY + (c & 1)));  // every MMA reading this stage has been issued
+        if (c + 1 < nchunks) {  // the next chunk's G (its M build overlaps the next state pass)
+          if (!(ok = mbar_wait(bar(B_FULL + ((c + 1) & 1)), ((c + 1) >> 1) & 1, abort_flag, P.err))) break;
+          tc_fence_after();
+          issue_g(c + 1);
+        }
+      }
+      umma_commit(bar(B_DONE));  // arrives once every MMA issued above has completed
+    }
+    __syncwarp();
+  } else if (warp < 4) {
+    // ------------------------------------------------------------------ warps 0-3: the state in TMEM
+    const int p = tid;  // state row = TMEM lane
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const bool init = P.has_init && P.has_init[seq];
+#pragma unroll 1
+    for (int c0n = 0; c0n < N; c0n += 16) {
+      uint32_t r[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) r[j] = __float_as_uint(init ? static_cast<float>(gstate[p * P.s_p + c0n + j]) : 0.f);
+      tmem_st16(t_lane + TM::S + c0n, r);
+    }
+    tmem_wait_st();
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const uint32_t par = c & 1;
+      ok = mbar_wait(bar(B_SCAN), par, abort_flag, P.err);  // this chunk's decay
+      if (ok && c > 0) ok = mbar_wait(bar(B_S), par ^ 1, abort_flag, P.err);  // the previous update done
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      const float dec = cum_buf(c)[4 * SQ];
+      // bf16 copy of the incoming state (Y's state term) and the decayed state (the update accumulates on it)
+#pragma unroll 1
+      for (int c0n = 0; c0n < N; c0n += 64) {
+        uint32_t r[64], b[32];
+        tmem_ld64(t_lane + TM::S + c0n, r);
         tmem_wait();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) b[j] = pack_bf16x2(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
 #pragma unroll
         for (int j = 0; j < 64; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * dec);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) tmem_st16(t_lane + T_S + c0n + 16 * k, r + 16 * k);
+        for (int k = 0; k < 4; ++k) tmem_st16(t_lane + TM::S + c0n + 16 * k, r + 16 * k);
+        tmem_st16(t_lane + TM::SBF + c0n / 2, b);
+        tmem_st16(t_lane + TM::SBF + c0n / 2 + 16, b + 16);
       }
       tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive1(bar(B_SP));
     }
-
-    // ---- G -> M (masked, decayed, dt-weighted, D on the diagonal); B rows *= w_s
-    ok = mbar_wait(bar_g, par, abort_flag, P.err);
-    ok = __all_sync(0xffffffffu, ok);
+    // final state -> the sequence's line (skipped after an abort: the line keeps its old value)
+    if (ok && nchunks > 0) ok = mbar_wait(bar(B_S), (nchunks - 1) & 1, abort_flag, P.err);
+    ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
     if (ok) {
       tc_fence_after();
-      // M=64 accumulator: row t = 16 q + l sits in lane 32 q + l (l < 16) of quadrant q; warps 0-3 take
-      // columns 0-31, warps 4-7 columns 32-63
-      uint32_t g[32];
-      tmem_ld16_nw(t_lane + T_G + half * 32, g);
-      tmem_ld16_nw(t_lane + T_G + half * 32 + 16, g + 16);
-      tmem_wait();
-      if (lane < 16) {
-        const int t = q * 16 + lane;
-        const float ct = sCum[t];
+#pragma unroll 1
+      for (int c0n = 0; c0n < N; c0n += 16) {
+        uint32_t r[16];
+        tmem_ld16_nw(t_lane + TM::S + c0n, r);
+        tmem_wait();
 #pragma unroll
-        for (int c8 = 0; c8 < 4; ++c8) {
-          uint32_t w4[4];
+        for (int j = 0; j < 16; ++j) gstate[p * P.s_p + c0n + j] = static_cast<ST>(__uint_as_float(r[j]));
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ warps 4-7: scan, M, scaling, y
+    const int tl = tid - 128;  // 0..127
+    const int q = warp & 3;    // TMEM lane quadrant
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
+    for (int c = 0; c < nchunks; ++c) {
+      const uint32_t par = c & 1;
+      const int c0 = t_begin + c * SQ;
+      const int qn = min(SQ, t_end - c0);
+      const uint32_t st_off = (c & 1) * L::STAGE;
+      float* sCum = cum_buf(c);
+      float* sDt = sCum + SQ;
+      float* sW = sDt + SQ;
+      float* sE = sW + SQ;
+      if (warp == 4) {
+        // dt' = softplus(dt + bias), inclusive running sum of dt' A, update weights, chunk decay
+        float d[2], cs[2];
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int s0 = half * 32 + c8 * 8 + 2 * j;
-            const int jj = c8 * 8 + 2 * j;
-            float a = (s0 <= t && s0 < qn) ? __uint_as_float(g[jj]) * __expf(ct - sCum[s0]) * sDt[s0] : 0.f;
-            float b = (s0 + 1 <= t && s0 + 1 < qn) ? __uint_as_float(g[jj + 1]) * __expf(ct - sCum[s0 + 1]) * sDt[s0 + 1] : 0.f;
-            if (s0 == t) a += Dh;
-            if (s0 + 1 == t) b += Dh;
-            w4[j] = pack_bf16x2(a, b);
+        for (int j = 0; j < 2; ++j) {
+          const int r = lane * 2 + j;
+          d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) + dtb) : 0.f;
+        }
+        cs[0] = d[0] * A;
+        cs[1] = cs[0] + d[1] * A;
+        float run = cs[1];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float v = __shfl_up_sync(0xffffffffu, run, o);
+          if (lane >= o) run += v;
+        }
+        const float excl = run - cs[1];
+        const float cum_last = __shfl_sync(0xffffffffu, run, 31);  // tokens past qn add nothing
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int r = lane * 2 + j;
+          const float cum = excl + cs[j];
+          sDt[r] = d[j];
+          sCum[r] = cum;
+          sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
+          sE[r] = __expf(cum);
+        }
+        if (lane == 0) sCum[4 * SQ] = __expf(cum_last);
+      }
+      asm volatile("bar.sync 2, 128;\n" ::: "memory");  // scan results visible to warps 4-7
+      mbar_arrive1(bar(B_SCAN));                          // and to the state pass (release)
+      if (!bar_and(2, 128, mbar_wait(bar(B_G), par, abort_flag, P.err))) break;
+      tc_fence_after();
+      // G -> M (masked, decayed, dt-weighted, D on the diagonal). M=64 accumulator: row t = 16 q + l sits in lane
+      // 32 q + l (l < 16) of quadrant q
+      {
+        uint32_t g[64];
+        tmem_ld64(t_lane + TM::G, g);
+        tmem_wait();
+        if (lane < 16) {
+          const int t = q * 16 + lane;
+          const float ct = sCum[t];
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            uint32_t w4[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int s0 = c8 * 8 + 2 * j;
+              float a = (s0 <= t && s0 < qn) ? __uint_as_float(g[s0]) * __expf(ct - sCum[s0]) * sDt[s0] : 0.f;
+              float b = (s0 + 1 <= t && s0 + 1 < qn) ? __uint_as_float(g[s0 + 1]) * __expf(ct - sCum[s0 + 1]) * sDt[s0 + 1] : 0.f;
+              if (s0 == t) a += Dh;
+              if (s0 + 1 == t) b += Dh;
+              w4[j] = pack_bf16x2(a, b);
+            }
+            *reinterpret_cast<uint4*>(smem + L::M_OFF + sw(t, c8)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
           }
-          *reinterpret_cast<uint4*>(smem + L::M_OFF + sw(t, half * 4 + c8)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
         }
       }
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // M -> tensor core reads
-    tc_fence_before();
-    __syncthreads();  // M built; the G MMAs are done with B (every thread passed bar_g)
-    if (*abort_flag) break;
-
-    // ---- y^T = x^T M^T ; ys^T = S C^T (B is not an operand: it is weighted meanwhile)
-    if (tid == 0) {
-      tc_fence_after();
-      constexpr uint32_t idy_x = umma_idesc_mn(128, 64) | IDESC_A_MN;
-      constexpr uint32_t idy = umma_idesc_mn(128, 64);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk)  // K = s, 16 rows of the x boxes per step
-        umma_f16(tmem + T_Y, umma_desc_mn(sb + L::X_OFF + kk * 2048, 8192), umma_desc(sb + L::M_OFF + kk * 32),
-                 idy_x, kk != 0);
-#pragma unroll
-      for (int kb = 0; kb < L::KB; ++kb)
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem + T_YS, umma_desc(sb + L::SB_OFF + kb * 16384 + kk * 32),
-                   umma_desc(sb + L::C_OFF + kb * 8192 + kk * 32), idy, (kb | kk) != 0);
-      umma_commit(bar_y);
-    }
-    if (ok) {
-      // row t = tid / 4 of B, a quarter of its 16-byte chunks each
-      const int t = tid >> 2, part = tid & 3;
-      const float wb = sW[t];
-#pragma unroll
-      for (int i = 0; i < L::KB * 2; ++i) {
-        const int cidx = part * (L::KB * 2) + i;  // chunk along n: block cidx / 8, chunk cidx % 8
-        uint4* pb = reinterpret_cast<uint4*>(smem + L::B_OFF + (cidx >> 3) * 8192 + sw(t, cidx & 7));
-        const uint4 v = *pb;
-        const float2 a0 = unpack_bf16x2(v.x), a1 = unpack_bf16x2(v.y), a2 = unpack_bf16x2(v.z), a3 = unpack_bf16x2(v.w);
-        *pb = make_uint4(pack_bf16x2(a0.x * wb, a0.y * wb), pack_bf16x2(a1.x * wb, a1.y * wb),
-                         pack_bf16x2(a2.x * wb, a2.y * wb), pack_bf16x2(a3.x * wb, a3.y * wb));
+      // C rows *= exp(cum_t), B rows *= w_s, in place (the G MMA is done with both): row tl / 2, half of its
+      // 16-byte chunks each
+      {
+        const int t = tl >> 1, part = tl & 1;
+        const float ec = sE[t], wb = sW[t];
+#pragma unroll 4
+        for (int i = 0; i < L::KB * 4; ++i) {
+          const int cidx = part * (L::KB * 4) + i;  // chunk along n: block cidx / 8, chunk cidx % 8
+          const uint32_t off = (cidx >> 3) * 8192 + sw(t, cidx & 7);
+          uint4* pc = reinterpret_cast<uint4*>(smem + st_off + L::C_OFF + off);
+          uint4* pb = reinterpret_cast<uint4*>(smem + st_off + L::B_OFF + off);
+          const uint4 vc = *pc, vb = *pb;
+          float2 a0 = unpack_bf16x2(vc.x), a1 = unpack_bf16x2(vc.y), a2 = unpack_bf16x2(vc.z), a3 = unpack_bf16x2(vc.w);
+          *pc = make_uint4(pack_bf16x2(a0.x * ec, a0.y * ec), pack_bf16x2(a1.x * ec, a1.y * ec),
+                           pack_bf16x2(a2.x * ec, a2.y * ec), pack_bf16x2(a3.x * ec, a3.y * ec));
+          a0 = unpack_bf16x2(vb.x), a1 = unpack_bf16x2(vb.y), a2 = unpack_bf16x2(vb.z), a3 = unpack_bf16x2(vb.w);
+          *pb = make_uint4(pack_bf16x2(a0.x * wb, a0.y * wb), pack_bf16x2(a1.x * wb, a1.y * wb),
+                           pack_bf16x2(a2.x * wb, a2.y * wb), pack_bf16x2(a3.x * wb, a3.y * wb));
+        }
       }
-    }
-    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
-    tc_fence_before();
-    __syncthreads();
-    if (*abort_flag) break;
-
-    // ---- S += x^T (w B)
-    if (tid == 0) {
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
+      tc_fence_before();
+      mbar_arrive1(bar(B_MB));
+      // y = Y^T out of TMEM (lane p, column t), staged as [t][p] bf16 and stored
+      if (!bar_and(2, 128, mbar_wait(bar(B_Y), par, abort_flag, P.err))) break;
       tc_fence_after();
-      constexpr uint32_t ids = umma_idesc_mn(128, N) | IDESC_A_MN | IDESC_B_MN;
+      {
+        uint32_t yv[64];
+        tmem_ld64(t_lane + TM::Y, yv);
+        tmem_wait();
+        tc_fence_before();
+        mbar_arrive1(bar(B_YFREE));  // Y may be overwritten by the next chunk
+        const int pr = q * 32 + lane;
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        umma_f16(tmem + T_S, umma_desc_mn(sb + L::X_OFF + kk * 2048, 8192),
-                 umma_desc_mn(sb + L::B_OFF + kk * 2048, 8192), ids, 1);
-      umma_commit(bar_s);
+        for (int j = 0; j < 64; ++j)
+          *reinterpret_cast<bf16*>(smem + L::Y_OFF + j * L::YLD + pr * 2) = f2bf(__uint_as_float(yv[j]));
+      }
+      asm volatile("bar.sync 2, 128;\n" ::: "memory");
+      for (int i = tl; i < SQ * (SP / 8); i += 128) {
+        const int t = i / (SP / 8), cc = i % (SP / 8);
+        if (t < qn)
+          st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + cc * 8,
+               *reinterpret_cast<const uint4*>(smem + L::Y_OFF + t * L::YLD + cc * 16));
+      }
+      asm volatile("bar.sync 2, 128;\n" ::: "memory");  // the y tile and this chunk's scan buffer are reusable
     }
-
-    // ---- y^T out of TMEM; once the state update is done too, the next chunk's loads go out and the y tile is
-    // staged and stored under them
-    ok = mbar_wait(bar_y, par, abort_flag, P.err);
-    ok = __all_sync(0xffffffffu, ok);
-    float yv[32];
-    if (ok) {
-      tc_fence_after();
-      uint32_t yi[32], ys[32];
-      tmem_ld16_nw(t_lane + T_Y + half * 32, yi);
-      tmem_ld16_nw(t_lane + T_Y + half * 32 + 16, yi + 16);
-      tmem_ld16_nw(t_lane + T_YS + half * 32, ys);
-      tmem_ld16_nw(t_lane + T_YS + half * 32 + 16, ys + 16);
-      tmem_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) yv[j] = fmaf(sE[half * 32 + j], __uint_as_float(ys[j]), __uint_as_float(yi[j]));
-    }
-    mbar_wait(bar_s, par, abort_flag, P.err);
-    tc_fence_after();
-    __syncthreads();  // every MMA of this chunk is done: C, B, x, M and the bf16 S are free
-    if (*abort_flag) break;
-    if (tid == 0 && c0 + SQ < t_end) issue_loads(c0 + SQ);
-    // bf16 copy of the outgoing state (the next chunk's state term) while the loads are in flight
-#pragma unroll 1
-    for (int c0n = half * (N / 2); c0n < (half + 1) * (N / 2); c0n += 64) {
-      uint32_t r[64];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) tmem_ld16_nw(t_lane + T_S + c0n + 16 * k, r + 16 * k);
-      tmem_wait();
-      store_sb<N>(smem, p, c0n, r);
-    }
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      *reinterpret_cast<bf16*>(smem + L::Y_OFF + (half * 32 + j) * L::YLD + p * 2) = f2bf(yv[j]);
-    __syncthreads();
-    for (int i = tid; i < SQ * (SP / 8); i += STHR) {
-      const int t = i / (SP / 8), c = i % (SP / 8);
-      if (t < qn)
-        st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + c * 8,
-             *reinterpret_cast<const uint4*>(smem + L::Y_OFF + t * L::YLD + c * 16));
-    }
-    // the y tile is rewritten after the next chunk's loads and MMAs, each behind a barrier
   }
 
-  // ---- final state -> the sequence's line (skipped after an abort: the line keeps its old value)
-  const bool aborted = *abort_flag != 0;
-  if (!aborted) {
-#pragma unroll 1
-    for (int c0n = half * (N / 2); c0n < (half + 1) * (N / 2); c0n += 16) {
-      uint32_t r[16];
-      tmem_ld16_nw(t_lane + T_S + c0n, r);
-      tmem_wait();
-#pragma unroll
-      for (int j = 0; j < 16; ++j) gstate[p * P.s_p + c0n + j] = static_cast<ST>(__uint_as_float(r[j]));
-    }
-  } else if (tid == 0) {
-    // copies of the chunk that was loading may still be in flight
-    mbar_drain(bar_load, it & 1);
-  }
+  // teardown: every MMA has completed (bounded) before TMEM is released
+  mbar_drain(bar(B_DONE), 0);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

@@ -1,5 +1,6 @@
 """Discrete-event model of the synchronisation of attn_prefill_tc_kernel (csrc/attn_prefill_tc.cu), test
-infrastructure. mbarriers keep arrival counts, transaction bytes and a phase counter, with try_wait.parity's
+infrastructure. One CTA serves one or two query heads (A, B) with one score buffer and one output accumulator
+each, one shared P buffer and a two-stage K/V ring. mbarriers keep arrival counts, transaction bytes and a phase counter, with try_wait.parity's
 meaning (true once the phase of that parity has completed; parity 1 passes before the first phase). The copy
 engine completes each page box at a random time; the tensor pipe completes MMAs in issue order at random times
 and a commit arrives once everything issued before it has completed. The producer (copies), the MMA thread and W
@@ -39,16 +40,20 @@ class Bar:
 
 
 class Sim:
-    def __init__(self, nkt: int, warps: int, nb: int, seed: int, tail: bool, rescale_p: float, bug: str = ""):
+    def __init__(self, nkt: int, warps: int, nb: int, seed: int, tail: bool, rescale_p: float, bug: str = "",
+                 heads: int = 2):
         self.rng = random.Random(seed)
         self.nkt, self.warps, self.nb, self.tail, self.rescale_p, self.bug = nkt, warps, nb, tail, rescale_p, bug
+        self.heads = "AB"[:heads]
         self.bars = {"Q": Bar(warps), "K0": Bar(1), "K1": Bar(1), "V0": Bar(1), "V1": Bar(1), "E0": Bar(1),
-                     "E1": Bar(1), "S0": Bar(1), "S1": Bar(1), "P": Bar(warps), "O": Bar(1), "DONE": Bar(1)}
-        self.version = {"K0": None, "K1": None, "V0": None, "V1": None, "S0": None, "S1": None, "P": None, "O": -1}
+                     "E1": Bar(1), "DONE": Bar(1)}
+        for h in "AB":
+            self.bars.update({"S" + h: Bar(1), "F" + h: Bar(warps), "P" + h: Bar(warps), "O" + h: Bar(1)})
+        self.version = {"K0": None, "K1": None, "V0": None, "V1": None, "SA": None, "SB": None, "P": None,
+                        "OA": -1, "OB": -1}
         self.readers = {k: 0 for k in self.version}   # MMAs in flight reading the buffer
         self.writers = {k: 0 for k in self.version}   # copies or MMAs in flight writing it
-        self.s_read = {"S0": None, "S1": None}         # last score tile every warp has read
-        self.warp_read = [{"S0": None, "S1": None} for _ in range(warps)]
+        self.warp_read = [{"SA": None, "SB": None} for _ in range(warps)]
         self.p_rows = [None] * warps                   # P tile each warp's rows hold
         self.copies: list = []                          # in flight: (bar, bytes, buffer, tile)
         self.mma_q: list = []                           # in order: ("mma", reads, writes, tile) / ("commit", bar)
@@ -79,7 +84,7 @@ class Sim:
                 self.err(f"{what} reads {buf}: holds {self.version[buf]} (writers {self.writers[buf]}), needs {ver}")
             self.readers[buf] += 1
         for buf in writes:
-            if buf in ("S0", "S1") and self.version[buf] is not None and any(
+            if buf in ("SA", "SB") and self.version[buf] is not None and any(
                     w[buf] != self.version[buf] for w in self.warp_read):
                 self.err(f"{what} overwrites {buf} before every warp read tile {self.version[buf]}")
             self.writers[buf] += 1
@@ -114,53 +119,69 @@ class Sim:
     def mma(self):
         yield ("Q", 0)
         yield ("K0", 0)
-        self.issue_mma({"K0": 0}, {"S0": 0}, "S(0)")
-        self.commit("S0")
+        for h in self.heads:
+            self.issue_mma({"K0": 0}, {"S" + h: 0}, f"S{h}(0)")
+            self.commit("S" + h)
         for j in range(self.nkt):
-            if j + 1 < self.nkt:
-                b = (j + 1) & 1
-                yield ("K" + str(b), ((j + 1) >> 1) & 1)
-                self.issue_mma({"K" + str(b): j + 1}, {"S" + str(b): j + 1}, f"S({j + 1})")
-                self.commit("S" + str(b))
-            yield ("P", j & 1)
-            if self.bug != "pv_before_v":
-                yield ("V" + str(j & 1), (j >> 1) & 1)
-            self.issue_mma({"P": j, "V" + str(j & 1): j}, {"O": j}, f"PV({j})")
-            self.commit("O")
+            b = (j + 1) & 1
+            for h in self.heads:
+                if j + 1 < self.nkt:
+                    if self.bug != "s_before_read":
+                        yield ("F" + h, j & 1)
+                    if h == "A":
+                        yield ("K" + str(b), ((j + 1) >> 1) & 1)
+                    self.issue_mma({"K" + str(b): j + 1}, {"S" + h: j + 1}, f"S{h}({j + 1})")
+                    self.commit("S" + h)
+                yield ("P" + h, j & 1)
+                if h == "A" and self.bug != "pv_before_v":
+                    yield ("V" + str(j & 1), (j >> 1) & 1)
+                self.issue_mma({"P": (h, j), "V" + str(j & 1): j}, {"O" + h: j}, f"PV{h}({j})")
+                self.commit("O" + h)
             self.commit("E" + str(j & 1))
         self.commit("DONE")
 
     def softmax(self, w):
         self.q_written += 1
         self.bars["Q"].arrive()
+        nh = len(self.heads)
         for j in range(self.nkt):
-            sb = "S" + str(j & 1)
-            yield (sb, (j >> 1) & 1)
-            if self.writers[sb] or self.version[sb] != j:
-                self.err(f"warp {w} reads {sb} holding {self.version[sb]} (writers {self.writers[sb]}) for tile {j}")
-            self.warp_read[w][sb] = j
-            o_ready = j == 0
-            if j > 0 and self.rng.random() < self.rescale_p:  # a row maximum grew: rescale O
-                yield ("O", (j - 1) & 1)
-                o_ready = True
-                if self.writers["O"] or self.version["O"] != j - 1:
-                    self.err(f"warp {w} rescales O holding {self.version['O']} while PV runs (tile {j})")
-            if not o_ready and self.bug != "p_before_pv":
-                yield ("O", (j - 1) & 1)
-            if self.tail and j == self.nkt - 1:
-                vb = "V" + str(j & 1)
-                yield (vb, (j >> 1) & 1)
-                if self.writers[vb] or self.readers[vb] or self.version[vb] != j:
-                    self.err(f"warp {w} zeroes the tail of {vb} holding {self.version[vb]} (tile {j})")
-            if self.readers["P"]:
-                self.err(f"warp {w} writes P({j}) while PV reads P")
-            self.p_rows[w] = j
-            if all(p == j for p in self.p_rows):
-                self.version["P"] = j
-            self.bars["P"].arrive()
-        yield ("O", (self.nkt - 1) & 1)
-        if self.writers["O"] or self.version["O"] != self.nkt - 1:
-            self.err(f"warp {w} reads the output holding {self.version['O']}")
+            for h in self.heads:
+                sb = "S" + h
+                yield (sb, j & 1)
+                if self.writers[sb] or self.version[sb] != j:
+                    self.err(f"warp {w} reads {sb} holding {self.version[sb]} (writers {self.writers[sb]}) "
+                             f"for tile {j}")
+                self.warp_read[w][sb] = j
+                self.bars["F" + h].arrive()
+                if j > 0 and self.rng.random() < self.rescale_p:  # a row maximum grew: rescale O_h
+                    yield ("O" + h, (j - 1) & 1)
+                    if self.writers["O" + h] or self.version["O" + h] != j - 1:
+                        self.err(f"warp {w} rescales O{h} holding {self.version['O' + h]} while PV runs (tile {j})")
+                # the P buffer's last reader: PV_B(j - 1) before A writes (PV_A(j - 1) with one head), PV_A(j)
+                # before B writes
+                ph, pj = ("A", j) if h == "B" else (self.heads[nh - 1], j - 1)
+                if pj >= 0 and self.bug != "p_before_pv":
+                    yield ("O" + ph, pj & 1)
+                if h == "A" and self.tail and j == self.nkt - 1:
+                    vb = "V" + str(j & 1)
+                    yield (vb, (j >> 1) & 1)
+                    if self.writers[vb] or self.readers[vb] or self.version[vb] != j:
+                        self.err(f"warp {w} zeroes the tail of {vb} holding {self.version[vb]} (tile {j})")
+                if self.readers["P"]:
+                    self.err(f"warp {w} writes P{h}({j}) while PV reads P")
+                self.p_rows[w] = (h, j)
+                if all(p == (h, j) for p in self.p_rows):
+                    self.version["P"] = (h, j)
+                self.bars["P" + h].arrive()
+        for h in self.heads:
+            yield ("O" + h, (self.nkt - 1) & 1)
+            if self.writers["O" + h] or self.version["O" + h] != self.nkt - 1:
+                self.err(f"warp {w} reads output {h} holding {self.version['O' + h]}")
+            # the epilogue stages head A's rows in the K ring and head B's in the V ring
+            ring = "K" if h == "A" else "V"
+            for st in (ring + "0", ring + "1"):
+                if self.readers[st] or self.writers[st]:
+                    self.err(f"warp {w} stages output {h} in {st} while it is in use")
 
     # ---------------------------------------------------------------- the scheduler
     def run(self) -> list[str]:

@@ -50,7 +50,7 @@ def _run(q, kc, vc, table, lens, starts):
     return out
 
 
-@pytest.mark.parametrize("nq,nkv,with_ctx", [(12, 2, False), (8, 8, True), (16, 2, True)])
+@pytest.mark.parametrize("nq,nkv,with_ctx", [(12, 2, False), (8, 8, True), (16, 2, True), (6, 2, True)])
 def test_tc_attn_prefill_matches_oracle(nq, nkv, with_ctx):
     lens = [1, 17, 64, 65, 130]
     starts = [0, 33, 5, 100, 16] if with_ctx else [0] * len(lens)

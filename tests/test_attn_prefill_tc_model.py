@@ -55,7 +55,18 @@ def test_ragged_chunked_prefill_matches_exact_attention(bs):
     scale = 1 / np.sqrt(128)
     out, flagged, ran = run_kernel_model(q, kc, vc, table, cu_q, st, max(lens), scale)
     assert not flagged
-    assert ran == 4 * (3 + 1 + 2 + 1)  # query tiles per sequence x heads; CTAs past a sequence exit at once
+    assert ran == 2 * (3 + 1 + 2 + 1)  # query tiles per sequence x head pairs; CTAs past a sequence exit at once
+    _check(out, exact_attention(q, kc, vc, table, cu_q, st, scale), cu_q)
+
+
+def test_odd_group_size_leaves_single_head_pairs():
+    """Three query heads per key/value head: each key/value head has a full pair and a single-head CTA."""
+    lens, starts = [200, 70], [0, 33]
+    q, kc, vc, table, cu_q, st = _problem(lens, starts, 16, nq=6, nkv=2, seed=11)
+    scale = 1 / np.sqrt(128)
+    out, flagged, ran = run_kernel_model(q, kc, vc, table, cu_q, st, max(lens), scale)
+    assert not flagged
+    assert ran == 4 * (2 + 1)  # 2 key/value heads x 2 CTAs (a pair and a single head) x query tiles
     _check(out, exact_attention(q, kc, vc, table, cu_q, st, scale), cu_q)
 
 

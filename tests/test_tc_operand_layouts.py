@@ -59,8 +59,10 @@ def test_attention_prefill_tc_operands():
     L = _consts("attn_prefill_tc.cu", "AttnTcSmem")
     for bs in (8, 16, 64, 128):
         mem = {}
-        # Q [128 queries x 128 dims] by threads; K, V stage 1 [128 keys x 128 dims] by page boxes; P by threads
-        thread_write(mem, L["Q_OFF"], 128, 16, lambda r, d: ("Q", r, d), block_bytes=16384)
+        # Q of both heads [128 queries x 128 dims] by threads; K, V stage 1 [128 keys x 128 dims] by page boxes; P
+        # by threads
+        for h in range(2):
+            thread_write(mem, L["Q_OFF"] + h * 32768, 128, 16, lambda r, d, h=h: ("Q", h, r, d), block_bytes=16384)
         stage = 1
         for lane in range(128 // bs):
             for hh in range(2):
@@ -71,10 +73,11 @@ def test_attention_prefill_tc_operands():
         kst, vst = L["K_OFF"] + stage * 32768, L["V_OFF"] + stage * 32768
         for kk in range(8):
             off = (kk >> 2) * 16384 + (kk & 3) * 32
-            # S = Q K^T: A = Q (M = 128 queries), B = K (N = 128 keys), this step's 16 dims
-            a = read_k_major(mem, L["Q_OFF"] + off, 128)
+            # S_h = Q_h K^T: A = Q_h (M = 128 queries), B = K (N = 128 keys), this step's 16 dims
+            for h in range(2):
+                a = read_k_major(mem, L["Q_OFF"] + h * 32768 + off, 128)
+                assert all(a[i][k] == ("Q", h, i, kk * 16 + k) for i in range(128) for k in range(16))
             b = read_k_major(mem, kst + off, 128)
-            assert all(a[i][k] == ("Q", i, kk * 16 + k) for i in range(128) for k in range(16))
             assert all(b[n][k] == ("K", n, kk * 16 + k) for n in range(128) for k in range(16))
             # O += P V: A = P (M = 128 queries, this step's 16 keys), B = V MN-major (N = 128 dims)
             a = read_k_major(mem, L["P_OFF"] + off, 128)
