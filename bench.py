@@ -49,7 +49,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--prefill-len", type=int, default=2048, help="0 skips the prefill measurement")
     ap.add_argument("--prefill-steps", type=int, default=20)
     ap.add_argument("--prefill-new", action="store_true",
-                    help="time the prefill with the tcgen05 attention kernel and the balanced-walk SSD scan")
+                    help="time the prefill with the balanced-walk SSD scan (segments and a join pass)")
     ap.add_argument("--workload", choices=["hybrid", "mamba2_sg", "qwen35"], default="hybrid",
                     help="mamba2_sg: the pure Mamba-2 layer under continuous batching (tp and SSM/gate split); "
                          "qwen35: the Gated DeltaNet hybrid block stack (tp and attention data-parallel)")
@@ -396,28 +396,25 @@ def time_prefill(args, layer, groups, wd: "Watchdog | None" = None) -> dict | No
         err = f"{type(e).__name__}: {e}"[:300]
     if not agree(err is None, groups):
         return {"error": err or "another rank could not build the prefill inputs"}
-    kernels = "attention mma.sync, SSD scan tcgen05"
+    kernels = "attention tcgen05, SSD scan tcgen05"
     agrees = None
     if args.prefill_new:
-        # the tcgen05 attention kernel and the balanced-walk scan, checked against the default kernels first
-        from multi_modal_parallelism_b200 import kernels as K
+        # the balanced-walk scan, checked against the default kernels first
         from multi_modal_parallelism_b200.correctness import compare, within_tolerance
 
-        with wd.phase("prefill: new kernels check", 300):
+        with wd.phase("prefill: balanced-walk scan check", 300):
             try:
                 ref = layer.prefill(h, pc).clone()
-                K.set_attn_prefill_tc(True)
                 layer.set_prefill_options(ssd_segments=True)
                 m = compare(layer.prefill(h, pc), ref)
                 ok = within_tolerance(m) and not device_error_flagged(groups.device)
             except Exception as e:
-                fatal("prefill: new kernels check", e)
+                fatal("prefill: balanced-walk scan check", e)
         agrees = agree(ok, groups)
         kernels = "attention tcgen05, SSD scan tcgen05 with balanced walks"
         if not agrees:  # time the default kernels instead
-            K.set_attn_prefill_tc(False)
             layer.set_prefill_options(ssd_segments=False)
-            kernels = "attention mma.sync, SSD scan tcgen05 (the new kernels disagreed: not timed)"
+            kernels = "attention tcgen05, SSD scan tcgen05 (balanced walks disagreed: not timed)"
     with wd.phase("prefill: timing", 300):
         try:
             for _ in range(3):
@@ -435,7 +432,6 @@ def time_prefill(args, layer, groups, wd: "Watchdog | None" = None) -> dict | No
     ms = max_over_ranks(statistics.median(per), groups)
     barrier_sync()
     if args.prefill_new:
-        K.set_attn_prefill_tc(False)
         layer.set_prefill_options(ssd_segments=False)
     fl = prefill_flops(layer.dims, [L] * nseq)
     peak, src = bf16_peak()

@@ -279,10 +279,10 @@ int mmp_paged_attn_prefill(const void* q, int64_t q_t, int64_t q_h,
                            int nseq, int max_q_len, int nq, int nkv, int hd, int block_size, int num_blocks,
                            float scale, int* err, void* stream);
 
-/* Selects the kernel behind mmp_paged_attn_prefill: 0 (default) the mma.sync kernel; 1 the tcgen05/TMEM kernel
- * (S and O accumulated in tensor memory, paged K/V gathered by TMA, lazy softmax rescaling) for requests it fits
- * (page of 8-128 tokens, a power of two; 16-byte aligned output rows), the mma.sync kernel otherwise. Process-wide;
- * returns the previous setting. */
+/* Selects the kernel behind mmp_paged_attn_prefill: 1 (default) the tcgen05/TMEM kernel (one CTA per pair of query
+ * heads sharing a key/value head, S, P and O in tensor memory, paged K/V gathered by TMA, lazy softmax rescaling)
+ * for requests it fits (head dim 128, page of 8-128 tokens, a power of two; 16-byte aligned output rows), the
+ * mma.sync kernel otherwise; 0 the mma.sync kernel always. Process-wide; returns the previous setting. */
 int mmp_set_attn_prefill_tc(int enable);
 
 /* ---- elementwise add (residual joins after a collective) -------------------------------------------

@@ -1,28 +1,29 @@
 // Causal GQA prefill attention over the paged KV cache on the 5th-generation tensor cores (tcgen05 / TMEM /
 // TMA), head dim 128: the same operation as attn_prefill.cu (FlashAttention-2 varlen, causal, in the serving stack
-// the reference measures), selected with mmp_set_attn_prefill_tc.
+// the reference measures). It is the default path for head dim 128; mmp_set_attn_prefill_tc(0) selects the mma.sync
+// kernel instead, which also serves every shape this kernel does not.
 //
 // Query token j of sequence i sits at position ctx_start[i] + j and sees cache positions [0, ctx_start[i] + j]
-// of that sequence. One CTA (6 warps) owns 128 query tokens of TWO query heads that read the same key/value
+// of that sequence. One CTA (10 warps) owns 128 query tokens of TWO query heads that read the same key/value
 // head (a head pair; the last pair of a key/value head holds one head when the group size is odd), so every
-// key/value tile it loads serves both, and the tensor pipe works on one head while the threads run the softmax
-// of the other:
-//   * warps 0-3 (one query row per thread = one TMEM lane) load both Q tiles with plain 16-byte loads into the
-//     128-byte-swizzled K-major operand layout, then, for every key tile, run the online softmax of head A and
-//     then of head B, and finally the epilogue;
-//   * warp 4 gathers each tile of 128 keys page by page with 4-D TMA boxes [block_size keys x 64 dims] straight
+// key/value tile it loads serves both, and each head has its own softmax warpgroup, so the two softmaxes share
+// the SM's issue slots and hide each other's latencies while the tensor pipe alternates between the heads:
+//   * warps 0-3 (head A) and 4-7 (head B), one query row per thread = one TMEM lane: load the head's Q tile with
+//     plain 16-byte loads into the 128-byte-swizzled K-major operand layout, run the online softmax of every key
+//     tile, write P (bf16) into TMEM over the scores it came from, and finally the epilogue;
+//   * warp 8 gathers each tile of 128 keys page by page with 4-D TMA boxes [block_size keys x 64 dims] straight
 //     from the paged K and V caches into a two-stage ring (pages past the sequence, or with a bad block id, are
 //     requested at an out-of-range block coordinate and arrive as zeros);
-//   * warp 5 (one thread) issues, per key tile j, S_A(j+1) = Q_A K_{j+1}^T as soon as the threads have read
-//     S_A(j), O_A += P_A(j) V_j once they have written P_A(j), then the same for head B. Each head has one
-//     score buffer and one output accumulator in TMEM (4 x 128 of the 512 columns); P goes through one shared
-//     bf16 buffer in shared memory (K-major), V is an MN-major operand straight from its TMA boxes.
+//   * warp 9 (one thread) issues, for each head as soon as its inputs are ready, S_h(j) = Q_h K_j^T into the
+//     head's score columns and O_h += P_h(j) V_j with P read from TMEM (the MMA's A operand) and V an MN-major
+//     operand straight from its TMA boxes; S_h(j + 1) is issued only once O_h's update from P_h(j) has completed,
+//     since it overwrites P_h(j)'s columns.
 // The softmax keeps its running maximum lazily: O (in TMEM) and the row sum are rescaled only when a row's
 // maximum grows by more than 2^8, so most tiles need no correction pass; P is rounded to bf16 as in the
 // mma.sync kernel. Scores of keys a row may not see are replaced (not added to) by -inf, and value rows past
-// the sequence's last key are zeroed before they meet P, so unwritten cache slots cannot turn 0 * x into NaN.
-// Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out of budget flags the error word, stops
-// issuing work, drains its copies and its MMAs, and frees TMEM.
+// the sequence's last key are zeroed (by head A's warps, before either head's last PV) so unwritten cache slots
+// cannot turn 0 * x into NaN. Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out of budget flags
+// the error word, stops issuing work, drains its copies and its MMAs, and frees TMEM.
 #include <algorithm>
 
 #include "mmp_common.cuh"
@@ -30,19 +31,18 @@
 
 namespace mmp {
 
-static int g_attn_prefill_tc = 0;  // off until selected: the mma.sync kernel stays the default path
+static int g_attn_prefill_tc = 1;  // on by default; mmp_set_attn_prefill_tc(0) selects the mma.sync kernel
 
 namespace {
 
 constexpr int TQ = 128, TK = 128, THD = 128;
-constexpr int TTHR = 192;  // warps 0-3 softmax and epilogue, warp 4 copies, warp 5 MMAs
+constexpr int TTHR = 320;  // warps 0-3 softmax head A, 4-7 head B, warp 8 copies, warp 9 MMAs
 
 struct AttnTcSmem {
   static constexpr int Q_OFF = 0;                  // Q: 2 heads x 2 blocks [128 q][64 dims] (128 B rows, swizzled)
   static constexpr int K_OFF = Q_OFF + 65536;      // K ring: 2 stages x 2 blocks [128 keys][64 dims]
   static constexpr int V_OFF = K_OFF + 65536;      // V ring: same
-  static constexpr int P_OFF = V_OFF + 65536;      // P: 2 blocks [128 q][64 keys], shared by the two heads
-  static constexpr int BAR_OFF = P_OFF + 32768;    // mbarriers (8 bytes each)
+  static constexpr int BAR_OFF = V_OFF + 65536;    // mbarriers (8 bytes each)
   static constexpr int NBAR = 16;
   static constexpr int FLAG_OFF = BAR_OFF + 8 * NBAR;
   static constexpr int USED = FLAG_OFF + 16;
@@ -52,9 +52,10 @@ struct AttnTcSmem {
 static_assert(AttnTcSmem::DYN <= 232448, "shared memory per CTA");
 static_assert(TQ * AttnTcSmem::OST <= 65536, "output staging of one head fits one ring");
 
-// mbarrier slots: per head h (0 = A, 1 = B) S ready, S read (free), P written, O updated (PV done)
-constexpr int B_Q = 0, B_K = 1, B_V = 3, B_EMPTY = 5, B_S = 7, B_F = 9, B_P = 11, B_O = 13, B_DONE = 15;
-// TMEM columns: head h's score buffer at T_S + 128 h, its output accumulator at T_O + 128 h
+// mbarrier slots (per head h: Q loaded, S ready, P written, O updated)
+constexpr int B_Q = 0, B_K = 2, B_V = 4, B_EMPTY = 6, B_S = 8, B_P = 10, B_O = 12, B_DONE = 14;
+// TMEM columns: head h's scores (and then its P, two bf16 per column, in the first 64) at T_S + 128 h, its output
+// accumulator at T_O + 128 h
 constexpr uint32_t T_S = 0, T_O = 256;
 
 struct AttnTcParams {
@@ -95,6 +96,13 @@ __device__ __forceinline__ uint64_t desc_mn(uint32_t saddr, uint32_t mn_block) {
   return d;
 }
 constexpr uint32_t IDESC_B_MN_MAJOR = 1u << 16;
+// MMA with the A operand in TMEM (K-major, two bf16 per 32-bit column, lane = row)
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\ntcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n"
+      ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate));
+}
 
 // grid (head pairs * nseq, q tiles): x = pair + pairs * sequence, pair = key/value head * pairs_per_kv + p; y counts
 // query tiles from the last, so the CTAs with the longest key ranges are dispatched first and the short ones fill
@@ -120,7 +128,7 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
   const int rows = min(TQ, qlen - q0);
   const int total = start + qlen;           // keys of the sequence
   const int kend = start + q0 + rows;       // keys any row of this tile can see
-  const int nkt = (kend + TK - 1) / TK;     // >= 1
+  const int nkt = (kend + TK - 1) / TK;     // >= 1; only the last tile can reach past the sequence's last key
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const uint32_t sb = smem_addr(smem);
   auto bar = [&](int i) { return sb + L::BAR_OFF + 8 * i; };
@@ -128,13 +136,12 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::FLAG_OFF + 4);
 
   if (tid == 0) {
-    mbar_init(bar(B_Q), 128);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(B_Q + s), 128);
       mbar_init(bar(B_K + s), 1);
       mbar_init(bar(B_V + s), 1);
       mbar_init(bar(B_EMPTY + s), 1);
       mbar_init(bar(B_S + s), 1);
-      mbar_init(bar(B_F + s), 128);
       mbar_init(bar(B_P + s), 128);
       mbar_init(bar(B_O + s), 1);
     }
@@ -153,7 +160,7 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- copies: K and V tiles, page by page
     const int bs = P.block_size, nb = TK / bs;  // boxes per tile and 64-dim half (nb <= 16)
     const int32_t* btab = P.block_table + static_cast<int64_t>(seq) * P.bt_stride;
@@ -204,12 +211,12 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
-    // ---------------------------------------------------------------- MMAs (one thread)
+  } else if (warp == 9) {
+    // ---------------------------------------------------------------- MMAs (one thread), head by head as ready
     if (lane == 0) {
       constexpr uint32_t id_s = umma_idesc_mn(TQ, TK);
       constexpr uint32_t id_o = umma_idesc_mn(TQ, THD) | IDESC_B_MN_MAJOR;
-      auto issue_s = [&](int h, int j) {  // S_h(j) = Q_h K_j^T into head h's score buffer
+      auto issue_s = [&](int h, int j) {  // S_h(j) = Q_h K_j^T into head h's score columns
         const uint32_t kst = sb + L::K_OFF + (j & 1) * 32768;
 #pragma unroll
         for (int kk = 0; kk < THD / 16; ++kk) {
@@ -219,188 +226,183 @@ __global__ void __launch_bounds__(TTHR, 1) attn_prefill_tc_kernel(const __grid_c
         }
         umma_commit(bar(B_S + h));
       };
-      auto issue_pv = [&](int h, int j) {  // O_h += P V_j, K = keys
+      auto issue_pv = [&](int h, int j) {  // O_h += P_h V_j (K = keys; P from TMEM, 16 keys = 8 columns per step)
         const uint32_t vst = sb + L::V_OFF + (j & 1) * 32768;
 #pragma unroll
         for (int kk = 0; kk < TK / 16; ++kk)
-          umma_f16(tmem + T_O + h * THD, umma_desc(sb + L::P_OFF + (kk >> 2) * 16384 + (kk & 3) * 32),
-                   desc_mn(vst + kk * 2048, 16384), id_o, (j | kk) != 0);
-        umma_commit(bar(B_O + h));  // PV_h(j) done: O_h stable, P free
+          umma_f16_ts(tmem + T_O + h * THD, tmem + T_S + h * TK + kk * 8, desc_mn(vst + kk * 2048, 16384), id_o,
+                      (j | kk) != 0);
+        umma_commit(bar(B_O + h));  // PV_h(j) done: O_h stable, P_h's columns free
       };
-      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, P.err) && mbar_wait(bar(B_K), 0, abort_flag, P.err);
+      bool ok = mbar_wait(bar(B_Q), 0, abort_flag, P.err) && (nh < 2 || mbar_wait(bar(B_Q + 1), 0, abort_flag, P.err)) &&
+                mbar_wait(bar(B_K), 0, abort_flag, P.err);
       if (ok) {
         tc_fence_after();
         for (int h = 0; h < nh; ++h) issue_s(h, 0);
       }
-      for (int j = 0; ok && j < nkt; ++j) {
-        const bool next = j + 1 < nkt;
-        for (int h = 0; ok && h < nh; ++h) {
-          if (next) {  // S_h(j + 1) once the threads have read S_h(j) and K_{j+1} has landed
-            if (!(ok = mbar_wait(bar(B_F + h), j & 1, abort_flag, P.err))) break;
-            if (h == 0 && !(ok = mbar_wait(bar(B_K + ((j + 1) & 1)), ((j + 1) >> 1) & 1, abort_flag, P.err))) break;
+      int jp[2] = {0, nh > 1 ? 0 : nkt};  // next PV tile per head
+      int js[2] = {1, nh > 1 ? 1 : nkt + 1};  // next S tile per head (S(0) issued)
+      long long last = clock64();
+      while (ok && (jp[0] < nkt || jp[1] < nkt)) {
+        bool progressed = false;
+        for (int h = 0; h < 2; ++h) {
+          const int j = jp[h];
+          if (j < nkt && js[h] == j + 1) {  // next: PV_h(j), once P_h(j) is written and V_j has landed (on the
+                                            // last tile, head B's after head A's, whose warps zero the V tail)
+            if (h == 1 && j == nkt - 1 && jp[0] <= j) continue;
+            if (!mbar_try(bar(B_P + h), j & 1) || !mbar_try(bar(B_V + (j & 1)), (j >> 1) & 1)) continue;
             tc_fence_after();
-            issue_s(h, j + 1);
+            issue_pv(h, j);
+            jp[h] = j + 1;
+            if (jp[1 - h] > j) umma_commit(bar(B_EMPTY + (j & 1)));  // both heads' MMAs reading K_j, V_j issued
+            progressed = true;
+          } else if (js[h] < nkt && js[h] == j) {  // next: S_h(js), once PV_h(js - 1) is done and K_js has landed
+            const int k = js[h];
+            if (!mbar_try(bar(B_O + h), (k - 1) & 1) || !mbar_try(bar(B_K + (k & 1)), (k >> 1) & 1)) continue;
+            tc_fence_after();
+            issue_s(h, k);
+            js[h] = k + 1;
+            progressed = true;
           }
-          if (!(ok = mbar_wait(bar(B_P + h), j & 1, abort_flag, P.err))) break;  // P_h(j) written
-          if (h == 0 && !(ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err))) break;
-          tc_fence_after();
-          issue_pv(h, j);
         }
-        if (ok) umma_commit(bar(B_EMPTY + (j & 1)));  // every MMA reading K_j and V_j has been issued
+        if (progressed) {
+          last = clock64();
+        } else if (*abort_flag) {
+          ok = false;
+        } else if (clock64() - last > WAIT_BUDGET_CYCLES) {
+          *abort_flag = 1;
+          flag_error(P.err, DEVERR_TIMEOUT);
+          ok = false;
+        }
       }
       umma_commit(bar(B_DONE));  // arrives once every MMA issued above has completed
     }
     __syncwarp();
-  } else {
-    // ---------------------------------------------------------------- warps 0-3: Q, softmax, epilogue
-    const int r = tid;  // query row = TMEM lane
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    // Q tiles: thread i copies 16-byte chunk i % 16 of rows i / 16 + 8 n of each head (rows past the sequence:
-    // zeros)
-    for (int h = 0; h < nh; ++h) {
-      for (int i = tid; i < TQ * 16; i += 128) {
-        const int qr = i >> 4, c = i & 15;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (qr < rows)
-          v = ld16(P.q + static_cast<int64_t>(qbase + q0 + qr) * P.q_t + (head_a + h) * P.q_h + c * 8);
-        *reinterpret_cast<uint4*>(smem + L::Q_OFF + h * 32768 + (c >> 3) * 16384 + swz128(qr, c & 7)) = v;
-      }
+  } else if (warp / 4 < nh) {
+    // ---------------------------------------------------------------- warps 0-3 / 4-7: Q, softmax, epilogue
+    const int h = warp / 4;
+    const int r = tid & 127;  // query row = TMEM lane
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t t_s = t_lane + T_S + h * TK, t_o = t_lane + T_O + h * THD;
+    // Q tile: thread i copies 16-byte chunk i % 16 of rows i / 16 + 8 n (rows past the sequence: zeros)
+    for (int i = r; i < TQ * 16; i += 128) {
+      const int qr = i >> 4, c = i & 15;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (qr < rows) v = ld16(P.q + static_cast<int64_t>(qbase + q0 + qr) * P.q_t + (head_a + h) * P.q_h + c * 8);
+      *reinterpret_cast<uint4*>(smem + L::Q_OFF + h * 32768 + (c >> 3) * 16384 + swz128(qr, c & 7)) = v;
     }
     asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic writes -> tensor core reads
-    mbar_arrive(bar(B_Q));
+    mbar_arrive(bar(B_Q + h));
 
     const int qpos = start + q0 + r;          // this row's position (rows >= `rows` are padding)
     const int vis = min(qpos, total - 1);     // last key this row sees
     const float sl = P.scale_log2;
-    float m_used[2] = {-INFINITY, -INFINITY};  // running maxima in the exp2 domain (lazy)
-    float lsum[2] = {0.f, 0.f};
+    float m_used = -INFINITY;                 // running maximum in the exp2 domain (lazy)
+    float lsum = 0.f;
     bool ok = true;
     int j = 0;
-    for (; ok && j < nkt; ++j) {
+    for (; j < nkt; ++j) {
+      ok = mbar_wait(bar(B_S + h), j & 1, abort_flag, P.err);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      tc_fence_after();
+      uint32_t s[TK];
+#pragma unroll
+      for (int c = 0; c < TK / 16; ++c) tmem_ld16_nw(t_s + c * 16, s + c * 16);
+      tmem_wait();
       const int k0 = j * TK;
       const int lim = vis - k0;  // keys k0 + c with c <= lim are visible
-      for (int h = 0; h < nh; ++h) {
-        ok = mbar_wait(bar(B_S + h), j & 1, abort_flag, P.err);
-        if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        tc_fence_after();
-        uint32_t s[TK];
+      float mx = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < TK / 16; ++c) tmem_ld16_nw(t_lane + T_S + h * TK + c * 16, s + c * 16);
-        tmem_wait();
-        tc_fence_before();  // the score reads precede the next S MMA into this buffer
-        mbar_arrive(bar(B_F + h));
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < TK; ++c) {
-          const float v = c <= lim ? __uint_as_float(s[c]) : -INFINITY;
-          s[c] = __float_as_uint(v);
-          mx = fmaxf(mx, v);
+      for (int c = 0; c < TK; ++c) {
+        const float v = c <= lim ? __uint_as_float(s[c]) : -INFINITY;
+        s[c] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = mx * sl;
+      const bool need = m_new > m_used + 8.f;  // false for -inf / NaN maxima
+      if (__any_sync(0xffffffffu, need)) {
+        const float alpha = need ? ex2f(m_used - m_new) : 1.f;  // 0 on the first visible tile
+        if (need) {
+          m_used = m_new;
+          lsum *= alpha;
         }
-        const float m_new = mx * sl;
-        const bool need = m_new > m_used[h] + 8.f;  // false for -inf / NaN maxima
-        if (__any_sync(0xffffffffu, need)) {
-          const float alpha = need ? ex2f(m_used[h] - m_new) : 1.f;  // 0 on the first visible tile
-          if (need) {
-            m_used[h] = m_new;
-            lsum[h] *= alpha;
-          }
-          if (j > 0) {  // O_h holds PV_h(0 .. j-1): wait for the last, then rescale this row in TMEM
-            ok = mbar_wait(bar(B_O + h), (j - 1) & 1, abort_flag, P.err);
-            if (!(ok = __all_sync(0xffffffffu, ok))) break;
-            tc_fence_after();
+        if (j > 0) {  // O holds PV(0 .. j-1), all complete (S(j) was issued after the last of them): rescale
 #pragma unroll 1
-            for (int c = 0; c < THD; c += 32) {
-              uint32_t o[32];
-              tmem_ld16_nw(t_lane + T_O + h * THD + c, o);
-              tmem_ld16_nw(t_lane + T_O + h * THD + c + 16, o + 16);
-              tmem_wait();
+          for (int c = 0; c < THD; c += 32) {
+            uint32_t o[32];
+            tmem_ld16_nw(t_o + c, o);
+            tmem_ld16_nw(t_o + c + 16, o + 16);
+            tmem_wait();
 #pragma unroll
-              for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-              tmem_st16(t_lane + T_O + h * THD + c, o);
-              tmem_st16(t_lane + T_O + h * THD + c + 16, o + 16);
-            }
-            tmem_wait_st();
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st16(t_o + c, o);
+            tmem_st16(t_o + c + 16, o + 16);
           }
         }
-        const float base = m_used[h] == -INFINITY ? 0.f : m_used[h];
-        float part = 0.f;
+      }
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      float part = 0.f;
 #pragma unroll
-        for (int c = 0; c < TK; ++c) {
-          const float p = ex2f(fmaf(__uint_as_float(s[c]), sl, -base));
-          s[c] = __float_as_uint(p);
-          part += p;
-        }
-        lsum[h] += part;
-        // the shared P buffer is free once the PV that read it last is done: head B's of the previous tile
-        // before head A writes (head A's own with a single head), head A's of this tile before head B writes
-        const int ph = h == 1 ? 0 : nh - 1, pj = h == 1 ? j : j - 1;
-        if (pj >= 0) {
-          ok = mbar_wait(bar(B_O + ph), pj & 1, abort_flag, P.err);
-          if (!(ok = __all_sync(0xffffffffu, ok))) break;
-        }
-        if (h == 0 && k0 + TK > total) {
-          // value rows past the sequence's last key (the tail of its last page) may hold anything: zero them
-          // once the tile has landed, before PV_A(j), their first reader
-          ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err);
-          if (!(ok = __all_sync(0xffffffffu, ok))) break;
-          if (r >= total - k0) {
-            uint8_t* vrow = smem + L::V_OFF + (j & 1) * 32768 + r * 128;
+      for (int c = 0; c < TK; c += 2) {
+        const float p0 = ex2f(fmaf(__uint_as_float(s[c]), sl, -base));
+        const float p1 = ex2f(fmaf(__uint_as_float(s[c + 1]), sl, -base));
+        part += p0 + p1;
+        s[c / 2] = pack_bf16x2(p0, p1);  // P (bf16 pairs) in place: column c / 2 of the score columns
+      }
+      lsum += part;
+      if (h == 0 && k0 + TK > total) {
+        // value rows past the sequence's last key (the tail of its last page) may hold anything: zero them once
+        // the tile has landed, before the PVs of either head read it
+        ok = mbar_wait(bar(B_V + (j & 1)), (j >> 1) & 1, abort_flag, P.err);
+        if (!(ok = __all_sync(0xffffffffu, ok))) break;
+        if (r >= total - k0) {
+          uint8_t* vrow = smem + L::V_OFF + (j & 1) * 32768 + r * 128;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
-              *reinterpret_cast<uint4*>(vrow + 16384 + c * 16) = make_uint4(0, 0, 0, 0);
-            }
+          for (int c = 0; c < 8; ++c) {
+            *reinterpret_cast<uint4*>(vrow + c * 16) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(vrow + 16384 + c * 16) = make_uint4(0, 0, 0, 0);
           }
-        }
-        // P row r (bf16) into the K-major operand layout: keys 0-63 in block 0, 64-127 in block 1
-#pragma unroll
-        for (int c8 = 0; c8 < TK / 8; ++c8) {
-          const uint32_t* pv = s + c8 * 8;
-          *reinterpret_cast<uint4*>(smem + L::P_OFF + (c8 >> 3) * 16384 + swz128(r, c8 & 7)) = make_uint4(
-              pack_bf16x2(__uint_as_float(pv[0]), __uint_as_float(pv[1])),
-              pack_bf16x2(__uint_as_float(pv[2]), __uint_as_float(pv[3])),
-              pack_bf16x2(__uint_as_float(pv[4]), __uint_as_float(pv[5])),
-              pack_bf16x2(__uint_as_float(pv[6]), __uint_as_float(pv[7])));
         }
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
-        tc_fence_before();  // this thread's O writes precede the MMAs issued after the arrive
-        mbar_arrive(bar(B_P + h));
       }
-    }
-    // epilogue per head: wait for its last PV, normalise, stage bf16 rows in an idle ring, store coalesced
-    bool fin = ok && j == nkt && !*abort_flag;
-    for (int h = 0; h < nh; ++h) {
-      bool okh = fin && mbar_wait(bar(B_O + h), (nkt - 1) & 1, abort_flag, P.err);
-      okh = __all_sync(0xffffffffu, okh);
-      if (okh) {
-        tc_fence_after();
-        const float inv = lsum[h] > 0.f ? 1.f / lsum[h] : 0.f;
-        uint8_t* orow = smem + (h ? L::V_OFF : L::K_OFF) + r * L::OST;
-#pragma unroll 1
-        for (int c = 0; c < THD; c += 32) {
-          uint32_t o[32];
-          tmem_ld16_nw(t_lane + T_O + h * THD + c, o);
-          tmem_ld16_nw(t_lane + T_O + h * THD + c + 16, o + 16);
-          tmem_wait();
 #pragma unroll
-          for (int e = 0; e < 32; e += 8)
-            *reinterpret_cast<uint4*>(orow + (c + e) * 2) = make_uint4(
-                pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
-                pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
-                pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
-                pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
-        }
+      for (int c = 0; c < TK / 2; c += 16) tmem_st16(t_s + c, s + c);
+      tmem_wait_st();
+      tc_fence_before();  // the P and O writes precede the MMAs issued after the arrive
+      mbar_arrive(bar(B_P + h));
+    }
+    // epilogue: once every MMA is done (the K / V rings are then idle), normalise O, stage bf16 rows in this
+    // head's ring, store coalesced
+    bool fin = ok && j == nkt && !*abort_flag;
+    fin = fin && mbar_wait(bar(B_DONE), 0, abort_flag, P.err);
+    fin = __all_sync(0xffffffffu, fin);
+    if (fin) {
+      tc_fence_after();
+      const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+      uint8_t* orow = smem + (h ? L::V_OFF : L::K_OFF) + r * L::OST;
+#pragma unroll 1
+      for (int c = 0; c < THD; c += 32) {
+        uint32_t o[32];
+        tmem_ld16_nw(t_o + c, o);
+        tmem_ld16_nw(t_o + c + 16, o + 16);
+        tmem_wait();
+#pragma unroll
+        for (int e = 0; e < 32; e += 8)
+          *reinterpret_cast<uint4*>(orow + (c + e) * 2) = make_uint4(
+              pack_bf16x2(__uint_as_float(o[e]) * inv, __uint_as_float(o[e + 1]) * inv),
+              pack_bf16x2(__uint_as_float(o[e + 2]) * inv, __uint_as_float(o[e + 3]) * inv),
+              pack_bf16x2(__uint_as_float(o[e + 4]) * inv, __uint_as_float(o[e + 5]) * inv),
+              pack_bf16x2(__uint_as_float(o[e + 6]) * inv, __uint_as_float(o[e + 7]) * inv));
       }
     }
-    asm volatile("bar.sync 1, 128;\n" ::: "memory");  // the four softmax warps only
+    if (h == 0) asm volatile("bar.sync 1, 128;\n" ::: "memory");  // this head's four warps only
+    else asm volatile("bar.sync 2, 128;\n" ::: "memory");
     if (!*abort_flag) {
-      for (int h = 0; h < nh; ++h) {
-        const uint8_t* stage = smem + (h ? L::V_OFF : L::K_OFF);
-        for (int i = tid; i < rows * (THD / 8); i += 128) {
-          const int qr = i / (THD / 8), c = i % (THD / 8);
-          st16(P.out + static_cast<int64_t>(qbase + q0 + qr) * P.o_t + (head_a + h) * P.o_h + c * 8,
-               *reinterpret_cast<const uint4*>(stage + qr * L::OST + c * 16));
-        }
+      const uint8_t* stage = smem + (h ? L::V_OFF : L::K_OFF);
+      for (int i = r; i < rows * (THD / 8); i += 128) {
+        const int qr = i / (THD / 8), c = i % (THD / 8);
+        st16(P.out + static_cast<int64_t>(qbase + q0 + qr) * P.o_t + (head_a + h) * P.o_h + c * 8,
+             *reinterpret_cast<const uint4*>(stage + qr * L::OST + c * 16));
       }
     }
   }

@@ -5,21 +5,23 @@
 // One CTA owns one head of one sequence and walks its chunks of 64 tokens in order. The fp32 state S [p = 128, N]
 // lives in TMEM for the whole walk (lane = p, column = n). Per chunk, with cum the running sum of dt' A inside the
 // chunk, the work is split over warp roles that run concurrently:
-//   * warp 8 (one thread) streams C, B [64 x N] and x [64 x 128] of each chunk through a two-stage ring of
-//     128-byte-swizzled TMA boxes, a chunk ahead of the math;
-//   * warp 9 (one thread) issues the MMAs: G = C B^T (M = 64 t, N = 64 s, K = N) into TMEM; then
-//     Y = x^T M^T + S_bf C'^T (M = 128 p, N = 64 t; the second term reads the bf16 copy of the incoming state
-//     straight from TMEM as its A operand, and C' = exp(cum_t) C_t carries the state term's decay) and
-//     S += x^T (w B) (M = 128 p, N = N); then the next chunk's G;
-//   * warps 0-3 (one state row p per thread) run the state pass once the previous chunk's update is done: the
-//     bf16 copy of S into TMEM for Y's state term and exp(cum_last) S back into the fp32 columns;
-//   * warps 4-7 run the per-chunk scan of dt (softplus, running sum, weights), turn G into M[t][s] =
-//     G exp(cum_t - cum_s) dt_s (s <= t, D on the diagonal, so the product also carries the D x skip term),
-//     scale C's rows by exp(cum_t) and B's rows by w_s = exp(cum_last - cum_s) dt_s in place, and finally read
-//     Y out of TMEM, stage the bf16 y tile and store it with 16-byte writes.
-// The critical path per chunk is the update MMA, the state pass and the next Y and update MMAs; loads, the M
-// build and the y stores run under them. Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out
-// of budget flags the error word, leaves its state line untouched, drains its copies and MMAs and frees TMEM.
+//   * warp 8: one thread streams C, B [64 x N] and x [64 x 128] of each chunk through a two-stage ring of
+//     128-byte-swizzled TMA boxes, a chunk ahead of the math; then the whole warp runs the chunk's scan of dt
+//     (softplus, running sum, update weights, decays) into a four-deep ring of small shared-memory buffers;
+//   * warp 9 (one thread) issues the MMAs: G = C B^T (M = 64 t, N = 64 s, K = N); Y = x^T M^T and
+//     YS = S_bf C^T (M = 128 p, N = 64 t; the second reads the bf16 copy of the incoming state straight from TMEM
+//     as its A operand, and shares its TMEM columns with G); S += (w x)^T B (M = 128 p, N = N);
+//   * warps 0-3 (one state row p per thread): the weighted copy w x of the chunk's x rows (w_s = exp(cum_last -
+//     cum_s) dt_s; double-buffered, made while the previous update still runs), then, once that update is done,
+//     the state pass: the bf16 copy of S into TMEM and exp(cum_last) S back into the fp32 columns;
+//   * warps 4-7 turn G into M[t][s] = G exp(cum_t - cum_s) dt_s (s <= t, D on the diagonal, so the product also
+//     carries the D x skip term), all 128 lanes on 32 elements each; read Y and YS out of TMEM as soon as they
+//     are done, build the next chunk's M, and then y = Y + exp(cum_t) YS is staged as bf16 and stored with
+//     16-byte writes.
+// The critical path per chunk is the update MMA, the state pass and the next Y and update MMAs; loads, the scan,
+// the weighted x, G, the M build and the y stores run under them. Every mbarrier wait is bounded (tc_common.cuh); a CTA
+// that runs out of budget flags the error word, leaves its state line untouched, drains its copies and MMAs and
+// frees TMEM.
 #include <algorithm>
 
 #include "mmp_common.cuh"
@@ -52,9 +54,10 @@ struct TcSsdSmem {
   static constexpr int M_OFF = 2 * STAGE;             // M: [64 t x 128 B] (s)
   static constexpr int YLD = SP * 2 + 16;             // y tile row bytes (padded)
   static constexpr int Y_OFF = M_OFF + 8192;          // y tile [64 t][128 p] bf16
-  static constexpr int CUM_OFF = Y_OFF + SQ * YLD;    // per chunk parity: cum, dt, w, exp(cum) [64] fp32 + decay
+  static constexpr int XW_OFF = Y_OFF + SQ * YLD;     // w-weighted x, per chunk parity: 2 blocks [64 t x 128 B]
+  static constexpr int CUM_OFF = XW_OFF + 2 * 16384;  // per chunk (ring of 4): cum log2e, dt, w, exp(cum) [64] + decay
   static constexpr int CUM_BYTES = 4 * SQ * 4 + 16;
-  static constexpr int BAR_OFF = CUM_OFF + 2 * CUM_BYTES;
+  static constexpr int BAR_OFF = CUM_OFF + 4 * CUM_BYTES;
   static constexpr int NBAR = 16;
   static constexpr int USED = BAR_OFF + 8 * NBAR + 16;
   static constexpr int DYN = USED + 1024;
@@ -62,16 +65,18 @@ struct TcSsdSmem {
 };
 static_assert(TcSsdSmem<256>::DYN <= 232448, "shared memory per CTA");
 
-// TMEM columns: fp32 state [N], bf16 state copy [N / 2] (two values per column), Y [64], G [64]
+// TMEM columns: fp32 state [N], bf16 state copy [N / 2] (two values per column), Y [64], and G / YS [64] (G is read
+// out before YS is written into the same columns, and YS before the next G)
 template <int N>
 struct TcSsdTmem {
-  static constexpr uint32_t S = 0, SBF = N, Y = N + N / 2, G = N + N / 2 + 64;
+  static constexpr uint32_t S = 0, SBF = N, Y = N + N / 2, G = N + N / 2 + 64, YS = G;
 };
 static_assert(TcSsdTmem<256>::G + 64 <= 512, "TMEM columns");
 
 // mbarriers
-constexpr int B_FULL = 0, B_EMPTY = 2, B_G = 4, B_MB = 5, B_SP = 6, B_YFREE = 7, B_Y = 8, B_S = 9, B_SCAN = 10,
-              B_DONE = 11;
+// (B_SCAN + i: the scan results in ring slot i are written; phase = chunk / 4, so no waiter can fall two phases
+// behind: a slot is rewritten only after every reader of its previous chunk is done)
+constexpr int B_FULL = 0, B_EMPTY = 2, B_G = 4, B_MB = 5, B_YFREE = 7, B_Y = 8, B_S = 9, B_SCAN = 10, B_DONE = 14;
 
 // byte offset of 16-byte chunk c of row r in a 128-byte-swizzled block of 128-byte rows
 __device__ __forceinline__ uint32_t sw(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
@@ -99,6 +104,11 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
 }
 __device__ __forceinline__ void mbar_arrive1(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ float ex2f(float x) {  // 2^x on the MUFU unit (ex2.approx.ftz)
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;\n" : "=f"(y) : "f"(x));
+  return y;
 }
 // AND of `v` over the `nthreads` threads of named barrier `id` (a barrier for them too): a decision every warp of
 // a group takes alike, so that none leaves a loop while the others wait at the group's next barrier
@@ -141,8 +151,9 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 8 * L::NBAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 8 * L::NBAR + 4);
   ST* gstate = reinterpret_cast<ST*>(P.state) + line * P.s_line + h * P.s_head;
-  // per-chunk scan results, double-buffered by chunk parity
-  auto cum_buf = [&](int c) { return reinterpret_cast<float*>(smem + L::CUM_OFF + (c & 1) * L::CUM_BYTES); };
+  // per-chunk scan results, a ring of four (chunk c's buffer is rewritten by chunk c + 4, whose loads wait for
+  // chunk c + 2's MMAs, which come after every reader of chunk c's buffer): cum log2(e), dt', w, exp(cum), decay
+  auto cum_buf = [&](int c) { return reinterpret_cast<float*>(smem + L::CUM_OFF + (c & 3) * L::CUM_BYTES); };
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -150,12 +161,11 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       mbar_init(bar(B_EMPTY + s), 1);
     }
     mbar_init(bar(B_G), 1);
-    mbar_init(bar(B_MB), 128);
-    mbar_init(bar(B_SP), 128);
+    mbar_init(bar(B_MB), 256);
     mbar_init(bar(B_YFREE), 128);
     mbar_init(bar(B_Y), 1);
     mbar_init(bar(B_S), 1);
-    mbar_init(bar(B_SCAN), 128);
+    for (int i = 0; i < 4; ++i) mbar_init(bar(B_SCAN + i), 32);
     mbar_init(bar(B_DONE), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
@@ -173,28 +183,76 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 8) {
-    // ------------------------------------------------------------------ copies: one chunk's boxes per stage
-    if (lane == 0) {
-      int issued = 0;
-      for (int c = 0; c < nchunks; ++c) {
-        const int s = c & 1;
-        if (c >= 2 && !mbar_wait(bar(B_EMPTY + s), ((c >> 1) - 1) & 1, abort_flag, P.err)) break;
-        if (*abort_flag) break;
-        const int c0 = t_begin + c * SQ;
-        const uint32_t st = sb + s * L::STAGE;
-        mbar_expect_tx(bar(B_FULL + s), L::LOAD_BYTES);
+    // ------------------------------------------------------------------ copies (one thread), then the scan (warp)
+    int issued = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int s = c & 1;
+      const int c0 = t_begin + c * SQ;
+      int go = 1;
+      if (lane == 0) {
+        if (c >= 2 && !mbar_wait(bar(B_EMPTY + s), ((c >> 1) - 1) & 1, abort_flag, P.err)) go = 0;
+        if (*abort_flag) go = 0;
+        if (go) {
+          const uint32_t st = sb + s * L::STAGE;
+          mbar_expect_tx(bar(B_FULL + s), L::LOAD_BYTES);
 #pragma unroll
-        for (int kb = 0; kb < L::KB; ++kb) {
-          tma_load_3d(st + L::C_OFF + kb * 8192, &mapC, bar(B_FULL + s), kb * 64, grp, c0);
-          tma_load_3d(st + L::B_OFF + kb * 8192, &mapB, bar(B_FULL + s), kb * 64, grp, c0);
+          for (int kb = 0; kb < L::KB; ++kb) {
+            tma_load_3d(st + L::C_OFF + kb * 8192, &mapC, bar(B_FULL + s), kb * 64, grp, c0);
+            tma_load_3d(st + L::B_OFF + kb * 8192, &mapB, bar(B_FULL + s), kb * 64, grp, c0);
+          }
+          tma_load_3d(st + L::X_OFF, &mapX, bar(B_FULL + s), 0, h, c0);
+          tma_load_3d(st + L::X_OFF + 8192, &mapX, bar(B_FULL + s), 64, h, c0);
+          if (c + 2 < nchunks) {  // the chunk after next into L2
+#pragma unroll
+            for (int kb = 0; kb < L::KB; ++kb) {
+              tma_prefetch_3d(&mapC, kb * 64, grp, c0 + 2 * SQ);
+              tma_prefetch_3d(&mapB, kb * 64, grp, c0 + 2 * SQ);
+            }
+            tma_prefetch_3d(&mapX, 0, h, c0 + 2 * SQ);
+            tma_prefetch_3d(&mapX, 64, h, c0 + 2 * SQ);
+          }
+          issued = c + 1;
         }
-        tma_load_3d(st + L::X_OFF, &mapX, bar(B_FULL + s), 0, h, c0);
-        tma_load_3d(st + L::X_OFF + 8192, &mapX, bar(B_FULL + s), 64, h, c0);
-        issued = c + 1;
       }
-      // copies in flight may still land after an abort: wait (bounded) for the last chunk of each stage
-      for (int c = max(0, issued - 2); c < issued; ++c) mbar_drain(bar(B_FULL + (c & 1)), (c >> 1) & 1);
+      if (!__shfl_sync(0xffffffffu, go, 0)) break;
+      // the scan: dt' = softplus(dt + bias), inclusive running sum of dt' A (kept times log2(e) for ex2), update
+      // weights w, exp(cum) and the chunk decay exp(cum_last)
+      const int qn = min(SQ, t_end - c0);
+      float* sCum = cum_buf(c);
+      float* sDt = sCum + SQ;
+      float* sW = sDt + SQ;
+      float* sE = sW + SQ;
+      float d[2], cs[2];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = lane * 2 + j;
+        d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) + dtb) : 0.f;
+      }
+      cs[0] = d[0] * A;
+      cs[1] = cs[0] + d[1] * A;
+      float run = cs[1];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float v = __shfl_up_sync(0xffffffffu, run, o);
+        if (lane >= o) run += v;
+      }
+      const float excl = run - cs[1];
+      const float cum_last = __shfl_sync(0xffffffffu, run, 31);  // tokens past qn add nothing
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int r = lane * 2 + j;
+        const float cum = excl + cs[j];
+        sDt[r] = d[j];
+        sCum[r] = cum * 1.4426950408889634f;
+        sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
+        sE[r] = __expf(cum);
+      }
+      if (lane == 0) sCum[4 * SQ] = __expf(cum_last);
+      mbar_arrive1(bar(B_SCAN + (c & 3)));
     }
+    // copies in flight may still land after an abort: wait (bounded) for the last chunk of each stage
+    if (lane == 0)
+      for (int c = max(0, issued - 2); c < issued; ++c) mbar_drain(bar(B_FULL + (c & 1)), (c >> 1) & 1);
     __syncwarp();
   } else if (warp == 9) {
     // ------------------------------------------------------------------ MMAs (one thread)
@@ -221,12 +279,11 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       for (int c = 0; ok && c < nchunks; ++c) {
         const uint32_t par = c & 1;
         const uint32_t st = sb + (c & 1) * L::STAGE;
-        // M, C' and w B built; the state pass done; the previous Y read out
+        // M built, the state pass done and B weighted; Y and YS of the previous chunk read out
         if (!(ok = mbar_wait(bar(B_MB), par, abort_flag, P.err))) break;
-        if (!(ok = mbar_wait(bar(B_SP), par, abort_flag, P.err))) break;
         if (c > 0 && !(ok = mbar_wait(bar(B_YFREE), par ^ 1, abort_flag, P.err))) break;
         tc_fence_after();
-        // Y = x^T M^T (K = s) + S_bf C'^T (K = n)
+        // Y = x^T M^T (K = s); YS = S_bf C^T (K = n), into G's columns (G is read out)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
           umma_f16(tmem + TM::Y, umma_desc_mn(st + L::X_OFF + kk * 2048, 8192), umma_desc(sb + L::M_OFF + kk * 32),
@@ -235,17 +292,18 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
         for (int kb = 0; kb < L::KB; ++kb)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_f16_ts(tmem + TM::Y, tmem + TM::SBF + kb * 32 + kk * 8,
-                        umma_desc(st + L::C_OFF + kb * 8192 + kk * 32), idy_s, 1);
+            umma_f16_ts(tmem + TM::YS, tmem + TM::SBF + kb * 32 + kk * 8,
+                        umma_desc(st + L::C_OFF + kb * 8192 + kk * 32), idy_s, (kb | kk) != 0);
         umma_commit(bar(B_Y));
-        // S += x^T (w B) (K = t)
+        // S += (w x)^T B (K = t)
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem + TM::S, umma_desc_mn(st + L::X_OFF + kk * 2048, 8192),
+          umma_f16(tmem + TM::S, umma_desc_mn(sb + L::XW_OFF + (c & 1) * 16384 + kk * 2048, 8192),
                    umma_desc_mn(st + L::B_OFF + kk * 2048, 8192), ids, 1);
         umma_commit(bar(B_S));
         umma_commit(bar(B_EMPTY + (c & 1)));  // every MMA reading this stage has been issued
-        if (c + 1 < nchunks) {  // the next chunk's G (its M build overlaps the next state pass)
+        if (c + 1 < nchunks) {  // the next chunk's G, once YS is read out of its columns
+          if (!(ok = mbar_wait(bar(B_YFREE), par, abort_flag, P.err))) break;
           if (!(ok = mbar_wait(bar(B_FULL + ((c + 1) & 1)), ((c + 1) >> 1) & 1, abort_flag, P.err))) break;
           tc_fence_after();
           issue_g(c + 1);
@@ -255,7 +313,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
     }
     __syncwarp();
   } else if (warp < 4) {
-    // ------------------------------------------------------------------ warps 0-3: the state in TMEM
+    // ------------------------------------------------------------------ warps 0-3: the state in TMEM, B weights
     const int p = tid;  // state row = TMEM lane
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const bool init = P.has_init && P.has_init[seq];
@@ -270,12 +328,32 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
     bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
       const uint32_t par = c & 1;
-      ok = mbar_wait(bar(B_SCAN), par, abort_flag, P.err);  // this chunk's decay
-      if (ok && c > 0) ok = mbar_wait(bar(B_S), par ^ 1, abort_flag, P.err);  // the previous update done
+      // this chunk's scan results and x tile: the weighted copy w x (row t = p / 2, one 64-wide block each)
+      ok = mbar_wait(bar(B_SCAN + (c & 3)), (c >> 2) & 1, abort_flag, P.err) &&
+           mbar_wait(bar(B_FULL + (c & 1)), (c >> 1) & 1, abort_flag, P.err);
+      if (!(ok = __all_sync(0xffffffffu, ok))) break;
+      const float* sCum = cum_buf(c);
+      {
+        const int t = p >> 1, blk = p & 1;
+        const float wt = sCum[2 * SQ + t];
+        const uint8_t* xs = smem + (c & 1) * L::STAGE + L::X_OFF + blk * 8192;
+        uint8_t* xd = smem + L::XW_OFF + (c & 1) * 16384 + blk * 8192;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint4 v = *reinterpret_cast<const uint4*>(xs + sw(t, k));
+          const float2 a0 = unpack_bf16x2(v.x), a1 = unpack_bf16x2(v.y), a2 = unpack_bf16x2(v.z),
+                       a3 = unpack_bf16x2(v.w);
+          *reinterpret_cast<uint4*>(xd + sw(t, k)) =
+              make_uint4(pack_bf16x2(a0.x * wt, a0.y * wt), pack_bf16x2(a1.x * wt, a1.y * wt),
+                         pack_bf16x2(a2.x * wt, a2.y * wt), pack_bf16x2(a3.x * wt, a3.y * wt));
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
+      if (c > 0) ok = mbar_wait(bar(B_S), par ^ 1, abort_flag, P.err);  // the previous update done
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
-      const float dec = cum_buf(c)[4 * SQ];
-      // bf16 copy of the incoming state (Y's state term) and the decayed state (the update accumulates on it)
+      const float dec = sCum[4 * SQ];
+      // bf16 copy of the incoming state (YS's A operand) and the decayed state (the update accumulates on it)
 #pragma unroll 1
       for (int c0n = 0; c0n < N; c0n += 64) {
         uint32_t r[64], b[32];
@@ -292,7 +370,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive1(bar(B_SP));
+      mbar_arrive1(bar(B_MB));
     }
     // final state -> the sequence's line (skipped after an abort: the line keeps its old value)
     if (ok && nchunks > 0) ok = mbar_wait(bar(B_S), (nchunks - 1) & 1, abort_flag, P.err);
@@ -309,122 +387,103 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       }
     }
   } else {
-    // ------------------------------------------------------------------ warps 4-7: scan, M, scaling, y
+    // ------------------------------------------------------------------ warps 4-7: M, then y
     const int tl = tid - 128;  // 0..127
     const int q = warp & 3;    // TMEM lane quadrant
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(q * 32) << 16);
-    for (int c = 0; c < nchunks; ++c) {
-      const uint32_t par = c & 1;
-      const int c0 = t_begin + c * SQ;
-      const int qn = min(SQ, t_end - c0);
-      const uint32_t st_off = (c & 1) * L::STAGE;
-      float* sCum = cum_buf(c);
-      float* sDt = sCum + SQ;
-      float* sW = sDt + SQ;
-      float* sE = sW + SQ;
-      if (warp == 4) {
-        // dt' = softplus(dt + bias), inclusive running sum of dt' A, update weights, chunk decay
-        float d[2], cs[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int r = lane * 2 + j;
-          d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) + dtb) : 0.f;
-        }
-        cs[0] = d[0] * A;
-        cs[1] = cs[0] + d[1] * A;
-        float run = cs[1];
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float v = __shfl_up_sync(0xffffffffu, run, o);
-          if (lane >= o) run += v;
-        }
-        const float excl = run - cs[1];
-        const float cum_last = __shfl_sync(0xffffffffu, run, 31);  // tokens past qn add nothing
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int r = lane * 2 + j;
-          const float cum = excl + cs[j];
-          sDt[r] = d[j];
-          sCum[r] = cum;
-          sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
-          sE[r] = __expf(cum);
-        }
-        if (lane == 0) sCum[4 * SQ] = __expf(cum_last);
-      }
-      asm volatile("bar.sync 2, 128;\n" ::: "memory");  // scan results visible to warps 4-7
-      mbar_arrive1(bar(B_SCAN));                          // and to the state pass (release)
-      if (!bar_and(2, 128, mbar_wait(bar(B_G), par, abort_flag, P.err))) break;
+    // G(c) -> M(c). The M=64 accumulator puts row t = 16 q + l in lane 32 q + l (l < 16) of quadrant q: lanes l and
+    // l + 16 share row t, columns 0-31 and 32-63 (the upper half passed over by a shuffle). False when a wait
+    // ran out (the same on every warp of the group).
+    auto build_m = [&](int c) -> bool {
+      const bool ok = mbar_wait(bar(B_SCAN + (c & 3)), (c >> 2) & 1, abort_flag, P.err) &&
+                      mbar_wait(bar(B_G), c & 1, abort_flag, P.err);
+      if (!bar_and(2, 128, ok)) return false;
       tc_fence_after();
-      // G -> M (masked, decayed, dt-weighted, D on the diagonal). M=64 accumulator: row t = 16 q + l sits in lane
-      // 32 q + l (l < 16) of quadrant q
-      {
-        uint32_t g[64];
-        tmem_ld64(t_lane + TM::G, g);
-        tmem_wait();
-        if (lane < 16) {
-          const int t = q * 16 + lane;
-          const float ct = sCum[t];
+      const float* sCum = cum_buf(c);
+      const float* sDt = sCum + SQ;
+      uint32_t g[64];
+      tmem_ld64(t_lane + TM::G, g);
+      tmem_wait();
+      tc_fence_before();  // G's columns are rewritten (YS) after the arrive below
+      const int l16 = lane & 15, cb = lane >= 16 ? 32 : 0;
+      const int t = q * 16 + l16;
+      float gv[32];
 #pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            uint32_t w4[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int s0 = c8 * 8 + 2 * j;
-              float a = (s0 <= t && s0 < qn) ? __uint_as_float(g[s0]) * __expf(ct - sCum[s0]) * sDt[s0] : 0.f;
-              float b = (s0 + 1 <= t && s0 + 1 < qn) ? __uint_as_float(g[s0 + 1]) * __expf(ct - sCum[s0 + 1]) * sDt[s0 + 1] : 0.f;
-              if (s0 == t) a += Dh;
-              if (s0 + 1 == t) b += Dh;
-              w4[j] = pack_bf16x2(a, b);
-            }
-            *reinterpret_cast<uint4*>(smem + L::M_OFF + sw(t, c8)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-          }
-        }
+      for (int j = 0; j < 32; ++j) {
+        const float hi = __uint_as_float(__shfl_sync(0xffffffffu, g[32 + j], l16));
+        gv[j] = lane >= 16 ? hi : __uint_as_float(g[j]);
       }
-      // C rows *= exp(cum_t), B rows *= w_s, in place (the G MMA is done with both): row tl / 2, half of its
-      // 16-byte chunks each
-      {
-        const int t = tl >> 1, part = tl & 1;
-        const float ec = sE[t], wb = sW[t];
-#pragma unroll 4
-        for (int i = 0; i < L::KB * 4; ++i) {
-          const int cidx = part * (L::KB * 4) + i;  // chunk along n: block cidx / 8, chunk cidx % 8
-          const uint32_t off = (cidx >> 3) * 8192 + sw(t, cidx & 7);
-          uint4* pc = reinterpret_cast<uint4*>(smem + st_off + L::C_OFF + off);
-          uint4* pb = reinterpret_cast<uint4*>(smem + st_off + L::B_OFF + off);
-          const uint4 vc = *pc, vb = *pb;
-          float2 a0 = unpack_bf16x2(vc.x), a1 = unpack_bf16x2(vc.y), a2 = unpack_bf16x2(vc.z), a3 = unpack_bf16x2(vc.w);
-          *pc = make_uint4(pack_bf16x2(a0.x * ec, a0.y * ec), pack_bf16x2(a1.x * ec, a1.y * ec),
-                           pack_bf16x2(a2.x * ec, a2.y * ec), pack_bf16x2(a3.x * ec, a3.y * ec));
-          a0 = unpack_bf16x2(vb.x), a1 = unpack_bf16x2(vb.y), a2 = unpack_bf16x2(vb.z), a3 = unpack_bf16x2(vb.w);
-          *pb = make_uint4(pack_bf16x2(a0.x * wb, a0.y * wb), pack_bf16x2(a1.x * wb, a1.y * wb),
-                           pack_bf16x2(a2.x * wb, a2.y * wb), pack_bf16x2(a3.x * wb, a3.y * wb));
+      const float ct = sCum[t];
+#pragma unroll
+      for (int c8 = 0; c8 < 4; ++c8) {
+        const float4 cs0 = *reinterpret_cast<const float4*>(sCum + cb + c8 * 8);
+        const float4 cs1 = *reinterpret_cast<const float4*>(sCum + cb + c8 * 8 + 4);
+        const float4 dt0 = *reinterpret_cast<const float4*>(sDt + cb + c8 * 8);
+        const float4 dt1 = *reinterpret_cast<const float4*>(sDt + cb + c8 * 8 + 4);
+        const float csv[8] = {cs0.x, cs0.y, cs0.z, cs0.w, cs1.x, cs1.y, cs1.z, cs1.w};
+        const float dtv[8] = {dt0.x, dt0.y, dt0.z, dt0.w, dt1.x, dt1.y, dt1.z, dt1.w};
+        float m[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const int sidx = cb + c8 * 8 + e;
+          // s <= t only: for s > t the exponent is positive and may overflow. dt' is 0 past the sequence
+          m[e] = sidx <= t ? gv[c8 * 8 + e] * ex2f(ct - csv[e]) * dtv[e] : 0.f;
+          if (sidx == t) m[e] += Dh;
         }
+        *reinterpret_cast<uint4*>(smem + L::M_OFF + sw(t, (cb >> 3) + c8)) =
+            make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
+                       pack_bf16x2(m[6], m[7]));
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
       tc_fence_before();
       mbar_arrive1(bar(B_MB));
-      // y = Y^T out of TMEM (lane p, column t), staged as [t][p] bf16 and stored
-      if (!bar_and(2, 128, mbar_wait(bar(B_Y), par, abort_flag, P.err))) break;
-      tc_fence_after();
-      {
-        uint32_t yv[64];
-        tmem_ld64(t_lane + TM::Y, yv);
-        tmem_wait();
-        tc_fence_before();
-        mbar_arrive1(bar(B_YFREE));  // Y may be overwritten by the next chunk
+      return true;
+    };
+    if (nchunks > 0 && build_m(0)) {
+      for (int c = 0; c < nchunks; ++c) {
+        const int c0 = t_begin + c * SQ;
+        const int qn = min(SQ, t_end - c0);
+        // y = Y + exp(cum_t) YS out of TMEM (lane p, column t), kept as bf16 pairs while the next M is built
+        if (!bar_and(2, 128, mbar_wait(bar(B_Y), c & 1, abort_flag, P.err))) break;
+        tc_fence_after();
+        uint32_t yp[32];
+        {
+          uint32_t yv[64], ys[64];
+          tmem_ld64(t_lane + TM::Y, yv);
+          tmem_ld64(t_lane + TM::YS, ys);
+          tmem_wait();
+          tc_fence_before();
+          mbar_arrive1(bar(B_YFREE));  // Y and YS may be overwritten
+          const float* sE = cum_buf(c) + 3 * SQ;
+#pragma unroll
+          for (int j4 = 0; j4 < 16; ++j4) {
+            const float4 e = *reinterpret_cast<const float4*>(sE + 4 * j4);
+            yp[2 * j4] = pack_bf16x2(fmaf(e.x, __uint_as_float(ys[4 * j4]), __uint_as_float(yv[4 * j4])),
+                                     fmaf(e.y, __uint_as_float(ys[4 * j4 + 1]), __uint_as_float(yv[4 * j4 + 1])));
+            yp[2 * j4 + 1] =
+                pack_bf16x2(fmaf(e.z, __uint_as_float(ys[4 * j4 + 2]), __uint_as_float(yv[4 * j4 + 2])),
+                            fmaf(e.w, __uint_as_float(ys[4 * j4 + 3]), __uint_as_float(yv[4 * j4 + 3])));
+          }
+        }
+        const bool more = c + 1 < nchunks && build_m(c + 1);
+        // stage the y tile as [t][p] and store it (the staging buffer's previous stores ended at the last barrier)
         const int pr = q * 32 + lane;
 #pragma unroll
-        for (int j = 0; j < 64; ++j)
-          *reinterpret_cast<bf16*>(smem + L::Y_OFF + j * L::YLD + pr * 2) = f2bf(__uint_as_float(yv[j]));
+        for (int j = 0; j < 32; ++j) {
+          *reinterpret_cast<uint16_t*>(smem + L::Y_OFF + (2 * j) * L::YLD + pr * 2) = static_cast<uint16_t>(yp[j]);
+          *reinterpret_cast<uint16_t*>(smem + L::Y_OFF + (2 * j + 1) * L::YLD + pr * 2) =
+              static_cast<uint16_t>(yp[j] >> 16);
+        }
+        asm volatile("bar.sync 2, 128;\n" ::: "memory");
+        for (int i = tl; i < SQ * (SP / 8); i += 128) {
+          const int t = i / (SP / 8), cc = i % (SP / 8);
+          if (t < qn)
+            st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + cc * 8,
+                 *reinterpret_cast<const uint4*>(smem + L::Y_OFF + t * L::YLD + cc * 16));
+        }
+        asm volatile("bar.sync 2, 128;\n" ::: "memory");  // the y tile is reusable
+        if (c + 1 < nchunks && !more) break;
       }
-      asm volatile("bar.sync 2, 128;\n" ::: "memory");
-      for (int i = tl; i < SQ * (SP / 8); i += 128) {
-        const int t = i / (SP / 8), cc = i % (SP / 8);
-        if (t < qn)
-          st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + cc * 8,
-               *reinterpret_cast<const uint4*>(smem + L::Y_OFF + t * L::YLD + cc * 16));
-      }
-      asm volatile("bar.sync 2, 128;\n" ::: "memory");  // the y tile and this chunk's scan buffer are reusable
     }
   }
 

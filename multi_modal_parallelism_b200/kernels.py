@@ -508,7 +508,7 @@ def ssd_prefill_segmented(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B:
 
 
 def set_attn_prefill_tc(enable: bool) -> bool:
-    """Select the tcgen05/TMEM kernel for attn_prefill (True) or the mma.sync kernel (False, the default);
+    """Select the tcgen05/TMEM kernel for attn_prefill (True, the default) or the mma.sync kernel (False);
     process-wide. Returns the previous setting."""
     return bool(_lib.lib().mmp_set_attn_prefill_tc(1 if enable else 0))
 

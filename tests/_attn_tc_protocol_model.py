@@ -1,6 +1,7 @@
 """Discrete-event model of the synchronisation of attn_prefill_tc_kernel (csrc/attn_prefill_tc.cu), test
-infrastructure. One CTA serves one or two query heads (A, B) with one score buffer and one output accumulator
-each, one shared P buffer and a two-stage K/V ring. mbarriers keep arrival counts, transaction bytes and a phase counter, with try_wait.parity's
+infrastructure. One CTA serves one or two query heads (A, B), each with its own softmax warpgroup, one TMEM score
+buffer (P is written over it) and one output accumulator, and a two-stage K/V ring; the MMA thread polls and
+issues each head's next MMA as soon as its inputs are ready. mbarriers keep arrival counts, transaction bytes and a phase counter, with try_wait.parity's
 meaning (true once the phase of that parity has completed; parity 1 passes before the first phase). The copy
 engine completes each page box at a random time; the tensor pipe completes MMAs in issue order at random times
 and a commit arrives once everything issued before it has completed. The producer (copies), the MMA thread and W
@@ -45,20 +46,20 @@ class Sim:
         self.rng = random.Random(seed)
         self.nkt, self.warps, self.nb, self.tail, self.rescale_p, self.bug = nkt, warps, nb, tail, rescale_p, bug
         self.heads = "AB"[:heads]
-        self.bars = {"Q": Bar(warps), "K0": Bar(1), "K1": Bar(1), "V0": Bar(1), "V1": Bar(1), "E0": Bar(1),
-                     "E1": Bar(1), "DONE": Bar(1)}
+        self.bars = {"K0": Bar(1), "K1": Bar(1), "V0": Bar(1), "V1": Bar(1), "E0": Bar(1), "E1": Bar(1),
+                     "DONE": Bar(1), "POLL": Bar(1)}
+        self.bars["POLL"].phase = 1  # a wait that always passes (the MMA thread's polling loop)
         for h in "AB":
-            self.bars.update({"S" + h: Bar(1), "F" + h: Bar(warps), "P" + h: Bar(warps), "O" + h: Bar(1)})
-        self.version = {"K0": None, "K1": None, "V0": None, "V1": None, "SA": None, "SB": None, "P": None,
-                        "OA": -1, "OB": -1}
+            self.bars.update({"Q" + h: Bar(warps), "S" + h: Bar(1), "P" + h: Bar(warps), "O" + h: Bar(1)})
+        # SA / SB hold ("S", j) after the score MMA, ("P", j) once every warp of the head wrote P over it
+        self.version = {"K0": None, "K1": None, "V0": None, "V1": None, "SA": None, "SB": None, "OA": -1, "OB": -1,
+                        "VZ": None}
         self.readers = {k: 0 for k in self.version}   # MMAs in flight reading the buffer
         self.writers = {k: 0 for k in self.version}   # copies or MMAs in flight writing it
-        self.warp_read = [{"SA": None, "SB": None} for _ in range(warps)]
-        self.p_rows = [None] * warps                   # P tile each warp's rows hold
+        self.p_written = {h: [None] * warps for h in "AB"}
         self.copies: list = []                          # in flight: (bar, bytes, buffer, tile)
         self.mma_q: list = []                           # in order: ("mma", reads, writes, tile) / ("commit", bar)
         self.errors: list[str] = []
-        self.q_written = 0
 
     def err(self, msg):
         self.errors.append(msg)
@@ -84,9 +85,10 @@ class Sim:
                 self.err(f"{what} reads {buf}: holds {self.version[buf]} (writers {self.writers[buf]}), needs {ver}")
             self.readers[buf] += 1
         for buf in writes:
-            if buf in ("SA", "SB") and self.version[buf] is not None and any(
-                    w[buf] != self.version[buf] for w in self.warp_read):
-                self.err(f"{what} overwrites {buf} before every warp read tile {self.version[buf]}")
+            if buf in ("SA", "SB") and self.readers[buf]:
+                self.err(f"{what} overwrites {buf} while a PV still reads P from it")
+            if buf in ("SA", "SB") and self.version[buf] is not None and self.version[buf][0] != "P":
+                self.err(f"{what} overwrites {buf} holding {self.version[buf]} before the warps turned it into P")
             self.writers[buf] += 1
         self.mma_q.append(("mma", reads, writes, what))
 
@@ -117,75 +119,79 @@ class Sim:
             self.issue_copy("V" + str(s), j)
 
     def mma(self):
-        yield ("Q", 0)
+        for h in self.heads:
+            yield ("Q" + h, 0)
         yield ("K0", 0)
         for h in self.heads:
-            self.issue_mma({"K0": 0}, {"S" + h: 0}, f"S{h}(0)")
+            self.issue_mma({"K0": 0}, {"S" + h: ("S", 0)}, f"S{h}(0)")
             self.commit("S" + h)
-        for j in range(self.nkt):
-            b = (j + 1) & 1
+        nh = len(self.heads)
+        jp = {h: 0 for h in self.heads}
+        js = {h: 1 for h in self.heads}
+        while any(jp[h] < self.nkt for h in self.heads):
+            progressed = False
             for h in self.heads:
-                if j + 1 < self.nkt:
-                    if self.bug != "s_before_read":
-                        yield ("F" + h, j & 1)
-                    if h == "A":
-                        yield ("K" + str(b), ((j + 1) >> 1) & 1)
-                    self.issue_mma({"K" + str(b): j + 1}, {"S" + h: j + 1}, f"S{h}({j + 1})")
+                j = jp[h]
+                if j < self.nkt and js[h] == j + 1:
+                    if h == "B" and j == self.nkt - 1 and jp["A"] <= j and self.bug != "tail_race":
+                        continue
+                    vb = "V" + str(j & 1)
+                    if not (self.bars["P" + h].passed(j & 1) and self.bars[vb].passed((j >> 1) & 1)):
+                        continue
+                    self.issue_mma({"S" + h: ("P", j), vb: j}, {"O" + h: j}, f"PV{h}({j})")
+                    if self.tail and j == self.nkt - 1 and self.version["VZ"] != j:
+                        self.err(f"PV{h}({j}) reads the value tile before its tail was zeroed")
+                    self.commit("O" + h)
+                    jp[h] = j + 1
+                    if nh == 1 or jp["B" if h == "A" else "A"] > j:
+                        self.commit("E" + str(j & 1))
+                    progressed = True
+                elif js[h] < self.nkt and js[h] == j:
+                    k = js[h]
+                    kb = "K" + str(k & 1)
+                    if not ((self.bug == "s_over_p" or self.bars["O" + h].passed((k - 1) & 1))
+                            and self.bars[kb].passed((k >> 1) & 1)):
+                        continue
+                    self.issue_mma({kb: k}, {"S" + h: ("S", k)}, f"S{h}({k})")
                     self.commit("S" + h)
-                yield ("P" + h, j & 1)
-                if h == "A" and self.bug != "pv_before_v":
-                    yield ("V" + str(j & 1), (j >> 1) & 1)
-                self.issue_mma({"P": (h, j), "V" + str(j & 1): j}, {"O" + h: j}, f"PV{h}({j})")
-                self.commit("O" + h)
-            self.commit("E" + str(j & 1))
+                    js[h] = k + 1
+                    progressed = True
+            yield ("POLL", 0)  # let other actors and engines move
         self.commit("DONE")
 
-    def softmax(self, w):
-        self.q_written += 1
-        self.bars["Q"].arrive()
-        nh = len(self.heads)
+    def softmax(self, h, w):
+        self.bars["Q" + h].arrive()
         for j in range(self.nkt):
-            for h in self.heads:
-                sb = "S" + h
-                yield (sb, j & 1)
-                if self.writers[sb] or self.version[sb] != j:
-                    self.err(f"warp {w} reads {sb} holding {self.version[sb]} (writers {self.writers[sb]}) "
-                             f"for tile {j}")
-                self.warp_read[w][sb] = j
-                self.bars["F" + h].arrive()
-                if j > 0 and self.rng.random() < self.rescale_p:  # a row maximum grew: rescale O_h
-                    yield ("O" + h, (j - 1) & 1)
-                    if self.writers["O" + h] or self.version["O" + h] != j - 1:
-                        self.err(f"warp {w} rescales O{h} holding {self.version['O' + h]} while PV runs (tile {j})")
-                # the P buffer's last reader: PV_B(j - 1) before A writes (PV_A(j - 1) with one head), PV_A(j)
-                # before B writes
-                ph, pj = ("A", j) if h == "B" else (self.heads[nh - 1], j - 1)
-                if pj >= 0 and self.bug != "p_before_pv":
-                    yield ("O" + ph, pj & 1)
-                if h == "A" and self.tail and j == self.nkt - 1:
-                    vb = "V" + str(j & 1)
-                    yield (vb, (j >> 1) & 1)
-                    if self.writers[vb] or self.readers[vb] or self.version[vb] != j:
-                        self.err(f"warp {w} zeroes the tail of {vb} holding {self.version[vb]} (tile {j})")
-                if self.readers["P"]:
-                    self.err(f"warp {w} writes P{h}({j}) while PV reads P")
-                self.p_rows[w] = (h, j)
-                if all(p == (h, j) for p in self.p_rows):
-                    self.version["P"] = (h, j)
-                self.bars["P" + h].arrive()
-        for h in self.heads:
-            yield ("O" + h, (self.nkt - 1) & 1)
-            if self.writers["O" + h] or self.version["O" + h] != self.nkt - 1:
-                self.err(f"warp {w} reads output {h} holding {self.version['O' + h]}")
-            # the epilogue stages head A's rows in the K ring and head B's in the V ring
-            ring = "K" if h == "A" else "V"
-            for st in (ring + "0", ring + "1"):
-                if self.readers[st] or self.writers[st]:
-                    self.err(f"warp {w} stages output {h} in {st} while it is in use")
+            sb = "S" + h
+            yield (sb, j & 1)
+            if self.writers[sb] or self.version[sb] != ("S", j):
+                self.err(f"warp {w} of {h} reads {sb} holding {self.version[sb]} (writers {self.writers[sb]}) "
+                         f"for tile {j}")
+            if j > 0 and self.rng.random() < self.rescale_p:  # a row maximum grew: rescale O_h
+                if self.writers["O" + h] or self.version["O" + h] != j - 1:
+                    self.err(f"warp {w} rescales O{h} holding {self.version['O' + h]} while PV runs (tile {j})")
+            if h == "A" and self.tail and j == self.nkt - 1:
+                vb = "V" + str(j & 1)
+                yield (vb, (j >> 1) & 1)
+                if self.writers[vb] or self.readers[vb] or self.version[vb] != j:
+                    self.err(f"warp {w} zeroes the tail of {vb} holding {self.version[vb]} (tile {j})")
+                self.version["VZ"] = j
+            if self.readers[sb] or self.writers[sb]:
+                self.err(f"warp {w} of {h} writes P over {sb} while an MMA uses it")
+            self.p_written[h][w] = j
+            if all(p == j for p in self.p_written[h]):
+                self.version[sb] = ("P", j)
+            self.bars["P" + h].arrive()
+        yield ("DONE", 0)
+        if self.writers["O" + h] or self.version["O" + h] != self.nkt - 1:
+            self.err(f"warp {w} of {h} reads the output holding {self.version['O' + h]}")
+        for st in ("K0", "K1", "V0", "V1"):
+            if self.readers[st] or self.writers[st]:
+                self.err(f"warp {w} of {h} stages its output while {st} is in use")
 
     # ---------------------------------------------------------------- the scheduler
     def run(self) -> list[str]:
-        actors = [self.producer(), self.mma()] + [self.softmax(w) for w in range(self.warps)]
+        actors = [self.producer(), self.mma()] + [self.softmax(h, w) for h in self.heads for w in range(self.warps)]
         waiting = [None] * len(actors)
         live = list(range(len(actors)))
         steps = 0

@@ -101,24 +101,25 @@ def _layout():
 def test_shared_memory_layout_bounds():
     L = _layout()
     swz = lambda r, c: r * 128 + ((c ^ (r & 7)) << 4)  # noqa: E731
-    # Q tile (threads) and P tile (threads): 2 blocks of 128 rows x 128 B
-    q_end = max(L["Q_OFF"] + (c >> 3) * 16384 + swz(r, c & 7) + 16 for r in range(128) for c in range(16))
-    p_end = max(L["P_OFF"] + (c >> 3) * 16384 + swz(r, c & 7) + 16 for r in range(128) for c in range(16))
-    assert q_end <= L["K_OFF"] and p_end <= L["BAR_OFF"]
+    # Q tiles of both heads (threads): 2 blocks of 128 rows x 128 B each
+    q_end = max(L["Q_OFF"] + h * 32768 + (c >> 3) * 16384 + swz(r, c & 7) + 16
+                for h in range(2) for r in range(128) for c in range(16))
+    assert q_end <= L["K_OFF"]
     # K / V rings (copies): stage s, page box `lane` of bs rows, hd half
     for bs in (8, 16, 32, 64, 128):
         nb = 128 // bs
         k_end = max(L["K_OFF"] + s * 32768 + lane * bs * 128 + h * 16384 + bs * 128
                     for s in range(2) for lane in range(nb) for h in range(2))
         v_end = k_end - L["K_OFF"] + L["V_OFF"]
-        assert k_end <= L["V_OFF"] and v_end <= L["P_OFF"]
+        assert k_end <= L["V_OFF"] and v_end <= L["BAR_OFF"]
         for s in range(2):  # every box starts on a 1024-byte swizzle atom
             for lane in range(nb):
                 assert (s * 32768 + lane * bs * 128) % 1024 == 0
-    # value-tail zeroing (threads) and output staging in the K ring (epilogue)
-    assert L["V_OFF"] + 32768 + 127 * 128 + 16384 + 128 <= L["P_OFF"]
+    # value-tail zeroing (threads) and output staging: head A in the K ring, head B in the V ring (epilogue)
+    assert L["V_OFF"] + 32768 + 127 * 128 + 16384 + 128 <= L["BAR_OFF"]
     assert L["K_OFF"] + 127 * L["OST"] + 256 <= L["V_OFF"] and L["OST"] % 16 == 0
+    assert L["V_OFF"] + 127 * L["OST"] + 256 <= L["BAR_OFF"]
     # barriers, abort flag, TMEM slot, and the total with the 1024-byte base alignment
     assert L["BAR_OFF"] + 8 * L["NBAR"] <= L["FLAG_OFF"] and L["FLAG_OFF"] + 8 <= L["USED"]
     assert L["DYN"] >= L["USED"] + 1023 and L["DYN"] <= 227 * 1024
-    assert all(L[k] % 1024 == 0 for k in ("Q_OFF", "K_OFF", "V_OFF", "P_OFF"))
+    assert all(L[k] % 1024 == 0 for k in ("Q_OFF", "K_OFF", "V_OFF"))

@@ -1,10 +1,10 @@
 """The synchronisation protocol of the tcgen05 prefill attention kernel, on CPU: a discrete-event model
 (tests/_attn_tc_protocol_model.py) runs the kernel's producer, MMA thread and softmax warps with random copy and
 MMA completion times and random interleavings, for one and two heads per CTA, 1 to 6 key tiles, 1 to 4 softmax
-warps, 1 to 16 page boxes per tile, with and without the value-tail zeroing and with O rescales at random tiles.
-No run may deadlock or touch a buffer out of turn. Three planted mistakes (the MMA not waiting for the value tile;
-the next score MMA not waiting for the threads to read the scores; the softmax writing P before the previous PV
-finished) must be caught, which shows the checks can fail."""
+warps per head, 1 to 16 page boxes per tile, with and without the value-tail zeroing and with O rescales at random
+tiles. No run may deadlock or touch a buffer out of turn. Two planted mistakes (the next score MMA issued over P
+before the PV reading it finished; head B's last PV issued before head A's warps zeroed the value tail) must be
+caught, which shows the checks can fail."""
 import itertools
 
 import pytest
@@ -22,12 +22,10 @@ def test_protocol_has_no_races_or_deadlocks(nkt, heads):
             assert not errors, (nkt, heads, warps, nb, tail, rescale, errors[:3])
 
 
-@pytest.mark.parametrize("heads", [1, 2])
-@pytest.mark.parametrize("bug,needle", [("pv_before_v", "PV"), ("s_before_read", "overwrites"),
-                                        ("p_before_pv", "P")])
-def test_planted_protocol_mistakes_are_caught(bug, needle, heads):
+@pytest.mark.parametrize("bug,needle", [("s_over_p", "overwrites"), ("tail_race", "tail")])
+def test_planted_protocol_mistakes_are_caught(bug, needle):
     caught = 0
-    for seed in range(200):
-        errors = Sim(3, 2, 4, seed, False, 0.0, bug=bug, heads=heads).run()
+    for seed in range(300):
+        errors = Sim(3, 2, 4, seed, True, 0.0, bug=bug, heads=2).run()
         caught += any(needle in e for e in errors)
     assert caught > 0

@@ -118,8 +118,18 @@ def paged_reference(q, kc, vc, table, starts, lens):
     return outs
 
 
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
 @pytest.mark.parametrize("nq,nkv,with_ctx", [(12, 2, False), (8, 8, True), (16, 2, True)])
-def test_attn_prefill_matches_oracle(nq, nkv, with_ctx):
+def test_attn_prefill_matches_oracle(nq, nkv, with_ctx, tc):
+    """Both prefill attention kernels: the tcgen05 one (the default) and the mma.sync one (selected off)."""
+    prev = K.set_attn_prefill_tc(tc)
+    try:
+        _attn_prefill_case(nq, nkv, with_ctx)
+    finally:
+        K.set_attn_prefill_tc(prev)
+
+
+def _attn_prefill_case(nq, nkv, with_ctx):
     g = torch.Generator().manual_seed(nq + nkv + with_ctx)
     hd, blk = 128, 16
     lens = [1, 17, 64, 65, 130]

@@ -59,8 +59,8 @@ def test_attention_prefill_tc_operands():
     L = _consts("attn_prefill_tc.cu", "AttnTcSmem")
     for bs in (8, 16, 64, 128):
         mem = {}
-        # Q of both heads [128 queries x 128 dims] by threads; K, V stage 1 [128 keys x 128 dims] by page boxes; P
-        # by threads
+        # Q of both heads [128 queries x 128 dims] by threads; K, V stage 1 [128 keys x 128 dims] by page boxes (P,
+        # the PV MMA's A operand, is read from TMEM: not a shared-memory layout)
         for h in range(2):
             thread_write(mem, L["Q_OFF"] + h * 32768, 128, 16, lambda r, d, h=h: ("Q", h, r, d), block_bytes=16384)
         stage = 1
@@ -69,7 +69,6 @@ def test_attention_prefill_tc_operands():
                 for which, off in (("K", L["K_OFF"]), ("V", L["V_OFF"])):
                     dst = off + stage * 32768 + hh * 16384 + lane * bs * 128
                     tma_write(mem, dst, bs, lambda r, e, w=which, l=lane, h=hh: (w, l * bs + r, h * 64 + e))
-        thread_write(mem, L["P_OFF"], 128, 16, lambda r, k: ("P", r, k), block_bytes=16384)
         kst, vst = L["K_OFF"] + stage * 32768, L["V_OFF"] + stage * 32768
         for kk in range(8):
             off = (kk >> 2) * 16384 + (kk & 3) * 32
@@ -79,10 +78,8 @@ def test_attention_prefill_tc_operands():
                 assert all(a[i][k] == ("Q", h, i, kk * 16 + k) for i in range(128) for k in range(16))
             b = read_k_major(mem, kst + off, 128)
             assert all(b[n][k] == ("K", n, kk * 16 + k) for n in range(128) for k in range(16))
-            # O += P V: A = P (M = 128 queries, this step's 16 keys), B = V MN-major (N = 128 dims)
-            a = read_k_major(mem, L["P_OFF"] + off, 128)
+            # O += P V: B = V MN-major (N = 128 dims), this step's 16 keys
             v = read_mn_major(mem, vst + kk * 2048, 128, 16384)
-            assert all(a[i][k] == ("P", i, kk * 16 + k) for i in range(128) for k in range(16))
             assert all(v[k][n] == ("V", kk * 16 + k, n) for k in range(16) for n in range(128))
 
 
