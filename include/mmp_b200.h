@@ -204,6 +204,12 @@ int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64_t ldw, voi
                      int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
                      int* err, void* stream);
 
+/* Split-K count of the decode (M <= 256) weight-streaming GEMMs: 0 (default) picks it from the tile count (enough
+ * CTAs to fill the GPU, at most 8, as a thread-block cluster); n > 0 uses min(n, 8) (1: no split). A tuning and
+ * measurement switch for the same operation (results differ only by the order of the fp32 partial sums);
+ * process-wide; returns the previous setting. No counterpart in the reference (cuBLAS picks its own split). */
+int mmp_set_gemm_decode_split(int split);
+
 /* ---- bf16 GEMM over two K segments with their own scales ---------------------------------------------
  * Replaces the reference layer's two output projections and their sum (harness/layer.py:51-53,103-105,
  * 213-219: o_proj * attn_out + out_proj * ssm_out) when one rank holds both branches: with the two

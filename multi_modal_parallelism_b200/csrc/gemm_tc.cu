@@ -681,6 +681,8 @@ int launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const TcPara
   return mmp_check_launch("mmp_gemm_bf16_tc");
 }
 
+int g_decode_split = 0;  // 0: the split-K count follows the rule below; > 0: that count (mmp_set_gemm_decode_split)
+
 // Decode (M <= 256): swap-AB, A = weight rows (the 128-row M side of the MMA), B = the activation rows (N);
 // K split over a cluster when the output tiles cannot fill the GPU. PUSH: output tiles go to every rank's
 // all-reduce buffer (P.push) instead of P.out.
@@ -698,6 +700,7 @@ int decode_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, int M, i
   const int slots = (bn == 64 ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
   int split = 1;
   if (tiles * ntiles_b < slots) split = std::min(8, std::max(1, std::min(slots / (tiles * ntiles_b), k_tiles / 2)));
+  if (g_decode_split > 0) split = std::min(std::min(8, g_decode_split), std::max(1, k_tiles));  // a fixed count
   // the staged and received owner blocks must fit in the ring
   auto fits = [&](int ns) {
     return ns == 1 || (bn == 64 ? TcLayout<64, 4>::split_fits(ns) : TcLayout<128, 5>::split_fits(ns));
@@ -790,4 +793,10 @@ extern "C" int mmp_gemm_bf16_push(const void* a, int64_t lda, const void* w, int
   TcParams P{0, 0, K, k_tiles, nullptr, N, alpha, k_seg_tile, alpha2, colscale, nullptr, 0, err,
              PeerBufs{bufs, rank, world, rows_max, N}};
   return decode_gemm<true>(a, lda, w, ldw, M, N, K, P, k_tiles, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int mmp_set_gemm_decode_split(int split) {
+  const int prev = mmp::g_decode_split;
+  mmp::g_decode_split = split < 0 ? 0 : split;
+  return prev;
 }

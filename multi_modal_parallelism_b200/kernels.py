@@ -507,6 +507,12 @@ def ssd_prefill_segmented(x: torch.Tensor, dt: torch.Tensor, A: torch.Tensor, B:
     return out
 
 
+def set_gemm_decode_split(split: int) -> int:
+    """Split-K count of the decode weight-streaming GEMMs: 0 (default) automatic, n > 0 fixed (at most 8);
+    process-wide. Returns the previous setting."""
+    return int(_lib.lib().mmp_set_gemm_decode_split(int(split)))
+
+
 def set_attn_prefill_tc(enable: bool) -> bool:
     """Select the tcgen05/TMEM kernel for attn_prefill (True, the default) or the mma.sync kernel (False);
     process-wide. Returns the previous setting."""

@@ -191,8 +191,20 @@ def only(args, g) -> dict:
         x = torch.randn(M, Kd, device=dev, generator=gen).to(BF)
         w = (torch.randn(N, Kd, device=dev, generator=gen) * 0.02).to(BF)
         out = torch.empty(M, N, device=dev, dtype=BF)
-        ms = timed(lambda: K.gemm(x, w, out=out))
-        res.update(shape=[M, N, Kd], ms=ms, tflops=2 * M * N * Kd / ms / 1e9)
+        # weight-streaming shapes: cycle through copies of the weight whose total exceeds L2 twice over, so each
+        # call reads its weight from HBM as in a layer step
+        ws = [w] + [w.clone() for _ in range(max(0, -(-256 * 2**20 // (w.numel() * 2)) - 1))] if M <= 256 else [w]
+        turn = [0]
+
+        def call():
+            K.gemm(x, ws[turn[0] % len(ws)], out=out)
+            turn[0] += 1
+
+        prev = K.set_gemm_decode_split(args.split)
+        ms = timed(call)
+        K.set_gemm_decode_split(prev)
+        res.update(shape=[M, N, Kd], ms=ms, tflops=2 * M * N * Kd / ms / 1e9, split=args.split,
+                   weight_gbs=N * Kd * 2 / ms / 1e6)
     elif args.only in ("ssd_prefill", "attn_prefill", "conv_prefill"):
         pc = make_prefill_ctx([args.len] * args.nseq, 16, dev)
         T = pc.T
@@ -241,6 +253,38 @@ def only(args, g) -> dict:
             cs = torch.zeros(args.nseq + 1, 3, rows, device=dev, dtype=BF)
             ms = timed(lambda: K.conv_prefill(xbc, cs.transpose(1, 2), w, b, pc.cu_seqlens, pc.state_idx, pc.has_init, out))
             res.update(tokens=T, ms=ms, gbs=2 * T * rows * 2 / ms / 1e6)
+    elif args.only in ("gdn_prefill", "gdn_decode"):
+        # the Gated DeltaNet layer's kernels at the qwen35_like head shape: 16 key heads shared by 32 value heads
+        # x 128, fp32 state; prefill of --nseq fresh sequences x --len tokens (64-token chunks), decode of --nseq
+        # rows, q and k L2-normalised as the layer feeds them
+        nk, nv, dk, dv = 16, 32, 128, 128
+        if args.only == "gdn_prefill":
+            pc = make_prefill_ctx([args.len] * args.nseq, 16, dev)
+            T = pc.T
+            lines = args.nseq + 1
+        else:
+            T = args.nseq
+            lines = T + 1
+        q = torch.nn.functional.normalize(torch.randn(T, nk, dk, device=dev, generator=gen), dim=-1).to(BF)
+        k = torch.nn.functional.normalize(torch.randn(T, nk, dk, device=dev, generator=gen), dim=-1).to(BF)
+        v = torch.randn(T, nv, dv, device=dev, generator=gen).to(BF)
+        z = torch.randn(T, nv, dv, device=dev, generator=gen).to(BF)
+        a = torch.randn(T, nv, device=dev, generator=gen).to(BF)
+        b = torch.randn(T, nv, device=dev, generator=gen).to(BF)
+        st = torch.randn(lines, nv, dv, dk, device=dev, generator=gen) * 0.05
+        out = torch.empty(T, nv, dv, device=dev, dtype=BF)
+        nw = torch.ones(dv, device=dev, dtype=BF)
+        if args.only == "gdn_prefill":
+            ms = timed(lambda: K.gdn_prefill(q, k, v, a, b, st, pc.cu_seqlens, pc.state_idx, pc.has_init, out, z=z,
+                                             norm_w=nw))
+            C = 64  # per token and value head: K K^T, Q K^T, S K^T, S Q^T, T R, Qm U and the state update
+            flops = T * nv * (4 * C * dk + 6 * dk * dv + 4 * C * dv)
+            res.update(tokens=T, ms=ms, tflops=flops / ms / 1e9)
+        else:
+            idx = torch.arange(1, T + 1, device=dev, dtype=torch.int32)
+            ms = timed(lambda: K.gdn_decode(q, k, v, a, b, st, idx, out, z=z, norm_w=nw))
+            nbytes = 2 * T * nv * dv * dk * 4
+            res.update(batch=T, ms=ms, gbs=nbytes / ms / 1e6)
     elif args.only == "decode_step":
         # the bench layer: falcon_h1_7b_like, batch 64, context 2048, tp1, fp32 SSM state, seed 0
         from .config import preset
@@ -268,8 +312,10 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default="microbench.csv")
     ap.add_argument("--quick", action="store_true")
-    ap.add_argument("--only", choices=["gemm", "ssd_prefill", "attn_prefill", "conv_prefill", "decode_step"])
+    ap.add_argument("--only", choices=["gemm", "ssd_prefill", "attn_prefill", "conv_prefill", "gdn_prefill",
+                                       "gdn_decode", "decode_step"])
     ap.add_argument("--shape", default="4096,8728,3072", help="gemm M,N,K")
+    ap.add_argument("--split", type=int, default=0, help="gemm: decode split-K count (0: automatic)")
     ap.add_argument("--nseq", type=int, default=2)
     ap.add_argument("--len", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
