@@ -209,6 +209,10 @@ int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64_t ldw, voi
  * measurement switch for the same operation (results differ only by the order of the fp32 partial sums);
  * process-wide; returns the previous setting. No counterpart in the reference (cuBLAS picks its own split). */
 int mmp_set_gemm_decode_split(int split);
+/* Ring depth of the decode GEMMs with at most 64 activation rows: 4 stages (two CTAs per SM) or 8 (one CTA per SM,
+ * twice the weight bytes in flight per CTA); other values select 4. A tuning switch like the one above; returns
+ * the previous setting. No counterpart in the reference. */
+int mmp_set_gemm_decode_stages(int stages);
 
 /* ---- bf16 GEMM over two K segments with their own scales ---------------------------------------------
  * Replaces the reference layer's two output projections and their sum (harness/layer.py:51-53,103-105,

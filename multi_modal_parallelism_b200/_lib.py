@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple] = {
     "mmp_set_pdl": (I32, [I32]),
     "mmp_set_attn_prefill_tc": (I32, [I32]),
     "mmp_set_gemm_decode_split": (I32, [I32]),
+    "mmp_set_gemm_decode_stages": (I32, [I32]),
     "mmp_scale_rows": (I32, [P, I64, P, I32, I32, F32, F32, P]),
     "mmp_ssu_decode": (I32, [P, I32, I64, I64, I64, P, I64, I64, P, I64, I64, P, P, P, P, I64, I64, P, I64, I64,
                              P, I64, I64, P, P, I32, P, I64, I64, I32, I32, I32, I32, I32, I32, I32, P, P]),

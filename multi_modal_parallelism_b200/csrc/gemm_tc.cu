@@ -682,6 +682,7 @@ int launch_persistent(const CUtensorMap& ma, const CUtensorMap& mb, const TcPara
 }
 
 int g_decode_split = 0;  // 0: the split-K count follows the rule below; > 0: that count (mmp_set_gemm_decode_split)
+int g_decode_stages = 4;  // ring depth of the M <= 64 decode GEMMs: 4 (two CTAs per SM) or 8 (one per SM)
 
 // Decode (M <= 256): swap-AB, A = weight rows (the 128-row M side of the MMA), B = the activation rows (N);
 // K split over a cluster when the output tiles cannot fill the GPU. PUSH: output tiles go to every rank's
@@ -697,13 +698,15 @@ int decode_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, int M, i
   if ((rc = make_map(&ma, w, N, K, ldw, TBM)) || (rc = make_map(&mb, a, M, K, lda, bn))) return rc;
   const int tiles = (N + TBM - 1) / TBM;
   const int ntiles_b = (M + bn - 1) / bn;
-  const int slots = (bn == 64 ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
+  const bool deep = bn == 64 && g_decode_stages == 8;  // 8-stage ring: one CTA per SM, 192 KB of weights in flight
+  const int slots = (bn == 64 && !deep ? 2 : 1) * g_tc_sms;  // CTAs that fit per SM at this tile shape
   int split = 1;
   if (tiles * ntiles_b < slots) split = std::min(8, std::max(1, std::min(slots / (tiles * ntiles_b), k_tiles / 2)));
   if (g_decode_split > 0) split = std::min(std::min(8, g_decode_split), std::max(1, k_tiles));  // a fixed count
   // the staged and received owner blocks must fit in the ring
   auto fits = [&](int ns) {
-    return ns == 1 || (bn == 64 ? TcLayout<64, 4>::split_fits(ns) : TcLayout<128, 5>::split_fits(ns));
+    return ns == 1 || (bn == 64 ? (deep ? TcLayout<64, 8>::split_fits(ns) : TcLayout<64, 4>::split_fits(ns))
+                                : TcLayout<128, 5>::split_fits(ns));
   };
   int ktps = (k_tiles + split - 1) / split;
   split = (k_tiles + ktps - 1) / ktps;
@@ -714,6 +717,8 @@ int decode_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, int M, i
   P.k_tiles_per_split = ktps;
   dim3 grid(ntiles_b, tiles, split);
   const bool cl = split > 1;
+  if (bn == 64 && deep)
+    return cl ? launch_tc<64, 8, true, true, PUSH>(ma, mb, P, grid, split, s) : launch_tc<64, 8, true, false, PUSH>(ma, mb, P, grid, 1, s);
   if (bn == 64) return cl ? launch_tc<64, 4, true, true, PUSH>(ma, mb, P, grid, split, s) : launch_tc<64, 4, true, false, PUSH>(ma, mb, P, grid, 1, s);
   return cl ? launch_tc<128, 5, true, true, PUSH>(ma, mb, P, grid, split, s) : launch_tc<128, 5, true, false, PUSH>(ma, mb, P, grid, 1, s);
 }
@@ -798,5 +803,11 @@ extern "C" int mmp_gemm_bf16_push(const void* a, int64_t lda, const void* w, int
 extern "C" int mmp_set_gemm_decode_split(int split) {
   const int prev = mmp::g_decode_split;
   mmp::g_decode_split = split < 0 ? 0 : split;
+  return prev;
+}
+
+extern "C" int mmp_set_gemm_decode_stages(int stages) {
+  const int prev = mmp::g_decode_stages;
+  mmp::g_decode_stages = stages == 8 ? 8 : 4;
   return prev;
 }

@@ -513,6 +513,12 @@ def set_gemm_decode_split(split: int) -> int:
     return int(_lib.lib().mmp_set_gemm_decode_split(int(split)))
 
 
+def set_gemm_decode_stages(stages: int) -> int:
+    """Ring depth of the decode GEMMs with at most 64 activation rows (4 or 8); process-wide. Returns the previous
+    setting."""
+    return int(_lib.lib().mmp_set_gemm_decode_stages(int(stages)))
+
+
 def set_attn_prefill_tc(enable: bool) -> bool:
     """Select the tcgen05/TMEM kernel for attn_prefill (True, the default) or the mma.sync kernel (False);
     process-wide. Returns the previous setting."""

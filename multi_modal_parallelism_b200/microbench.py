@@ -174,15 +174,25 @@ def only(args, g) -> dict:
     it = args.iters
 
     def timed(fn) -> float:
+        """Device time per call: `it` calls captured in one CUDA graph (no host launch cost between them),
+        replayed after the warm-up calls."""
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
+        st = torch.cuda.Stream(device=dev)
+        st.wait_stream(torch.cuda.current_stream(dev))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=st):
+            for _ in range(it):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(it):
-            fn()
+        graph.replay()
         e1.record()
         torch.cuda.synchronize()
+        del graph
         return e0.elapsed_time(e1) / it
 
     res: dict = {"kernel": args.only}
@@ -201,9 +211,11 @@ def only(args, g) -> dict:
             turn[0] += 1
 
         prev = K.set_gemm_decode_split(args.split)
+        prev_st = K.set_gemm_decode_stages(args.stages)
         ms = timed(call)
         K.set_gemm_decode_split(prev)
-        res.update(shape=[M, N, Kd], ms=ms, tflops=2 * M * N * Kd / ms / 1e9, split=args.split,
+        K.set_gemm_decode_stages(prev_st)
+        res.update(shape=[M, N, Kd], ms=ms, tflops=2 * M * N * Kd / ms / 1e9, split=args.split, stages=args.stages,
                    weight_gbs=N * Kd * 2 / ms / 1e6)
     elif args.only in ("ssd_prefill", "attn_prefill", "conv_prefill"):
         pc = make_prefill_ctx([args.len] * args.nseq, 16, dev)
@@ -253,6 +265,22 @@ def only(args, g) -> dict:
             cs = torch.zeros(args.nseq + 1, 3, rows, device=dev, dtype=BF)
             ms = timed(lambda: K.conv_prefill(xbc, cs.transpose(1, 2), w, b, pc.cu_seqlens, pc.state_idx, pc.has_init, out))
             res.update(tokens=T, ms=ms, gbs=2 * T * rows * 2 / ms / 1e6)
+    elif args.only == "attn_decode":
+        # paged decode attention at the bench shape: --nseq sequences at context --len (+1: the new key), 12 query
+        # / 2 key-value heads x 128, 16-token pages in a random block order; --split splits (0: automatic)
+        B, c, nq, nkv, hd = args.nseq, args.len + 1, 12, 2, 128
+        ctx = make_decode_ctx(B, args.len, 16, dev)
+        nb = B * ctx.nblk + 1
+        kv, kc, vc, _ = K.alloc_kv(nb, 16, nkv, hd, dev)
+        kv.normal_(generator=gen)
+        q = torch.randn(B, nq, hd, device=dev, dtype=BF, generator=gen)
+        out = torch.empty_like(q)
+        splits = args.split if args.split > 0 else K.attn_default_splits(B, nkv, c)
+        ws = K.attn_workspace(B, nq, hd, splits, dev)
+        ms = timed(lambda: K.attn_decode(q, kc, vc, ctx.cu_q, ctx.seqused_k, ctx.max_k, ctx.block_table, out,
+                                         workspace=ws, splits=splits))
+        nbytes = B * nkv * c * hd * 2 * 2
+        res.update(batch=B, ctx=c, splits=splits, ms=ms, gbs=nbytes / ms / 1e6)
     elif args.only in ("gdn_prefill", "gdn_decode"):
         # the Gated DeltaNet layer's kernels at the qwen35_like head shape: 16 key heads shared by 32 value heads
         # x 128, fp32 state; prefill of --nseq fresh sequences x --len tokens (64-token chunks), decode of --nseq
@@ -312,10 +340,12 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--out", default="microbench.csv")
     ap.add_argument("--quick", action="store_true")
-    ap.add_argument("--only", choices=["gemm", "ssd_prefill", "attn_prefill", "conv_prefill", "gdn_prefill",
-                                       "gdn_decode", "decode_step"])
+    ap.add_argument("--only", choices=["gemm", "ssd_prefill", "attn_prefill", "attn_decode", "conv_prefill",
+                                       "gdn_prefill", "gdn_decode", "decode_step"])
     ap.add_argument("--shape", default="4096,8728,3072", help="gemm M,N,K")
-    ap.add_argument("--split", type=int, default=0, help="gemm: decode split-K count (0: automatic)")
+    ap.add_argument("--split", type=int, default=0,
+                    help="gemm: decode split-K count; attn_decode: key-range splits (0: automatic)")
+    ap.add_argument("--stages", type=int, default=4, help="gemm: decode ring depth (4 or 8)")
     ap.add_argument("--nseq", type=int, default=2)
     ap.add_argument("--len", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)

@@ -17,10 +17,12 @@ import sys
 
 import torch
 
-from .config import FalconH1Dims, RunSpec
+from .config import CONFIG_DIR, FalconH1Dims, RunSpec
 from .dist import barrier_sync, destroy, init_groups
 from .measure import measure
 from .model import BwTables
+
+BUNDLED_BW = CONFIG_DIR / "microbench_b200.csv"  # the microbench run on one B200 (the byte model's default table)
 from .weights import load_layer_from_safetensors, random_layer
 
 
@@ -42,7 +44,8 @@ def add_common_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--layer-idx", type=int, default=0)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--bw", default="results/raw/microbench.csv",
-                    help="microbench CSV for the byte model (--k model, predicted ms per op); used when it exists")
+                    help="microbench CSV for the byte model (--k model, predicted ms per op); when it does not exist, "
+                         "the B200 table bundled with the package (configs/microbench_b200.csv)")
     ap.add_argument("--out", default="results/raw/dev.csv")
     ap.add_argument("--correctness-out", default="results/raw/correctness.csv")
     ap.add_argument("--tag", default="")
@@ -85,7 +88,8 @@ def main(argv: list[str] | None = None) -> int:
     groups = init_groups()
     dims, full = load_dims_and_weights(args)
     ssm_dtype = torch.float32 if args.ssm_dtype == "fp32" else torch.bfloat16
-    bw = BwTables.from_csv(args.bw) if args.bw and os.path.exists(args.bw) else None
+    bw_path = args.bw if args.bw and os.path.exists(args.bw) else str(BUNDLED_BW)
+    bw = BwTables.from_csv(bw_path) if os.path.exists(bw_path) else None
     rows = measure(spec, groups, dims, full, args.out, args.correctness_out, args.check, bw,
                    os.environ.get("MMP_IMAGE_TAG", ""), ssm_dtype=ssm_dtype, ar_impl=args.ar_impl,
                    branch_chains=args.branch_chains, defer_norm=args.defer_norm)

@@ -76,3 +76,20 @@ def test_run_k_model_resolves_through_the_byte_model():
     w, k, src = resolve_k(spec, DIMS["falcon_h1_7b"], 4, BW)
     assert (k, src) == (case["k"], "model")
     assert resolve_k(spec, DIMS["falcon_h1_7b"], 4, None)[2] == "neutral(no-bw)"
+
+
+def test_bundled_b200_table_calibrates_the_model():
+    """The microbench table measured on one B200 (configs/microbench_b200.csv) loads, covers every op the model
+    reads, and orders the 4-GPU layouts as the B200 bench measured them: the byte-balanced split13 and the even
+    split22 ahead of tp4_fused (measured 0.088 / 0.094 / 0.114 ms). The model sums a rank's ops serially, so its
+    tp1 step (168 us) sits above the measured 130 us, where the two branches overlap on two streams."""
+    from multi_modal_parallelism_b200.config import CONFIG_DIR, preset
+    from multi_modal_parallelism_b200.model import BwTables, predict_step
+
+    bw = BwTables.from_csv(CONFIG_DIR / "microbench_b200.csv")
+    assert bw.stream > 4000 and bw.gemv and bw.attn
+    d = preset("falcon_h1_7b_like")
+    t = {m: predict_step(d, m, 0.0, None, 64, 2048, bw, "graph", world=4)[0] for m in ("split13", "split22", "tp4_fused")}
+    assert t["split13"] < t["tp4_fused"] and t["split22"] < t["tp4_fused"]
+    tp1 = predict_step(d, "tp1", 0.0, None, 64, 2048, bw, "graph", world=1)[0]
+    assert 0.130 <= tp1 <= 0.130 * 1.5

@@ -299,3 +299,26 @@ def test_gemm_two_segments(M, N, K_, kseg):
     ref = 0.3 * (xf[:, :kseg] @ wf[:, :kseg].T) + 1.7 * (xf[:, kseg:] @ wf[:, kseg:].T) + add.float()
     out = K.gemm(x.to(DEV), w.to(DEV), alpha=0.3, k_seg=kseg, alpha2=1.7, addend=add.to(DEV))
     close(npf(out), ref.numpy())
+
+
+@pytest.mark.parametrize("stages", [4, 8])
+@pytest.mark.parametrize("split", [0, 1, 2, 3, 8])
+@pytest.mark.parametrize("M,N,K_,kseg", [(64, 8728, 3072, 3072), (64, 3072, 4608, 1536), (17, 2048, 3072, 3072),
+                                         (1, 300, 640, 256)])
+def test_decode_gemm_ring_depths_and_splits(stages, split, M, N, K_, kseg):
+    """The decode weight-streaming GEMM with either ring depth and any split-K count (the tuning switches
+    kernels.set_gemm_decode_stages / set_gemm_decode_split): two K segments and the addend."""
+    g = torch.Generator().manual_seed(M + N + K_ + split + stages)
+    x = torch.randn(M, K_, generator=g).to(BF)
+    w = (torch.randn(N, K_, generator=g) * 0.02).to(BF)
+    add = torch.randn(M, N, generator=g).to(BF)
+    xf, wf = x.float(), w.float()
+    ref = 0.3 * (xf[:, :kseg] @ wf[:, :kseg].T) + 1.7 * (xf[:, kseg:] @ wf[:, kseg:].T) + add.float()
+    p_st, p_sp = K.set_gemm_decode_stages(stages), K.set_gemm_decode_split(split)
+    try:
+        out = K.gemm(x.to(DEV), w.to(DEV), alpha=0.3, k_seg=kseg, alpha2=1.7, addend=add.to(DEV))
+        torch.cuda.synchronize()
+    finally:
+        K.set_gemm_decode_stages(p_st)
+        K.set_gemm_decode_split(p_sp)
+    close(npf(out), ref.numpy())
