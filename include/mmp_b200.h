@@ -336,6 +336,23 @@ int mmp_gdn_prefill(const void* q, int64_t q_t, int64_t q_h, const void* k, int6
                     void* out, int64_t o_t, int64_t o_h,
                     int nseq, int ntok, int nk, int nv, int dk, int dv, int lines, int* err, void* stream);
 
+/* The same chunked prefill on the tensor cores, in two passes: every chunk of every sequence at once (the chunk's
+ * [K; Q] K^T on tcgen05, the inverse of its unit lower-triangular matrix T in fp32, T and the masked Q K^T
+ * written to `workspace` as bf16), then one walk per (value head, sequence) with the state in tensor memory.
+ * Arguments as mmp_gdn_prefill; q/k/v additionally need 16-byte aligned rows and head strides (TMA). workspace:
+ * 16-byte aligned, at least mmp_gdn_prefill_workspace_size(ntok, nv) bytes; its contents are scratch.
+ * Same results as mmp_gdn_prefill within bf16 rounding (the chunk algebra is regrouped, not changed). */
+size_t mmp_gdn_prefill_workspace_size(int ntok, int nv);
+int mmp_gdn_prefill_tc(const void* q, int64_t q_t, int64_t q_h, const void* k, int64_t k_t, int64_t k_h,
+                       const void* v, int64_t v_t, int64_t v_h, const void* a, int64_t a_t,
+                       const void* b, int64_t b_t, const float* A_log, const float* dt_bias,
+                       const void* z, int64_t z_t, int64_t z_h, const void* norm_w, float eps,
+                       float* state, int64_t s_line, int64_t s_head, int64_t s_row,
+                       const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init,
+                       void* out, int64_t o_t, int64_t o_h,
+                       int nseq, int ntok, int nk, int nv, int dk, int dv, int lines,
+                       void* workspace, size_t workspace_bytes, int* err, void* stream);
+
 /* ---- peer-memory all-reduce fused with the residual add and RMSNorm (decode-sized messages) ------------
  * Replaces the NCCL all-reduce of the layer's partial sums (`ParallelHybridLayer._ar`, harness/layer.py:175-181)
  * and the residual / pre-MLP norm after it (harness/layer.py:217-227) on ranks of one node.

@@ -63,6 +63,10 @@ SIGNATURES: dict[str, tuple] = {
                              P, I64, I64, P, F32, P, I32, P, I64, I64, I32, I32, I32, I32, I32, I32, P, P]),
     "mmp_gdn_prefill": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, P, I64, P, P, P, I64, I64, P, F32,
                               P, I64, I64, I64, P, P, P, P, I64, I64, I32, I32, I32, I32, I32, I32, I32, P, P]),
+    "mmp_gdn_prefill_workspace_size": (SZ, [I32, I32]),
+    "mmp_gdn_prefill_tc": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, P, I64, P, I64, P, P, P, I64, I64, P, F32,
+                                 P, I64, I64, I64, P, P, P, P, I64, I64, I32, I32, I32, I32, I32, I32, I32, P, SZ, P,
+                                 P]),
 }
 
 _lib: C.CDLL | None = None

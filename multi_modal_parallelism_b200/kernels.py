@@ -590,24 +590,53 @@ def gdn_decode(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tenso
     return out
 
 
+_gdn_ws: dict[int, torch.Tensor] = {}
+GDN_PREFILL_TC = True  # the tensor-core kernels (mmp_gdn_prefill_tc) wherever their alignment rules hold
+
+
+def gdn_prefill_workspace(ntok: int, nv: int, device: torch.device) -> torch.Tensor:
+    """Scratch for gdn_prefill's tensor-core path (the chunks' T and Qm matrices): [ntok, nv, 2, 64] bf16."""
+    n = _lib.lib().mmp_gdn_prefill_workspace_size(ntok, nv)
+    return torch.empty(max(1, (n + 15) // 16), 16, dtype=torch.uint8, device=device)
+
+
 def gdn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tensor, b: torch.Tensor,
                 state: torch.Tensor, cu_seqlens: torch.Tensor, state_idx: torch.Tensor, has_init: torch.Tensor | None,
                 out: torch.Tensor, z: torch.Tensor | None = None, norm_w: torch.Tensor | None = None,
                 eps: float = 1e-6, A_log: torch.Tensor | None = None,
-                dt_bias: torch.Tensor | None = None) -> torch.Tensor:
+                dt_bias: torch.Tensor | None = None, workspace: torch.Tensor | None = None,
+                tc: bool | None = None) -> torch.Tensor:
     """Chunked gated delta rule over variable-length sequences (tokens [cu[i], cu[i+1]) of q/k [T, nk, dk],
     v/z/out [T, nv, dv], a/b [T, nv]); initial state from state[state_idx[i]] where has_init[i], final state
-    written back there."""
+    written back there.
+
+    tc (default GDN_PREFILL_TC): the tensor-core kernels (a chunk-parallel pass, then the walk with the state in
+    tensor memory), which need 16-byte aligned q/k/v rows and a workspace (gdn_prefill_workspace; one per device
+    is kept here when none is given); otherwise the mma.sync kernel."""
     lines, nv, dv, dk, zs = _gdn_common("gdn_prefill", q, k, v, a, b, state, A_log, dt_bias, z, norm_w)
-    _cuda("gdn_prefill", cu_seqlens, state_idx, has_init, out)
+    _cuda("gdn_prefill", cu_seqlens, state_idx, has_init, out, workspace)
     _dtype("gdn_prefill", out, BF16)
     for t in (cu_seqlens, state_idx, has_init):
         if t is not None:
             _dtype("gdn_prefill", t, torch.int32)
-    nseq = cu_seqlens.numel() - 1
-    _lib.call("mmp_gdn_prefill", _p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1),
-              _p(v), v.stride(0), v.stride(1), _p(a), a.stride(0), _p(b), b.stride(0), _p(A_log), _p(dt_bias),
-              _p(z), zs[0], zs[1], _p(norm_w), float(eps), _p(state), state.stride(0), state.stride(1),
-              state.stride(2), _p(cu_seqlens), _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1),
-              nseq, q.shape[0], q.shape[1], nv, dk, dv, lines, _p(error_word(q.device)), _stream(q))
+    nseq, T = cu_seqlens.numel() - 1, q.shape[0]
+    args = [_p(q), q.stride(0), q.stride(1), _p(k), k.stride(0), k.stride(1),
+            _p(v), v.stride(0), v.stride(1), _p(a), a.stride(0), _p(b), b.stride(0), _p(A_log), _p(dt_bias),
+            _p(z), zs[0], zs[1], _p(norm_w), float(eps), _p(state), state.stride(0), state.stride(1),
+            state.stride(2), _p(cu_seqlens), _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1),
+            nseq, T, q.shape[1], nv, dk, dv, lines]
+    use_tc = GDN_PREFILL_TC if tc is None else tc
+    aligned = all(t.data_ptr() % 16 == 0 and t.stride(0) % 8 == 0 and t.stride(1) % 8 == 0 for t in (q, k, v))
+    if use_tc and T > 0 and dk == 128 and dv == 128 and aligned:
+        need = _lib.lib().mmp_gdn_prefill_workspace_size(T, nv)
+        if workspace is None:
+            dev = q.device.index or 0
+            ws = _gdn_ws.get(dev)
+            if ws is None or ws.numel() < need:
+                ws = _gdn_ws[dev] = gdn_prefill_workspace(T, nv, q.device)
+            workspace = ws
+        _lib.call("mmp_gdn_prefill_tc", *args, _p(workspace), workspace.numel() * workspace.element_size(),
+                  _p(error_word(q.device)), _stream(q), kernels=2)
+    else:
+        _lib.call("mmp_gdn_prefill", *args, _p(error_word(q.device)), _stream(q))
     return out

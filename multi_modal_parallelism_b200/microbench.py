@@ -303,11 +303,12 @@ def only(args, g) -> dict:
         out = torch.empty(T, nv, dv, device=dev, dtype=BF)
         nw = torch.ones(dv, device=dev, dtype=BF)
         if args.only == "gdn_prefill":
+            ws = K.gdn_prefill_workspace(T, nv, dev)
             ms = timed(lambda: K.gdn_prefill(q, k, v, a, b, st, pc.cu_seqlens, pc.state_idx, pc.has_init, out, z=z,
-                                             norm_w=nw))
+                                             norm_w=nw, tc=not args.mma, workspace=ws))
             C = 64  # per token and value head: K K^T, Q K^T, S K^T, S Q^T, T R, Qm U and the state update
             flops = T * nv * (4 * C * dk + 6 * dk * dv + 4 * C * dv)
-            res.update(tokens=T, ms=ms, tflops=flops / ms / 1e9)
+            res.update(tokens=T, ms=ms, tflops=flops / ms / 1e9, kernel="mma.sync" if args.mma else "tcgen05")
         else:
             idx = torch.arange(1, T + 1, device=dev, dtype=torch.int32)
             ms = timed(lambda: K.gdn_decode(q, k, v, a, b, st, idx, out, z=z, norm_w=nw))
@@ -350,6 +351,7 @@ def main() -> None:
     ap.add_argument("--len", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tc", action="store_true", help="attn_prefill: the tcgen05/TMEM kernel")
+    ap.add_argument("--mma", action="store_true", help="gdn_prefill: the mma.sync kernel instead of the tcgen05 pair")
     ap.add_argument("--segments", action="store_true", help="ssd_prefill: balanced walks (segments + join)")
     args = ap.parse_args()
     g = init_groups()

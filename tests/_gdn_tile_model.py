@@ -94,6 +94,56 @@ def prefill_head(q, k, v, g, beta, S0=None, chunk: int = 64):
     return o, S
 
 
+def prefill_head_tc(q, k, v, g, beta, S0=None, chunk: int = 64, eps: float = 1e-6):
+    """One (sequence, value head) as the two tensor-core kernels of csrc/gdn_prefill_tc.cu compute it.
+
+    Chunk pass (every chunk at once, from the raw bf16 q / k rows; r_k = |k|^-1, r_q = dk^-1/2 |q|^-1):
+        N_ij  = beta_i exp(cum_i - cum_j) r_k,i r_k,j (k_i.k_j)   (j < i)   T = bf16((I + N)^-1)
+        Qm_ij = bf16(exp(cum_i - cum_j) r_q,i r_k,j (q_i.k_j))      (j <= i)
+    Walk (state S fp32, bf16(S) as the contraction operand):
+        W^T  = bf16(beta gam K^)^T T^T  (then bf16),   U0^T = bf16(beta V)^T T^T  (fp32)
+        U^T  = U0^T - bf16(S) W^T
+        O^T  = bf16(S) bf16(gam Q^)^T + bf16(U^T) Qm^T
+        S'   = exp(cum_C) S + bf16(U^T diag(exp(cum_C - cum_i))) bf16(K^)
+    with K^ = r_k k and Q^ = r_q q, each product rounded to bf16 once from the raw row."""
+    L, dk = k.shape
+    dv = v.shape[1]
+    S = np.zeros((dv, dk), F32) if S0 is None else S0.astype(F32).copy()
+    o = np.zeros((L, dv), F32)
+    ii, jj = np.meshgrid(np.arange(chunk), np.arange(chunk), indexing="ij")
+    for c0 in range(0, L, chunk):
+        n = min(chunk, L - c0)
+        Q = np.zeros((chunk, dk), F32)
+        Kr = np.zeros((chunk, dk), F32)
+        V = np.zeros((chunk, dv), F32)
+        G = np.zeros(chunk, F32)
+        Bt = np.zeros(chunk, F32)
+        Q[:n], Kr[:n], V[:n] = bf(q[c0:c0 + n]), bf(k[c0:c0 + n]), bf(v[c0:c0 + n])
+        G[:n], Bt[:n] = g[c0:c0 + n], beta[c0:c0 + n]
+        rk = (1 / np.sqrt(np.sum(Kr * Kr, -1) + F32(eps))).astype(F32)
+        rq = (F32(dk ** -0.5) / np.sqrt(np.sum(Q * Q, -1) + F32(eps))).astype(F32)
+        cum = np.cumsum(G, dtype=F32)
+        gam = np.where(np.arange(chunk) < n, np.exp(cum), 0).astype(F32)
+        ratio = np.exp(np.where(jj <= ii, cum[:, None] - cum[None, :], 0)).astype(F32)
+        valid = ii < n
+        Nm = np.where((jj < ii) & valid, Bt[:, None] * ratio * rk[:, None] * rk[None, :] * (Kr @ Kr.T), 0).astype(F32)
+        Qm = bf(np.where((jj <= ii) & valid, ratio * rq[:, None] * rk[None, :] * (Q @ Kr.T), 0))
+        T = bf(unit_lower_inverse(Nm))
+        Kh = bf(Kr * rk[:, None])
+        KW = bf(Kr * (rk * Bt * gam)[:, None])
+        Qg = bf(Q * (rq * gam)[:, None])
+        BV = bf(V * Bt[:, None])
+        W = bf((T @ KW))                       # [chunk, dk]
+        U0T = (T @ BV).T                        # [dv, chunk]
+        Sb = bf(S)
+        UT = U0T - Sb @ W.T
+        w = np.where(np.arange(chunk) < n, np.exp(cum[chunk - 1] - cum), 0).astype(F32)
+        OT = Sb @ Qg.T + bf(UT) @ Qm.T
+        S = np.exp(cum[chunk - 1]) * S + bf(UT * w[None, :]) @ Kh
+        o[c0:c0 + n] = OT.T[:n]
+    return o, S
+
+
 def decode_head(q, k, v, g, beta, S):
     """One token of one (sequence, value head) as the decode kernel computes it: o = a S q + u (k.q) with
     u = beta (v - a S k), then S' = a S + u k^T (a = exp(g)); q, k normalised in fp32."""

@@ -137,7 +137,7 @@ def test_gdn_stack_calls_validate(validating_library, mode):
     stack.step(torch.zeros(pc.T, d.hidden, dtype=torch.bfloat16), pc)
     stack.step(torch.zeros(len(lens), d.hidden, dtype=torch.bfloat16), decode_ctx_after(pc))
     names = {n for n, _ in validating_library}
-    assert {"mmp_gdn_prefill", "mmp_gdn_decode", "mmp_conv1d_prefill", "mmp_conv1d_update", "mmp_paged_attn_prefill",
+    assert {"mmp_gdn_prefill_tc", "mmp_gdn_decode", "mmp_conv1d_prefill", "mmp_conv1d_update", "mmp_paged_attn_prefill",
             "mmp_paged_attn_decode", "mmp_silu_mul", "mmp_rmsnorm"} <= names
 
 

@@ -35,7 +35,7 @@ def _no_device_errors():
     K.check_device_errors(DEV)
 
 
-def fused_inputs(T, g):
+def fused_inputs(T, g, NK=NK, NV=NV):
     """One [T, 2 nk dk + nv dv + nv dv + 2 nv] bf16 projection row: q | k | v | z | a | b (padded to 8 columns)."""
     width = 2 * NK * DK + 2 * NV * DV + 2 * NV
     width8 = (width + 7) // 8 * 8
@@ -52,7 +52,7 @@ def fused_inputs(T, g):
     return q, k, v, z, a, b
 
 
-def decay_params(kind, g):
+def decay_params(kind, g, NV=NV):
     if kind == "plain":
         return None, None
     return (torch.randn(NV, generator=g) * 0.5).to(DEV), (torch.randn(NV, generator=g) * 0.5).to(DEV)
@@ -60,7 +60,7 @@ def decay_params(kind, g):
 
 def ref_head(q, k, v, a, b, j, S0, A_log, dt_bias):
     """Oracle outputs [L, dv] (before the norm) and final state of value head j."""
-    kh = j // (NV // NK)
+    kh = j // (v.shape[1] // q.shape[1])
     qn = l2norm(npf(q[:, kh])) * np.float32(DK ** -0.5)
     kn = l2norm(npf(k[:, kh]))
     gg, beta = gates(npf(a[:, j]), npf(b[:, j]), None if A_log is None else npf(A_log)[j:j + 1],
@@ -97,28 +97,33 @@ def test_gdn_decode_matches_recurrence(kind):
 LENS = [1, 5, 63, 64, 65, 130]
 
 
-@pytest.mark.parametrize("kind,fused_norm", [("plain", True), ("alog", True), ("plain", False)])
-def test_gdn_prefill_matches_recurrence(kind, fused_norm):
-    g = torch.Generator().manual_seed(21 + len(kind) + int(fused_norm))
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("kind,fused_norm,nk,nv", [("plain", True, NK, NV), ("alog", True, NK, NV),
+                                                   ("plain", False, NK, NV), ("alog", True, 2, 2),
+                                                   ("plain", True, 1, 4)])
+def test_gdn_prefill_matches_recurrence(kind, fused_norm, nk, nv, tc):
+    """Both prefill kernels against the recurrence: the tensor-core pair (mmp_gdn_prefill_tc) and the mma.sync
+    kernel, at 1, 2 and 4 value heads per key head."""
+    g = torch.Generator().manual_seed(21 + len(kind) + int(fused_norm) + 7 * nv + nk)
     T = sum(LENS)
     lines = len(LENS) + 3
-    q, k, v, z, a, b = fused_inputs(T, g)
-    A_log, dt_bias = decay_params(kind, g)
-    state0 = torch.randn(lines, NV, DV, DK, generator=g) * 0.3
+    q, k, v, z, a, b = fused_inputs(T, g, nk, nv)
+    A_log, dt_bias = decay_params(kind, g, nv)
+    state0 = torch.randn(lines, nv, DV, DK, generator=g) * 0.3
     st = state0.to(DEV)
     idx = torch.tensor([3, 7, 1, 8, 5, 2], dtype=torch.int32)
     init = torch.tensor([1, 0, 1, 1, 0, 1], dtype=torch.int32)
     cu = torch.tensor(np.concatenate([[0], np.cumsum(LENS)]), dtype=torch.int32)
     w = (1 + 0.1 * torch.randn(DV, generator=g)).to(BF)
-    out = torch.empty(T, NV, DV, dtype=BF, device=DEV)
+    out = torch.empty(T, nv, DV, dtype=BF, device=DEV)
     K.gdn_prefill(q, k, v, a, b, st, cu.to(DEV), idx.to(DEV), init.to(DEV), out, z=z if fused_norm else None,
-                  norm_w=w.to(DEV) if fused_norm else None, eps=EPS, A_log=A_log, dt_bias=dt_bias)
+                  norm_w=w.to(DEV) if fused_norm else None, eps=EPS, A_log=A_log, dt_bias=dt_bias, tc=tc)
     got_state = st.cpu()
     c = cu.numpy()
     for i in range(len(LENS)):
         sl = slice(int(c[i]), int(c[i + 1]))
         line = int(idx[i])
-        for j in range(NV):
+        for j in range(nv):
             S0 = npf(state0[line, j]) if init[i] else None
             o, S = ref_head(q[sl], k[sl], v[sl], a[sl], b[sl], j, S0, A_log, dt_bias)
             ref = gated_norm(o, npf(z[sl, j]), npf(w), EPS) if fused_norm else o
@@ -126,6 +131,36 @@ def test_gdn_prefill_matches_recurrence(kind, fused_norm):
             close(npf(got_state[line, j]), S)
     for line in set(range(lines)) - set(idx.tolist()):
         assert torch.equal(got_state[line], state0[line])
+
+
+def test_gdn_prefill_tc_agrees_with_mma_sync_at_length():
+    """Long ragged sequences (many chunks, empty and one-token sequences among them): the tensor-core pair and the
+    mma.sync kernel agree on outputs and final states, on a reused workspace, twice in a row."""
+    g = torch.Generator().manual_seed(41)
+    lens = [1500, 0, 777, 64, 1, 2049]
+    T = sum(lens)
+    q, k, v, z, a, b = fused_inputs(T, g)
+    A_log, dt_bias = decay_params("alog", g)
+    lines = len(lens) + 1
+    state0 = torch.randn(lines, NV, DV, DK, generator=g) * 0.3
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lens)]), dtype=torch.int32, device=DEV)
+    idx = torch.tensor([1, 2, 3, 4, 5, 6], dtype=torch.int32, device=DEV)
+    init = torch.tensor([1, 1, 0, 1, 0, 1], dtype=torch.int32, device=DEV)
+    w = (1 + 0.1 * torch.randn(DV, generator=g)).to(BF).to(DEV)
+    ws = K.gdn_prefill_workspace(T, NV, DEV)
+    res = {}
+    for tc in (False, True, True):
+        st = state0.to(DEV)
+        out = torch.empty(T, NV, DV, dtype=BF, device=DEV)
+        K.gdn_prefill(q, k, v, a, b, st, cu, idx, init, out, z=z, norm_w=w, eps=EPS, A_log=A_log, dt_bias=dt_bias,
+                      tc=tc, workspace=ws if tc else None)
+        res.setdefault(tc, []).append((npf(out), st.cpu()))
+    (o_m, s_m), = res[False]
+    for o_t, s_t in res[True]:
+        close(o_t, o_m)
+        close(npf(s_t[1:]), npf(s_m[1:]))
+        assert torch.equal(s_t[0], state0[0])
+    assert np.array_equal(res[True][0][0], res[True][1][0])  # deterministic
 
 
 def test_gdn_prefill_then_decode_continues_the_sequence():
