@@ -339,7 +339,7 @@ int mmp_gdn_prefill(const void* q, int64_t q_t, int64_t q_h, const void* k, int6
 /* The same chunked prefill on the tensor cores, in two passes: every chunk of every sequence at once (the chunk's
  * [K; Q] K^T on tcgen05, the inverse of its unit lower-triangular matrix T in fp32, T and the masked Q K^T
  * written to `workspace` as bf16), then one walk per (value head, sequence) with the state in tensor memory.
- * Arguments as mmp_gdn_prefill; q/k/v additionally need 16-byte aligned rows and head strides (TMA). workspace:
+ * Arguments as mmp_gdn_prefill; q/k/v/z/out additionally need 16-byte aligned rows and head strides. workspace:
  * 16-byte aligned, at least mmp_gdn_prefill_workspace_size(ntok, nv) bytes; its contents are scratch.
  * Same results as mmp_gdn_prefill within bf16 rounding (the chunk algebra is regrouped, not changed). */
 size_t mmp_gdn_prefill_workspace_size(int ntok, int nv);

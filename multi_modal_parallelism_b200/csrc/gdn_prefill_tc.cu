@@ -30,7 +30,8 @@
 //   * warps 4-7 (state, one dv row per thread): the state pass (bf16 copy of S into TMEM, gam_C S back) and
 //     U^T = U0^T - X into TMEM as bf16, plain and times w;
 //   * warps 8-11 (output, one dv row per thread): O out of TMEM, the per-token RMS over the head's 128 values
-//     (warp reduce-scatter + 4 partials), gate silu(z), bf16 stores.
+//     (warp reduce-scatter + 4 partials), staged as token rows over the chunk's dead q / k boxes, gate silu(z)
+//     and bf16 stores as 16-byte pieces of rows.
 // The critical path per chunk is the state pass, X, U and the state update; the W / U0 MMAs, their copy, the
 // output and the loads run beside it. Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out of
 // budget flags the error word, leaves its state line untouched, drains its copies and MMAs and frees TMEM.
@@ -132,6 +133,33 @@ __device__ __forceinline__ bool locate_chunk(const int32_t* cu, int nseq, int ci
 
 __device__ __forceinline__ uint32_t swz128(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
+// Bounded wait whose threads sleep in the barrier (try_wait with a suspend-time hint: a suspended thread resumes
+// when the phase completes) instead of spinning: a waiting warp leaves its issue slots to the working ones.
+constexpr uint32_t WAIT_HINT_NS = 20000;
+// Non-blocking test of a phase (test_wait never suspends)
+__device__ __forceinline__ bool phase_done(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n.reg .pred p;\nmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\nselp.u32 %0, 1, 0, p;\n}\n"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool wait_sleep(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err) {
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t ok;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok) : "r"(bar), "r"(parity), "r"(WAIT_HINT_NS) : "memory");
+    if (ok) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > WAIT_BUDGET_CYCLES) {
+      *abort_flag = 1;
+      flag_error(err, DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
 // UMMA descriptor of an MN-major operand stored as boxes [K rows][64 MN elements] (128-byte swizzle): 8-row K groups
 // 1024 bytes apart, 64-element MN blocks `mn_block` bytes apart
 __device__ __forceinline__ uint64_t desc_mn(uint32_t saddr, uint32_t mn_block) {
@@ -192,7 +220,7 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
                                                                  const GdnTcParams P) {
   using L = PrepSmem;
   extern __shared__ uint8_t dsmem[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = dsmem + ((1024u - (smem_addr(dsmem) & 1023u)) & 1023u);  // 1024-aligned, still a shared pointer
   pdl_trigger();
   pdl_wait();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -229,7 +257,7 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
       tma_load_3d(sb + L::QK + kb * 16384 + 8192, &mapQ, bar_ld, kb * 64, kh, c0);
     }
   }
-  bool ok = mbar_wait(bar_ld, 0, abort_flag, P.err);
+  bool ok = wait_sleep(bar_ld, 0, abort_flag, P.err);
   if (tid == 0 && ok) {
     // D = [K; Q] K^T: M = 128 (rows of K, then of Q), N = 64 (rows of K), K = 128 (two 64-wide k-blocks)
     tc_fence_after();
@@ -267,7 +295,7 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
     }
   }
   __syncthreads();
-  ok = ok && mbar_wait(bar_mma, 0, abort_flag, P.err);
+  ok = ok && wait_sleep(bar_mma, 0, abort_flag, P.err);
   ok = __syncthreads_and(ok);
   if (ok) {
     tc_fence_after();
@@ -443,7 +471,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
   using L = WalkSmem;
   using TM = WalkTmem;
   extern __shared__ uint8_t dsmem[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem = dsmem + ((1024u - (smem_addr(dsmem) & 1023u)) & 1023u);  // 1024-aligned, still a shared pointer
   pdl_trigger();
   pdl_wait();
   const uint32_t sb = smem_addr(smem);
@@ -466,7 +494,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
   if (tid == 0) {
     for (int s = 0; s < L::NST; ++s) {
       mbar_init(bar(WB_FULL + s), 1);
-      mbar_init(bar(WB_EMPTY + s), 1);
+      mbar_init(bar(WB_EMPTY + s), 2);  // the MMAs reading the stage, and the output group's staging over it
     }
     for (int i = 0; i < 4; ++i) mbar_init(bar(WB_GATES + i), 32);
     mbar_init(bar(WB_PREP), 128);
@@ -505,7 +533,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       const int c0 = t_begin + c * GC;
       int go = 1;
       if (lane == 0) {
-        if (c >= L::NST && !mbar_wait(bar(WB_EMPTY + s), ((c / L::NST) - 1) & 1, abort_flag, P.err)) go = 0;
+        if (c >= L::NST && !wait_sleep(bar(WB_EMPTY + s), ((c / L::NST) - 1) & 1, abort_flag, P.err)) go = 0;
         if (*abort_flag) go = 0;
         if (go) {
           const uint32_t st = sb + s * L::STAGE, full = bar(WB_FULL + s);
@@ -562,8 +590,8 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       constexpr uint32_t id_w = umma_idesc_mn(128, 64) | A_MN;   // W^T, U0^T           (A: K / V rows, MN-major)
       auto stage = [&](int c) { return sb + (c % L::NST) * L::STAGE; };
       auto ready = [&](int c) {  // chunk c prepared by warps 0-3 and its copies landed
-        return mbar_wait(bar(WB_PREP), c & 1, abort_flag, P.err) &&
-               mbar_wait(bar(WB_FULL + c % L::NST), (c / L::NST) & 1, abort_flag, P.err);
+        return wait_sleep(bar(WB_PREP), c & 1, abort_flag, P.err) &&
+               wait_sleep(bar(WB_FULL + c % L::NST), (c / L::NST) & 1, abort_flag, P.err);
       };
       auto issue_wu = [&](int c) {  // W^T = K^^T (T beta gam)^T, U0^T = V^T (T beta)^T (K = 64 tokens)
         const uint32_t st = stage(c);
@@ -583,7 +611,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       for (int c = 0; ok && c < nchunks; ++c) {
         const uint32_t par = c & 1, st = stage(c);
         // W(c) in shared memory and the state pass done: X = S_bf W^T (K = 128 over d)
-        if (!(ok = mbar_wait(bar(WB_WREADY), par, abort_flag, P.err) && mbar_wait(bar(WB_SP), par, abort_flag, P.err)))
+        if (!(ok = wait_sleep(bar(WB_WREADY), par, abort_flag, P.err) && wait_sleep(bar(WB_SP), par, abort_flag, P.err)))
           break;
         tc_fence_after();
 #pragma unroll
@@ -591,7 +619,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
           mma_ts(tmem + TM::X, tmem + TM::SBF + kk * 8, desc_mn(sb + L::W + kk * 2048, 8192), id_x, kk != 0);
         umma_commit(bar(WB_XDONE));
         // O = S_bf (gam Q^)^T, once the previous O is read out
-        if (c > 0 && !(ok = mbar_wait(bar(WB_OFREE), par ^ 1, abort_flag, P.err))) break;
+        if (c > 0 && !(ok = wait_sleep(bar(WB_OFREE), par ^ 1, abort_flag, P.err))) break;
         tc_fence_after();
 #pragma unroll
         for (int kb = 0; kb < 2; ++kb)
@@ -600,7 +628,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
             mma_ts(tmem + TM::O, tmem + TM::SBF + kb * 32 + kk * 8, umma_desc(st + L::Q + kb * 8192 + kk * 32), id_o,
                    (kb | kk) != 0);
         // U in TMEM: S += (U w)_bf K^ (K = 64 tokens)
-        if (!(ok = mbar_wait(bar(WB_UREADY), par, abort_flag, P.err))) break;
+        if (!(ok = wait_sleep(bar(WB_UREADY), par, abort_flag, P.err))) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
@@ -608,8 +636,8 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
         umma_commit(bar(WB_SDONE));
         // the next chunk's W^T / U0^T ahead of O += U Qm^T when it is prepared already (U0^T and W^T are read out)
         bool wu = false;
-        if (c + 1 < nchunks && mbar_try(bar(WB_PREP), (c + 1) & 1) &&
-            mbar_try(bar(WB_FULL + (c + 1) % L::NST), ((c + 1) / L::NST) & 1)) {
+        if (c + 1 < nchunks && phase_done(bar(WB_PREP), (c + 1) & 1) &&
+            phase_done(bar(WB_FULL + (c + 1) % L::NST), ((c + 1) / L::NST) & 1)) {
           tc_fence_after();
           issue_wu(c + 1);
           wu = true;
@@ -633,8 +661,8 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
     const int u = tid;
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % L::NST;
-      bool ok = mbar_wait(bar(WB_FULL + s), (c / L::NST) & 1, abort_flag, P.err) &&
-                mbar_wait(bar(WB_GATES + (c & 3)), (c >> 2) & 1, abort_flag, P.err);
+      bool ok = wait_sleep(bar(WB_FULL + s), (c / L::NST) & 1, abort_flag, P.err) &&
+                wait_sleep(bar(WB_GATES + (c & 3)), (c >> 2) & 1, abort_flag, P.err);
       if (!__all_sync(0xffffffffu, ok)) break;
       uint8_t* st = smem + s * L::STAGE;
       const float* g = gates(c);
@@ -694,7 +722,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       proxy_fence();  // generic shared-memory writes -> tensor-core reads
       arrive1(bar(WB_PREP));
       // W^T(c) out of TMEM (lane d) into the X operand: row d of [128 d][64 i] bf16
-      ok = mbar_wait(bar(WB_WU), c & 1, abort_flag, P.err);
+      ok = wait_sleep(bar(WB_WU), c & 1, abort_flag, P.err);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
       uint32_t r[64];
@@ -737,8 +765,8 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
     for (int c = 0; c < nchunks; ++c) {
       const uint32_t par = c & 1;
       const int qn = min(GC, t_end - t_begin - c * GC);
-      if (c > 0) ok = mbar_wait(bar(WB_SDONE), par ^ 1, abort_flag, P.err);
-      ok = ok && mbar_wait(bar(WB_GATES + (c & 3)), (c >> 2) & 1, abort_flag, P.err);
+      if (c > 0) ok = wait_sleep(bar(WB_SDONE), par ^ 1, abort_flag, P.err);
+      ok = ok && wait_sleep(bar(WB_GATES + (c & 3)), (c >> 2) & 1, abort_flag, P.err);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
       const float* g = gates(c);
@@ -762,7 +790,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       tc_fence_before();
       arrive1(bar(WB_SP));
       // U^T = U0^T - X (zero past the sequence end), as bf16 plain and times w
-      ok = mbar_wait(bar(WB_XDONE), par, abort_flag, P.err);
+      ok = wait_sleep(bar(WB_XDONE), par, abort_flag, P.err);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
       tc_fence_after();
       const float* w = g + 128;
@@ -788,7 +816,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       arrive1(bar(WB_UREADY));
     }
     // final state -> the sequence's line (skipped after an abort: the line keeps its old value)
-    if (ok && nchunks > 0) ok = mbar_wait(bar(WB_SDONE), (nchunks - 1) & 1, abort_flag, P.err);
+    if (ok && nchunks > 0) ok = wait_sleep(bar(WB_SDONE), (nchunks - 1) & 1, abort_flag, P.err);
     ok = __all_sync(0xffffffffu, ok) && !*abort_flag;
     if (ok) {
       tc_fence_after();
@@ -806,6 +834,10 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
     }
   } else {
     // ------------------------------------------------------------------ warps 8-11: output rows
+    // O (lane v, column i) times 1 / RMS and the norm weight is staged as fp32 [64 i][128 v] over the chunk's q / k
+    // boxes (their last readers, the O1 and state MMAs, completed before O2), then each thread takes 16-byte pieces of
+    // token rows: times silu(z) from coalesced 16-byte loads, bf16, coalesced 16-byte stores. The stage is released
+    // to the copy warp (its second EMPTY arrival) once the staging has been read.
     const int u = tid - 256;  // dv row = TMEM lane
     const int wq = warp & 3;
     const float wv = P.norm_w ? bf2f(P.norm_w[u]) : 1.f;
@@ -813,19 +845,17 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
     for (int c = 0; c < nchunks; ++c) {
       const int c0 = t_begin + c * GC;
       const int qn = min(GC, t_end - c0);
-      // the gate values of this row for the chunk's tokens, all requested before the wait (bf16 pairs)
-      uint32_t zr[GC / 2];
-      if (P.z) {
-        const unsigned short* zp = reinterpret_cast<const unsigned short*>(P.z + static_cast<int64_t>(c0) * P.z_t +
-                                                                           j * P.z_h + u);
+      float* ys = reinterpret_cast<float*>(smem + (c % L::NST) * L::STAGE + L::Q);  // [64][128] fp32, 32 KB
+      // this thread's pieces: row (u + 128 k) / 16, values 8 ((u + 128 k) % 16) .. + 7; gates requested before the wait
+      uint4 zv[8];
 #pragma unroll
-        for (int e = 0; e < GC / 2; ++e) {
-          const uint32_t lo = 2 * e < qn ? __ldg(zp + static_cast<int64_t>(2 * e) * P.z_t) : 0u;
-          const uint32_t hi = 2 * e + 1 < qn ? __ldg(zp + static_cast<int64_t>(2 * e + 1) * P.z_t) : 0u;
-          zr[e] = lo | (hi << 16);
-        }
+      for (int k = 0; k < 8; ++k) {
+        const int idx = u + 128 * k, i = idx >> 4, cc = idx & 15;
+        zv[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (P.z && i < qn)
+          zv[k] = __ldg(reinterpret_cast<const uint4*>(P.z + static_cast<int64_t>(c0 + i) * P.z_t + j * P.z_h + cc * 8));
       }
-      if (!and_bar(3, 128, mbar_wait(bar(WB_ODONE), c & 1, abort_flag, P.err))) break;
+      if (!and_bar(3, 128, wait_sleep(bar(WB_ODONE), c & 1, abort_flag, P.err))) break;
       tc_fence_after();
       uint32_t o[64];
       tmem_ld64(t_lane + TM::O, o);
@@ -867,16 +897,35 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
         rs0 = rsqrtf(t0 / static_cast<float>(GD) + P.eps);
         rs1 = rsqrtf(t1 / static_cast<float>(GD) + P.eps);
       }
-      bf16* op = P.out + static_cast<int64_t>(c0) * P.o_t + j * P.o_h + u;
 #pragma unroll
       for (int i = 0; i < GC; ++i) {
         const float rs = __shfl_sync(0xffffffffu, (i & 1) ? rs1 : rs0, i >> 1);
+        ys[i * GD + u] = __uint_as_float(o[i]) * rs * wv;
+      }
+      asm volatile("bar.sync 3, 128;\n" ::: "memory");
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int idx = u + 128 * k, i = idx >> 4, cc = idx & 15;
         if (i < qn) {
-          float y = __uint_as_float(o[i]) * rs * wv;
-          if (P.z) y *= silu(__uint_as_float((i & 1) ? (zr[i >> 1] & 0xffff0000u) : (zr[i >> 1] << 16)));
-          op[static_cast<int64_t>(i) * P.o_t] = f2bf(y);
+          const float4 a0 = *reinterpret_cast<const float4*>(ys + i * GD + cc * 8);
+          const float4 a1 = *reinterpret_cast<const float4*>(ys + i * GD + cc * 8 + 4);
+          float y[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+          if (P.z) {
+            const uint32_t zw[4] = {zv[k].x, zv[k].y, zv[k].z, zv[k].w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 zf = unpack_bf16x2(zw[e]);
+              y[2 * e] *= silu(zf.x);
+              y[2 * e + 1] *= silu(zf.y);
+            }
+          }
+          st16(P.out + static_cast<int64_t>(c0 + i) * P.o_t + j * P.o_h + cc * 8,
+               make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                          pack_bf16x2(y[6], y[7])));
         }
       }
+      asm volatile("bar.sync 3, 128;\n" ::: "memory");  // the staging is read: the stage may be reloaded
+      if (u == 0) arrive1(bar(WB_EMPTY + c % L::NST));
     }
   }
 
@@ -954,6 +1003,8 @@ extern "C" int mmp_gdn_prefill_tc(const void* q, int64_t q_t, int64_t q_h, const
     return mmp_set_error(MMP_ERR_INVALID, "mmp_gdn_prefill_tc: q, k and v rows must be 16-byte aligned");
   if (!aligned16(state) || s_line % 4 || s_head % 4 || s_row % 4)
     return mmp_set_error(MMP_ERR_INVALID, "mmp_gdn_prefill_tc: state rows must be 16-byte aligned");
+  if (!aligned16(out) || o_t % 8 || o_h % 8 || (z && (!aligned16(z) || z_t % 8 || z_h % 8)))
+    return mmp_set_error(MMP_ERR_INVALID, "mmp_gdn_prefill_tc: out and z rows must be 16-byte aligned");
   if (ntok == 0)  // every sequence is empty: only the state lines are written
     return mmp_gdn_prefill(q, q_t, q_h, k, k_t, k_h, v, v_t, v_h, a, a_t, b, b_t, A_log, dt_bias, z, z_t, z_h, norm_w,
                            eps, state, s_line, s_head, s_row, cu_seqlens, state_idx, has_init, out, o_t, o_h, nseq, ntok,

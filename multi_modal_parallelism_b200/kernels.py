@@ -611,7 +611,7 @@ def gdn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tens
     written back there.
 
     tc (default GDN_PREFILL_TC): the tensor-core kernels (a chunk-parallel pass, then the walk with the state in
-    tensor memory), which need 16-byte aligned q/k/v rows and a workspace (gdn_prefill_workspace; one per device
+    tensor memory), which need 16-byte aligned q/k/v/z/out rows and a workspace (gdn_prefill_workspace; one per device
     is kept here when none is given); otherwise the mma.sync kernel."""
     lines, nv, dv, dk, zs = _gdn_common("gdn_prefill", q, k, v, a, b, state, A_log, dt_bias, z, norm_w)
     _cuda("gdn_prefill", cu_seqlens, state_idx, has_init, out, workspace)
@@ -626,7 +626,8 @@ def gdn_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, a: torch.Tens
             state.stride(2), _p(cu_seqlens), _p(state_idx), _p(has_init), _p(out), out.stride(0), out.stride(1),
             nseq, T, q.shape[1], nv, dk, dv, lines]
     use_tc = GDN_PREFILL_TC if tc is None else tc
-    aligned = all(t.data_ptr() % 16 == 0 and t.stride(0) % 8 == 0 and t.stride(1) % 8 == 0 for t in (q, k, v))
+    aligned = all(t.data_ptr() % 16 == 0 and t.stride(0) % 8 == 0 and t.stride(1) % 8 == 0
+                  for t in (q, k, v, out) + ((z,) if z is not None else ()))
     if use_tc and T > 0 and dk == 128 and dv == 128 and aligned:
         need = _lib.lib().mmp_gdn_prefill_workspace_size(T, nv)
         if workspace is None:

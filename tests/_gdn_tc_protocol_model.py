@@ -4,7 +4,8 @@ mbarriers keep arrival counts, transaction bytes and a phase counter with try_wa
 completes MMAs in issue order at random times and a commit arrives once everything issued before it has completed.
 The copy warp (loads into a three-stage ring, then the chunk's gates into a ring of four buffers), the MMA thread,
 the operand group (warps 0-3: in-place scaling of the stage, T beta gam, W^T out of TMEM), the state group (warps
-4-7: state pass, U) and the output group (warps 8-11: O out of TMEM) run the kernel's sequence of waits, arrivals,
+4-7: state pass, U) and the output group (warps 8-11: O out of TMEM, rows staged over the chunk's stage, which it
+then releases with the MMAs' commit) run the kernel's sequence of waits, arrivals,
 issues, reads and writes, each group as `warps` actors that arrive separately. Every access is checked: an MMA may
 only read a buffer holding the version it needs with nothing writing it, copies and threads may only overwrite
 what nothing still reads, threads may only read what the MMAs have finished. A run also fails if every actor waits
@@ -26,7 +27,8 @@ class GdnWalkSim:
                      "OFREE": Bar(warps), "UREADY": Bar(warps), "SDONE": Bar(1), "ODONE": Bar(1), "DONE": Bar(1)}
         for s in range(NST):
             self.bars[f"FULL{s}"] = Bar(1)
-            self.bars[f"EMPTY{s}"] = Bar(1)
+            # the commit after the chunk's last MMA, and the output group (planted mistake: the commit alone)
+            self.bars[f"EMPTY{s}"] = Bar(1 if bug == "empty_one" else 2)
         for i in range(4):
             self.bars[f"GATES{i}"] = Bar(1)
         # versions: ST{s} ("raw" | "prep", chunk); S ("init" | "dec" | "upd", chunk); O ("o1" | "o", chunk); the rest
@@ -40,7 +42,7 @@ class GdnWalkSim:
         self.readers = {k: 0 for k in self.version}
         self.writers = {k: 0 for k in self.version}
         self.mma_pending = {k: [0, None] for k in self.version}  # MMAs in flight writing the buffer, last version
-        self.done = {k: {} for k in ("prep", "tbg", "w", "sp", "u")}  # step -> chunk -> warps finished
+        self.done = {k: {} for k in ("prep", "tbg", "w", "sp", "u", "stage", "read")}  # step -> chunk -> warps finished
         self.o_read = [None] * warps
         self.gate_users: dict[int, int] = {}
         self.copies: list = []
@@ -120,7 +122,7 @@ class GdnWalkSim:
             if c >= NST and self.bug != "load_early":
                 yield (f"EMPTY{s}", ((c // NST) - 1) & 1)
             st = f"ST{s}"
-            if self.readers[st] or (self.version[st] is not None and self.version[st][1] != c - NST):
+            if self.readers[st] or (self.version[st] is not None and self.version[st] != ("out", c - NST)):
                 self.err(f"load of chunk {c} into {st} while it holds {self.version[st]} (readers {self.readers[st]})")
             if self.bars[f"FULL{s}"].pending == 0:
                 self.err(f"load of chunk {c} arms FULL{s} before its previous load completed")
@@ -235,10 +237,21 @@ class GdnWalkSim:
 
     def output_warp(self, w):
         for c in range(self.n):
+            st = f"ST{c % NST}"
             yield ("ODONE", c & 1)
             self.thread_read("O", ("o", c), f"output warp {w}")
             self.o_read[w] = c
             self.bars["OFREE"].arrive()
+            # the output rows staged over the chunk's q / k boxes (a group barrier), then read back (another)
+            self.thread_read(st, ("prep", c), f"output warp {w} (staging over chunk {c})")
+            self.thread_write(st, f"output warp {w} (staging over chunk {c})")
+            if self.finish("stage", c):
+                self.version[st] = ("out", c)
+            yield ("COND", lambda c=c: self.done["stage"].get(c, 0) >= self.warps)
+            self.thread_read(st, ("out", c), f"output warp {w} (reading chunk {c}'s rows)")
+            if self.finish("read", c) and self.bug != "empty_one":
+                self.bars[f"EMPTY{c % NST}"].arrive()
+            yield ("COND", lambda c=c: self.done["read"].get(c, 0) >= self.warps)
 
     # ---------------------------------------------------------------- scheduler
     def run(self) -> list[str]:
@@ -254,7 +267,7 @@ class GdnWalkSim:
             choices = []
             for a in live:
                 wt = waiting[a]
-                if wt is None or self.bars[wt[0]].passed(wt[1]):
+                if wt is None or (wt[1]() if wt[0] == "COND" else self.bars[wt[0]].passed(wt[1])):
                     choices.append(("actor", a))
             choices += [("copy", i) for i in range(len(self.copies))]
             if self.mma_q:
