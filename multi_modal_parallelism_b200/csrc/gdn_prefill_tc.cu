@@ -14,8 +14,8 @@
 // Pass 1, gdn_chunk_prep_kernel: one CTA per (chunk, key head), every chunk of every sequence at once. The raw q
 // and k rows arrive by TMA; one tcgen05.mma computes [K; Q] K^T (M = 128, N = 64, K = 128) into TMEM, and each
 // warpgroup, for one value head of the key head, scales it by the row norms and the decays into N (fp32, shared
-// memory) and Qm (bf16, to a workspace), then inverts I + N in fp32 on the CUDA cores (16 x 16 diagonal blocks by
-// forward substitution, then the blocks below them by distance from the diagonal) and writes T (bf16) to the
+// memory) and Qm (bf16, to a workspace), then inverts I + N in fp32 on the CUDA cores (forward substitution, one
+// column per thread, held in registers, the rows of N read as shared-memory broadcasts) and writes T (bf16) to the
 // workspace. Nothing here depends on the state.
 //
 // Pass 2, gdn_walk_tc_kernel: one CTA per (value head, sequence) walks the chunks with S [dv = 128 lanes x dk = 128
@@ -67,29 +67,32 @@ __device__ __forceinline__ float gdn_g(float a_raw, float dtb, float A_log, bool
   return -(has_A ? __expf(A_log) : 1.f) * softplus(a_raw + dtb);
 }
 
-// Raw gate projections of one chunk for value head j, tokens 2 lane and 2 lane + 1 (zero past qn).
-__device__ __forceinline__ void gate_raw(const GdnTcParams& P, int64_t t0, int qn, int j, int lane, float (&ar)[2],
-                                         float (&br)[2]) {
+// Raw gate projections of one chunk for value head j, tokens 2 lane and 2 lane + 1, as bf16 bit patterns (nothing
+// is computed from them here, so a load in flight does not hold the warp up until chunk_gates needs it).
+__device__ __forceinline__ void gate_raw(const GdnTcParams& P, int64_t t0, int qn, int j, int lane, uint32_t (&ar)[2],
+                                         uint32_t (&br)[2]) {
+  const unsigned short* pa = reinterpret_cast<const unsigned short*>(P.a);
+  const unsigned short* pb = reinterpret_cast<const unsigned short*>(P.b);
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const int r = lane * 2 + e;
-    ar[e] = r < qn ? bf2f(P.a[(t0 + r) * P.a_t + j]) : 0.f;
-    br[e] = r < qn ? bf2f(P.b[(t0 + r) * P.b_t + j]) : 0.f;
+    ar[e] = r < qn ? __ldg(pa + (t0 + r) * P.a_t + j) : 0u;
+    br[e] = r < qn ? __ldg(pb + (t0 + r) * P.b_t + j) : 0u;
   }
 }
 
 // Gates of one chunk from its raw projections (gate_raw): inclusive running sum of g (cum), beta (zero past qn),
 // and the chunk total. Both passes call this, so their decays agree bit for bit.
-__device__ __forceinline__ void chunk_gates(const GdnTcParams& P, const float (&ar)[2], const float (&br)[2], int qn,
-                                            int j, int lane, float (&cum)[2], float (&beta)[2], float& total) {
+__device__ __forceinline__ void chunk_gates(const GdnTcParams& P, const uint32_t (&ar)[2], const uint32_t (&br)[2],
+                                            int qn, int j, int lane, float (&cum)[2], float (&beta)[2], float& total) {
   const bool has_A = P.A_log != nullptr;
   const float A_log = has_A ? P.A_log[j] : 0.f, dtb = P.dt_bias ? P.dt_bias[j] : 0.f;
   float gg[2];
 #pragma unroll
   for (int e = 0; e < 2; ++e) {
     const bool ok = lane * 2 + e < qn;
-    gg[e] = ok ? gdn_g(ar[e], dtb, A_log, has_A) : 0.f;
-    beta[e] = ok ? __fdividef(1.f, 1.f + __expf(-br[e])) : 0.f;
+    gg[e] = ok ? gdn_g(__uint_as_float(ar[e] << 16), dtb, A_log, has_A) : 0.f;
+    beta[e] = ok ? __fdividef(1.f, 1.f + __expf(-__uint_as_float(br[e] << 16))) : 0.f;
   }
   const float c1 = gg[0] + gg[1];
   float run = c1;
@@ -201,14 +204,13 @@ __device__ __forceinline__ bool and_bar(int id, int nthreads, bool v) {
 // ============================================================================================ pass 1
 constexpr int PTHR = 256;  // two warpgroups, one value head each at a time
 constexpr int NLD = 68;    // fp32 row stride of N and T (float4 rows without bank conflicts)
-constexpr int XLD = 17;
 
 struct PrepSmem {
   static constexpr int QK = 0;            // k-block kb at kb * 16384: K rows 0-63, then Q rows 0-63 (128 B each)
   static constexpr int RK = 32768;        // [64] |k|^-1, then [64] dk^-1/2 |q|^-1
   static constexpr int WG = RK + 512;     // per warpgroup:
-  static constexpr int CUM = 0, BETA = 256, N = 512, TF = N + 64 * NLD * 4, X = TF + 64 * NLD * 4;
-  static constexpr int WG_BYTES = X + 3 * 16 * XLD * 4 + 64;
+  static constexpr int CUM = 0, BETA = 256, N = 512, TF = N + 64 * NLD * 4;
+  static constexpr int WG_BYTES = TF + 64 * NLD * 4;
   static constexpr int BAR = WG + 2 * WG_BYTES;
   static constexpr int USED = BAR + 32;
   static constexpr int DYN = USED + 1024;
@@ -257,6 +259,10 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
       tma_load_3d(sb + L::QK + kb * 16384 + 8192, &mapQ, bar_ld, kb * 64, kh, c0);
     }
   }
+  // the first value head's raw gates, requested before the wait on q / k (warp 0 of each warpgroup)
+  const int rheads = P.nv / P.nk;
+  uint32_t g_ar[2] = {0u, 0u}, g_br[2] = {0u, 0u};
+  if ((warp & 3) == 0 && (warp >> 2) < rheads) gate_raw(P, c0, qn, kh * rheads + (warp >> 2), lane, g_ar, g_br);
   bool ok = wait_sleep(bar_ld, 0, abort_flag, P.err);
   if (tid == 0 && ok) {
     // D = [K; Q] K^T: M = 128 (rows of K, then of Q), N = 64 (rows of K), K = 128 (two 64-wide k-blocks)
@@ -306,19 +312,17 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
     float* sBeta = reinterpret_cast<float*>(wgs + L::BETA);
     float* sN = reinterpret_cast<float*>(wgs + L::N);
     float* sTf = reinterpret_cast<float*>(wgs + L::TF);
-    float* sX = reinterpret_cast<float*>(wgs + L::X);
-    const int r = P.nv / P.nk;
-    for (int jj = wg; jj < r; jj += 2) {
-      const int j = kh * r + jj;
+    for (int jj = wg; jj < rheads; jj += 2) {
+      const int j = kh * rheads + jj;
       if (wq == 0) {
-        float ar[2], br[2], cum[2], beta[2], tot;
-        gate_raw(P, c0, qn, j, lane, ar, br);
-        chunk_gates(P, ar, br, qn, j, lane, cum, beta, tot);
+        if (jj != wg) gate_raw(P, c0, qn, j, lane, g_ar, g_br);
+        float cum[2], beta[2], tot;
+        chunk_gates(P, g_ar, g_br, qn, j, lane, cum, beta, tot);
         *reinterpret_cast<float2*>(sCum + 2 * lane) = make_float2(cum[0], cum[1]);
         *reinterpret_cast<float2*>(sBeta + 2 * lane) = make_float2(beta[0], beta[1]);
       }
       asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");
-      // row u of D: rows 0-63 give N, rows 64-127 give Qm
+      // row u of D: rows 0-63 give N (fp32, shared memory), rows 64-127 give Qm (bf16, straight to the workspace)
       uint32_t d[64];
       tmem_ld64(tmem + (static_cast<uint32_t>(wq * 32) << 16), d);
       tmem_wait();
@@ -336,6 +340,37 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
           }
           *reinterpret_cast<float4*>(sN + i * NLD + c4 * 4) = make_float4(n[0], n[1], n[2], n[3]);
         }
+        // T = (I + N)^-1 by forward substitution, one column per thread (column u), in registers: t_i = -sum_{m < i}
+        // N_im t_m below the diagonal, with the rows of N read as broadcasts (every thread reads the same row)
+        asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id + 2) : "memory");
+        float t[GC];
+#pragma unroll
+        for (int ii = 0; ii < GC; ++ii) {
+          float acc = 0.f;
+#pragma unroll
+          for (int m4 = 0; m4 < (ii + 3) / 4; ++m4) {  // N_im = 0 for m >= i
+            const float4 nv4 = *reinterpret_cast<const float4*>(sN + ii * NLD + 4 * m4);
+            acc = fmaf(nv4.x, t[4 * m4], acc);
+            if (4 * m4 + 1 < ii) acc = fmaf(nv4.y, t[4 * m4 + 1], acc);
+            if (4 * m4 + 2 < ii) acc = fmaf(nv4.z, t[4 * m4 + 2], acc);
+            if (4 * m4 + 3 < ii) acc = fmaf(nv4.w, t[4 * m4 + 3], acc);
+          }
+          t[ii] = ii == u ? 1.f : (ii < u ? 0.f : -acc);
+        }
+        // column u into T's rows (a warp writes 32 consecutive floats of each row), then each thread one row
+#pragma unroll
+        for (int ii = 0; ii < GC; ++ii) sTf[ii * NLD + u] = t[ii];
+        asm volatile("bar.sync %0, 64;\n" ::"r"(bar_id + 2) : "memory");
+        if (u < qn) {
+          bf16* dst = P.Tw + (static_cast<int64_t>(c0 + i) * P.nv + j) * GC;
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const float4 x0 = *reinterpret_cast<const float4*>(sTf + i * NLD + c8 * 8);
+            const float4 x1 = *reinterpret_cast<const float4*>(sTf + i * NLD + c8 * 8 + 4);
+            st16(dst + c8 * 8, make_uint4(pack_bf16x2(x0.x, x0.y), pack_bf16x2(x0.z, x0.w), pack_bf16x2(x1.x, x1.y),
+                                          pack_bf16x2(x1.z, x1.w)));
+          }
+        }
       } else {
         const int i = u - 64;
         if (i < qn) {
@@ -352,68 +387,6 @@ __global__ void __launch_bounds__(PTHR, 2) gdn_chunk_prep_kernel(const __grid_co
             st16(dst + c8 * 8, make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
                                           pack_bf16x2(m[6], m[7])));
           }
-        }
-      }
-      asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");
-      // T = (I + N)^-1: the 16 x 16 diagonal blocks, one column per thread
-      if (u < 64) {
-        const int o = (u >> 4) * 16, e = u & 15;
-        float t[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) t[i] = i == e ? 1.f : 0.f;
-#pragma unroll
-        for (int i = 1; i < 16; ++i) {
-          if (i > e) {
-            float s = 0.f;
-#pragma unroll
-            for (int m = 0; m < i; ++m)
-              if (m >= e) s = fmaf(sN[(o + i) * NLD + o + m], t[m], s);
-            t[i] = -s;
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sTf[(o + i) * NLD + o + e] = t[i];
-      }
-      asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");
-      // the blocks below, by distance from the diagonal: T_ab = -T_aa sum_{b <= c < a} N_ac T_cb
-#pragma unroll 1
-      for (int dist = 1; dist < 4; ++dist) {
-        const int nblk = 4 - dist;
-        for (int idx = u; idx < nblk * 256; idx += 128) {
-          const int bj = idx >> 8, rr = (idx >> 4) & 15, c = idx & 15, bi = bj + dist;
-          float x = 0.f;
-          for (int kb = bj; kb < bi; ++kb) {
-#pragma unroll
-            for (int m = 0; m < 16; ++m)
-              x = fmaf(sN[(bi * 16 + rr) * NLD + kb * 16 + m], sTf[(kb * 16 + m) * NLD + bj * 16 + c], x);
-          }
-          sX[(bj * 16 + rr) * XLD + c] = x;
-        }
-        asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");
-        for (int idx = u; idx < nblk * 256; idx += 128) {
-          const int bj = idx >> 8, rr = (idx >> 4) & 15, c = idx & 15, bi = bj + dist;
-          float x = 0.f;
-#pragma unroll
-          for (int m = 0; m < 16; ++m)
-            if (m <= rr) x = fmaf(sTf[(bi * 16 + rr) * NLD + bi * 16 + m], sX[(bj * 16 + m) * XLD + c], x);
-          sTf[(bi * 16 + rr) * NLD + bj * 16 + c] = -x;
-        }
-        asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");
-      }
-      // T rows of this chunk's tokens -> workspace (zero above the block diagonal)
-      if (u < qn) {
-        const int i = u;
-        bf16* dst = P.Tw + (static_cast<int64_t>(c0 + i) * P.nv + j) * GC;
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          float t[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) {
-            const int jx = c8 * 8 + e;
-            t[e] = (jx >> 4) <= (i >> 4) ? sTf[i * NLD + jx] : 0.f;
-          }
-          st16(dst + c8 * 8, make_uint4(pack_bf16x2(t[0], t[1]), pack_bf16x2(t[2], t[3]), pack_bf16x2(t[4], t[5]),
-                                        pack_bf16x2(t[6], t[7])));
         }
       }
       asm volatile("bar.sync %0, 128;\n" ::"r"(bar_id) : "memory");  // buffers are rewritten for the next head
@@ -526,7 +499,7 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
   if (warp == 12) {
     // ------------------------------------------------------------------ copies (one thread), then the gates (warp)
     int issued = 0;
-    float ar[2], br[2];  // raw gates of the chunk about to be loaded, requested a chunk ahead
+    uint32_t ar[2], br[2];  // raw gates of the chunk about to be loaded, requested a chunk ahead
     if (nchunks > 0) gate_raw(P, t_begin, min(GC, t_end - t_begin), j, lane, ar, br);
     for (int c = 0; c < nchunks; ++c) {
       const int s = c % L::NST;
@@ -673,17 +646,19 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
         for (int m = 0; m < 2; ++m) {
           uint8_t* base = st + (m == 0 ? L::K : L::Q) + kb * 8192;
           uint4 w[8];
-          float ss = 0.f;
+          float sq[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums
+#pragma unroll
+          for (int ch = 0; ch < 8; ++ch) w[ch] = *reinterpret_cast<const uint4*>(base + swz128(row, ch));
 #pragma unroll
           for (int ch = 0; ch < 8; ++ch) {
-            w[ch] = *reinterpret_cast<const uint4*>(base + swz128(row, ch));
             const uint32_t ws[4] = {w[ch].x, w[ch].y, w[ch].z, w[ch].w};
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const float2 f = unpack_bf16x2(ws[e]);
-              ss = fmaf(f.x, f.x, fmaf(f.y, f.y, ss));
+              sq[e] = fmaf(f.x, f.x, fmaf(f.y, f.y, sq[e]));
             }
           }
+          float ss = (sq[0] + sq[1]) + (sq[2] + sq[3]);
           ss += __shfl_xor_sync(0xffffffffu, ss, 1);
           const float sc = m == 0 ? rsqrtf(ss + 1e-6f) : rsqrtf(ss + 1e-6f) * rsqrtf(static_cast<float>(GD)) * g[row];
 #pragma unroll
@@ -836,72 +811,80 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
     // ------------------------------------------------------------------ warps 8-11: output rows
     // O (lane v, column i) times 1 / RMS and the norm weight is staged as fp32 [64 i][128 v] over the chunk's q / k
     // boxes (their last readers, the O1 and state MMAs, completed before O2), then each thread takes 16-byte pieces of
-    // token rows: times silu(z) from coalesced 16-byte loads, bf16, coalesced 16-byte stores. The stage is released
-    // to the copy warp (its second EMPTY arrival) once the staging has been read.
+    // token rows: times silu(z) from coalesced 16-byte loads (requested a chunk ahead), bf16, coalesced 16-byte
+    // stores. The stage is released to the copy warp (its second EMPTY arrival) once the staging has been read.
     const int u = tid - 256;  // dv row = TMEM lane
     const int wq = warp & 3;
     const float wv = P.norm_w ? bf2f(P.norm_w[u]) : 1.f;
     float* part = reinterpret_cast<float*>(smem + L::PART);
+    // this thread's pieces of a chunk: row (u + 128 k) / 16, values 8 ((u + 128 k) % 16) .. + 7
+    auto load_z = [&](int c, uint4 (&zz)[8]) {
+      const int c0 = t_begin + c * GC, qn = min(GC, t_end - c0);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int idx = u + 128 * k, i = idx >> 4, cc = idx & 15;
+        zz[k] = make_uint4(0u, 0u, 0u, 0u);
+        if (P.z && i < qn)
+          zz[k] = __ldg(reinterpret_cast<const uint4*>(P.z + static_cast<int64_t>(c0 + i) * P.z_t + j * P.z_h + cc * 8));
+      }
+    };
+    uint4 zv[8], zn[8];
+    if (nchunks > 0) load_z(0, zv);
     for (int c = 0; c < nchunks; ++c) {
       const int c0 = t_begin + c * GC;
       const int qn = min(GC, t_end - c0);
       float* ys = reinterpret_cast<float*>(smem + (c % L::NST) * L::STAGE + L::Q);  // [64][128] fp32, 32 KB
-      // this thread's pieces: row (u + 128 k) / 16, values 8 ((u + 128 k) % 16) .. + 7; gates requested before the wait
-      uint4 zv[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int idx = u + 128 * k, i = idx >> 4, cc = idx & 15;
-        zv[k] = make_uint4(0u, 0u, 0u, 0u);
-        if (P.z && i < qn)
-          zv[k] = __ldg(reinterpret_cast<const uint4*>(P.z + static_cast<int64_t>(c0 + i) * P.z_t + j * P.z_h + cc * 8));
-      }
+      if (c + 1 < nchunks) load_z(c + 1, zn);
       if (!and_bar(3, 128, wait_sleep(bar(WB_ODONE), c & 1, abort_flag, P.err))) break;
       tc_fence_after();
-      uint32_t o[64];
-      tmem_ld64(t_lane + TM::O, o);
-      tmem_wait();
-      tc_fence_before();
-      arrive1(bar(WB_OFREE));  // O may be overwritten
-      float rs0 = 1.f, rs1 = 1.f;  // 1 / RMS of tokens 2 lane, 2 lane + 1
+      float rsA = 1.f, rsB = 1.f;  // 1 / RMS of tokens lane and 32 + lane
       if (P.norm_w) {
-        // sums of squares over this warp's 32 rows, reduce-scattered: lane ends with tokens 2 lane, 2 lane + 1
-        float s[32];
+        // per half of the chunk: squares over this warp's 32 rows, reduce-scattered so that lane l holds token l of the half
+        float* pp = part + (c & 1) * 256;
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float lo = __uint_as_float(o[k]), hi = __uint_as_float(o[32 + k]);
-          const bool up = lane & 16;
-          const float send = up ? lo * lo : hi * hi, keep = up ? hi * hi : lo * lo;
-          s[k] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
-        }
+        for (int h = 0; h < 2; ++h) {
+          uint32_t oh[32];
+          tmem_ld32(t_lane + TM::O + 32 * h, oh);
+          tmem_wait();
+          float s[32];
 #pragma unroll
-        for (int hs = 16, bit = 8; hs >= 2; hs >>= 1, bit >>= 1) {
+          for (int k = 0; k < 32; ++k) s[k] = __uint_as_float(oh[k]) * __uint_as_float(oh[k]);
 #pragma unroll
-          for (int k = 0; k < 16; ++k) {
-            if (k < hs) {
-              const bool up = lane & bit;
-              const float send = up ? s[k] : s[hs + k], keep = up ? s[hs + k] : s[k];
-              s[k] = keep + __shfl_xor_sync(0xffffffffu, send, bit);
+          for (int hs = 16; hs >= 1; hs >>= 1) {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              if (k < hs) {
+                const bool up = lane & hs;
+                const float send = up ? s[k] : s[hs + k], keep = up ? s[hs + k] : s[k];
+                s[k] = keep + __shfl_xor_sync(0xffffffffu, send, hs);
+              }
             }
           }
+          pp[wq * 64 + 32 * h + lane] = s[0];
         }
-        float* pp = part + (c & 1) * 256;
-        *reinterpret_cast<float2*>(pp + wq * 64 + 2 * lane) = make_float2(s[0], s[1]);
         asm volatile("bar.sync 3, 128;\n" ::: "memory");
         float t0 = 0.f, t1 = 0.f;
 #pragma unroll
         for (int w4 = 0; w4 < 4; ++w4) {
-          const float2 v = *reinterpret_cast<const float2*>(pp + w4 * 64 + 2 * lane);
-          t0 += v.x;
-          t1 += v.y;
+          t0 += pp[w4 * 64 + lane];
+          t1 += pp[w4 * 64 + 32 + lane];
         }
-        rs0 = rsqrtf(t0 / static_cast<float>(GD) + P.eps);
-        rs1 = rsqrtf(t1 / static_cast<float>(GD) + P.eps);
+        rsA = rsqrtf(t0 / static_cast<float>(GD) + P.eps);
+        rsB = rsqrtf(t1 / static_cast<float>(GD) + P.eps);
       }
 #pragma unroll
-      for (int i = 0; i < GC; ++i) {
-        const float rs = __shfl_sync(0xffffffffu, (i & 1) ? rs1 : rs0, i >> 1);
-        ys[i * GD + u] = __uint_as_float(o[i]) * rs * wv;
+      for (int h = 0; h < 2; ++h) {
+        uint32_t oh[32];
+        tmem_ld32(t_lane + TM::O + 32 * h, oh);
+        tmem_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float rs = __shfl_sync(0xffffffffu, h ? rsB : rsA, e);
+          ys[(32 * h + e) * GD + u] = __uint_as_float(oh[e]) * rs * wv;
+        }
       }
+      tc_fence_before();
+      arrive1(bar(WB_OFREE));  // O may be overwritten
       asm volatile("bar.sync 3, 128;\n" ::: "memory");
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
@@ -926,6 +909,8 @@ __global__ void __launch_bounds__(WTHR, 1) gdn_walk_tc_kernel(const __grid_const
       }
       asm volatile("bar.sync 3, 128;\n" ::: "memory");  // the staging is read: the stage may be reloaded
       if (u == 0) arrive1(bar(WB_EMPTY + c % L::NST));
+#pragma unroll
+      for (int k = 0; k < 8; ++k) zv[k] = zn[k];
     }
   }
 
