@@ -243,10 +243,10 @@ int mmp_conv1d_prefill(const void* x, int64_t x_t, void* out, int64_t o_t, void*
  * measures). For each sequence i and head h, runs s_t = exp(dt'_t A) s_{t-1} + dt'_t x_t B_t^T,
  * y_t = s_t C_t + D x_t over its tokens (dt' = softplus(dt + dt_bias)), starting from state line state_idx[i]
  * when has_init[i] != 0 (else zero) and writing the final state back to that line; evaluated chunk-wise (64
- * tokens) on the tensor cores (tcgen05 with TMEM-resident state for p = 128 and N in {128, 256}, mma.sync
- * otherwise). x, out: [ntok, nh, p] bf16 (ntok = cu_seqlens[nseq], the packed rows); dt: [ntok, nh] bf16;
- * B, C: [ntok, ngroups, N] bf16; state as mmp_ssu_decode. N in {64, 128, 256}, p % 8 == 0, 16-byte aligned
- * rows.
+ * tokens) on the tensor cores (tcgen05 with TMEM-resident state for p = 128 with N in {128, 256}, and for p = 64
+ * with N = 128 when each B/C group has an even number of heads, two heads per CTA; mma.sync otherwise). x, out:
+ * [ntok, nh, p] bf16 (ntok = cu_seqlens[nseq], the packed rows); dt: [ntok, nh] bf16; B, C: [ntok, ngroups, N]
+ * bf16; state as mmp_ssu_decode. N in {64, 128, 256}, p % 8 == 0, 16-byte aligned rows.
  */
 int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h,
                     const float* A, const float* D, const float* dt_bias,
@@ -255,6 +255,9 @@ int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const void* dt, int
                     const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init,
                     void* out, int64_t o_t, int64_t o_h,
                     int nseq, int ntok, int nh, int p, int N, int ngroups, int lines, int* err, void* stream);
+/* Selects the kernel behind mmp_ssd_prefill: 1 (default) the tcgen05 kernel where it applies, 0 the mma.sync kernel
+ * always (no counterpart in the reference; for comparisons). Process-wide; returns the previous setting. */
+int mmp_set_ssd_prefill_tc(int enable);
 
 /* ---- prefill: the chunked SSD scan with balanced walks ---------------------------------------------------
  * Same result as mmp_ssd_prefill (up to rounding) for head dim 128. The host cuts each sequence at 64-token chunk

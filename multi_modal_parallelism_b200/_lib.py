@@ -23,6 +23,7 @@ SIGNATURES: dict[str, tuple] = {
     "mmp_last_error": (C.c_char_p, []),
     "mmp_set_pdl": (I32, [I32]),
     "mmp_set_attn_prefill_tc": (I32, [I32]),
+    "mmp_set_ssd_prefill_tc": (I32, [I32]),
     "mmp_set_gemm_decode_split": (I32, [I32]),
     "mmp_set_gemm_decode_stages": (I32, [I32]),
     "mmp_scale_rows": (I32, [P, I64, P, I32, I32, F32, F32, P]),

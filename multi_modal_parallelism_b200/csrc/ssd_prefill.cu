@@ -370,6 +370,7 @@ int launch_ssd(const SsdParams& P, int nseq, cudaStream_t s) {
 using namespace mmp;
 
 namespace mmp {
+static int g_ssd_prefill_tc = 1;  // mmp_set_ssd_prefill_tc(0): the mma.sync kernel for every shape
 int ssd_prefill_tc(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h, const float* A,
                    const float* D, const float* dt_bias, const void* B, int64_t B_t, int64_t B_g, const void* C,
                    int64_t C_t, int64_t C_g, void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
@@ -402,10 +403,10 @@ extern "C" int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const vo
               static_cast<bf16*>(out), o_t, o_h, nh, p, ngroups, lines, err};
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (ntok < 0) return mmp_set_error(MMP_ERR_INVALID, "mmp_ssd_prefill: ntok %d", ntok);
-  // head dim 128 with d_state 128 / 256: the tcgen05 kernel (ssd_prefill_tc.cu)
-  const int tc = ssd_prefill_tc(x, x_t, x_h, dt, dt_t, dt_h, A, D, dt_bias, B, B_t, B_g, C, C_t, C_g, state,
+  // head dim 128 with d_state 128 / 256, head dim 64 with d_state 128: the tcgen05 kernel (ssd_prefill_tc.cu)
+  const int tc = !g_ssd_prefill_tc ? MMP_ERR_UNSUPPORTED : ssd_prefill_tc(x, x_t, x_h, dt, dt_t, dt_h, A, D, dt_bias, B, B_t, B_g, C, C_t, C_g, state,
                                 state_dtype, s_line, s_head, s_p, cu_seqlens, state_idx, has_init, out, o_t, o_h,
-                                nseq, ntok, nh, p, N, ngroups, lines, err, s);
+                                                         nseq, ntok, nh, p, N, ngroups, lines, err, s);
   if (tc != MMP_ERR_UNSUPPORTED) return tc;
   const bool f32 = state_dtype == MMP_F32;
   switch (N) {
@@ -414,4 +415,10 @@ extern "C" int mmp_ssd_prefill(const void* x, int64_t x_t, int64_t x_h, const vo
     case 256: return f32 ? launch_ssd<float, 256>(P, nseq, s) : launch_ssd<bf16, 256>(P, nseq, s);
   }
   return mmp_set_error(MMP_ERR_UNSUPPORTED, "mmp_ssd_prefill: d_state %d not in {64, 128, 256}", N);
+}
+
+extern "C" int mmp_set_ssd_prefill_tc(int enable) {
+  const int prev = mmp::g_ssd_prefill_tc;
+  mmp::g_ssd_prefill_tc = enable ? 1 : 0;
+  return prev;
 }

@@ -44,26 +44,33 @@ struct SsdTcParams {
   int* err;
 };
 
-template <int N>
+// HP = heads per CTA: 1 for head dim 128; 2 for head dim 64, two heads of one B/C group stacked in the 128 TMEM lanes
+// (lane = 64 h + p). With two heads the chunk's x is stored as the block-diagonal MN-major operand of Y = x^T M^T over
+// K = (head, s): [x of head 0 | zeros | zeros | x of head 1], 8 KB each, so one K = 128 MMA chain applies each head's
+// own M (the zero blocks are written once; the loads never touch them).
+template <int N, int HP>
 struct TcSsdSmem {
   static constexpr int KB = N / 64;                   // 64-wide k-blocks along n
-  static constexpr int STAGE = 2 * KB * 8192 + 2 * 8192;  // one chunk's C, B and x boxes
+  static constexpr int X_BYTES = 2 * 8192 * HP;
+  static constexpr int STAGE = 2 * KB * 8192 + X_BYTES;  // one chunk's C, B and x boxes
   static constexpr int C_OFF = 0;                     // stage 0 C chunk: KB blocks [64 t x 128 B]
   static constexpr int B_OFF = C_OFF + KB * 8192;     // stage 0 B chunk: same
   static constexpr int X_OFF = B_OFF + KB * 8192;     // stage 0 x chunk: 2 blocks [64 t x 128 B] (p 0-63, 64-127)
-  static constexpr int M_OFF = 2 * STAGE;             // M: [64 t x 128 B] (s)
+  static constexpr int X_HEAD = 8192 + 16384 * (HP - 1);  // offset of the second block / head's x
+  static constexpr int M_OFF = 2 * STAGE;             // M: per head [64 t x 128 B] (s)
   static constexpr int YLD = SP * 2 + 16;             // y tile row bytes (padded)
-  static constexpr int Y_OFF = M_OFF + 8192;          // y tile [64 t][128 p] bf16
+  static constexpr int Y_OFF = M_OFF + HP * 8192;     // y tile [64 t][128 p] bf16
   static constexpr int XW_OFF = Y_OFF + SQ * YLD;     // w-weighted x, per chunk parity: 2 blocks [64 t x 128 B]
-  static constexpr int CUM_OFF = XW_OFF + 2 * 16384;  // per chunk (ring of 4): cum log2e, dt, w, exp(cum) [64] + decay
-  static constexpr int CUM_BYTES = 4 * SQ * 4 + 16;
+  static constexpr int CUM_OFF = XW_OFF + 2 * 16384;  // per chunk (ring of 4), per head: cum log2e, dt, w, exp(cum) [64] + decay
+  static constexpr int CUM_HEAD = 4 * SQ * 4 + 16;
+  static constexpr int CUM_BYTES = HP * CUM_HEAD;
   static constexpr int BAR_OFF = CUM_OFF + 4 * CUM_BYTES;
   static constexpr int NBAR = 16;
   static constexpr int USED = BAR_OFF + 8 * NBAR + 16;
   static constexpr int DYN = USED + 1024;
-  static constexpr uint32_t LOAD_BYTES = STAGE;
+  static constexpr uint32_t LOAD_BYTES = 2 * KB * 8192 + 2 * 8192;  // the zero blocks are not loaded
 };
-static_assert(TcSsdSmem<256>::DYN <= 232448, "shared memory per CTA");
+static_assert(TcSsdSmem<256, 1>::DYN <= 232448 && TcSsdSmem<128, 2>::DYN <= 232448, "shared memory per CTA");
 
 // TMEM columns: fp32 state [N], bf16 state copy [N / 2] (two values per column), Y [64], and G / YS [64] (G is read
 // out before YS is written into the same columns, and YS before the next G)
@@ -124,19 +131,19 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, uint32_t* r) {
   for (int k = 0; k < 4; ++k) tmem_ld16_nw(taddr + 16 * k, r + 16 * k);
 }
 
-template <typename ST, int N>
+template <typename ST, int N, int HP>
 __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_constant__ CUtensorMap mapX,
                                                                 const __grid_constant__ CUtensorMap mapB,
                                                                 const __grid_constant__ CUtensorMap mapC,
                                                                 const SsdTcParams P) {
-  using L = TcSsdSmem<N>;
+  using L = TcSsdSmem<N, HP>;
   using TM = TcSsdTmem<N>;
   extern __shared__ uint8_t dsmem[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsmem) + 1023) & ~uintptr_t(1023));
   pdl_trigger();
   pdl_wait();
   const uint32_t sb = smem_addr(smem);
-  const int h = blockIdx.x, seq = blockIdx.y;
+  const int h = blockIdx.x * HP, seq = blockIdx.y;  // the CTA's (first) head
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t_begin = P.cu_seqlens[seq], t_end = P.cu_seqlens[seq + 1];
   const int line = P.state_idx[seq];
@@ -146,14 +153,30 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
   }
   const int nchunks = (t_end - t_begin + SQ - 1) / SQ;
   const int grp = h / (P.nh / P.ngroups);
-  const float A = P.A[h], Dh = P.D ? P.D[h] : 0.f, dtb = P.dt_bias ? P.dt_bias[h] : 0.f;
+  float A_[HP], D_[HP], dtb_[HP];
+#pragma unroll
+  for (int hh = 0; hh < HP; ++hh) {
+    A_[hh] = P.A[h + hh];
+    D_[hh] = P.D ? P.D[h + hh] : 0.f;
+    dtb_[hh] = P.dt_bias ? P.dt_bias[h + hh] : 0.f;
+  }
   auto bar = [&](int i) { return sb + L::BAR_OFF + 8 * i; };
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::BAR_OFF + 8 * L::NBAR);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + 8 * L::NBAR + 4);
-  ST* gstate = reinterpret_cast<ST*>(P.state) + line * P.s_line + h * P.s_head;
+  // this thread's state row when it is a state-pass thread (tid < 128: lane = head hh * 64 + row)
+  ST* gstate = reinterpret_cast<ST*>(P.state) + line * P.s_line + (h + (HP == 2 ? (tid & 127) / 64 : 0)) * P.s_head;
   // per-chunk scan results, a ring of four (chunk c's buffer is rewritten by chunk c + 4, whose loads wait for
   // chunk c + 2's MMAs, which come after every reader of chunk c's buffer): cum log2(e), dt', w, exp(cum), decay
-  auto cum_buf = [&](int c) { return reinterpret_cast<float*>(smem + L::CUM_OFF + (c & 3) * L::CUM_BYTES); };
+  auto cum_buf = [&](int c, int hh) {
+    return reinterpret_cast<float*>(smem + L::CUM_OFF + (c & 3) * L::CUM_BYTES + hh * L::CUM_HEAD);
+  };
+  if constexpr (HP == 2) {  // the zero blocks of the block-diagonal x operand, both stages (before the first MMA)
+    for (int i = tid; i < 2 * 2 * 8192 / 16; i += STHR) {
+      const int stg = i / 1024, blk = (i / 512) & 1, off = (i & 511) * 16;
+      *reinterpret_cast<uint4*>(smem + stg * L::STAGE + L::X_OFF + 8192 + blk * 8192 + off) = make_uint4(0u, 0u, 0u, 0u);
+    }
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  }
 
   if (tid == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -200,8 +223,9 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
             tma_load_3d(st + L::C_OFF + kb * 8192, &mapC, bar(B_FULL + s), kb * 64, grp, c0);
             tma_load_3d(st + L::B_OFF + kb * 8192, &mapB, bar(B_FULL + s), kb * 64, grp, c0);
           }
+          // x: p 0-63 and 64-127 of the head, or the two heads (64 each) into the block-diagonal operand
           tma_load_3d(st + L::X_OFF, &mapX, bar(B_FULL + s), 0, h, c0);
-          tma_load_3d(st + L::X_OFF + 8192, &mapX, bar(B_FULL + s), 64, h, c0);
+          tma_load_3d(st + L::X_OFF + L::X_HEAD, &mapX, bar(B_FULL + s), HP == 1 ? 64 : 0, h + HP - 1, c0);
           if (c + 2 < nchunks) {  // the chunk after next into L2
 #pragma unroll
             for (int kb = 0; kb < L::KB; ++kb) {
@@ -209,7 +233,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
               tma_prefetch_3d(&mapB, kb * 64, grp, c0 + 2 * SQ);
             }
             tma_prefetch_3d(&mapX, 0, h, c0 + 2 * SQ);
-            tma_prefetch_3d(&mapX, 64, h, c0 + 2 * SQ);
+            tma_prefetch_3d(&mapX, HP == 1 ? 64 : 0, h + HP - 1, c0 + 2 * SQ);
           }
           issued = c + 1;
         }
@@ -218,36 +242,40 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       // the scan: dt' = softplus(dt + bias), inclusive running sum of dt' A (kept times log2(e) for ex2), update
       // weights w, exp(cum) and the chunk decay exp(cum_last)
       const int qn = min(SQ, t_end - c0);
-      float* sCum = cum_buf(c);
-      float* sDt = sCum + SQ;
-      float* sW = sDt + SQ;
-      float* sE = sW + SQ;
-      float d[2], cs[2];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = lane * 2 + j;
-        d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + h * P.dt_h]) + dtb) : 0.f;
-      }
-      cs[0] = d[0] * A;
-      cs[1] = cs[0] + d[1] * A;
-      float run = cs[1];
+      for (int hh = 0; hh < HP; ++hh) {
+        const float A = A_[hh], dtb = dtb_[hh];
+        float* sCum = cum_buf(c, hh);
+        float* sDt = sCum + SQ;
+        float* sW = sDt + SQ;
+        float* sE = sW + SQ;
+        float d[2], cs[2];
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float v = __shfl_up_sync(0xffffffffu, run, o);
-        if (lane >= o) run += v;
-      }
-      const float excl = run - cs[1];
-      const float cum_last = __shfl_sync(0xffffffffu, run, 31);  // tokens past qn add nothing
+        for (int j = 0; j < 2; ++j) {
+          const int r = lane * 2 + j;
+          d[j] = r < qn ? softplus(bf2f(P.dt[static_cast<int64_t>(c0 + r) * P.dt_t + (h + hh) * P.dt_h]) + dtb) : 0.f;
+        }
+        cs[0] = d[0] * A;
+        cs[1] = cs[0] + d[1] * A;
+        float run = cs[1];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int r = lane * 2 + j;
-        const float cum = excl + cs[j];
-        sDt[r] = d[j];
-        sCum[r] = cum * 1.4426950408889634f;
-        sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
-        sE[r] = __expf(cum);
+        for (int o = 1; o < 32; o <<= 1) {
+          const float v = __shfl_up_sync(0xffffffffu, run, o);
+          if (lane >= o) run += v;
+        }
+        const float excl = run - cs[1];
+        const float cum_last = __shfl_sync(0xffffffffu, run, 31);  // tokens past qn add nothing
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int r = lane * 2 + j;
+          const float cum = excl + cs[j];
+          sDt[r] = d[j];
+          sCum[r] = cum * 1.4426950408889634f;
+          sW[r] = r < qn ? __expf(cum_last - cum) * d[j] : 0.f;
+          sE[r] = __expf(cum);
+        }
+        if (lane == 0) sCum[4 * SQ] = __expf(cum_last);
       }
-      if (lane == 0) sCum[4 * SQ] = __expf(cum_last);
       mbar_arrive1(bar(B_SCAN + (c & 3)));
     }
     // copies in flight may still land after an abort: wait (bounded) for the last chunk of each stage
@@ -283,11 +311,14 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
         if (!(ok = mbar_wait(bar(B_MB), par, abort_flag, P.err))) break;
         if (c > 0 && !(ok = mbar_wait(bar(B_YFREE), par ^ 1, abort_flag, P.err))) break;
         tc_fence_after();
-        // Y = x^T M^T (K = s); YS = S_bf C^T (K = n), into G's columns (G is read out)
+        // Y = x^T M^T (K = s; with two heads K = (head, s) over the block-diagonal x and the heads' M side by side);
+        // YS = S_bf C^T (K = n), into G's columns (G is read out)
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_f16(tmem + TM::Y, umma_desc_mn(st + L::X_OFF + kk * 2048, 8192), umma_desc(sb + L::M_OFF + kk * 32),
-                   idy_x, kk != 0);
+        for (int kb = 0; kb < HP; ++kb)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + TM::Y, umma_desc_mn(st + L::X_OFF + kb * 8192 + kk * 2048, HP == 1 ? 8192 : 16384),
+                     umma_desc(sb + L::M_OFF + kb * 8192 + kk * 32), idy_x, (kb | kk) != 0);
 #pragma unroll
         for (int kb = 0; kb < L::KB; ++kb)
 #pragma unroll
@@ -314,7 +345,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
     __syncwarp();
   } else if (warp < 4) {
     // ------------------------------------------------------------------ warps 0-3: the state in TMEM, B weights
-    const int p = tid;  // state row = TMEM lane
+    const int p = HP == 1 ? tid : (tid & 63);  // state row of this thread's head (TMEM lane = tid)
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const bool init = P.has_init && P.has_init[seq];
 #pragma unroll 1
@@ -332,11 +363,12 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
       ok = mbar_wait(bar(B_SCAN + (c & 3)), (c >> 2) & 1, abort_flag, P.err) &&
            mbar_wait(bar(B_FULL + (c & 1)), (c >> 1) & 1, abort_flag, P.err);
       if (!(ok = __all_sync(0xffffffffu, ok))) break;
-      const float* sCum = cum_buf(c);
+      const float* sCum = cum_buf(c, HP == 1 ? 0 : tid / 64);
       {
-        const int t = p >> 1, blk = p & 1;
-        const float wt = sCum[2 * SQ + t];
-        const uint8_t* xs = smem + (c & 1) * L::STAGE + L::X_OFF + blk * 8192;
+        // one 64-wide block each: p 0-63 / 64-127 of the head, or one of the two heads (its own weights)
+        const int t = tid >> 1, blk = tid & 1;
+        const float wt = cum_buf(c, HP == 1 ? 0 : blk)[2 * SQ + t];
+        const uint8_t* xs = smem + (c & 1) * L::STAGE + L::X_OFF + blk * L::X_HEAD;
         uint8_t* xd = smem + L::XW_OFF + (c & 1) * 16384 + blk * 8192;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -399,8 +431,6 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
                       mbar_wait(bar(B_G), c & 1, abort_flag, P.err);
       if (!bar_and(2, 128, ok)) return false;
       tc_fence_after();
-      const float* sCum = cum_buf(c);
-      const float* sDt = sCum + SQ;
       uint32_t g[64];
       tmem_ld64(t_lane + TM::G, g);
       tmem_wait();
@@ -413,26 +443,32 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
         const float hi = __uint_as_float(__shfl_sync(0xffffffffu, g[32 + j], l16));
         gv[j] = lane >= 16 ? hi : __uint_as_float(g[j]);
       }
-      const float ct = sCum[t];
 #pragma unroll
-      for (int c8 = 0; c8 < 4; ++c8) {
-        const float4 cs0 = *reinterpret_cast<const float4*>(sCum + cb + c8 * 8);
-        const float4 cs1 = *reinterpret_cast<const float4*>(sCum + cb + c8 * 8 + 4);
-        const float4 dt0 = *reinterpret_cast<const float4*>(sDt + cb + c8 * 8);
-        const float4 dt1 = *reinterpret_cast<const float4*>(sDt + cb + c8 * 8 + 4);
-        const float csv[8] = {cs0.x, cs0.y, cs0.z, cs0.w, cs1.x, cs1.y, cs1.z, cs1.w};
-        const float dtv[8] = {dt0.x, dt0.y, dt0.z, dt0.w, dt1.x, dt1.y, dt1.z, dt1.w};
-        float m[8];
+      for (int hh = 0; hh < HP; ++hh) {  // the head's own decays on the group's shared C B^T
+        const float* sCum = cum_buf(c, hh);
+        const float* sDt = sCum + SQ;
+        const float Dh = D_[hh];
+        const float ct = sCum[t];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int sidx = cb + c8 * 8 + e;
-          // s <= t only: for s > t the exponent is positive and may overflow. dt' is 0 past the sequence
-          m[e] = sidx <= t ? gv[c8 * 8 + e] * ex2f(ct - csv[e]) * dtv[e] : 0.f;
-          if (sidx == t) m[e] += Dh;
+        for (int c8 = 0; c8 < 4; ++c8) {
+          const float4 cs0 = *reinterpret_cast<const float4*>(sCum + cb + c8 * 8);
+          const float4 cs1 = *reinterpret_cast<const float4*>(sCum + cb + c8 * 8 + 4);
+          const float4 dt0 = *reinterpret_cast<const float4*>(sDt + cb + c8 * 8);
+          const float4 dt1 = *reinterpret_cast<const float4*>(sDt + cb + c8 * 8 + 4);
+          const float csv[8] = {cs0.x, cs0.y, cs0.z, cs0.w, cs1.x, cs1.y, cs1.z, cs1.w};
+          const float dtv[8] = {dt0.x, dt0.y, dt0.z, dt0.w, dt1.x, dt1.y, dt1.z, dt1.w};
+          float m[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const int sidx = cb + c8 * 8 + e;
+            // s <= t only: for s > t the exponent is positive and may overflow. dt' is 0 past the sequence
+            m[e] = sidx <= t ? gv[c8 * 8 + e] * ex2f(ct - csv[e]) * dtv[e] : 0.f;
+            if (sidx == t) m[e] += Dh;
+          }
+          *reinterpret_cast<uint4*>(smem + L::M_OFF + hh * 8192 + sw(t, (cb >> 3) + c8)) =
+              make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
+                         pack_bf16x2(m[6], m[7]));
         }
-        *reinterpret_cast<uint4*>(smem + L::M_OFF + sw(t, (cb >> 3) + c8)) =
-            make_uint4(pack_bf16x2(m[0], m[1]), pack_bf16x2(m[2], m[3]), pack_bf16x2(m[4], m[5]),
-                       pack_bf16x2(m[6], m[7]));
       }
       asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic smem writes -> tensor core reads
       tc_fence_before();
@@ -454,7 +490,7 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
           tmem_wait();
           tc_fence_before();
           mbar_arrive1(bar(B_YFREE));  // Y and YS may be overwritten
-          const float* sE = cum_buf(c) + 3 * SQ;
+          const float* sE = cum_buf(c, HP == 1 ? 0 : q / 2) + 3 * SQ;  // lanes 64 h .. 64 h + 63: head h
 #pragma unroll
           for (int j4 = 0; j4 < 16; ++j4) {
             const float4 e = *reinterpret_cast<const float4*>(sE + 4 * j4);
@@ -477,8 +513,10 @@ __global__ void __launch_bounds__(STHR, 1) ssd_prefill_tc_kernel(const __grid_co
         asm volatile("bar.sync 2, 128;\n" ::: "memory");
         for (int i = tl; i < SQ * (SP / 8); i += 128) {
           const int t = i / (SP / 8), cc = i % (SP / 8);
+          // 16-byte piece cc of the row: p 8 cc of the head, or p 8 (cc % 8) of head cc / 8
           if (t < qn)
-            st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + h * P.o_h + cc * 8,
+            st16(P.out + static_cast<int64_t>(c0 + t) * P.o_t + (h + (HP == 1 ? 0 : cc / 8)) * P.o_h +
+                     (HP == 1 ? cc : cc % 8) * 8,
                  *reinterpret_cast<const uint4*>(smem + L::Y_OFF + t * L::YLD + cc * 16));
         }
         asm volatile("bar.sync 2, 128;\n" ::: "memory");  // the y tile is reusable
@@ -510,11 +548,11 @@ int make_map3(CUtensorMap* map, const void* base, int inner, int mid, int rows, 
   return MMP_OK;
 }
 
-template <typename ST, int N>
+template <typename ST, int N, int HP>
 int launch_ssd_tc(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMap& mc, const SsdTcParams& P, int nseq,
                   cudaStream_t s) {
-  using L = TcSsdSmem<N>;
-  auto kern = ssd_prefill_tc_kernel<ST, N>;
+  using L = TcSsdSmem<N, HP>;
+  auto kern = ssd_prefill_tc_kernel<ST, N, HP>;
   static bool attr[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -523,36 +561,40 @@ int launch_ssd_tc(const CUtensorMap& mx, const CUtensorMap& mb, const CUtensorMa
     if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_ssd_prefill: smem attribute: %s", cudaGetErrorString(e));
     attr[dev] = true;
   }
-  cudaError_t e = mmp::launch(kern, dim3(P.nh, nseq), dim3(STHR), L::DYN, s, nullptr, 0, mx, mb, mc, P);
+  cudaError_t e = mmp::launch(kern, dim3(P.nh / HP, nseq), dim3(STHR), L::DYN, s, nullptr, 0, mx, mb, mc, P);
   if (e != cudaSuccess) return mmp_set_error(MMP_ERR_CUDA, "mmp_ssd_prefill: %s", cudaGetErrorString(e));
   return mmp_check_launch("mmp_ssd_prefill");
 }
 
 }  // namespace
 
-// The tensor-core path for head dim 128, d_state 128 / 256 with TMA-compatible strides; MMP_UNSUPPORTED
-// otherwise (the caller then runs the mma.sync kernel).
+// The tensor-core path for head dim 128 with d_state 128 / 256, and head dim 64 with d_state 128 (two heads of one
+// B/C group per CTA) with TMA-compatible strides; MMP_UNSUPPORTED otherwise (the caller then runs the mma.sync kernel).
 int ssd_prefill_tc(const void* x, int64_t x_t, int64_t x_h, const void* dt, int64_t dt_t, int64_t dt_h, const float* A,
                    const float* D, const float* dt_bias, const void* B, int64_t B_t, int64_t B_g, const void* C,
                    int64_t C_t, int64_t C_g, void* state, int state_dtype, int64_t s_line, int64_t s_head, int64_t s_p,
                    const int32_t* cu_seqlens, const int32_t* state_idx, const int32_t* has_init, void* out,
                    int64_t o_t, int64_t o_h, int nseq, int ntok, int nh, int p, int N, int ngroups, int lines, int* err,
                    cudaStream_t stream) {
-  if (p != SP || (N != 128 && N != 256) || ntok <= 0 || nh > 65535 || nseq > 65535) return MMP_ERR_UNSUPPORTED;
+  const bool two_heads = p == 64 && N == 128 && ngroups > 0 && nh % ngroups == 0 && (nh / ngroups) % 2 == 0;
+  if ((p != SP && !two_heads) || (N != 128 && N != 256) || ntok <= 0 || nh > 65535 || nseq > 65535)
+    return MMP_ERR_UNSUPPORTED;
   if (x_h % 8 || x_t % 8 || B_g % 8 || B_t % 8 || C_g % 8 || C_t % 8 || !aligned16(x) || !aligned16(B) ||
       !aligned16(C) || o_t % 8 || o_h % 8 || !aligned16(out) || s_p < N)
     return MMP_ERR_UNSUPPORTED;
   int rc = get_encoder();
   if (rc != MMP_OK) return rc;
   CUtensorMap mx, mb, mc;
-  if ((rc = make_map3(&mx, x, SP, nh, ntok, x_h, x_t)) || (rc = make_map3(&mb, B, N, ngroups, ntok, B_g, B_t)) ||
+  if ((rc = make_map3(&mx, x, p, nh, ntok, x_h, x_t)) || (rc = make_map3(&mb, B, N, ngroups, ntok, B_g, B_t)) ||
       (rc = make_map3(&mc, C, N, ngroups, ntok, C_g, C_t)))
     return rc;
   SsdTcParams P{static_cast<const bf16*>(dt), dt_t, dt_h, A, D, dt_bias, state, s_line, s_head, s_p,
                 cu_seqlens, state_idx, has_init, static_cast<bf16*>(out), o_t, o_h, nh, ngroups, lines, err};
   const bool f32 = state_dtype == MMP_F32;
-  if (N == 256) return f32 ? launch_ssd_tc<float, 256>(mx, mb, mc, P, nseq, stream) : launch_ssd_tc<bf16, 256>(mx, mb, mc, P, nseq, stream);
-  return f32 ? launch_ssd_tc<float, 128>(mx, mb, mc, P, nseq, stream) : launch_ssd_tc<bf16, 128>(mx, mb, mc, P, nseq, stream);
+  if (two_heads)
+    return f32 ? launch_ssd_tc<float, 128, 2>(mx, mb, mc, P, nseq, stream) : launch_ssd_tc<bf16, 128, 2>(mx, mb, mc, P, nseq, stream);
+  if (N == 256) return f32 ? launch_ssd_tc<float, 256, 1>(mx, mb, mc, P, nseq, stream) : launch_ssd_tc<bf16, 256, 1>(mx, mb, mc, P, nseq, stream);
+  return f32 ? launch_ssd_tc<float, 128, 1>(mx, mb, mc, P, nseq, stream) : launch_ssd_tc<bf16, 128, 1>(mx, mb, mc, P, nseq, stream);
 }
 
 }  // namespace mmp

@@ -519,6 +519,12 @@ def set_gemm_decode_stages(stages: int) -> int:
     return int(_lib.lib().mmp_set_gemm_decode_stages(int(stages)))
 
 
+def set_ssd_prefill_tc(enable: bool) -> bool:
+    """Select the tcgen05 kernel for ssd_prefill where it applies (True, the default) or the mma.sync kernel for every
+    shape (False); process-wide. Returns the previous setting."""
+    return bool(_lib.lib().mmp_set_ssd_prefill_tc(1 if enable else 0))
+
+
 def set_attn_prefill_tc(enable: bool) -> bool:
     """Select the tcgen05/TMEM kernel for attn_prefill (True, the default) or the mma.sync kernel (False);
     process-wide. Returns the previous setting."""

@@ -64,9 +64,20 @@ def test_conv_prefill_matches_oracle():
         assert torch.equal(got_state[line], state[line])
 
 
-@pytest.mark.parametrize("N,G,p", [(64, 1, 64), (128, 2, 64), (256, 1, 128), (128, 1, 128)])
+@pytest.mark.parametrize("tc", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("N,G,p", [(64, 1, 64), (128, 2, 64), (128, 1, 64), (256, 1, 128), (128, 1, 128)])
 @pytest.mark.parametrize("state_dtype", [torch.float32, BF])
-def test_ssd_prefill_matches_sequential_recurrence(N, G, p, state_dtype):
+def test_ssd_prefill_matches_sequential_recurrence(N, G, p, state_dtype, tc):
+    """Both scan kernels (tcgen05 where it applies: head dim 128 with d_state 128 / 256, head dim 64 with d_state 128
+    as two heads of a group per CTA; mma.sync for the rest and when selected off) against the recurrence."""
+    prev = K.set_ssd_prefill_tc(tc)
+    try:
+        _ssd_case(N, G, p, state_dtype)
+    finally:
+        K.set_ssd_prefill_tc(prev)
+
+
+def _ssd_case(N, G, p, state_dtype):
     g = torch.Generator().manual_seed(N + G + p)
     nh, lines = 4, len(LENS) + 2
     T = sum(LENS)

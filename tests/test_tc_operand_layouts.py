@@ -45,11 +45,11 @@ def read_mn_major(mem, start, n_extent, lbo, sbo=1024):
              for n in range(n_extent)] for k in range(16)]
 
 
-def _consts(name: str, struct: str) -> dict:
+def _consts(name: str, struct: str, **over) -> dict:
     src = (SRC / name).read_text()
     body = src[src.index(f"struct {struct}"):]
     body = body[:body.index("};")]
-    env = {"THD": 128, "TQ": 128, "TK": 128, "JP": 128, "SQ": 64, "SP": 128, "N": 256, "KB": 4}
+    env = {"THD": 128, "TQ": 128, "TK": 128, "JP": 128, "SQ": 64, "SP": 128, "N": 256, "KB": 4, "HP": 1, **over}
     for n, expr in re.findall(r"static constexpr int (\w+) = ([^;]+);", body):
         env[n] = eval(expr.replace("/", "//"), {}, env)  # noqa: S307 - the file's own integer constants
     return env
@@ -110,6 +110,36 @@ def test_ssd_scan_tc_operands_agree_with_the_model():
         # S += x^T (w B): B = B MN-major (N = 256 over n, K = tokens)
         bb = read_mn_major(mem, L["B_OFF"] + kk * 2048, 256, 8192)
         assert all(bb[k][n] == ("B", kk * 16 + k, n) for k in range(16) for n in range(256))
+
+
+def test_ssd_scan_tc_two_heads_operands():
+    """The head-dim-64 form of the SSD scan (two heads of one group per CTA, d_state 128): each head's x box lands
+    in the block-diagonal operand of Y over K = (head, s), whose off-diagonal blocks hold the zeros written at start;
+    Y's B operand is the two heads' M side by side; the state update reads the two heads' weighted x as the two
+    64-row halves of M = 128."""
+    L = _consts("ssd_prefill_tc.cu", "TcSsdSmem", N=128, HP=2)
+    assert L["X_HEAD"] == 24576 and L["STAGE"] == 65536
+    mem = {}
+    for hh in range(2):
+        tma_write(mem, L["X_OFF"] + hh * L["X_HEAD"], 64, lambda r, e, hh=hh: ("x", hh, r, e))
+        thread_write(mem, L["M_OFF"] + hh * 8192, 64, 8, lambda t, s_, hh=hh: ("M", hh, t, s_), block_bytes=8192)
+        # the weighted copy: thread (t, block hh) writes row t of block hh
+        thread_write(mem, L["XW_OFF"] + hh * 8192, 64, 8, lambda t, p_, hh=hh: ("xw", hh, t, p_), block_bytes=8192)
+    for zb in (8192, 16384):  # the zero blocks, plain 16-byte stores
+        for a in range(L["X_OFF"] + zb, L["X_OFF"] + zb + 8192, 2):
+            mem[a] = ("z",)
+    for kb in range(2):
+        for kk in range(4):
+            a = read_mn_major(mem, L["X_OFF"] + kb * 8192 + kk * 2048, 128, 16384)
+            b = read_k_major(mem, L["M_OFF"] + kb * 8192 + kk * 32, 64)
+            for k in range(16):
+                for m in range(128):
+                    want = ("x", kb, kk * 16 + k, m % 64) if m // 64 == kb else ("z",)
+                    assert a[k][m] == want, (kb, kk, k, m, a[k][m])
+            assert all(b[t][k] == ("M", kb, t, kk * 16 + k) for t in range(64) for k in range(16))
+    for kk in range(4):
+        xw = read_mn_major(mem, L["XW_OFF"] + kk * 2048, 128, 8192)
+        assert all(xw[k][m] == ("xw", m // 64, kk * 16 + k, m % 64) for k in range(16) for m in range(128))
 
 
 def test_a_wrong_block_stride_is_caught():
