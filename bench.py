@@ -21,6 +21,7 @@ import argparse
 import json
 import math
 import os
+import signal
 import statistics
 import subprocess
 import sys
@@ -272,6 +273,22 @@ def log(msg: str) -> None:
           flush=True)
 
 
+# rank 0's result line once the headline is measured: printed at the end, or, if the job has to end early (an
+# exception in a phase with collectives, a phase over its time limit, another rank ending the job), printed then with
+# the configurations measured so far and a note naming what cut the run short
+_PENDING: dict = {"line": None, "printed": False}
+
+
+def emit_pending(note: str | None = None) -> None:
+    line = _PENDING["line"]
+    if line is None or _PENDING["printed"]:
+        return
+    _PENDING["printed"] = True
+    if note:
+        line = dict(line, incomplete=note[:300])
+    print(json.dumps(line), flush=True)
+
+
 class Watchdog:
     """Host-side bound on each phase of the run. NCCL's watchdog does not see collectives replayed from a CUDA
     graph, so a rank whose peers never join a replayed all-reduce would wait forever; here a phase that outlives
@@ -293,6 +310,7 @@ class Watchdog:
                 d, name = self.deadline, self.name
             if d is not None and time.perf_counter() > d:
                 log(f"phase '{name}' exceeded its time limit: ending the job")
+                emit_pending(f"phase '{name}' exceeded its time limit")
                 os._exit(3)
 
     def clear(self) -> None:
@@ -323,6 +341,7 @@ def fatal(where: str, e: BaseException) -> None:
 
     log(f"{where}: {type(e).__name__}: {e}; ending the job")
     traceback.print_exc(file=sys.stderr)
+    emit_pending(f"{where}: {type(e).__name__}: {e}")
     sys.stderr.flush()
     sys.stdout.flush()
     os._exit(2)
@@ -885,6 +904,14 @@ def our_arm(args) -> None:
     line = run_hybrid(args, groups, wd)
     if groups.rank == 0 and (line is None or "error" in line):
         raise SystemExit(f"no decode recipe agrees with the single-GPU layer step: {line}")
+    if groups.rank == 0:
+        _PENDING["line"] = line
+
+        def on_term(signum, frame):  # another rank ended the job (torchrun stops the rest)
+            emit_pending("the job was ended by another rank or by the launcher")
+            os._exit(143)
+
+        signal.signal(signal.SIGTERM, on_term)
     extra = {}
     if args.configs:
         # the other configurations, each a bounded sub-measurement with its own roofline, CPU baseline and e2e
@@ -894,16 +921,20 @@ def our_arm(args) -> None:
                                    "prefill_steps": min(args.prefill_steps, 10), "soak_s": 0.5,
                                    "cpu_s": min(args.cpu_s, 10.0)})
         extra["config2"] = run_hybrid(a2, groups, wd, modes=config2_modes(world), oracle=False, cpu_batch=4)
+        if groups.rank == 0:
+            line["config2"] = extra["config2"]
         a3 = argparse.Namespace(**{**vars(args), "steps": min(args.steps, 20), "warmup": 3,
                                    "cpu_s": min(args.cpu_s, 10.0)})
         extra["config3"] = run_mamba2(a3, groups, wd)
+        if groups.rank == 0:
+            line["config3"] = extra["config3"]
         a4 = argparse.Namespace(**{**vars(args), "batch": 64, "ctx": 4096, "prefill_seqs": 4, "prefill_len": 4096,
                                    "steps": min(args.steps, 50), "warmup": max(3, min(args.warmup, 10)),
                                    "prefill_steps": min(args.prefill_steps, 5), "cpu_s": min(args.cpu_s, 10.0)})
         extra["config4"] = run_qwen35(a4, groups, wd)
     if groups.rank == 0:
         line.update(extra)
-        print(json.dumps(line), flush=True)
+        emit_pending()
     destroy()
 
 
