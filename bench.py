@@ -1176,7 +1176,8 @@ def run_qwen35(args, groups, wd) -> dict | None:
             ms_p, p50_p = time_replays(lambda: stack.step(h_pre, pc), max(1, args.prefill_steps), 2, groups)
             fl = stack_flops(d, lens)
             r["prefill"] = {"ms": ms_p, "p50_ms": p50_p, "tokens_per_s": sum(lens) / ms_p * 1e3,
-                            "tflops": fl / ms_p / 1e9, "frac_of_bf16_peak": fl / ms_p / 1e9 / tf}
+                            "tflops": fl / ms_p / 1e9, "frac_of_bf16_peak": fl / ms_p / 1e9 / (world * tf),
+                            "peak_note": f"frac = aggregate TFLOP/s / ({world} x the per-GPU bf16 peak)"}
         results[mode] = r
         del graph, stack
         torch.cuda.empty_cache()
