@@ -31,10 +31,12 @@
 //     U^T = U0^T - X into TMEM as bf16, plain and times w;
 //   * warps 8-11 (output, one dv row per thread): O out of TMEM, the per-token RMS over the head's 128 values
 //     (warp reduce-scatter + 4 partials), staged as token rows over the chunk's dead q / k boxes, gate silu(z)
-//     and bf16 stores as 16-byte pieces of rows.
-// The critical path per chunk is the state pass, X, U and the state update; the W / U0 MMAs, their copy, the
-// output and the loads run beside it. Every mbarrier wait is bounded (tc_common.cuh); a CTA that runs out of
-// budget flags the error word, leaves its state line untouched, drains its copies and MMAs and frees TMEM.
+//     (16-byte loads requested a chunk ahead) and bf16 stores as 16-byte pieces of rows; the stage returns to the
+//     copy warp once the staging has been read.
+// The state chain per chunk is the state pass, X, U and the state update; the W / U0 MMAs, their copy, the output
+// and the loads run beside it, and the ring's recycling (load, operand preparation, output staging over the stage)
+// sets the pace. Every mbarrier wait is bounded (wait_sleep, with the clock budget of tc_common.cuh); a CTA that
+// runs out of budget flags the error word, leaves its state line untouched, drains its copies and MMAs and frees TMEM.
 #include <algorithm>
 
 #include "mmp_common.cuh"
