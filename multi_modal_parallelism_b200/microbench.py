@@ -221,7 +221,10 @@ def only(args, g) -> dict:
         pc = make_prefill_ctx([args.len] * args.nseq, 16, dev)
         T = pc.T
         if args.only == "ssd_prefill":
-            nh, p, N, G = 24, 128, 256, 1
+            # the 7B-like layer's scan (24 heads x 128, d_state 256, one group), or with --p64 the pure Mamba-2 layer's
+            # (128 heads x 64, d_state 128, 8 groups); --mma: the mma.sync kernel
+            nh, p, N, G = (128, 64, 128, 8) if args.p64 else (24, 128, 256, 1)
+            prev_tc = K.set_ssd_prefill_tc(not args.mma)
             x = torch.randn(T, nh, p, device=dev, dtype=BF, generator=gen)
             dt = (torch.randn(T, nh, device=dev, generator=gen) - 1).to(BF)
             A = -torch.exp(torch.rand(nh, device=dev, generator=gen) * 2)
@@ -243,7 +246,9 @@ def only(args, g) -> dict:
             else:
                 ms = timed(lambda: K.ssd_prefill(x, dt, A, Bm, Cm, D, dtb, st, pc.cu_seqlens, pc.state_idx,
                                                  pc.has_init, y))
-            res.update(tokens=T, ms=ms, tokens_per_s=T / ms * 1e3)
+            K.set_ssd_prefill_tc(prev_tc)
+            res.update(tokens=T, ms=ms, tokens_per_s=T / ms * 1e3, heads=nh, head_dim=p, d_state=N,
+                       kernel="mma.sync" if args.mma else "tcgen05 where it applies")
         elif args.only == "attn_prefill":
             nq, nkv, hd = 12, 2, 128
             kv, kc, vc, _ = K.alloc_kv(args.nseq * pc.nblk, 16, nkv, hd, dev)
@@ -351,7 +356,8 @@ def main() -> None:
     ap.add_argument("--len", type=int, default=2048)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--tc", action="store_true", help="attn_prefill: the tcgen05/TMEM kernel")
-    ap.add_argument("--mma", action="store_true", help="gdn_prefill: the mma.sync kernel instead of the tcgen05 pair")
+    ap.add_argument("--mma", action="store_true", help="gdn_prefill, ssd_prefill: the mma.sync kernel")
+    ap.add_argument("--p64", action="store_true", help="ssd_prefill: head dim 64 (128 heads, d_state 128, 8 groups)")
     ap.add_argument("--segments", action="store_true", help="ssd_prefill: balanced walks (segments + join)")
     args = ap.parse_args()
     g = init_groups()
