@@ -583,9 +583,9 @@ def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nc
     one rank runs tp1 with fused projections and tp1 with the branch-chains schedule (`_chains`: each branch's
     whole chain on its own stream); more run the even branch split, the split whose busiest rank moves the fewest
     step bytes (more ranks on the Mamba-2 branch when its state dominates), at two ranks the byte-balanced
-    mix{k} layouts, each also with the deferred norm statistic (`_dn`) where some rank would defer it, and
-    tp4_fused in both schedules (the chains schedule is not combined with a pushed out-projection). Every rank
-    derives the same list."""
+    mix{k} layouts, each also with the deferred norm statistic (`_dn`) where some rank would defer it and, the
+    mix{k} ones, with the branch-chains schedule on rank 0, and tp4_fused in both schedules (the chains schedule is
+    not combined with a pushed out-projection). Every rank derives the same list."""
     from multi_modal_parallelism_b200.measure import mix_by_bytes, split_by_bytes
 
     if world == 1:
@@ -603,6 +603,8 @@ def layout_candidates(dims, world: int, batch: int, ctx: int, ar_impl: str = "nc
                       if plan_ok(f"mix{kk}", dims, world)]
     if ar_impl == "nccl":  # the deferred norm statistic where some rank would defer it
         modes = [x for m in modes for x in ([m, f"{m}_dn"] if defers(m, dims, world) else [m])]
+    if ar_impl != "p2p_fused":  # mix{k} with the attention chain on rank 0's side stream
+        modes += [f"{m}_chains" for m in modes if m.startswith("mix")]
     return modes + ["tp4_fused"] + ([] if ar_impl == "p2p_fused" else ["tp4_fused_chains"])
 
 

@@ -70,8 +70,10 @@ def test_bench_layout_candidates_are_valid_and_rank_independent():
     assert bench.layout_candidates(d, 1, 64, 2048) == ["tp1", "tp1_chains"]
     assert bench.layout_candidates(d, 4, 64, 2048) == ["split22", "split22_dn", "split13", "split13_dn", "tp4_fused",
                                                        "tp4_fused_chains"]
-    assert bench.layout_candidates(d, 2, 64, 2048) == ["split11", "mix8", "mix8_dn", "mix6", "mix6_dn", "tp4_fused",
-                                                       "tp4_fused_chains"]
+    assert bench.layout_candidates(d, 2, 64, 2048) == ["split11", "mix8", "mix8_dn", "mix6", "mix6_dn",
+                                                       "mix8_chains", "mix8_dn_chains", "mix6_chains",
+                                                       "mix6_dn_chains", "tp4_fused", "tp4_fused_chains"]
+    assert bench.parse_recipe("mix8_dn_chains") == ("mix8", True, True)
     assert bench.layout_candidates(d, 4, 64, 2048, "p2p_fused") == ["split22", "split13", "tp4_fused"]
     assert bench.parse_recipe("tp4_fused_chains") == ("tp4_fused", True, False)
     assert bench.parse_recipe("split26") == ("split26", False, False)

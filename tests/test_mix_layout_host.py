@@ -3,7 +3,8 @@ projections; rank 1: the other heads; one all-reduce) through ParallelHybridLaye
 kernel wrappers replaced by torch stand-ins (tests/_kernel_stand_ins.py): every rank's output equals the whole
 layer run on one rank within bf16 tolerance, for one and two B/C groups (two: the cut on a group boundary, each
 rank normalising its own groups; one: the gated norm's statistic spans both ranks and is divided by the group's
-full width), with the NCCL-style and peer-memory all-reduce and with the branch-chains schedule on rank 0; and
+full width), with the NCCL-style and peer-memory all-reduce, with the branch-chains schedule on rank 0 and with
+the deferred norm statistic on rank 1 (each alone and both together); and
 the prefill of ragged sequences in the same layouts against the single-rank prefill."""
 import multiprocessing as mp
 import os
@@ -48,7 +49,8 @@ def _worker(rank, world, port, cases, q):
         groups = init_groups(backend="gloo", timeout_s=120)
         cpu = torch.device("cpu")
         res = {}
-        for groups_n, mode, impl, chains in cases:
+        for case in cases:
+            groups_n, mode, impl, chains, defer = (*case, False)[:5]
             dims = DIMS.replace(n_groups=groups_n)
             full = random_layer(dims, SEED)
             h = input_hidden(SEED, B, dims.hidden, cpu)
@@ -61,8 +63,10 @@ def _worker(rank, world, port, cases, q):
             plan = plan_for(mode, rank, world, dims)
             layer = L.ParallelHybridLayer(plan, shard_to_device(full, plan, dims, cpu), dims, groups,
                                           alloc_and_fill(plan, dims, ctx, SEED, cpu), ctx, cpu, overlap_branches=False,
-                                          ar_impl=impl, branch_chains=chains)
-            res[(groups_n, mode, impl, chains)] = (layer.step(h).float().numpy().copy(), ref)
+                                          ar_impl=impl, branch_chains=chains, defer_norm=defer)
+            if chains and defer:  # both schedules engaged: the attention chain on rank 0, the deferral on rank 1
+                assert layer.chains if rank == 0 else layer.ssm.defer, (case, rank)
+            res[case] = (layer.step(h).float().numpy().copy(), ref)
         # prefill of two fresh ragged sequences in the same layouts (NCCL-style collectives, as prefill runs)
         from multi_modal_parallelism_b200.state import alloc_states, decode_ctx_after, make_prefill_ctx
 
@@ -88,8 +92,8 @@ def _worker(rank, world, port, cases, q):
 
 def test_mix_layout_matches_the_single_rank_layer():
     cases = [(1, "mix3", "nccl", False), (1, "mix5", "p2p", False), (1, "mix3", "p2p_fused", False),
-             (2, "mix4", "nccl", False), (1, "mix3", "nccl", True), (1, "split11", "nccl", False),
-             (1, "tp4_fused", "nccl", False)]
+             (2, "mix4", "nccl", False), (1, "mix3", "nccl", True), (1, "mix3", "nccl", True, True),
+             (1, "mix5", "nccl", False, True), (1, "split11", "nccl", False), (1, "tp4_fused", "nccl", False)]
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

@@ -165,7 +165,8 @@ def test_branch_chains_schedule(world, mode, extra, tmp_path):
 
 @pytest.mark.run_last
 @pytest.mark.skipif(ngpu() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("extra", [(), ("--ar-impl", "p2p"), ("--ar-impl", "p2p_fused"), ("--branch-chains",)])
+@pytest.mark.parametrize("extra", [(), ("--ar-impl", "p2p"), ("--ar-impl", "p2p_fused"), ("--branch-chains",),
+                                   ("--branch-chains", "--defer-norm")])
 def test_two_gpu_mix_layout(extra, tmp_path):
     """mix8: rank 0 the attention branch and 8 Mamba-2 heads (fused projections), rank 1 the other 16 heads."""
     run_check(2, "mix8", tmp_path, extra)
