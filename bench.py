@@ -1226,6 +1226,11 @@ def qwen35_arm(args) -> None:
 def main() -> None:
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
+    # NCCL's NVLink SHARP path binds every rank's buffers to one NVLink multicast object; a rank that ends the job
+    # early (a failed phase exits at once) while bound to it can raise NVLink faults on its peers' GPUs. The
+    # collectives here are small ([B, H] bf16 rows), where plain ring / tree kernels are as fast, so NVLS stays
+    # off unless the caller sets the variable itself.
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     if args.workload == "qwen35":
         if args.impl == "reference":
             if rank == 0:
