@@ -728,6 +728,14 @@ int decode_gemm(const void* a, int64_t lda, const void* w, int64_t ldw, int M, i
 
 using namespace mmp;
 
+// The reference-named entry point (F.linear / @ and the layer's scalings, harness/kernels.py:147-154): the same
+// tensor-core kernel without a device error word.
+extern "C" int mmp_gemm_bf16(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
+                             int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
+                             void* stream) {
+  return mmp_gemm_bf16_tc(a, lda, w, ldw, out, ldo, M, N, K, alpha, colscale, addend, ldd, nullptr, stream);
+}
+
 extern "C" int mmp_gemm_bf16_tc(const void* a, int64_t lda, const void* w, int64_t ldw, void* out, int64_t ldo,
                                 int M, int N, int K, float alpha, const float* colscale, const void* addend, int64_t ldd,
                                 int* err, void* stream) {
