@@ -39,6 +39,11 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // 16-byte global accesses with streaming (evict-first) cache hints.
 __device__ __forceinline__ uint4 ld_stream16(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
 __device__ __forceinline__ void st_stream16(void* p, uint4 v) { __stcs(reinterpret_cast<uint4*>(p), v); }
+// L2 prefetch of `bytes` contiguous bytes (16-byte aligned address, bytes a multiple of 16); a hint: no data is
+// returned and nothing completes.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ uint4 ld16(const void* p) { return *reinterpret_cast<const uint4*>(p); }
 __device__ __forceinline__ void st16(void* p, uint4 v) { *reinterpret_cast<uint4*>(p) = v; }
 

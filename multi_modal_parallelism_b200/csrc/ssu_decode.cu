@@ -75,13 +75,29 @@ struct SsuShape {
 template <typename ST, int N, int WARPS>
 __global__ void __launch_bounds__(WARPS * 32) ssu_decode_kernel(const SsuParams P) {
   pdl_trigger();
-  pdl_wait();
   using S = SsuShape<ST, N, WARPS>;
   constexpr int EV = S::EV, VPL = S::VPL, LPR = S::LPR, RPP = S::RPP, R = S::R;
   const int b = blockIdx.z, h = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane / LPR, li = lane % LPR;
   const int row0 = blockIdx.x * S::ROWS_CTA + warp * S::ROWS_WARP + sub;
+
+  // While the previous kernel finishes (the in-projection's epilogue, the conv), ask L2 for this CTA's state rows:
+  // the state is the step's bulk traffic and no kernel before this one in a step writes it. Only a hint: the line
+  // index read here feeds nothing but the prefetch address (lines outside [0, lines) are skipped), and every value
+  // used below is read after the dependency wait.
+  if (li == 0) {
+    const int line = P.idx_in ? P.idx_in[b] : b;
+    if (line >= 0 && line < P.lines && line != P.pad_slot) {
+      const ST* rows = reinterpret_cast<const ST*>(P.state) + line * P.s_line + h * P.s_head;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        const int row = row0 + r * RPP;
+        if (row < P.p) prefetch_l2_bulk(rows + row * P.s_p, N * sizeof(ST));
+      }
+    }
+  }
+  pdl_wait();
 
   const int line_in = P.idx_in ? P.idx_in[b] : b;
   bf16* outp = P.out + b * P.o_b + h * P.o_h;
