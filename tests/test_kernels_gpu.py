@@ -177,6 +177,19 @@ def test_silu_mul():
     close(npf(out), oracle.silu(npf(a)[:, :256] * 0.5) * npf(a)[:, 256:])
 
 
+def test_reference_named_wrappers_silu_and_mul_and_gemm_T():
+    """The harness/kernels.py names a drop-in caller uses: silu_and_mul on a [gate | up] row and gemm_T on the
+    transpose of a row-major weight."""
+    g = torch.Generator().manual_seed(8)
+    a = torch.randn(7, 640, generator=g).to(BF)
+    out = K.silu_and_mul(a.to(DEV))
+    close(npf(out), oracle.silu(npf(a)[:, :320]) * npf(a)[:, 320:])
+    x = torch.randn(5, 256, generator=g).to(BF)
+    w = (torch.randn(384, 256, generator=g) * 0.05).to(BF)
+    y = K.gemm_T(x.to(DEV), w.to(DEV).t())
+    close(npf(y), (x.float() @ w.float().T).numpy())
+
+
 # ----------------------------------------------------------------------------- rope + kv write
 def test_qkv_rope_kv_write():
     g = torch.Generator().manual_seed(11)
